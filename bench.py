@@ -1,0 +1,483 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized decode GEMV on B200.
+
+Headline workload: Q4_K weight, 4096 output rows x 14336 inputs, M = 1 token,
+the shape the decode-GEMV target is quoted on.  One step = one pass over a
+ring of R distinct weight copies (R * 33 MB > 4 x the 126 MB L2, so every
+GEMV streams its weights from HBM), each copy with its own activation row:
+per copy one activation-quantise kernel and one GEMV kernel, replayed from a
+CUDA graph with programmatic dependent launch.
+
+Reported (one JSON line on rank 0):
+  value       whole-job algorithmic GB/s (weights + x + y bytes / time)
+  e2e         same metric through odi_cuda_matmul_host (host x -> device,
+              product, device -> host y, per call), the reference-facing call
+  roofline    the GEMV kernel alone: algorithmic bytes / average launch time
+              (CUDA events around a graph of GEMV-only launches) vs the
+              measured HBM copy bandwidth in MEASURED_PEAKS.json
+  cpu_baseline the oracle's restatement of the reference loop on the host
+              cores (the reference itself throws on Q4_K), bounded sample
+
+Multi-GPU (torchrun, N > 1): weak scaling by output-row sharding -- every
+rank holds a 4096-row shard of each weight (the full matrix has 4096*N
+rows), computes its slice and the slices are all-gathered with NCCL after
+every GEMV.
+
+--impl reference: the reference's CPU loop (oracle restatement for Q4_K,
+since CPUBackend::matmul throws for K-quants) on the host cores, same
+metric, each step one GEMV of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DT_NAME = "Q4_K"
+N_ROWS, K_COLS, M_TOK = 4096, 14336, 1
+L2_BYTES = 126 * 1024 * 1024
+SWEEPS = 64  # passes over the weight ring per step
+
+
+def q4k_bytes(N, K):
+    return N * (K // 256) * 144
+
+
+def algo_bytes(N, K, M):
+    """Algorithmic bytes of one GEMV: packed weights + fp32 x + fp32 y."""
+    return q4k_bytes(N, K) + M * K * 4 + M * N * 4
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def wait_first_sample(self, timeout=5.0):
+        """Block until nvidia-smi is producing samples, then drop the idle ones."""
+        t0 = time.time()
+        while self.proc and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.01)
+        self.lines.clear()
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline
+# ---------------------------------------------------------------------------
+def cpu_port_gemv_time(nthreads: int, budget_s: float, N=N_ROWS, K=K_COLS):
+    """Oracle restatement of the reference loop (matmul_q4_0's structure over
+    Q4_K blocks) on nthreads host threads; returns (seconds per GEMV, reps)."""
+    import oracle as O
+
+    w = O.seeded_weights(N, K, seed=0)
+    b = O.quantize(O.Q4_K, w)
+    x = O.seeded_acts(M_TOK, K, seed=1)
+    O.matmul_ref(O.Q4_K, x, b, N, nthreads)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.matmul_ref(O.Q4_K, x, b, N, nthreads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 200:
+            return el / reps, reps
+
+
+def reference_q4_0_config1(budget_s: float):
+    """The UNMODIFIED reference CPUBackend::matmul (oracle/_ref) on config 1:
+    Q4_0 4096x4096, M=1.  Returns (GB/s, seconds per call, threads used) or None."""
+    import oracle as O
+
+    L = O.ref_lib()
+    if L is None:
+        return None
+    w = O.seeded_weights(4096, 4096, seed=0)
+    b = O.quantize(O.Q4_0, w)
+    x = O.seeded_acts(1, 4096, seed=1)
+    out = np.zeros((1, 4096), np.float32)
+    nproc = os.cpu_count() or 1
+    t1 = L.ref_matmul_time(O.Q4_0, out.ctypes.data, x.ctypes.data, b.ctypes.data, 1, 4096, 4096, nproc, 1)
+    reps = max(1, int(budget_s / max(t1, 1e-4)))
+    t = L.ref_matmul_time(O.Q4_0, out.ctypes.data, x.ctypes.data, b.ctypes.data, 1, 4096, 4096, nproc, reps)
+    per = t / reps
+    gb = (b.nbytes + 4096 * 4 + 4096 * 4) / per / 1e9
+    # parallel_for runs serially when M < 4 * threads (cpu_backend.cpp:149)
+    return gb, per, 1 if 1 < 4 * nproc else nproc
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    nthreads = os.cpu_count() or 1
+    step_bytes = algo_bytes(N_ROWS, K_COLS, M_TOK)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t = _one_port_gemv(nthreads)
+        if i >= args.warmup:
+            times.append(t)
+    tmed = sum(times) / len(times)
+    value = step_bytes / tmed / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(tmed * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(workload_config(max(4, -(-4 * L2_BYTES // q4k_bytes(N_ROWS, K_COLS))), args.gpus),
+                       act_mode="f32 (the reference's arithmetic)",
+                       reference_step="one GEMV of the workload on the host cores"),
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": nthreads, "kind": "port",
+                         "sample": "one Q4_K 4096x14336 M=1 GEMV per step (oracle restatement of the "
+                                   "reference block loop; CPUBackend::matmul throws for K-quants)"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+_PORT = {}
+
+
+def _one_port_gemv(nthreads):
+    import oracle as O
+
+    if not _PORT:
+        w = O.seeded_weights(N_ROWS, K_COLS, seed=0)
+        _PORT["b"] = O.quantize(O.Q4_K, w)
+        _PORT["x"] = O.seeded_acts(M_TOK, K_COLS, seed=1)
+    t0 = time.perf_counter()
+    O.matmul_ref(O.Q4_K, _PORT["x"], _PORT["b"], N_ROWS, nthreads)
+    return time.perf_counter() - t0
+
+
+METRIC = "Q4_K decode GEMV HBM GB/s (4096x14336, M=1)"
+
+
+def workload_config(R, world):
+    return {
+        "workload": f"Q4_K GEMV {N_ROWS}x{K_COLS} (out x in), M={M_TOK}; a step = {SWEEPS} passes over a "
+                    f"ring of {R} weight copies",
+        "dtype": DT_NAME, "N_per_gpu": N_ROWS, "N_total": N_ROWS * world, "K": K_COLS, "M": M_TOK,
+        "ring_copies": R, "l2": "inputs larger than L2: each step streams the whole ring "
+                                 f"({R} x {q4k_bytes(N_ROWS, K_COLS) / 1e6:.1f} MB > 126 MB L2)",
+        "act_mode": "q8 (activations quantised to Q8_0, int8 dp4a dots, fp32 scales)",
+        "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+    }
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import ctypes
+
+    import torch
+
+    import odiengine_b200 as ob
+
+    torch.cuda.set_device(local_rank)
+    ob.init(local_rank)
+    L = ob.lib()
+    dev = torch.device("cuda", local_rank)
+    dt = ob.ODI_DTYPE_Q4_K
+    N, K, M = N_ROWS, K_COLS, M_TOK
+    wbytes = q4k_bytes(N, K)
+    R = max(4, -(-4 * L2_BYTES // wbytes))  # ring >= 4 x L2
+    if args.profile:
+        R = 4
+    stream = torch.cuda.Stream(device=dev)
+    s_ptr = stream.cuda_stream
+
+    # --- weights: seeded N(0, 0.02) fp32 on the device, quantised on the device
+    gen = torch.Generator(device=dev)
+    weights = []
+    with torch.cuda.stream(stream):
+        for r in range(R):
+            gen.manual_seed(1000 * rank + r)
+            wf = torch.empty((N, K), dtype=torch.float32, device=dev).normal_(0.0, 0.02, generator=gen)
+            blocks = ob.quantize_weight(dt, wf, stream=stream)
+            del wf
+            weights.append(ob.repack(dt, blocks, N, K, stream=stream))
+            del blocks
+        gen.manual_seed(7 + rank)
+        xs = [torch.empty((M, K), dtype=torch.float32, device=dev).normal_(0.0, 1.0, generator=gen) for _ in range(R)]
+        ys = [torch.zeros((M, N), dtype=torch.float32, device=dev) for _ in range(R)]
+        gathered = [torch.zeros((world, M, N), dtype=torch.float32, device=dev) for _ in range(R)] if world > 1 else None
+    stream.synchronize()
+    ws_bytes = ob.workspace_bytes(dt, M, N, K, ob.ACT_Q8)
+    ws = ob.new_workspace(ws_bytes, dev)
+
+    if args.profile:
+        # Small case for ncu: three eager products on distinct ring copies
+        # (each weight 33 MB, the ring > L2), nothing else.
+        for r in range(3):
+            ob.check(L.odi_cuda_matmul(dt, weights[r].data_ptr(), xs[r].data_ptr(), ys[r].data_ptr(), M, N, K,
+                                       ob.ACT_Q8, ws.data_ptr(), ws.numel(), 0, s_ptr))
+        stream.synchronize()
+        assert ob.workspace_status(ws) == 0
+        print(json.dumps({"profile": "ok", "launches": 6}))
+        return 0
+
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+
+        pg = dist.group.WORLD
+
+    def step_body(flags=ob.FLAG_PDL, gemv_only=False):
+        for r in range(R):
+            f = flags | (ob.FLAG_REUSE_ACT if gemv_only else 0)
+            ob.check(L.odi_cuda_matmul(dt, weights[r].data_ptr(), xs[r].data_ptr(), ys[r].data_ptr(), M, N, K,
+                                       ob.ACT_Q8, ws.data_ptr(), ws.numel(), f, s_ptr))
+            if world > 1 and not gemv_only:
+                import torch.distributed as dist
+
+                dist.all_gather_into_tensor(gathered[r], ys[r], group=pg)
+
+    # warm up eagerly (sets kernel attributes, NCCL comms) then capture graphs
+    with torch.cuda.stream(stream):
+        step_body()
+        step_body(gemv_only=True)
+    stream.synchronize()
+    g_step = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step, stream=stream):
+        step_body()
+    g_gemv = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_gemv, stream=stream):
+        step_body(gemv_only=True)
+    stream.synchronize()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # --- headline: whole steps.  A step = SWEEPS passes over the ring (graph
+    # replays on `stream`, where the events are recorded).
+    def run_steps(graph, n):
+        with torch.cuda.stream(stream):
+            for _ in range(n * SWEEPS):
+                graph.replay()
+
+    run_steps(g_step, args.warmup)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        clk.wait_first_sample()
+        ev0.record(stream)
+        run_steps(g_step, args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    bytes_step = SWEEPS * R * (world * wbytes + M * K * 4 * world + M * N * 4 * world)
+    value = bytes_step / (ms_step * 1e-3) / 1e9
+
+    # --- roofline: the GEMV kernel alone (activation tiles reused)
+    run_steps(g_gemv, 1)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(5, args.steps)
+    e0.record(stream)
+    run_steps(g_gemv, reps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us_gemv = e0.elapsed_time(e1) * 1e3 / (reps * SWEEPS * R)
+    achieved = algo_bytes(N, K, M) / (us_gemv * 1e-6) / 1e9
+    peak, peak_kind = measured_peak()
+
+    # --- e2e through the host-buffer C ABI (per-call H2D x, product, D2H y)
+    import numpy as _np
+
+    e2e = None
+    if world == 1:
+        hw = []
+        for r in range(R):
+            h = ctypes.c_void_p()
+            # upload once: the device copy made by odi_cuda_weight_upload from host GGUF bytes
+            hb = ob.unpack(dt, weights[r], N, K).cpu().numpy()
+            ob.check(L.odi_cuda_weight_upload(hb.ctypes.data_as(ctypes.c_void_p), dt, N, K, ctypes.byref(h)))
+            hw.append(h)
+        hx = torch.empty((R, M, K), dtype=torch.float32).pin_memory()
+        hy = torch.empty((R, M, N), dtype=torch.float32).pin_memory()
+        hx.copy_(torch.stack([x.cpu() for x in xs]))
+        e2e_steps = max(3, min(args.steps, 20))
+        for _ in range(args.warmup * SWEEPS):
+            for r in range(R):
+                ob.check(L.odi_cuda_matmul_host(hw[r], hx[r].data_ptr(), hy[r].data_ptr(), M, ob.ACT_Q8, s_ptr))
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps * SWEEPS):
+            for r in range(R):
+                ob.check(L.odi_cuda_matmul_host(hw[r], hx[r].data_ptr(), hy[r].data_ptr(), M, ob.ACT_Q8, s_ptr))
+        el = (time.perf_counter() - t0) / e2e_steps
+        e2e = {"value": round(bytes_step / el / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": SWEEPS * R * M * K * 4, "d2h_bytes_per_step": SWEEPS * R * M * N * 4,
+               "steps": e2e_steps,
+               "ms_per_step": round(el * 1e3, 4),
+               "call": "odi_cuda_matmul_host per weight (pinned host x/y, synchronous per call)"}
+        ref_y = ys[-1].cpu().numpy()
+        _np.testing.assert_allclose(hy[-1].numpy(), ref_y, rtol=0, atol=0)
+        for h in hw:
+            L.odi_cuda_weight_free(h)
+
+    # --- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    ref_cfg1 = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        nth = os.cpu_count() or 1
+        per, reps_c = cpu_port_gemv_time(nth, args.cpu_budget)
+        cpu = {"value": round(algo_bytes(N, K, M) / per / 1e9, 4), "unit": "GB/s", "cores": nth, "kind": "port",
+               "sample": f"{reps_c} Q4_K {N}x{K} M=1 GEMVs on {nth} threads (oracle restatement of the "
+                         "reference loop; the reference throws on K-quants)"}
+        r1 = reference_q4_0_config1(min(5.0, args.cpu_budget))
+        if r1:
+            ref_cfg1 = {"value": round(r1[0], 4), "unit": "GB/s", "ms_per_call": round(r1[1] * 1e3, 3),
+                        "threads_used": r1[2], "kind": "reference",
+                        "sample": "unmodified CPUBackend::matmul, Q4_0 4096x4096 M=1 (config 1)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4_k weights x q8_0 activations (int8 dp4a, fp32 accumulate)", "data": "synthetic",
+            "config": workload_config(R, world),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(),
+                         "kernel": "qgemv_kernel<Q4_K,1,false>", "us_per_launch": round(us_gemv, 3),
+                         "algorithmic_bytes_per_launch": algo_bytes(N, K, M), "peak_kind": peak_kind},
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "reference_cpu_config1": ref_cfg1,
+            "clocks": clk.summary(),
+            "gpu_launches": args.steps * SWEEPS * R * 2,
+        }
+        print(json.dumps(line), flush=True)
+    del g_step, g_gemv
+    return 0
+
+
+def traffic_per_launch():
+    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "qgemv_q4k_4096x14336_m1.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="small case for ncu: 3 products, no timing")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

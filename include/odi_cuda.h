@@ -1,0 +1,181 @@
+/*
+ * odi_cuda.h -- C ABI of the B200 (sm_100a) quantized matrix-product backend
+ * for ODIEngine.
+ *
+ * Every entry point is plain C: pointers, sizes, int status codes, and an
+ * opaque cudaStream_t passed as void* (NULL = the legacy default stream).
+ * Nothing here throws.  Status codes are odi_error_t values from the
+ * reference's include/odi/odi_error.h:11-48 so the C++ backend can hand them
+ * to the C API unchanged; a thread-local message explains the last failure.
+ *
+ * Weight matrices follow the reference's GGUF convention: a weight of
+ * GGUF shape [K, N] (ne0 = K inputs, ne1 = N outputs) is stored as N output
+ * rows of ceil(K / block) packed blocks (src/compute/cpu/cpu_backend.cpp:804,
+ * 839).  On the device it lives in a "tiled" layout: rows grouped in tiles of
+ * 64, columns in spans of 256, each (tile, span) unit contiguous, so one
+ * bulk copy moves one unit.  The transform is a byte permutation and is
+ * invertible (odi_cuda_unpack).
+ *
+ * dtype ids are odi_dtype_t values (include/odi/odi_types.h:32-49):
+ *   ODI_DTYPE_Q8_0 = 6, ODI_DTYPE_Q4_0 = 7, ODI_DTYPE_Q4_K = 11,
+ *   ODI_DTYPE_Q5_K = 12, ODI_DTYPE_Q6_K = 13.
+ */
+#ifndef ODI_CUDA_H
+#define ODI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: the odi_error_t values (odi_error.h:11-48). */
+enum {
+  ODI_CUDA_OK = 0,
+  ODI_CUDA_ERR_INVALID_ARGUMENT = 2,
+  ODI_CUDA_ERR_OUT_OF_MEMORY = 3,
+  ODI_CUDA_ERR_NOT_IMPLEMENTED = 4,
+  ODI_CUDA_ERR_INVALID_STATE = 5,
+  ODI_CUDA_ERR_OPERATION_FAILED = 6,
+  ODI_CUDA_ERR_UNSUPPORTED_DTYPE = 202,
+  ODI_CUDA_ERR_BACKEND_UNAVAILABLE = 300,
+  ODI_CUDA_ERR_BACKEND_INIT_FAILED = 301,
+  ODI_CUDA_ERR_GPU_OUT_OF_MEMORY = 303
+};
+
+/* Activation modes for odi_cuda_matmul.
+ *   ODI_CUDA_ACT_Q8  -- activations are quantised to Q8_0 first (bit-exact
+ *                       with the GGUF Q8_0 quantiser) and dotted against the
+ *                       weight codes in integer arithmetic; fp32 block scales.
+ *   ODI_CUDA_ACT_F32 -- fp32 activations times the fp32-decoded weights, the
+ *                       arithmetic of the reference's matmul_q4_0 /
+ *                       matmul_q8_0 (cpu_backend.cpp:786-854) up to
+ *                       summation order. */
+enum { ODI_CUDA_ACT_Q8 = 0, ODI_CUDA_ACT_F32 = 1 };
+
+/* Flags for odi_cuda_matmul. */
+enum {
+  /* Launch with programmatic dependent launch: the kernel may start, and
+   * prefetch weights, while earlier kernels on the stream are still running.
+   * Only valid when no kernel still in flight on the stream writes the
+   * weight buffer. */
+  ODI_CUDA_FLAG_PDL = 1,
+  /* Skip staging x: the workspace already holds the activation tiles of this
+   * same x (same M, K and act_mode), written by the previous call that used
+   * it.  Lets projections that share an input (Q/K/V, gate/up) quantise it
+   * once.  d_x is then not read. */
+  ODI_CUDA_FLAG_REUSE_ACT = 2
+};
+
+/* --- device / backend ---------------------------------------------------- */
+
+/* Select and initialise a CUDA device.  Replaces the CPU fallback that
+ * create_backend(ODI_BACKEND_CUDA) returns today (cpu_backend.cpp:1010-1013):
+ * fails with ODI_CUDA_ERR_BACKEND_UNAVAILABLE when there is no usable device
+ * or it is not sm_100. */
+int odi_cuda_init(int device);
+
+/* Number of CUDA devices (0 if none).  Backs is_backend_available
+ * (backend.hpp:150). */
+int odi_cuda_device_count(void);
+
+/* Backend::device_info (backend.hpp:23): "NVIDIA B200 (sm_100, 148 SMs, ...)". */
+int odi_cuda_device_info(char* buf, size_t len);
+
+/* Backend::available_memory / used_memory (backend.hpp:26-27). */
+int odi_cuda_memory_info(size_t* free_bytes, size_t* total_bytes);
+
+/* Backend::supports_dtype (backend.hpp:30): 1 for Q8_0, Q4_0, Q4_K, Q5_K,
+ * Q6_K, else 0. */
+int odi_cuda_supports_dtype(int dtype);
+
+/* Message for the last non-zero status returned on this thread
+ * (odi_get_last_error_message, odi_error.h:55). */
+const char* odi_cuda_last_error(void);
+
+/* Block until all work on `stream` is done (Backend::sync, backend.hpp:130). */
+int odi_cuda_sync(void* stream);
+
+/* --- layout ----------------------------------------------------------------- */
+
+/* Bytes of the GGUF packing of an N x K weight: N * ceil(K/block) * block
+ * bytes (Tensor::nbytes, tensor.cpp:281-288).  -1 for unsupported dtypes. */
+int64_t odi_cuda_gguf_bytes(int dtype, int64_t N, int64_t K);
+
+/* Bytes of the tiled device layout (rows padded to 64, columns to 256). */
+int64_t odi_cuda_tiled_bytes(int dtype, int64_t N, int64_t K);
+
+/* GGUF blocks -> tiled layout and back, both buffers in device memory.
+ * K-quant rows must be whole 256-value super-blocks (K % 256 == 0). */
+int odi_cuda_repack(int dtype, const void* d_gguf, void* d_tiled, int64_t N, int64_t K,
+                    void* stream);
+int odi_cuda_unpack(int dtype, const void* d_tiled, void* d_gguf, int64_t N, int64_t K,
+                    void* stream);
+
+/* --- weights: upload packed blocks to HBM once (gguf_parser.cpp:614-628) ----- */
+
+typedef struct odi_cuda_weight odi_cuda_weight;
+
+/* Copy host GGUF blocks to the device and repack them into the tiled layout.
+ * The returned handle owns the device copy until odi_cuda_weight_free. */
+int odi_cuda_weight_upload(const void* host_blocks, int dtype, int64_t N, int64_t K,
+                           odi_cuda_weight** out);
+int odi_cuda_weight_free(odi_cuda_weight* w);
+/* Device pointer of the tiled bytes, and the weight's shape. */
+const void* odi_cuda_weight_data(const odi_cuda_weight* w);
+int odi_cuda_weight_shape(const odi_cuda_weight* w, int* dtype, int64_t* N, int64_t* K);
+
+/* fp32 weights [N, K] (device) -> GGUF blocks [N][ceil(K/block)] (device).
+ * Q4_0 / Q8_0 are byte-identical to the GGUF quantisers; Q4_K / Q5_K / Q6_K
+ * use this library's own quantisers of the GGML formats.  The reference has
+ * no quantiser (Tensor::to throws for quantized dtypes, tensor.cpp:654-656);
+ * this brings fp32 checkpoints and synthetic models up on the device. */
+int odi_cuda_quantize_weight(int dtype, const float* d_w, void* d_blocks, int64_t N, int64_t K,
+                             void* stream);
+
+/* --- activation quantisation -------------------------------------------------- */
+
+/* x fp32 [M, K] (device) -> GGUF Q8_0 blocks [M][ceil(K/32)] x 34 bytes
+ * (device), bit-exact with the GGUF Q8_0 quantiser: d = amax/127,
+ * q = round-half-away(x / d), d stored as fp16.  A partial last block is
+ * quantised as if zero-padded. */
+int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t K, void* stream);
+
+/* --- the quantized matrix product ------------------------------------------ */
+
+/* Device scratch needed by odi_cuda_matmul for these sizes and mode. */
+size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode);
+
+/* y[M, N] = x[M, K] . dequant(W)^T in fp32 -- Backend::matmul /
+ * quantized_matmul (backend.hpp:38, 114) with a = x, b = W.
+ *   d_w_tiled : tiled weight (odi_cuda_repack / odi_cuda_weight_data)
+ *   d_x, d_y  : device fp32, row-major, contiguous
+ *   d_workspace: at least odi_cuda_matmul_workspace_bytes; it must be zero
+ *     the first time it is used -- every call leaves it ready for the next.
+ *     Calls that share a workspace must not overlap on the GPU.
+ * Asynchronous on `stream`. */
+int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M,
+                    int64_t N, int64_t K, int act_mode, void* d_workspace,
+                    size_t workspace_bytes, int flags, void* stream);
+
+/* Reads and clears the device-side error word of a workspace (kernel waits
+ * that gave up set it).  Synchronises `stream`.  *status = 0 when clean. */
+int odi_cuda_workspace_status(void* d_workspace, int* status, void* stream);
+
+/* Tiled weight -> fp32 [N, K] on the device (Backend::dequantize,
+ * backend.hpp:111; cpu_backend.cpp:625-648). */
+int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t N, int64_t K,
+                        void* stream);
+
+/* Host-buffer form of Backend::matmul as the reference Context calls it
+ * (context.cpp:152, 188-190): h_x [M, K] and h_y [M, N] are host memory;
+ * the call copies x in, runs the product on the weight's device copy,
+ * copies y out and waits.  Uses a library-owned per-device workspace. */
+int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
+                         int act_mode, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,118 @@
+// act.cu -- activation staging kernels.
+//
+// act_quant_q8: fp32 x [M, K] -> Q8_0, one warp per 32-value block.  The
+// arithmetic is the GGUF Q8_0 quantiser's, in IEEE fp32 with no contraction:
+//   amax = max |x|;  d = amax / 127;  id = d ? 1 / d : 0;
+//   q = round-half-away(x * id);  d stored as fp16 (round to nearest even).
+// It writes the span-major activation tiles the GEMV kernels stream (codes,
+// fp32-widened scale, half-block code sums) and/or GGUF Q8_0 blocks.
+//
+// act_pack_f32: fp32 x [M, K] -> span-major fp32 tiles, zero past K.
+#include "internal.h"
+
+namespace odi_cuda {
+
+__global__ void act_quant_q8_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t Kp,
+                                    uint8_t* __restrict__ tiles, uint8_t* __restrict__ blocks) {
+  pdl_wait();  // x may be written by the previous kernel on the stream
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t nbp = Kp / 32;
+  const int64_t nbk = (K + 31) / 32;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < M * nbp; w += nwarps) {
+    const int64_t m = w / nbp, b = w - m * nbp;
+    const int64_t k = b * 32 + lane;
+    const float v = k < K ? x[m * K + k] : 0.0f;
+    float a = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    const float d = __fdiv_rn(a, 127.0f);
+    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+    const int q = (int)roundf(__fmul_rn(v, id));
+    const __half dh = __float2half_rn(d);
+    int s = q;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);  // within 16-lane halves
+    const int s_lo = __shfl_sync(0xffffffffu, s, 0);
+    const int s_hi = __shfl_sync(0xffffffffu, s, 16);
+    if (tiles) {
+      const int64_t kb = b >> 3;
+      const int j = (int)(b & 7);
+      uint8_t* rec = tiles + (kb * M + m) * ACT_Q8_BYTES;
+      rec[j * 32 + lane] = (uint8_t)(int8_t)q;
+      if (lane == 0) {
+        ActRec r;
+        r.d = __half2float(dh);
+        r.s_lo = (short)s_lo;
+        r.s_hi = (short)s_hi;
+        *reinterpret_cast<ActRec*>(rec + 256 + 8 * j) = r;
+      }
+    }
+    if (blocks && b < nbk) {
+      uint8_t* blk = blocks + (m * nbk + b) * 34;
+      blk[2 + lane] = (uint8_t)(int8_t)q;
+      if (lane == 0) {
+        const uint16_t hb = __half_as_ushort(dh);
+        blk[0] = (uint8_t)(hb & 0xFF);
+        blk[1] = (uint8_t)(hb >> 8);
+      }
+    }
+  }
+}
+
+__global__ void act_pack_f32_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t Kp,
+                                    float* __restrict__ tiles) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t total = M * Kp;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    // i enumerates the tile layout: (kb, m, j)
+    const int64_t kb = i / (M * 256);
+    const int64_t rem = i - kb * M * 256;
+    const int64_t m = rem / 256, j = rem & 255;
+    const int64_t k = kb * 256 + j;
+    tiles[i] = k < K ? x[m * K + k] : 0.0f;
+  }
+}
+
+static int grid_for(int64_t threads_needed, int block) {
+  int64_t g = (threads_needed + block - 1) / block;
+  if (g < 1) g = 1;
+  if (g > 148 * 32) g = 148 * 32;
+  return (int)g;
+}
+
+static cudaLaunchConfig_t small_cfg(int grid, bool pdl, cudaStream_t stream, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cfg;
+}
+
+cudaError_t launch_act_quant(const float* x, int64_t M, int64_t K, uint8_t* tiles, uint8_t* blocks,
+                             bool pdl, cudaStream_t stream) {
+  const int64_t Kp = (K + 255) / 256 * 256;
+  const int64_t warps = M * (Kp / 32);
+  if (warps == 0) return cudaSuccess;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = small_cfg(grid_for(warps * 32, 256), pdl, stream, attr);
+  return cudaLaunchKernelEx(&cfg, act_quant_q8_kernel, x, M, K, Kp, tiles, blocks);
+}
+
+cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* tiles, bool pdl,
+                                cudaStream_t stream) {
+  const int64_t Kp = (K + 255) / 256 * 256;
+  if (M * Kp == 0) return cudaSuccess;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = small_cfg(grid_for(M * Kp, 256), pdl, stream, attr);
+  return cudaLaunchKernelEx(&cfg, act_pack_f32_kernel, x, M, K, Kp, tiles);
+}
+
+}  // namespace odi_cuda

@@ -1,0 +1,362 @@
+// capi.cu -- the extern "C" boundary (include/odi_cuda.h).
+//
+// Nothing here throws.  Every entry point returns an odi_error_t code and
+// records a thread-local message; CUDA failures are mapped to
+// ODI_ERROR_GPU_OUT_OF_MEMORY (allocation) or ODI_ERROR_OPERATION_FAILED.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/odi_cuda.h"
+#include "internal.h"
+
+using namespace odi_cuda;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  const int code = (e == cudaErrorMemoryAllocation) ? ODI_CUDA_ERR_GPU_OUT_OF_MEMORY
+                                                    : ODI_CUDA_ERR_OPERATION_FAILED;
+  return fail(code, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define CK(call, what)                         \
+  do {                                         \
+    cudaError_t e_ = (call);                   \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+int num_sms_current() {
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!sms[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    sms[dev] = v;
+  }
+  return sms[dev];
+}
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+struct WsLayout {
+  size_t counters, partial, act, total;
+};
+
+// Workspace: header | activation tiles | fixup counters | fixup partials.
+// The activation tiles come first so their offset depends only on (K, M,
+// mode): calls that share an input x (Q/K/V, gate/up) can reuse them.
+WsLayout ws_layout(const GemvPlan& p, int dt, int64_t M, bool f32) {
+  (void)dt;
+  WsLayout L;
+  L.act = WS_HEADER;
+  L.counters = L.act + align256((size_t)p.KB * (size_t)M * (f32 ? ACT_F32_BYTES : ACT_Q8_BYTES));
+  L.partial = L.counters + align256((size_t)p.G * sizeof(int));
+  L.total = L.partial + align256(gemv_partial_floats(p, (int)M) * sizeof(float));
+  return L;
+}
+
+int check_shape(int dt, int64_t N, int64_t K) {
+  if (!dtype_ok(dt)) return fail(ODI_CUDA_ERR_UNSUPPORTED_DTYPE, "dtype %d is not supported by the CUDA backend", dt);
+  if (N < 1 || K < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid weight shape N=%lld K=%lld", (long long)N, (long long)K);
+  if (block_elems(dt) == 256 && K % 256)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "K-quant rows must be whole 256-value super-blocks (K=%lld)", (long long)K);
+  if ((N + UNIT_ROWS - 1) / UNIT_ROWS * ((K + UNIT_COLS - 1) / UNIT_COLS) > 0x7FFFFFFFLL / 2)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight too large");
+  return ODI_CUDA_OK;
+}
+
+}  // namespace
+
+struct odi_cuda_weight {
+  int dtype;
+  int64_t N, K;
+  void* data;
+  int device;
+};
+
+extern "C" {
+
+const char* odi_cuda_last_error(void) { return g_err.c_str(); }
+
+int odi_cuda_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+int odi_cuda_init(int device) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0)
+    return fail(ODI_CUDA_ERR_BACKEND_UNAVAILABLE, "no CUDA device: %s", e == cudaSuccess ? "count is 0" : cudaGetErrorString(e));
+  if (device < 0 || device >= n)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "device %d out of range (0..%d)", device, n - 1);
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return fail(ODI_CUDA_ERR_BACKEND_UNAVAILABLE, "device %d is sm_%d%d; this backend is built for sm_100a (B200)",
+                device, prop.major, prop.minor);
+  CK(cudaSetDevice(device), "cudaSetDevice");
+  CK(cudaFree(nullptr), "context init");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_device_info(char* buf, size_t len) {
+  if (!buf || !len) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  int dev = 0;
+  CK(cudaGetDevice(&dev), "cudaGetDevice");
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties");
+  snprintf(buf, len, "%s (sm_%d%d, %d SMs, %.1f GiB HBM, L2 %d MiB)", prop.name, prop.major, prop.minor,
+           prop.multiProcessorCount, prop.totalGlobalMem / 1073741824.0, prop.l2CacheSize >> 20);
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_memory_info(size_t* free_bytes, size_t* total_bytes) {
+  size_t f = 0, t = 0;
+  CK(cudaMemGetInfo(&f, &t), "cudaMemGetInfo");
+  if (free_bytes) *free_bytes = f;
+  if (total_bytes) *total_bytes = t;
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_supports_dtype(int dtype) { return dtype_ok(dtype) ? 1 : 0; }
+
+int odi_cuda_sync(void* stream) {
+  CK(cudaStreamSynchronize((cudaStream_t)stream), "cudaStreamSynchronize");
+  return ODI_CUDA_OK;
+}
+
+int64_t odi_cuda_gguf_bytes(int dtype, int64_t N, int64_t K) {
+  if (!dtype_ok(dtype) || N < 0 || K < 0) return -1;
+  const int be = block_elems(dtype);
+  return N * ((K + be - 1) / be) * block_bytes(dtype);
+}
+
+int64_t odi_cuda_tiled_bytes(int dtype, int64_t N, int64_t K) {
+  if (!dtype_ok(dtype) || N < 0 || K < 0) return -1;
+  return ((N + UNIT_ROWS - 1) / UNIT_ROWS) * ((K + UNIT_COLS - 1) / UNIT_COLS) * unit_bytes(dtype);
+}
+
+int odi_cuda_repack(int dtype, const void* d_gguf, void* d_tiled, int64_t N, int64_t K, void* stream) {
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (!d_gguf || !d_tiled) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  CK(launch_repack(dtype, d_gguf, d_tiled, N, K, (cudaStream_t)stream), "repack");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_unpack(int dtype, const void* d_tiled, void* d_gguf, int64_t N, int64_t K, void* stream) {
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (!d_gguf || !d_tiled) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  CK(launch_unpack(dtype, d_tiled, d_gguf, N, K, (cudaStream_t)stream), "unpack");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_weight_upload(const void* host_blocks, int dtype, int64_t N, int64_t K, odi_cuda_weight** out) {
+  if (!out || !host_blocks) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  const int64_t gb = odi_cuda_gguf_bytes(dtype, N, K), tb = odi_cuda_tiled_bytes(dtype, N, K);
+  void* staging = nullptr;
+  void* tiled = nullptr;
+  cudaError_t e = cudaMalloc(&staging, (size_t)gb);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (upload staging)");
+  e = cudaMalloc(&tiled, (size_t)tb);
+  if (e == cudaSuccess) e = cudaMemcpy(staging, host_blocks, (size_t)gb, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = launch_repack(dtype, staging, tiled, N, K, nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(staging);
+  if (e != cudaSuccess) {
+    if (tiled) cudaFree(tiled);
+    return cuda_fail(e, "weight upload");
+  }
+  odi_cuda_weight* w = new (std::nothrow) odi_cuda_weight;
+  if (!w) {
+    cudaFree(tiled);
+    return fail(ODI_CUDA_ERR_OUT_OF_MEMORY, "host allocation failed");
+  }
+  w->dtype = dtype;
+  w->N = N;
+  w->K = K;
+  w->data = tiled;
+  cudaGetDevice(&w->device);
+  *out = w;
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_weight_free(odi_cuda_weight* w) {
+  if (!w) return ODI_CUDA_OK;
+  cudaError_t e = cudaFree(w->data);
+  delete w;
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree");
+  return ODI_CUDA_OK;
+}
+
+const void* odi_cuda_weight_data(const odi_cuda_weight* w) { return w ? w->data : nullptr; }
+
+int odi_cuda_weight_shape(const odi_cuda_weight* w, int* dtype, int64_t* N, int64_t* K) {
+  if (!w) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null weight");
+  if (dtype) *dtype = w->dtype;
+  if (N) *N = w->N;
+  if (K) *K = w->K;
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_quantize_weight(int dtype, const float* d_w, void* d_blocks, int64_t N, int64_t K, void* stream) {
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (!d_w || !d_blocks) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  CK(launch_quant_weights(dtype, d_w, d_blocks, N, K, (cudaStream_t)stream), "quantize_weight");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t K, void* stream) {
+  if (M < 0 || K < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid shape M=%lld K=%lld", (long long)M, (long long)K);
+  if (M == 0) return ODI_CUDA_OK;
+  if (!d_x || !d_blocks) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  CK(launch_act_quant(d_x, M, K, nullptr, (uint8_t*)d_blocks, false, (cudaStream_t)stream), "quantize_q8_0");
+  return ODI_CUDA_OK;
+}
+
+size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode) {
+  if (!dtype_ok(dtype) || M < 1 || N < 1 || K < 1) return 0;
+  const bool f32 = act_mode == ODI_CUDA_ACT_F32;
+  const GemvPlan p = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
+  return ws_layout(p, dtype, M, f32).total;
+}
+
+int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N,
+                    int64_t K, int act_mode, void* d_workspace, size_t workspace_bytes, int flags,
+                    void* stream) {
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (M < 0 || M > (1 << 20)) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M=%lld", (long long)M);
+  if (M == 0) return ODI_CUDA_OK;
+  if (act_mode != ODI_CUDA_ACT_Q8 && act_mode != ODI_CUDA_ACT_F32)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "unknown act_mode %d", act_mode);
+  if (!d_w_tiled || !d_x || !d_y || !d_workspace) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  if (((uintptr_t)d_w_tiled | (uintptr_t)d_workspace) & 15)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight and workspace must be 16-byte aligned");
+  const bool f32 = act_mode == ODI_CUDA_ACT_F32;
+  const bool pdl = (flags & ODI_CUDA_FLAG_PDL) != 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
+  const WsLayout L = ws_layout(plan, dtype, M, f32);
+  if (workspace_bytes < L.total)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, L.total);
+  uint8_t* ws = (uint8_t*)d_workspace;
+  if (!(flags & ODI_CUDA_FLAG_REUSE_ACT)) {
+    if (f32) CK(launch_act_pack_f32(d_x, M, K, (float*)(ws + L.act), pdl, s), "act pack");
+    else CK(launch_act_quant(d_x, M, K, ws + L.act, nullptr, pdl, s), "act quantize");
+  }
+  for (int64_t m0 = 0; m0 < M; m0 += plan.mt) {
+    GemvArgs a;
+    a.w = (const uint8_t*)d_w_tiled;
+    a.act = ws + L.act;
+    a.y = d_y + m0 * N;
+    a.partial = (float*)(ws + L.partial);
+    a.counters = (int*)(ws + L.counters);
+    a.err = (int*)ws;
+    a.N = N;
+    a.M = (int)((M - m0) < plan.mt ? (M - m0) : plan.mt);
+    a.M_total = (int)M;
+    a.m0 = (int)m0;
+    CK(launch_gemv(dtype, f32, plan, a, pdl, s), "qgemv launch");
+  }
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_workspace_status(void* d_workspace, int* status, void* stream) {
+  if (!d_workspace || !status) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  int v = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  CK(cudaMemcpyAsync(&v, d_workspace, sizeof(int), cudaMemcpyDeviceToHost, s), "read error word");
+  CK(cudaStreamSynchronize(s), "sync");
+  if (v) CK(cudaMemsetAsync(d_workspace, 0, sizeof(int), s), "clear error word");
+  CK(cudaStreamSynchronize(s), "sync");
+  *status = v;
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t N, int64_t K, void* stream) {
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (!d_w_tiled || !d_out) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  CK(launch_dequant(dtype, d_w_tiled, d_out, N, K, (cudaStream_t)stream), "dequantize");
+  return ODI_CUDA_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Host-buffer matmul with a library-owned per-device arena.
+// ---------------------------------------------------------------------------
+namespace {
+struct Arena {
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  float* x = nullptr;
+  size_t x_bytes = 0;
+  float* y = nullptr;
+  size_t y_bytes = 0;
+};
+std::mutex g_arena_mu;
+Arena g_arena[64];
+
+cudaError_t grow(void** p, size_t* have, size_t need, bool zero) {
+  if (*have >= need) return cudaSuccess;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *have = 0;
+  cudaError_t e = cudaMalloc(p, need);
+  if (e != cudaSuccess) return e;
+  if (zero) {
+    e = cudaMemset(*p, 0, need);
+    if (e != cudaSuccess) return e;
+  }
+  *have = need;
+  return cudaSuccess;
+}
+}  // namespace
+
+extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
+                                    int act_mode, void* stream) {
+  if (!w || !h_x || !h_y) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  if (M < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M");
+  if (M == 0) return ODI_CUDA_OK;
+  int dev = 0;
+  CK(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != w->device) return fail(ODI_CUDA_ERR_INVALID_STATE, "weight lives on device %d, current is %d", w->device, dev);
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  Arena& A = g_arena[dev & 63];
+  const size_t wsb = odi_cuda_matmul_workspace_bytes(w->dtype, M, w->N, w->K, act_mode);
+  CK(grow(&A.ws, &A.ws_bytes, wsb, true), "workspace alloc");
+  CK(grow((void**)&A.x, &A.x_bytes, (size_t)(M * w->K) * sizeof(float), false), "x alloc");
+  CK(grow((void**)&A.y, &A.y_bytes, (size_t)(M * w->N) * sizeof(float), false), "y alloc");
+  cudaStream_t s = (cudaStream_t)stream;
+  CK(cudaMemcpyAsync(A.x, h_x, (size_t)(M * w->K) * sizeof(float), cudaMemcpyHostToDevice, s), "H2D x");
+  int rc = odi_cuda_matmul(w->dtype, w->data, A.x, A.y, M, w->N, w->K, act_mode, A.ws, A.ws_bytes, 0, stream);
+  if (rc) return rc;
+  CK(cudaMemcpyAsync(h_y, A.y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
+  CK(cudaStreamSynchronize(s), "sync");
+  return ODI_CUDA_OK;
+}

@@ -1,0 +1,142 @@
+// common.cuh -- shared device helpers for the sm_100a quantized-matmul backend:
+// the tiled weight layout, the activation tile layout, mbarrier / bulk-copy
+// PTX wrappers with bounded waits, and the device error word.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace odi_cuda {
+
+// odi_dtype_t ids (include/odi/odi_types.h:32-49).
+enum DType : int { Q8_0 = 6, Q4_0 = 7, Q4_K = 11, Q5_K = 12, Q6_K = 13 };
+
+// ----------------------------------------------------------------------------
+// Tiled weight layout.  A unit = 64 output rows x 256 input columns.  Each
+// unit is 64 row slices of SLICE bytes followed by a tail plane:
+//   Q4_0 slice 144 B: d[8] fp16, qs[8][16]           (8 GGUF blocks)
+//   Q8_0 slice 272 B: d[8] fp16, qs[8][32]           (8 GGUF blocks)
+//   Q4_K slice 144 B: the GGUF super-block verbatim  (d, dmin, scales[12], qs[128])
+//   Q5_K slice 176 B: the GGUF super-block verbatim  (d, dmin, scales[12], qh[32], qs[128])
+//   Q6_K slice 208 B: scales[16], ql[128], qh[64]; tail plane d[64] fp16
+// Units are stored tile-major: unit (g, kb) at (g * KB + kb) * UNIT_BYTES.
+// Rows >= N and blocks past the end of a row are zero bytes.
+// ----------------------------------------------------------------------------
+constexpr int UNIT_ROWS = 64;
+constexpr int UNIT_COLS = 256;
+
+__host__ __device__ constexpr int slice_bytes(int dt) {
+  return dt == Q4_0 ? 144 : dt == Q8_0 ? 272 : dt == Q4_K ? 144 : dt == Q5_K ? 176 : dt == Q6_K ? 208 : 0;
+}
+__host__ __device__ constexpr int unit_bytes(int dt) {
+  return slice_bytes(dt) * UNIT_ROWS + (dt == Q6_K ? 2 * UNIT_ROWS : 0);
+}
+__host__ __device__ constexpr int block_elems(int dt) {
+  return (dt == Q4_0 || dt == Q8_0) ? 32 : (dt == Q4_K || dt == Q5_K || dt == Q6_K) ? 256 : 0;
+}
+__host__ __device__ constexpr int block_bytes(int dt) {
+  return dt == Q4_0 ? 18 : dt == Q8_0 ? 34 : dt == Q4_K ? 144 : dt == Q5_K ? 176 : dt == Q6_K ? 210 : 0;
+}
+inline bool dtype_ok(int dt) { return dt == Q4_0 || dt == Q8_0 || dt == Q4_K || dt == Q5_K || dt == Q6_K; }
+
+// ----------------------------------------------------------------------------
+// Activation tile layout (device scratch written by the activation kernels).
+// For span kb and token m, a record of ACT_Q8_BYTES:
+//   xq[256] int8  then  8 x {float d; int16 s_lo; int16 s_hi}
+// (d = the fp16 Q8_0 scale widened to fp32; s_lo / s_hi = sums of the codes
+// of the first / second 16 values of the 32-value block).  Records are
+// stored span-major: offset (kb * M + m) * ACT_Q8_BYTES, so the M tokens of
+// one span are one contiguous copy.  The fp32 form (ACT_F32_BYTES = 1024)
+// holds the 256 fp32 values, zero past K.
+// ----------------------------------------------------------------------------
+constexpr int ACT_Q8_BYTES = 320;
+constexpr int ACT_F32_BYTES = 1024;
+
+struct ActRec {
+  float d;
+  short s_lo;
+  short s_hi;
+};
+
+// ----------------------------------------------------------------------------
+// Workspace header.  The first 256 bytes of every matmul workspace:
+//   int error word (set by kernels whose bounded waits gave up), padding.
+// Then the fixup counters (one int per row tile), then fp32 partial sums,
+// then the activation tiles.
+// ----------------------------------------------------------------------------
+constexpr int WS_HEADER = 256;
+enum : int { ERR_FULL_WAIT = 1, ERR_EMPTY_WAIT = 2, ERR_DRAIN_WAIT = 4 };
+
+// ~1 s at the B200's clock: far beyond any legitimate wait in these kernels.
+constexpr long long WAIT_BUDGET_CYCLES = 2000000000LL;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete, giving up after
+// WAIT_BUDGET_CYCLES.  On give-up, ORs `code` into the error word and
+// returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > WAIT_BUDGET_CYCLES) {
+      if (err) atomicOr(err, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+// One bulk copy global -> this CTA's shared memory, completing on `bar`.
+// No multicast.  dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Programmatic dependent launch controls (no-ops when not launched with PDL).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+}  // namespace odi_cuda

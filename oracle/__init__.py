@@ -1,0 +1,221 @@
+"""CPU oracle for the quantized matrix product -- TEST INFRASTRUCTURE ONLY.
+
+Thin ctypes bindings over two checker libraries:
+
+* ``liboracle.so`` -- this project's C restatement (odi_oracle.c) of the
+  reference path: the fp32 block loops of ``CPUBackend::matmul_q4_0`` /
+  ``matmul_q8_0`` (src/compute/cpu/cpu_backend.cpp:786-854), the same loop
+  order for Q4_K/Q5_K/Q6_K, the Q4_0/Q8_0 quantisers of gguf 0.19.0, the Q8_0
+  activation quantiser, the Q8-activation integer dot and error bounds, and
+  the tiled device layout.
+* ``_ref/libodi_ref.so`` -- the reference's own, unmodified CPU backend
+  (cpu_backend.cpp + tensor.cpp) behind ref_harness.cpp.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's cpu_baseline leg use
+this package; the product path never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+Q8_0, Q4_0, Q4_K, Q5_K, Q6_K = 6, 7, 11, 12, 13
+DTYPES = {"Q8_0": Q8_0, "Q4_0": Q4_0, "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K}
+BLOCK_ELEMS = {Q8_0: 32, Q4_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+BLOCK_BYTES = {Q8_0: 34, Q4_0: 18, Q4_K: 144, Q5_K: 176, Q6_K: 210}
+
+_lib = None
+_ref = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+
+
+def build() -> None:
+    """Compile liboracle.so (and _ref when the reference tree is present)."""
+    import subprocess
+
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = ctypes.CDLL(path)
+        L.orc_fp16_to_fp32.restype = ctypes.c_float
+        L.orc_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+        L.orc_fp16_to_fp32_ref.restype = ctypes.c_float
+        L.orc_fp16_to_fp32_ref.argtypes = [ctypes.c_uint16]
+        L.orc_fp32_to_fp16.restype = ctypes.c_uint16
+        L.orc_fp32_to_fp16.argtypes = [ctypes.c_float]
+        L.orc_row_bytes.restype = _i64
+        L.orc_row_bytes.argtypes = [ctypes.c_int, _i64]
+        L.orc_quantize.argtypes = [ctypes.c_int, _vp, _i64, _i64, _vp]
+        L.orc_dequantize.argtypes = [ctypes.c_int, _vp, _i64, _i64, _vp, ctypes.c_int]
+        L.orc_matmul_ref.argtypes = [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_int]
+        L.orc_quantize_q8_0_act.argtypes = [_vp, _i64, _i64, _vp]
+        L.orc_quantize_act_planes.argtypes = [_vp, _i64, _i64, _vp, _vp]
+        L.orc_matmul_q8act.argtypes = [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]
+        L.orc_fp32_bound.argtypes = [ctypes.c_int, _vp, _vp, _i64, _i64, _i64, _vp]
+        L.orc_tiled_bytes.restype = _i64
+        L.orc_tiled_bytes.argtypes = [ctypes.c_int, _i64, _i64]
+        L.orc_unit_bytes.restype = _i64
+        L.orc_unit_bytes.argtypes = [ctypes.c_int]
+        L.orc_repack.argtypes = [ctypes.c_int, _vp, _vp, _i64, _i64]
+        L.orc_unpack.argtypes = [ctypes.c_int, _vp, _vp, _i64, _i64]
+        _lib = L
+    return _lib
+
+
+def ref_lib():
+    """The unmodified reference CPU backend, or None if it was not built."""
+    global _ref
+    if _ref is None:
+        path = os.path.join(HERE, "_ref", "libodi_ref.so")
+        if not os.path.exists(path):
+            return None
+        L = ctypes.CDLL(path)
+        L.ref_matmul.argtypes = [ctypes.c_int, _vp, _vp, _vp, ctypes.c_longlong,
+                                 ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int]
+        L.ref_matmul_time.restype = ctypes.c_double
+        L.ref_matmul_time.argtypes = L.ref_matmul.argtypes + [ctypes.c_int]
+        L.ref_last_error.restype = ctypes.c_char_p
+        _ref = L
+    return _ref
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_vp)
+
+
+def row_bytes(dtype: int, K: int) -> int:
+    return int(lib().orc_row_bytes(dtype, K))
+
+
+def quantize(dtype: int, w: np.ndarray) -> np.ndarray:
+    """fp32 [N, K] -> GGUF blocks uint8 [N, row_bytes]."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    out = np.zeros((N, row_bytes(dtype, K)), dtype=np.uint8)
+    rc = lib().orc_quantize(dtype, _p(w), N, K, _p(out))
+    if rc:
+        raise ValueError(f"orc_quantize failed ({rc})")
+    return out
+
+
+def dequantize(dtype: int, blocks: np.ndarray, N: int, K: int, ref_fp16: bool = False) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.zeros((N, K), dtype=np.float32)
+    rc = lib().orc_dequantize(dtype, _p(blocks), N, K, _p(out), int(ref_fp16))
+    if rc:
+        raise ValueError(f"orc_dequantize failed ({rc})")
+    return out
+
+
+def matmul_ref(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int, nthreads: int = 1) -> np.ndarray:
+    """Restated reference product: out[M,N] = x[M,K] . dequant(W)^T."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    out = np.zeros((M, N), dtype=np.float32)
+    rc = lib().orc_matmul_ref(dtype, _p(out), _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, nthreads)
+    if rc:
+        raise ValueError(f"orc_matmul_ref failed ({rc})")
+    return out
+
+
+def matmul_reference_impl(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int, nthreads: int = 1) -> np.ndarray:
+    """The reference's own CPUBackend::matmul (oracle/_ref).  Raises
+    RuntimeError with the reference's message when it throws."""
+    L = ref_lib()
+    if L is None:
+        raise FileNotFoundError("oracle/_ref/libodi_ref.so not built")
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    out = np.zeros((M, N), dtype=np.float32)
+    rc = L.ref_matmul(dtype, _p(out), _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, nthreads)
+    if rc:
+        raise RuntimeError(L.ref_last_error().decode())
+    return out
+
+
+def quantize_q8_0_act(x: np.ndarray) -> np.ndarray:
+    """fp32 [M, K] -> Q8_0 blocks uint8 [M, ceil(K/32)*34]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    out = np.zeros((M, (K + 31) // 32 * 34), dtype=np.uint8)
+    lib().orc_quantize_q8_0_act(_p(x), M, K, _p(out))
+    return out
+
+
+def quantize_act_planes(x: np.ndarray):
+    """fp32 [M, K] -> (xq int8 [M, Kp], xs records uint8 [M, Kp/32, 8])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    Kp = (K + 255) // 256 * 256
+    xq = np.zeros((M, Kp), dtype=np.int8)
+    xs = np.zeros((M, Kp // 32, 8), dtype=np.uint8)
+    lib().orc_quantize_act_planes(_p(x), M, K, _p(xq), _p(xs))
+    return xq, xs
+
+
+def matmul_q8act(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int, with_mag: bool = False):
+    """Q8-activation product and its bound against the exact real product.
+    With with_mag, also the sum of |block terms| (for fp32 reordering bounds)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    out = np.zeros((M, N), dtype=np.float32)
+    bound = np.zeros((M, N), dtype=np.float32)
+    mag = np.zeros((M, N), dtype=np.float32)
+    rc = lib().orc_matmul_q8act(dtype, _p(out), _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, _p(bound), _p(mag))
+    if rc:
+        raise ValueError(f"orc_matmul_q8act failed ({rc})")
+    return (out, bound, mag) if with_mag else (out, bound)
+
+
+def fp32_bound(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    bound = np.zeros((M, N), dtype=np.float32)
+    rc = lib().orc_fp32_bound(dtype, _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, _p(bound))
+    if rc:
+        raise ValueError(f"orc_fp32_bound failed ({rc})")
+    return bound
+
+
+def tiled_bytes(dtype: int, N: int, K: int) -> int:
+    return int(lib().orc_tiled_bytes(dtype, N, K))
+
+
+def repack(dtype: int, blocks: np.ndarray, N: int, K: int) -> np.ndarray:
+    out = np.zeros(tiled_bytes(dtype, N, K), dtype=np.uint8)
+    rc = lib().orc_repack(dtype, _p(np.ascontiguousarray(blocks)), _p(out), N, K)
+    if rc:
+        raise ValueError(f"orc_repack failed ({rc})")
+    return out
+
+
+def unpack(dtype: int, tiled: np.ndarray, N: int, K: int) -> np.ndarray:
+    out = np.zeros((N, row_bytes(dtype, K)), dtype=np.uint8)
+    rc = lib().orc_unpack(dtype, _p(np.ascontiguousarray(tiled)), _p(out), N, K)
+    if rc:
+        raise ValueError(f"orc_unpack failed ({rc})")
+    return out
+
+
+def seeded_weights(N: int, K: int, seed: int = 0, std: float = 0.02) -> np.ndarray:
+    """W ~ N(0, std) fp32 [N, K] from numpy default_rng(seed)."""
+    return np.random.default_rng(seed).normal(0.0, std, (N, K)).astype(np.float32)
+
+
+def seeded_acts(M: int, K: int, seed: int = 1) -> np.ndarray:
+    """x ~ N(0, 1) fp32 [M, K] from numpy default_rng(seed)."""
+    return np.random.default_rng(seed).normal(0.0, 1.0, (M, K)).astype(np.float32)

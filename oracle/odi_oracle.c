@@ -1,0 +1,806 @@
+/*
+ * odi_oracle.c -- CPU restatement of ODIEngine's quantized matrix product.
+ * TEST INFRASTRUCTURE ONLY (the checker; never linked into the product).
+ * See odi_oracle.h for what is restated and where each piece comes from.
+ */
+#include "odi_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------- */
+/* fp16 <-> fp32                                                              */
+/* ------------------------------------------------------------------------- */
+
+static float bits_to_f32(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+static uint32_t f32_to_bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+/* IEEE binary16 -> binary32, exact for every code. */
+float orc_fp16_to_fp32(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1Fu;
+  uint32_t mant = h & 0x3FFu;
+  if (exp == 0) {
+    /* zero or subnormal: value = mant * 2^-24, exact in fp32 */
+    float v = (float)mant * (1.0f / 16777216.0f);
+    return sign ? -v : v;
+  }
+  if (exp == 31) return bits_to_f32(sign | 0x7F800000u | (mant << 13));
+  return bits_to_f32(sign | ((exp + 112u) << 23) | (mant << 13));
+}
+
+/* The reference converter, cpu_backend.cpp:660-684: correct for normal
+ * numbers, zeros, inf and NaN; subnormals take the normalisation loop but
+ * skip the exponent rebias, so they come out wrong.  Restated so the oracle
+ * reproduces the reference bit for bit on every code. */
+float orc_fp16_to_fp32_ref(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (uint32_t)(h & 0x7C00u) >> 10;
+  uint32_t mant = (uint32_t)(h & 0x03FFu);
+  if (exp == 0) {
+    if (mant == 0) return bits_to_f32(sign);
+    exp = 1;
+    while ((mant & 0x400u) == 0) {
+      mant <<= 1;
+      exp--;
+    }
+    mant &= 0x3FFu;
+  } else if (exp == 31) {
+    exp = 255;
+  } else {
+    exp = exp + 127 - 15;
+  }
+  return bits_to_f32(sign | (exp << 23) | (mant << 13));
+}
+
+/* binary32 -> binary16, round to nearest even (numpy astype(float16)). */
+uint16_t orc_fp32_to_fp16(float f) {
+  uint32_t x = f32_to_bits(f);
+  uint32_t sign = (x >> 16) & 0x8000u;
+  uint32_t exp = (x >> 23) & 0xFFu;
+  uint32_t mant = x & 0x7FFFFFu;
+  if (exp == 255) return (uint16_t)(sign | 0x7C00u | (mant ? (0x200u | (mant >> 13)) : 0));
+  int e = (int)exp - 127 + 15;
+  if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+  if (e <= 0) {
+    if (e < -10) return (uint16_t)sign;
+    uint32_t m = mant | 0x800000u;
+    int shift = 14 - e; /* 24-bit significand -> subnormal field */
+    uint32_t q = m >> shift;
+    uint32_t rem = m & ((1u << shift) - 1);
+    uint32_t half = 1u << (shift - 1);
+    if (rem > half || (rem == half && (q & 1u))) q++;
+    return (uint16_t)(sign | q);
+  }
+  uint32_t q = ((uint32_t)e << 10) | (mant >> 13);
+  uint32_t rem = mant & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) q++;
+  return (uint16_t)(sign | q);
+}
+
+static uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+static void wr16(uint8_t* p, uint16_t v) {
+  p[0] = (uint8_t)(v & 0xFF);
+  p[1] = (uint8_t)(v >> 8);
+}
+
+typedef float (*cvt_fn)(uint16_t);
+
+/* ------------------------------------------------------------------------- */
+/* Type table: GGUF block sizes (gguf_types.hpp:167-223, tensor.cpp:42-62)    */
+/* ------------------------------------------------------------------------- */
+
+int orc_block_elems(int dtype) {
+  switch (dtype) {
+    case ORC_Q8_0: case ORC_Q4_0: case ORC_Q4_1: case ORC_Q5_0: case ORC_Q5_1: return 32;
+    case ORC_Q4_K: case ORC_Q5_K: case ORC_Q6_K: return 256;
+    default: return 0;
+  }
+}
+
+int orc_block_bytes(int dtype) {
+  switch (dtype) {
+    case ORC_Q8_0: return 34;
+    case ORC_Q4_0: return 18;
+    case ORC_Q4_1: return 20;
+    case ORC_Q5_0: return 22;
+    case ORC_Q5_1: return 24;
+    case ORC_Q4_K: return 144;
+    case ORC_Q5_K: return 176;
+    case ORC_Q6_K: return 210;
+    default: return 0;
+  }
+}
+
+static int supported(int dtype) {
+  return dtype == ORC_Q8_0 || dtype == ORC_Q4_0 || dtype == ORC_Q4_K || dtype == ORC_Q5_K ||
+         dtype == ORC_Q6_K;
+}
+
+int64_t orc_row_bytes(int dtype, int64_t K) {
+  int be = orc_block_elems(dtype);
+  if (!be) return -1;
+  return ((K + be - 1) / be) * orc_block_bytes(dtype);
+}
+
+/* ------------------------------------------------------------------------- */
+/* Block decoders.  One 32- or 256-element block -> fp32, in the arithmetic    */
+/* order of the reference (Q4_0, Q8_0) or of gguf 0.19.0 dequantize (K-quants) */
+/* ------------------------------------------------------------------------- */
+
+/* Q4_0: value = (q - 8) * d   (cpu_backend.cpp:693-700, 808-811) */
+static void dec_q4_0(const uint8_t* blk, float* out, cvt_fn cvt) {
+  float d = cvt(rd16(blk));
+  const uint8_t* qs = blk + 2;
+  for (int j = 0; j < 16; ++j) {
+    out[j] = (float)((qs[j] & 0x0F) - 8) * d;
+    out[j + 16] = (float)((qs[j] >> 4) - 8) * d;
+  }
+}
+
+/* Q8_0: value = q * d  (cpu_backend.cpp:776-778) */
+static void dec_q8_0(const uint8_t* blk, float* out, cvt_fn cvt) {
+  float d = cvt(rd16(blk));
+  const int8_t* qs = (const int8_t*)(blk + 2);
+  for (int j = 0; j < 32; ++j) out[j] = (float)qs[j] * d;
+}
+
+/* K-quant 6-bit scale/min unpacking (GGML format, 12 bytes for 8 pairs). */
+static void kq_scale_min(const uint8_t* s, int j, int* sc, int* m) {
+  if (j < 4) {
+    *sc = s[j] & 63;
+    *m = s[j + 4] & 63;
+  } else {
+    *sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+    *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+/* Q4_K block: d, dmin (fp16), scales[12], qs[128].  Sub-block j (32 values)
+ * uses qs[32*(j/2) .. +32], low nibbles for even j, high for odd j.
+ * value = (d*sc_j) * q - (dmin*m_j). */
+static void dec_q4_k(const uint8_t* blk, float* out, cvt_fn cvt) {
+  float d = cvt(rd16(blk)), dmin = cvt(rd16(blk + 2));
+  const uint8_t* sc = blk + 4;
+  const uint8_t* qs = blk + 16;
+  for (int j = 0; j < 8; ++j) {
+    int s, m;
+    kq_scale_min(sc, j, &s, &m);
+    float d1 = d * (float)s, m1 = dmin * (float)m;
+    const uint8_t* q = qs + 32 * (j / 2);
+    int sh = (j & 1) ? 4 : 0;
+    for (int l = 0; l < 32; ++l) out[32 * j + l] = d1 * (float)((q[l] >> sh) & 0x0F) - m1;
+  }
+}
+
+/* Q5_K block: d, dmin, scales[12], qh[32], qs[128]; the fifth bit of
+ * sub-block j element l is bit j of qh[l]. */
+static void dec_q5_k(const uint8_t* blk, float* out, cvt_fn cvt) {
+  float d = cvt(rd16(blk)), dmin = cvt(rd16(blk + 2));
+  const uint8_t* sc = blk + 4;
+  const uint8_t* qh = blk + 16;
+  const uint8_t* qs = blk + 48;
+  for (int j = 0; j < 8; ++j) {
+    int s, m;
+    kq_scale_min(sc, j, &s, &m);
+    float d1 = d * (float)s, m1 = dmin * (float)m;
+    const uint8_t* q = qs + 32 * (j / 2);
+    int sh = (j & 1) ? 4 : 0;
+    for (int l = 0; l < 32; ++l) {
+      int v = ((q[l] >> sh) & 0x0F) | (((qh[l] >> j) & 1) << 4);
+      out[32 * j + l] = d1 * (float)v - m1;
+    }
+  }
+}
+
+/* Q6_K block: ql[128], qh[64], scales[16] (int8), d (fp16).  Element e of
+ * half h (e in 0..127): l = e%32, group c = e/32 (0..3);
+ * low 4 bits = ql[64h + l + 32*(c&1)] >> (4*(c>>1)), high 2 bits =
+ * qh[32h + l] >> (2c); scale = scales[e_global/16].  value = (d*sc)*(q-32). */
+static int q6_code(const uint8_t* blk, int e) {
+  const uint8_t* ql = blk;
+  const uint8_t* qh = blk + 128;
+  int h = e / 128, r = e % 128, c = r / 32, l = r % 32;
+  int lo = (ql[64 * h + l + 32 * (c & 1)] >> (4 * (c >> 1))) & 0x0F;
+  int hi = (qh[32 * h + l] >> (2 * c)) & 3;
+  return lo | (hi << 4);
+}
+
+static void dec_q6_k(const uint8_t* blk, float* out, cvt_fn cvt) {
+  const int8_t* sc = (const int8_t*)(blk + 192);
+  float d = cvt(rd16(blk + 208));
+  for (int e = 0; e < 256; ++e) {
+    float ds = d * (float)sc[e / 16];
+    out[e] = ds * (float)(q6_code(blk, e) - 32);
+  }
+}
+
+static void dec_block(int dtype, const uint8_t* blk, float* out, cvt_fn cvt) {
+  switch (dtype) {
+    case ORC_Q4_0: dec_q4_0(blk, out, cvt); break;
+    case ORC_Q8_0: dec_q8_0(blk, out, cvt); break;
+    case ORC_Q4_K: dec_q4_k(blk, out, cvt); break;
+    case ORC_Q5_K: dec_q5_k(blk, out, cvt); break;
+    case ORC_Q6_K: dec_q6_k(blk, out, cvt); break;
+    default: break;
+  }
+}
+
+int orc_dequantize(int dtype, const void* blocks, int64_t N, int64_t K, float* out, int ref_fp16) {
+  if (!supported(dtype) || N < 0 || K < 0) return -1;
+  int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
+  int64_t nb = (K + be - 1) / be;
+  cvt_fn cvt = ref_fp16 ? orc_fp16_to_fp32_ref : orc_fp16_to_fp32;
+  float tmp[256];
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t b = 0; b < nb; ++b) {
+      dec_block(dtype, (const uint8_t*)blocks + (n * nb + b) * bb, tmp, cvt);
+      for (int j = 0; j < be && b * be + j < K; ++j) out[n * K + b * be + j] = tmp[j];
+    }
+  }
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* Quantisers                                                                 */
+/* ------------------------------------------------------------------------- */
+
+/* Round half away from zero (numpy np_roundf in gguf 0.19.0 == C roundf). */
+static float round_away(float v) { return roundf(v); }
+
+/* Q8_0 block, gguf 0.19.0 Q8_0.quantize_blocks: d = amax/127 (fp32),
+ * id = d ? 1/d : 0, q = roundf(x*id), d stored as fp16 (RNE). */
+static void quant_q8_0_block(const float* x, uint8_t* blk) {
+  float amax = 0.0f;
+  for (int j = 0; j < 32; ++j) {
+    float a = fabsf(x[j]);
+    if (a > amax) amax = a;
+  }
+  float d = amax / 127.0f;
+  float id = (d == 0.0f) ? 0.0f : 1.0f / d;
+  wr16(blk, orc_fp32_to_fp16(d));
+  for (int j = 0; j < 32; ++j) blk[2 + j] = (uint8_t)(int8_t)round_away(x[j] * id);
+}
+
+/* Q4_0 block, gguf 0.19.0 Q4_0.quantize_blocks: max = the signed value of
+ * largest magnitude (first on ties), d = max / -8, id = d ? 1/d : 0,
+ * q = min(15, trunc(x*id + 8.5)); element j in the low nibble of byte j,
+ * element j+16 in the high nibble. */
+static void quant_q4_0_block(const float* x, uint8_t* blk) {
+  float amax = -1.0f, mx = 0.0f;
+  for (int j = 0; j < 32; ++j) {
+    float a = fabsf(x[j]);
+    if (a > amax) {
+      amax = a;
+      mx = x[j];
+    }
+  }
+  float d = mx / -8.0f;
+  float id = (d == 0.0f) ? 0.0f : 1.0f / d;
+  wr16(blk, orc_fp32_to_fp16(d));
+  uint8_t q[32];
+  for (int j = 0; j < 32; ++j) {
+    float t = truncf(x[j] * id + 8.5f);
+    int v = (int)t;
+    if (v < 0) v = 0;
+    if (v > 15) v = 15;
+    q[j] = (uint8_t)v;
+  }
+  for (int j = 0; j < 16; ++j) blk[2 + j] = (uint8_t)(q[j] | (q[j + 16] << 4));
+}
+
+static int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+/* Q4_K / Q5_K quantiser (this project's own; the format is GGML's).
+ * Per 32-value sub-block: min mn (clamped to <= 0) and range; scale =
+ * range / levels.  The 8 scales and 8 mins are coded as 6-bit multiples of
+ * the super-block d = max scale / 63 and dmin = max min / 63 (fp16), then
+ * each value is coded against the decoded (fp16-exact) scale and min. */
+static void quant_kq45_block(const float* x, uint8_t* blk, int levels, int five) {
+  float scale[8], mins[8], maxs = 0.0f, maxm = 0.0f;
+  for (int j = 0; j < 8; ++j) {
+    float mn = x[32 * j], mx = x[32 * j];
+    for (int l = 1; l < 32; ++l) {
+      float v = x[32 * j + l];
+      if (v < mn) mn = v;
+      if (v > mx) mx = v;
+    }
+    if (mn > 0.0f) mn = 0.0f;
+    scale[j] = (mx - mn) / (float)levels;
+    mins[j] = -mn;
+    if (scale[j] > maxs) maxs = scale[j];
+    if (mins[j] > maxm) maxm = mins[j];
+  }
+  uint16_t dh = orc_fp32_to_fp16(maxs / 63.0f), mh = orc_fp32_to_fp16(maxm / 63.0f);
+  float dd = orc_fp16_to_fp32(dh), dm = orc_fp16_to_fp32(mh);
+  int ls[8], lm[8];
+  for (int j = 0; j < 8; ++j) {
+    ls[j] = dd > 0.0f ? clampi((int)round_away(scale[j] / dd), 0, 63) : 0;
+    lm[j] = dm > 0.0f ? clampi((int)round_away(mins[j] / dm), 0, 63) : 0;
+  }
+  memset(blk, 0, five ? 176 : 144);
+  wr16(blk, dh);
+  wr16(blk + 2, mh);
+  uint8_t* s = blk + 4;
+  for (int j = 0; j < 4; ++j) {
+    s[j] = (uint8_t)(ls[j] | ((ls[j + 4] >> 4) << 6));
+    s[j + 4] = (uint8_t)(lm[j] | ((lm[j + 4] >> 4) << 6));
+    s[j + 8] = (uint8_t)((ls[j + 4] & 0x0F) | ((lm[j + 4] & 0x0F) << 4));
+  }
+  uint8_t* qh = five ? blk + 16 : NULL;
+  uint8_t* qs = blk + (five ? 48 : 16);
+  for (int j = 0; j < 8; ++j) {
+    float es = dd * (float)ls[j], em = dm * (float)lm[j];
+    for (int l = 0; l < 32; ++l) {
+      int q = 0;
+      if (es > 0.0f) q = clampi((int)round_away((x[32 * j + l] + em) / es), 0, levels);
+      qs[32 * (j / 2) + l] |= (uint8_t)((q & 0x0F) << ((j & 1) ? 4 : 0));
+      if (five) qh[l] |= (uint8_t)(((q >> 4) & 1) << j);
+    }
+  }
+}
+
+/* Q6_K quantiser (own design; GGML format).  16 sub-blocks of 16 values;
+ * per sub-block the signed value of largest magnitude v gives scale v/-32;
+ * scales are coded as int8 multiples of d = max|scale|/127 (fp16); values
+ * as q in [0,63] with value = d*sc*(q-32). */
+static void quant_q6_k_block(const float* x, uint8_t* blk) {
+  float scale[16], amax = 0.0f;
+  for (int j = 0; j < 16; ++j) {
+    float best = -1.0f, v = 0.0f;
+    for (int l = 0; l < 16; ++l) {
+      float a = fabsf(x[16 * j + l]);
+      if (a > best) {
+        best = a;
+        v = x[16 * j + l];
+      }
+    }
+    scale[j] = v / -32.0f;
+    if (fabsf(scale[j]) > amax) amax = fabsf(scale[j]);
+  }
+  uint16_t dh = orc_fp32_to_fp16(amax / 127.0f);
+  float d = orc_fp16_to_fp32(dh);
+  memset(blk, 0, 210);
+  int8_t* sc = (int8_t*)(blk + 192);
+  uint8_t q[256];
+  for (int j = 0; j < 16; ++j) {
+    int s = d > 0.0f ? clampi((int)round_away(scale[j] / d), -128, 127) : 0;
+    sc[j] = (int8_t)s;
+    float es = d * (float)s;
+    for (int l = 0; l < 16; ++l) {
+      int v = 32;
+      if (es != 0.0f) v = clampi((int)round_away(x[16 * j + l] / es), -32, 31) + 32;
+      q[16 * j + l] = (uint8_t)v;
+    }
+  }
+  uint8_t* ql = blk;
+  uint8_t* qh = blk + 128;
+  for (int h = 0; h < 2; ++h) {
+    for (int l = 0; l < 32; ++l) {
+      int q1 = q[128 * h + l], q2 = q[128 * h + l + 32], q3 = q[128 * h + l + 64],
+          q4 = q[128 * h + l + 96];
+      ql[64 * h + l] = (uint8_t)((q1 & 0x0F) | ((q3 & 0x0F) << 4));
+      ql[64 * h + l + 32] = (uint8_t)((q2 & 0x0F) | ((q4 & 0x0F) << 4));
+      qh[32 * h + l] = (uint8_t)((q1 >> 4) | ((q2 >> 4) << 2) | ((q3 >> 4) << 4) | ((q4 >> 4) << 6));
+    }
+  }
+  wr16(blk + 208, dh);
+}
+
+int orc_quantize(int dtype, const float* w, int64_t N, int64_t K, void* out) {
+  if (!supported(dtype) || N < 0 || K < 0) return -1;
+  int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
+  if (be == 256 && K % 256) return -2; /* K-quant rows are whole super-blocks */
+  int64_t nb = (K + be - 1) / be;
+  float tmp[256];
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t b = 0; b < nb; ++b) {
+      for (int j = 0; j < be; ++j) {
+        int64_t k = b * be + j;
+        tmp[j] = k < K ? w[n * K + k] : 0.0f;
+      }
+      uint8_t* blk = (uint8_t*)out + (n * nb + b) * bb;
+      switch (dtype) {
+        case ORC_Q4_0: quant_q4_0_block(tmp, blk); break;
+        case ORC_Q8_0: quant_q8_0_block(tmp, blk); break;
+        case ORC_Q4_K: quant_kq45_block(tmp, blk, 15, 0); break;
+        case ORC_Q5_K: quant_kq45_block(tmp, blk, 31, 1); break;
+        case ORC_Q6_K: quant_q6_k_block(tmp, blk); break;
+      }
+    }
+  }
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* Reference-order fp32 matmul                                                */
+/* ------------------------------------------------------------------------- */
+
+typedef struct {
+  int dtype;
+  float* out;
+  const float* a;
+  const uint8_t* b;
+  int64_t M, K, N, n0, n1;
+} mm_job;
+
+/* For each (m, n): sum over blocks kb of sequential sum += a[k] * w[k], with
+ * the block decoded to fp32 first (matmul_q4_0, cpu_backend.cpp:800-822).
+ * Q8_0 keeps its own expression a * q * d (cpu_backend.cpp:846). */
+static void* mm_worker(void* arg) {
+  mm_job* j = (mm_job*)arg;
+  int be = orc_block_elems(j->dtype), bb = orc_block_bytes(j->dtype);
+  int64_t nb = (j->K + be - 1) / be;
+  float temp[256];
+  for (int64_t m = 0; m < j->M; ++m) {
+    const float* am = j->a + m * j->K;
+    for (int64_t n = j->n0; n < j->n1; ++n) {
+      float sum = 0.0f;
+      for (int64_t kb = 0; kb < nb; ++kb) {
+        const uint8_t* blk = j->b + (n * nb + kb) * bb;
+        int64_t k0 = kb * be, k1 = k0 + be < j->K ? k0 + be : j->K;
+        if (j->dtype == ORC_Q8_0) {
+          float d = orc_fp16_to_fp32_ref(rd16(blk));
+          const int8_t* qs = (const int8_t*)(blk + 2);
+          for (int64_t k = k0; k < k1; ++k) sum += am[k] * (float)qs[k - k0] * d;
+        } else {
+          /* Q4_0 uses the reference's own converter; the K-quants have no
+           * reference code, so their semantics are gguf's IEEE decode. */
+          dec_block(j->dtype, blk, temp,
+                    j->dtype == ORC_Q4_0 ? orc_fp16_to_fp32_ref : orc_fp16_to_fp32);
+          for (int64_t k = k0; k < k1; ++k) sum += am[k] * temp[k - k0];
+        }
+      }
+      j->out[m * j->N + n] = sum;
+    }
+  }
+  return NULL;
+}
+
+int orc_matmul_ref(int dtype, float* out, const float* a, const void* b, int64_t M, int64_t K,
+                   int64_t N, int nthreads) {
+  if (!supported(dtype) || M < 0 || N < 0 || K < 0) return -1;
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > 256) nthreads = 256;
+  if (nthreads > N) nthreads = (int)(N > 0 ? N : 1);
+  mm_job jobs[256];
+  pthread_t th[256];
+  for (int t = 0; t < nthreads; ++t) {
+    jobs[t] = (mm_job){dtype, out, a, (const uint8_t*)b, M, K, N, N * t / nthreads,
+                       N * (t + 1) / nthreads};
+  }
+  if (nthreads == 1) {
+    mm_worker(&jobs[0]);
+    return 0;
+  }
+  for (int t = 0; t < nthreads; ++t) pthread_create(&th[t], NULL, mm_worker, &jobs[t]);
+  for (int t = 0; t < nthreads; ++t) pthread_join(th[t], NULL);
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* Activation quantisation (Q8_0)                                             */
+/* ------------------------------------------------------------------------- */
+
+void orc_quantize_q8_0_act(const float* x, int64_t M, int64_t K, void* blocks) {
+  int64_t nb = (K + 31) / 32;
+  float tmp[32];
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t b = 0; b < nb; ++b) {
+      for (int j = 0; j < 32; ++j) {
+        int64_t k = b * 32 + j;
+        tmp[j] = k < K ? x[m * K + k] : 0.0f;
+      }
+      quant_q8_0_block(tmp, (uint8_t*)blocks + (m * nb + b) * 34);
+    }
+  }
+}
+
+typedef struct {
+  float d;
+  int16_t s_lo;
+  int16_t s_hi;
+} act_rec;
+
+void orc_quantize_act_planes(const float* x, int64_t M, int64_t K, int8_t* xq, void* xs) {
+  int64_t Kp = (K + 255) / 256 * 256, nb = Kp / 32;
+  act_rec* rec = (act_rec*)xs;
+  float tmp[32];
+  uint8_t blk[34];
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t b = 0; b < nb; ++b) {
+      for (int j = 0; j < 32; ++j) {
+        int64_t k = b * 32 + j;
+        tmp[j] = k < K ? x[m * K + k] : 0.0f;
+      }
+      quant_q8_0_block(tmp, blk);
+      int slo = 0, shi = 0;
+      for (int j = 0; j < 32; ++j) {
+        int8_t q = (int8_t)blk[2 + j];
+        xq[m * Kp + b * 32 + j] = q;
+        if (j < 16) slo += q; else shi += q;
+      }
+      rec[m * nb + b].d = orc_fp16_to_fp32(rd16(blk));
+      rec[m * nb + b].s_lo = (int16_t)slo;
+      rec[m * nb + b].s_hi = (int16_t)shi;
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------- */
+/* Q8-activation product and bounds                                           */
+/* ------------------------------------------------------------------------- */
+
+/* Integer codes and fp32 scale/min factors of one weight block, as the CUDA
+ * kernels see them: for each 32-value group g (16-value group for Q6_K) the
+ * value is  A_g * q - B_g  with integer q. */
+typedef struct {
+  int q[256];
+  float A[16];  /* per group scale factor (d, d*sc) */
+  float B[16];  /* per group min factor (8*d for Q4_0, dmin*m for Q4_K/Q5_K) */
+  int gsize;    /* 32 or 16 */
+  int ngroups;
+  int has_min;  /* B term present */
+} wcodes;
+
+static void block_codes(int dtype, const uint8_t* blk, wcodes* c) {
+  memset(c, 0, sizeof(*c));
+  switch (dtype) {
+    case ORC_Q4_0: {
+      float d = orc_fp16_to_fp32(rd16(blk));
+      for (int j = 0; j < 16; ++j) {
+        c->q[j] = blk[2 + j] & 0x0F;
+        c->q[j + 16] = blk[2 + j] >> 4;
+      }
+      c->A[0] = d;
+      c->B[0] = 8.0f * d; /* (q-8)*d = d*q - 8d */
+      c->gsize = 32; c->ngroups = 1; c->has_min = 1;
+      break;
+    }
+    case ORC_Q8_0: {
+      c->A[0] = orc_fp16_to_fp32(rd16(blk));
+      for (int j = 0; j < 32; ++j) c->q[j] = (int8_t)blk[2 + j];
+      c->gsize = 32; c->ngroups = 1; c->has_min = 0;
+      break;
+    }
+    case ORC_Q4_K:
+    case ORC_Q5_K: {
+      float d = orc_fp16_to_fp32(rd16(blk)), dmin = orc_fp16_to_fp32(rd16(blk + 2));
+      int five = dtype == ORC_Q5_K;
+      const uint8_t* qh = blk + 16;
+      const uint8_t* qs = blk + (five ? 48 : 16);
+      for (int j = 0; j < 8; ++j) {
+        int s, m;
+        kq_scale_min(blk + 4, j, &s, &m);
+        c->A[j] = d * (float)s;
+        c->B[j] = dmin * (float)m;
+        for (int l = 0; l < 32; ++l) {
+          int v = (qs[32 * (j / 2) + l] >> ((j & 1) ? 4 : 0)) & 0x0F;
+          if (five) v |= ((qh[l] >> j) & 1) << 4;
+          c->q[32 * j + l] = v;
+        }
+      }
+      c->gsize = 32; c->ngroups = 8; c->has_min = 1;
+      break;
+    }
+    case ORC_Q6_K: {
+      const int8_t* sc = (const int8_t*)(blk + 192);
+      float d = orc_fp16_to_fp32(rd16(blk + 208));
+      for (int j = 0; j < 16; ++j) c->A[j] = d * (float)sc[j];
+      for (int e = 0; e < 256; ++e) c->q[e] = q6_code(blk, e) - 32;
+      c->gsize = 16; c->ngroups = 16; c->has_min = 0;
+      break;
+    }
+  }
+}
+
+int orc_matmul_q8act(int dtype, float* out, const float* a, const void* b, int64_t M, int64_t K,
+                     int64_t N, float* bound, float* mag_out) {
+  if (!supported(dtype) || M < 0 || N < 0 || K < 0) return -1;
+  int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
+  int64_t nb = (K + be - 1) / be;
+  int64_t Kp = (K + 255) / 256 * 256;
+  int8_t* xq = (int8_t*)calloc((size_t)(M * Kp + 1), 1);
+  act_rec* xs = (act_rec*)calloc((size_t)(M * (Kp / 32) + 1), sizeof(act_rec));
+  if (!xq || !xs) {
+    free(xq);
+    free(xs);
+    return -3;
+  }
+  orc_quantize_act_planes(a, M, K, xq, xs);
+  wcodes c;
+  const double u = 1.0 / 16777216.0;
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t m = 0; m < M; ++m) {
+      float y = 0.0f;
+      double mag = 0.0, act_err = 0.0;
+      int64_t terms = 0;
+      for (int64_t kb = 0; kb < nb; ++kb) {
+        block_codes(dtype, (const uint8_t*)b + (n * nb + kb) * bb, &c);
+        for (int g = 0; g < c.ngroups; ++g) {
+          int64_t k0 = kb * be + (int64_t)g * c.gsize;
+          int64_t xb = k0 / 32;
+          const act_rec* r = &xs[m * (Kp / 32) + xb];
+          int isum = 0, xsum = 0;
+          for (int h0 = 0; h0 < c.gsize; h0 += 16) {
+            /* The kernels convert each 16-value partial dot separately, so
+             * the reordering magnitude is summed over 16-value halves. */
+            int ih = 0, xh = 0;
+            for (int l = h0; l < h0 + 16; ++l) {
+              int xv = xq[m * Kp + k0 + l];
+              ih += c.q[g * c.gsize + l] * xv;
+              xh += xv;
+            }
+            isum += ih;
+            xsum += xh;
+            mag += fabs((double)ih * c.A[g] * r->d) + (c.has_min ? fabs((double)xh * c.B[g] * r->d) : 0.0);
+          }
+          float t1 = (float)isum * (c.A[g] * r->d);
+          float t2 = c.has_min ? (float)xsum * (c.B[g] * r->d) : 0.0f;
+          y += t1;
+          y -= t2;
+          terms += 2;
+          if (bound) {
+            /* activation error: |x - q*d_x| <= 0.5*d32 + 127*|d32 - d16|
+             * where d32 is the unrounded scale; bounded by 0.5625*d16. */
+            double dsum = 0.0;
+            for (int l = 0; l < c.gsize && k0 + l < K; ++l) {
+              double w = (double)c.A[g] * c.q[g * c.gsize + l] - (c.has_min ? (double)c.B[g] : 0.0);
+              dsum += fabs(w);
+            }
+            act_err += 0.5625 * (double)r->d * dsum;
+          }
+        }
+      }
+      out[m * N + n] = y;
+      if (mag_out) mag_out[m * N + n] = (float)mag;
+      if (bound) bound[m * N + n] = (float)(act_err + 2.0 * (double)(terms + 8) * u * mag + 1e-30);
+    }
+  }
+  free(xq);
+  free(xs);
+  return 0;
+}
+
+int orc_fp32_bound(int dtype, const float* a, const void* b, int64_t M, int64_t K, int64_t N,
+                   float* bound) {
+  if (!supported(dtype)) return -1;
+  int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
+  int64_t nb = (K + be - 1) / be;
+  const double u = 1.0 / 16777216.0;
+  wcodes c;
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t m = 0; m < M; ++m) {
+      double mag = 0.0;
+      for (int64_t kb = 0; kb < nb; ++kb) {
+        block_codes(dtype, (const uint8_t*)b + (n * nb + kb) * bb, &c);
+        for (int e = 0; e < be && kb * be + e < K; ++e) {
+          int g = e / c.gsize;
+          double w = fabs((double)c.A[g] * c.q[e]) + (c.has_min ? fabs((double)c.B[g]) : 0.0);
+          mag += fabs((double)a[m * K + kb * be + e]) * w;
+        }
+      }
+      bound[m * N + n] = (float)(2.0 * (double)(K + 16) * u * mag + 1e-30);
+    }
+  }
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* Tiled device layout                                                        */
+/*                                                                            */
+/* Rows are grouped in tiles of 64, columns in spans of 256.  One unit =      */
+/* (row tile g, span kb) = 64 row slices of S bytes, then a tail plane.       */
+/* Units are stored g-major: offset = (g * KBu + kb) * unit_bytes.            */
+/*   Q4_0 slice (144 B): d[8] fp16, then qs[8][16]                            */
+/*   Q8_0 slice (272 B): d[8] fp16, then qs[8][32]                            */
+/*   Q4_K slice (144 B): the GGUF block verbatim                              */
+/*   Q5_K slice (176 B): the GGUF block verbatim                              */
+/*   Q6_K slice (208 B): scales[16], ql[128], qh[64]; tail: d[64] fp16        */
+/* Rows >= N and blocks past the row end are zero bytes.                      */
+/* ------------------------------------------------------------------------- */
+
+static int slice_bytes(int dtype) {
+  switch (dtype) {
+    case ORC_Q4_0: return 144;
+    case ORC_Q8_0: return 272;
+    case ORC_Q4_K: return 144;
+    case ORC_Q5_K: return 176;
+    case ORC_Q6_K: return 208;
+    default: return 0;
+  }
+}
+
+int64_t orc_unit_bytes(int dtype) {
+  if (!supported(dtype)) return -1;
+  return (int64_t)slice_bytes(dtype) * ORC_UNIT_ROWS + (dtype == ORC_Q6_K ? 2 * ORC_UNIT_ROWS : 0);
+}
+
+int64_t orc_tiled_bytes(int dtype, int64_t N, int64_t K) {
+  if (!supported(dtype) || N < 0 || K < 0) return -1;
+  int64_t G = (N + ORC_UNIT_ROWS - 1) / ORC_UNIT_ROWS;
+  int64_t KB = (K + ORC_UNIT_COLS - 1) / ORC_UNIT_COLS;
+  return G * KB * orc_unit_bytes(dtype);
+}
+
+/* Copy one row slice between GGUF order (row n, span kb) and the tile.
+ * dir = 0: gguf -> tile, dir = 1: tile -> gguf. */
+static void move_slice(int dtype, uint8_t* row_gguf, int64_t nb_row, int64_t kb, uint8_t* slice,
+                       uint8_t* tail_d, int dir) {
+  int bb = orc_block_bytes(dtype);
+  if (dtype == ORC_Q4_0 || dtype == ORC_Q8_0) {
+    int qb = bb - 2;
+    for (int j = 0; j < 8; ++j) {
+      int64_t b = kb * 8 + j;
+      if (b >= nb_row) break;
+      uint8_t* blk = row_gguf + b * bb;
+      if (dir == 0) {
+        memcpy(slice + 2 * j, blk, 2);
+        memcpy(slice + 16 + qb * j, blk + 2, (size_t)qb);
+      } else {
+        memcpy(blk, slice + 2 * j, 2);
+        memcpy(blk + 2, slice + 16 + qb * j, (size_t)qb);
+      }
+    }
+    return;
+  }
+  uint8_t* blk = row_gguf + kb * bb;
+  if (dtype == ORC_Q4_K || dtype == ORC_Q5_K) {
+    if (dir == 0) memcpy(slice, blk, (size_t)bb);
+    else memcpy(blk, slice, (size_t)bb);
+    return;
+  }
+  /* Q6_K: gguf ql 0..127, qh 128..191, scales 192..207, d 208..209 */
+  if (dir == 0) {
+    memcpy(slice, blk + 192, 16);
+    memcpy(slice + 16, blk, 128);
+    memcpy(slice + 144, blk + 128, 64);
+    memcpy(tail_d, blk + 208, 2);
+  } else {
+    memcpy(blk + 192, slice, 16);
+    memcpy(blk, slice + 16, 128);
+    memcpy(blk + 128, slice + 144, 64);
+    memcpy(blk + 208, tail_d, 2);
+  }
+}
+
+static int tile_walk(int dtype, uint8_t* gguf, uint8_t* tiled, int64_t N, int64_t K, int dir) {
+  if (!supported(dtype) || N < 0 || K < 0) return -1;
+  int be = orc_block_elems(dtype);
+  if (be == 256 && K % 256) return -2;
+  int64_t nb_row = (K + be - 1) / be;
+  int64_t row_bytes = nb_row * orc_block_bytes(dtype);
+  int64_t G = (N + 63) / 64, KB = (K + 255) / 256, ub = orc_unit_bytes(dtype);
+  int sb = slice_bytes(dtype);
+  if (dir == 0) memset(tiled, 0, (size_t)(G * KB * ub));
+  for (int64_t g = 0; g < G; ++g) {
+    for (int64_t kb = 0; kb < KB; ++kb) {
+      uint8_t* unit = tiled + (g * KB + kb) * ub;
+      for (int r = 0; r < 64; ++r) {
+        int64_t n = g * 64 + r;
+        if (n >= N) break;
+        move_slice(dtype, gguf + n * row_bytes, nb_row, kb, unit + (int64_t)r * sb,
+                   unit + 64 * (int64_t)sb + 2 * r, dir);
+      }
+    }
+  }
+  return 0;
+}
+
+int orc_repack(int dtype, const void* gguf, void* tiled, int64_t N, int64_t K) {
+  return tile_walk(dtype, (uint8_t*)gguf, (uint8_t*)tiled, N, K, 0);
+}
+
+int orc_unpack(int dtype, const void* tiled, void* gguf, int64_t N, int64_t K) {
+  return tile_walk(dtype, (uint8_t*)gguf, (uint8_t*)tiled, N, K, 1);
+}

@@ -1,0 +1,169 @@
+"""The oracle, pinned against golden vectors (gguf 0.19.0 and the unmodified
+reference CPU backend) -- CPU only."""
+import numpy as np
+import pytest
+
+import oracle as O
+
+NAMES = {O.Q4_0: "q4_0", O.Q8_0: "q8_0", O.Q4_K: "q4k", O.Q5_K: "q5k", O.Q6_K: "q6k"}
+
+
+def f32eq(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+def test_fp16_ieee_exhaustive(oracle_mod):
+    L = O.lib()
+    codes = np.arange(65536, dtype=np.uint16)
+    want = codes.view(np.float16).astype(np.float32)
+    got = np.array([L.orc_fp16_to_fp32(int(c)) for c in codes], dtype=np.float32)
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    assert same.all()
+
+
+def test_reference_fp16_converter_matches_ieee_on_normals(oracle_mod):
+    """cpu_backend.cpp:660-684 is exact for normal codes and zero, wrong for subnormals."""
+    L = O.lib()
+    codes = np.arange(65536, dtype=np.uint16)
+    exp = (codes >> 10) & 0x1F
+    normal = (exp > 0) & (exp < 31)
+    for c in codes[normal][::97]:
+        assert L.orc_fp16_to_fp32_ref(int(c)) == L.orc_fp16_to_fp32(int(c))
+    sub = codes[(exp == 0) & ((codes & 0x3FF) != 0)]
+    wrong = sum(L.orc_fp16_to_fp32_ref(int(c)) != L.orc_fp16_to_fp32(int(c)) for c in sub)
+    assert wrong == len(sub)  # the documented defect: every subnormal is mis-converted
+
+
+def test_fp32_to_fp16_rne(oracle_mod):
+    L = O.lib()
+    rng = np.random.default_rng(5)
+    v = (rng.normal(0, 1, 20000) * 10.0 ** rng.integers(-9, 5, 20000)).astype(np.float32)
+    got = np.array([L.orc_fp32_to_fp16(float(a)) for a in v], dtype=np.uint16)
+    assert np.array_equal(got, v.astype(np.float16).view(np.uint16))
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+def test_quantize_matches_gguf_golden(golden, dt):
+    got = O.quantize(dt, golden["w"])
+    assert np.array_equal(got, golden[f"{NAMES[dt]}_bytes"])
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+def test_fixture_scales_not_subnormal(golden, dt):
+    """Q4_0/Q8_0 scales must be normal fp16 so the reference converter is exact."""
+    b = golden[f"{NAMES[dt]}_bytes"]
+    bb = O.BLOCK_BYTES[dt]
+    d = b.reshape(-1, bb)[:, :2].copy().view(np.uint16).ravel()
+    exp = (d >> 10) & 0x1F
+    assert ((exp > 0) | (d & 0x7FFF == 0)).all()
+
+
+def test_activation_quantize_matches_gguf_golden(golden):
+    assert np.array_equal(O.quantize_q8_0_act(golden["x"]), golden["act_q8_0_bytes"])
+
+
+def test_activation_planes_consistent_with_blocks(golden):
+    x = golden["x"]
+    blocks = O.quantize_q8_0_act(x)
+    xq, xs = O.quantize_act_planes(x)
+    M, K = x.shape
+    nb = K // 32
+    blk = blocks.reshape(M, nb, 34)
+    assert np.array_equal(xq[:, :K].view(np.uint8).reshape(M, nb, 32), blk[:, :, 2:])
+    d16 = blk[:, :, :2].copy().view(np.float16).reshape(M, nb).astype(np.float32)
+    assert f32eq(xs[:, :nb, :4].copy().view(np.float32).reshape(M, nb), d16)
+    sums = xs[:, :nb, 4:8].copy().view(np.int16).reshape(M, nb, 2)
+    q = xq[:, :K].reshape(M, nb, 32).astype(np.int32)
+    assert np.array_equal(sums[..., 0], q[..., :16].sum(-1))
+    assert np.array_equal(sums[..., 1], q[..., 16:].sum(-1))
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+def test_dequantize_matches_gguf_golden(golden, dt):
+    b = golden[f"{NAMES[dt]}_bytes"]
+    N, K = golden["w"].shape
+    assert f32eq(O.dequantize(dt, b, N, K), golden[f"{NAMES[dt]}_dequant"])
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q5_K, O.Q6_K])
+def test_dequantize_random_kquant_blocks_golden(golden, dt):
+    rb = golden[f"{NAMES[dt]}_rand_bytes"]
+    got = O.dequantize(dt, rb, rb.shape[0], 256)
+    assert f32eq(got, golden[f"{NAMES[dt]}_rand_dequant"])
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q5_K, O.Q6_K])
+def test_kquant_quantizer_reconstruction(golden, dt):
+    """Own K-quant quantiser: parity pinned through decode; error bounded."""
+    w = golden["w"]
+    b = O.quantize(dt, w)
+    assert np.array_equal(b, golden[f"{NAMES[dt]}_bytes"])
+    dq = O.dequantize(dt, b, *w.shape)
+    rel = np.abs(dq - w).max() / np.abs(w).max()
+    assert rel < {O.Q4_K: 0.1, O.Q5_K: 0.05, O.Q6_K: 0.05}[dt]
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+def test_matmul_restatement_bit_exact_vs_reference_golden(golden, dt):
+    b = golden[f"{NAMES[dt]}_bytes"]
+    y = O.matmul_ref(dt, golden["x"], b, golden["w"].shape[0])
+    assert f32eq(y, golden[f"ref_{NAMES[dt]}_y"])
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+def test_matmul_ragged_k_bit_exact_vs_reference_golden(golden, dt):
+    b = golden[f"ragged_{NAMES[dt]}_bytes"]
+    y = O.matmul_ref(dt, golden["ragged_x"], b, 8)
+    assert f32eq(y, golden[f"ragged_ref_{NAMES[dt]}_y"])
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+def test_matmul_restatement_vs_live_reference(dt):
+    if O.ref_lib() is None:
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    w = O.seeded_weights(48, 1024, seed=11)
+    x = O.seeded_acts(5, 1024, seed=12)
+    b = O.quantize(dt, w)
+    assert f32eq(O.matmul_ref(dt, x, b, 48), O.matmul_reference_impl(dt, x, b, 48))
+
+
+def test_reference_throws_on_kquants():
+    if O.ref_lib() is None:
+        pytest.skip("oracle/_ref not built")
+    w = O.seeded_weights(8, 256)
+    with pytest.raises(RuntimeError, match="Unsupported quantization type"):
+        O.matmul_reference_impl(O.Q4_K, O.seeded_acts(1, 256), O.quantize(O.Q4_K, w), 8)
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+@pytest.mark.parametrize("N,K", [(1, 256), (65, 512), (130, 768), (64, 4096)])
+def test_repack_roundtrip(dt, N, K):
+    w = O.seeded_weights(N, K, seed=N + K)
+    b = O.quantize(dt, w)
+    t = O.repack(dt, b, N, K)
+    assert t.size == O.tiled_bytes(dt, N, K)
+    assert np.array_equal(O.unpack(dt, t, N, K), b)
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("K", [32, 80, 288, 300])
+def test_repack_roundtrip_ragged(dt, K):
+    Kb = (K + 31) // 32 * 32
+    b = O.quantize(dt, O.seeded_weights(70, Kb, seed=K))
+    t = O.repack(dt, b, 70, K)
+    assert np.array_equal(O.unpack(dt, t, 70, K), b)
+
+
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+def test_q8act_bound_holds(dt):
+    """The Q8-activation product stays within its analytic bound of the exact
+    real product of fp32 x and the decoded weights."""
+    N, K = 40, 1024
+    w = O.seeded_weights(N, K, seed=21)
+    x = O.seeded_acts(4, K, seed=22)
+    b = O.quantize(dt, w)
+    y, bound = O.matmul_q8act(dt, x, b, N)
+    exact = x.astype(np.float64) @ O.dequantize(dt, b, N, K).astype(np.float64).T
+    assert (np.abs(y - exact) <= bound).all()
+    fb = O.fp32_bound(dt, x, b, N)
+    assert (np.abs(O.matmul_ref(dt, x, b, N) - exact) <= fb).all()
