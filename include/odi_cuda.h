@@ -60,12 +60,7 @@ enum {
    * prefetch weights, while earlier kernels on the stream are still running.
    * Only valid when no kernel still in flight on the stream writes the
    * weight buffer. */
-  ODI_CUDA_FLAG_PDL = 1,
-  /* Skip staging x: the workspace already holds the activation tiles of this
-   * same x (same M, K and act_mode), written by the previous call that used
-   * it.  Lets projections that share an input (Q/K/V, gate/up) quantise it
-   * once.  d_x is then not read. */
-  ODI_CUDA_FLAG_REUSE_ACT = 2
+  ODI_CUDA_FLAG_PDL = 1
 };
 
 /* --- device / backend ---------------------------------------------------- */
@@ -144,17 +139,18 @@ int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t 
 
 /* --- the quantized matrix product ------------------------------------------ */
 
-/* Device scratch needed by odi_cuda_matmul for these sizes and mode. */
+/* Device scratch needed by odi_cuda_matmul: 256 bytes holding the device
+ * error word (activations are staged on chip, never in global memory). */
 size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode);
 
 /* y[M, N] = x[M, K] . dequant(W)^T in fp32 -- Backend::matmul /
  * quantized_matmul (backend.hpp:38, 114) with a = x, b = W.
  *   d_w_tiled : tiled weight (odi_cuda_repack / odi_cuda_weight_data)
  *   d_x, d_y  : device fp32, row-major, contiguous
- *   d_workspace: at least odi_cuda_matmul_workspace_bytes; it must be zero
- *     the first time it is used -- every call leaves it ready for the next.
- *     Calls that share a workspace must not overlap on the GPU.
- * Asynchronous on `stream`. */
+ *   d_workspace: at least odi_cuda_matmul_workspace_bytes, zero before its
+ *     first use (a call leaves it zero unless a kernel wait gave up; see
+ *     odi_cuda_workspace_status).
+ * One kernel launch per 8 tokens.  Asynchronous on `stream`. */
 int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M,
                     int64_t N, int64_t K, int act_mode, void* d_workspace,
                     size_t workspace_bytes, int flags, void* stream);

@@ -38,7 +38,6 @@ BLOCK_BYTES = {ODI_DTYPE_Q8_0: 34, ODI_DTYPE_Q4_0: 18, ODI_DTYPE_Q4_K: 144, ODI_
 ACT_Q8 = 0
 ACT_F32 = 1
 FLAG_PDL = 1
-FLAG_REUSE_ACT = 2
 
 # odi_error_t values (include/odi/odi_error.h:11-48)
 ODI_SUCCESS = 0

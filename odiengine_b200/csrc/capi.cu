@@ -52,25 +52,6 @@ int num_sms_current() {
   return sms[dev];
 }
 
-size_t align256(size_t v) { return (v + 255) / 256 * 256; }
-
-struct WsLayout {
-  size_t counters, partial, act, total;
-};
-
-// Workspace: header | activation tiles | fixup counters | fixup partials.
-// The activation tiles come first so their offset depends only on (K, M,
-// mode): calls that share an input x (Q/K/V, gate/up) can reuse them.
-WsLayout ws_layout(const GemvPlan& p, int dt, int64_t M, bool f32) {
-  (void)dt;
-  WsLayout L;
-  L.act = WS_HEADER;
-  L.counters = L.act + align256((size_t)p.KB * (size_t)M * (f32 ? ACT_F32_BYTES : ACT_Q8_BYTES));
-  L.partial = L.counters + align256((size_t)p.G * sizeof(int));
-  L.total = L.partial + align256(gemv_partial_floats(p, (int)M) * sizeof(float));
-  return L;
-}
-
 int check_shape(int dt, int64_t N, int64_t K) {
   if (!dtype_ok(dt)) return fail(ODI_CUDA_ERR_UNSUPPORTED_DTYPE, "dtype %d is not supported by the CUDA backend", dt);
   if (N < 1 || K < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid weight shape N=%lld K=%lld", (long long)N, (long long)K);
@@ -238,10 +219,9 @@ int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t 
 }
 
 size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode) {
+  (void)act_mode;
   if (!dtype_ok(dtype) || M < 1 || N < 1 || K < 1) return 0;
-  const bool f32 = act_mode == ODI_CUDA_ACT_F32;
-  const GemvPlan p = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
-  return ws_layout(p, dtype, M, f32).total;
+  return WS_HEADER;  // the device error word; activations are staged on chip
 }
 
 int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N,
@@ -256,30 +236,23 @@ int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d
   if (!d_w_tiled || !d_x || !d_y || !d_workspace) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
   if (((uintptr_t)d_w_tiled | (uintptr_t)d_workspace) & 15)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight and workspace must be 16-byte aligned");
+  if (workspace_bytes < WS_HEADER)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %d bytes", workspace_bytes, WS_HEADER);
   const bool f32 = act_mode == ODI_CUDA_ACT_F32;
   const bool pdl = (flags & ODI_CUDA_FLAG_PDL) != 0;
   cudaStream_t s = (cudaStream_t)stream;
   const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
-  const WsLayout L = ws_layout(plan, dtype, M, f32);
-  if (workspace_bytes < L.total)
-    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, L.total);
-  uint8_t* ws = (uint8_t*)d_workspace;
-  if (!(flags & ODI_CUDA_FLAG_REUSE_ACT)) {
-    if (f32) CK(launch_act_pack_f32(d_x, M, K, (float*)(ws + L.act), pdl, s), "act pack");
-    else CK(launch_act_quant(d_x, M, K, ws + L.act, nullptr, pdl, s), "act quantize");
-  }
+  if (plan.C == 0)
+    return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
   for (int64_t m0 = 0; m0 < M; m0 += plan.mt) {
     GemvArgs a;
     a.w = (const uint8_t*)d_w_tiled;
-    a.act = ws + L.act;
+    a.x = d_x + m0 * K;
     a.y = d_y + m0 * N;
-    a.partial = (float*)(ws + L.partial);
-    a.counters = (int*)(ws + L.counters);
-    a.err = (int*)ws;
+    a.err = (int*)d_workspace;
     a.N = N;
+    a.K = K;
     a.M = (int)((M - m0) < plan.mt ? (M - m0) : plan.mt);
-    a.M_total = (int)M;
-    a.m0 = (int)m0;
     CK(launch_gemv(dtype, f32, plan, a, pdl, s), "qgemv launch");
   }
   return ODI_CUDA_OK;

@@ -14,36 +14,32 @@ cudaError_t launch_unpack(int dt, const void* tiled, void* gguf, int64_t N, int6
 cudaError_t launch_dequant(int dt, const void* tiled, float* out, int64_t N, int64_t K, cudaStream_t s);
 cudaError_t launch_quant_weights(int dt, const float* w, void* out, int64_t N, int64_t K, cudaStream_t s);
 
-// Work split of the streaming GEMV: the G*KB units of a weight, in tile-major
-// order, are cut into P contiguous ranges, one per CTA (stream-K style).
-// Row tiles cut between CTAs are finished by a deterministic fixup: each
-// contributor writes its partial sums to a slot, the last to arrive (by an
-// atomic counter) adds the slots in CTA order and writes y.
+// Work split of the streaming GEMV.  The weight is G row tiles of KB units.
+// Each row tile is handled by one thread-block cluster of C CTAs; CTA rank j
+// takes the contiguous chunk of spans [j*chunk, min(KB, (j+1)*chunk)) and the
+// C partial tiles are added in rank order through distributed shared memory.
 struct GemvPlan {
-  int G, KB, U, P;
-  int maxc;          // max contributors to one row tile
-  int stages;        // ring depth
-  int stage_bytes;   // weights unit + activation slice, 128-aligned
+  int G, KB;
+  int C;             // cluster size (CTAs per row tile), 1..8
+  int chunk;         // spans per CTA
+  int stages;        // weight ring depth
+  int stage_bytes;   // one unit, 128-aligned
+  int xq_bytes;      // per-warp staged activations: chunk * mt * (80 | 256)
   int smem_bytes;    // dynamic shared memory per CTA
   int mt;            // tokens per pass (template instantiation)
 };
 
 struct GemvArgs {
   const uint8_t* w;   // tiled weight
-  const uint8_t* act; // activation tiles (span-major, M_total tokens)
-  float* y;           // output [M_total][N] (already offset to the first token of the pass)
-  float* partial;     // fixup slots
-  int* counters;      // fixup counters, one per row tile (zero between calls)
+  const float* x;     // activations of this pass [M][K] fp32, row stride K
+  float* y;           // outputs of this pass [M][N] fp32, row stride N
   int* err;           // device error word
-  int64_t N;
+  int64_t N, K;
   int M;              // tokens in this pass (<= mt)
-  int M_total;        // tokens in the activation tiles
-  int m0;             // first token of this pass
 };
 
-// Plan for dtype / tokens-per-pass / fp32-activation mode on the current device.
+// Plan for dtype / tokens / fp32-activation mode on a device with num_sms SMs.
 GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms);
-size_t gemv_partial_floats(const GemvPlan& p, int M);
 cudaError_t launch_gemv(int dt, bool f32act, const GemvPlan& plan, const GemvArgs& a, bool pdl,
                         cudaStream_t s);
 

@@ -4,35 +4,70 @@
 
 namespace odi_cuda {
 
-// ---------------------------------------------------------------------------
-// Host side: plan and launch.
-// ---------------------------------------------------------------------------
 static int tokens_per_pass(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
+// Cluster size C per row tile: splitting a tile's spans over C CTAs fills the
+// GPU when there are few tiles (decode shapes), at the cost of one
+// distributed-shared-memory reduction per tile.  Estimated time in units of
+// one span, per CTA slot: waves * (chunk + 1) (+ half a CTA of tail when the
+// grid needs more than one wave) (+ the reduction).
 GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms) {
   GemvPlan p{};
-  p.mt = tokens_per_pass(M);
   p.G = (int)((N + UNIT_ROWS - 1) / UNIT_ROWS);
   p.KB = (int)((K + UNIT_COLS - 1) / UNIT_COLS);
-  p.U = p.G * p.KB;
-  const int slots = 2 * (num_sms > 0 ? num_sms : 148);
-  p.P = p.U < slots ? p.U : slots;
-  if (p.P < 1) p.P = 1;
-  const int per = p.U / p.P > 0 ? p.U / p.P : 1;
-  p.maxc = (p.KB + per - 1) / per + 1;
-  if (p.maxc > p.P) p.maxc = p.P;
-  const int xb = f32act ? ACT_F32_BYTES : ACT_Q8_BYTES;
-  p.stage_bytes = (unit_bytes(dt) + p.mt * xb + 127) / 128 * 128;
-  int st = RING_BUDGET / p.stage_bytes;
+  const int slots = CTAS_PER_SM * (num_sms > 0 ? num_sms : 148);
+  (void)f32act;
+  p.mt = tokens_per_pass(M);
+  for (;;) {
+    double best = 1e30;
+    int bestC = 0, bestChunk = 0;
+    for (int C = 1; C <= 8; C *= 2) {
+      if (C > p.KB) break;
+      const int chunk = (p.KB + C - 1) / C;
+      const int ceff = (p.KB + chunk - 1) / chunk;
+      if ((int64_t)chunk * p.mt * XR_STRIDE > XR_BUDGET) continue;
+      const double ctas = (double)p.G * ceff;
+      const double waves = ctas / slots;
+      double t = (waves > 1.0 ? waves : 1.0) * (chunk + 1);
+      if (waves > 1.0) t += 0.5 * (chunk + 1);
+      if (ceff > 1) t += 0.5;
+      if (t < best) {
+        best = t;
+        bestC = ceff;
+        bestChunk = chunk;
+      }
+    }
+    if (bestC) {
+      p.C = bestC;
+      p.chunk = bestChunk;
+      break;
+    }
+    if (p.mt == 1) {  // activations of one chunk do not fit: signalled by C = 0
+      p.C = 0;
+      return p;
+    }
+    p.mt /= 2;
+  }
+  p.xq_bytes = (p.chunk * p.mt * XR_STRIDE + 127) / 128 * 128;
+  p.stage_bytes = (unit_bytes(dt) + 127) / 128 * 128;
+  const int xr_off = p.mt == 1 ? SmemMap<1>::xr
+                     : p.mt == 2 ? SmemMap<2>::xr
+                     : p.mt == 4 ? SmemMap<4>::xr
+                                 : SmemMap<8>::xr;
+  const int ring_off = xr_off + p.xq_bytes;
+  int st = (SMEM_PER_CTA - ring_off) / p.stage_bytes;
   if (st > MAX_STAGES) st = MAX_STAGES;
+  if (st > p.chunk) st = p.chunk;  // never more stages than units
+  // The two consumer pairs take alternate units.  With an even ring depth
+  // each pair owns its own slots (unit parity = slot parity) and visits them
+  // in order, so a parity wait can never be two phases ahead of its slot.
+  // An odd depth would let a pair wait on a slot the other pair has not yet
+  // released, where the parity test passes a phase early.
+  st -= st & 1;
   if (st < 2) st = 2;
   p.stages = st;
-  p.smem_bytes = RING_OFFSET + p.stages * p.stage_bytes;
+  p.smem_bytes = ring_off + p.stages * p.stage_bytes;
   return p;
-}
-
-size_t gemv_partial_floats(const GemvPlan& p, int /*M*/) {
-  return (size_t)p.G * p.maxc * UNIT_ROWS * p.mt;
 }
 
 template <int DT, int MT, bool F32>
@@ -45,20 +80,31 @@ static cudaError_t launch_t(const GemvPlan& pl, const GemvArgs& a, bool pdl, cud
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.P);
+  cfg.gridDim = dim3(pl.G * pl.C);
   cfg.blockDim = dim3(NTHREADS);
   cfg.dynamicSmemBytes = pl.smem_bytes;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pl.C > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = pl.C;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kern, a, pl);
 }
 

@@ -1,45 +1,77 @@
 // qgemv_device.cuh -- the streaming quantized GEMV kernel (device side).
 //
 // y[M, N] = x[M, K] . dequant(W)^T for M <= 8 tokens per pass, W in the
-// tiled layout (common.cuh).  Structure:
-//   * The G*KB units of the weight (64 rows x 256 columns, contiguous) are cut
-//     into P contiguous ranges, one per CTA (stream-K), so every SM streams
-//     the same number of bytes.
-//   * Warp 8 is the producer: one lane issues a bulk copy (cp.async.bulk, no
-//     multicast) of each unit and of the matching activation slice into a
-//     ring of shared-memory stages, completing on an mbarrier.
-//   * Warps 0-7 consume.  Lane = output row: warp w owns rows 32*(w&1) ..+31
-//     of the unit and the 64-column quarter kq = w>>1 of its 256 columns.
-//     A lane reads its row's codes for that quarter with 128-bit shared
-//     loads (the slice strides 144/176/208/272 B keep a quarter-warp on
-//     distinct banks), decodes the header once per 64 weights, and
-//     reads the activations as broadcast loads.
-//       ACT_Q8 : codes x int8 activations with dp4a, exact int32 per
+// tiled layout (common.cuh: units of 64 rows x 256 columns, contiguous).
+//   * Each 64-row tile is handled by a thread-block cluster of C CTAs; CTA
+//     rank j streams the contiguous chunk j of the tile's units (spans).
+//   * Warp 4 is the producer: one lane issues a bulk copy (cp.async.bulk, no
+//     multicast) of each unit into a ring of shared-memory stages, completing
+//     on an mbarrier.  Weights do not depend on earlier kernels, so the
+//     producer starts at once, also under programmatic dependent launch.
+//   * Warps 0-3 consume.  After griddepcontrol.wait they stage the
+//     activations of the chunk in shared memory (cp.async, all spans in
+//     flight at once) and, in ACT_Q8 mode, quantise them in place to Q8_0
+//     (bit-identical to odi_cuda_quantize_q8_0).  Then warp w takes every
+//     other unit (parity w>>1) and lane l owns row 32*(w&1)+l across the
+//     whole 256-column span: it decodes the row's header once per unit,
+//     reads the codes with 128-bit shared loads (the slice strides
+//     144/176/208/272 B keep each quarter-warp on distinct banks) and dots:
+//       ACT_Q8 : codes x int8 activations with dp4a (high nibbles kept in
+//                place, x16, via the unsigned x signed form), exact int32 per
 //                32-value block (16 for Q6_K), fp32 scale per block;
 //       ACT_F32: codes widened to fp32 exactly (2^23 magic), fp32 FMA with
 //                fp32 activations.
-//   * At the end of a row tile the four quarter sums of each row meet in
-//     shared memory (added in fixed order).  A tile wholly inside one CTA's
-//     range is written to y; a tile cut between CTAs goes through the fixup:
-//     partial sums into per-CTA slots, an atomic counter, and the last CTA to
-//     arrive adds the slots in CTA order (deterministic) and writes y,
-//     resetting the counter for the next call.
-//   * Every mbarrier wait is bounded; a wait that gives up sets the error
-//     word, and the producer drains its copies before the CTA exits.
+//   * End of tile: the two unit-parity sums of each row are added in
+//     shared memory; with C > 1 rank 0 adds the C partial tiles in rank
+//     order over distributed shared memory (deterministic) and writes y.
+//   * Every mbarrier wait is bounded (and sleeps in hardware while waiting);
+//     a wait that gives up sets the error word, the producer drains its
+//     copies, and every thread still reaches the cluster barriers.
 #pragma once
 
 #include "internal.h"
 
 namespace odi_cuda {
 
-constexpr int NCW = 8;                    // consumer warps: 2 row halves x 4 column quarters
+constexpr int NCW = 4;                    // consumer warps
 constexpr int NTHREADS = (NCW + 1) * 32;  // + producer warp
-constexpr int BAR_BYTES = 1024;           // mbarriers + flag
+constexpr int CTAS_PER_SM = 4;
+constexpr int BAR_BYTES = 1024;           // mbarriers
 constexpr int MAX_STAGES = 16;
 constexpr int MAX_MT = 8;
-constexpr int RED_BYTES = 4 * UNIT_ROWS * MAX_MT * 4;  // quarter sums at tile end
-constexpr int RING_OFFSET = BAR_BYTES + RED_BYTES;
-constexpr int RING_BUDGET = 96 * 1024;    // two CTAs per SM
+constexpr int SMEM_PER_CTA = 54 * 1024;   // four CTAs per SM
+constexpr int XR_BUDGET = 24 * 1024;      // staged activations per CTA
+// One staged (span, token): 256 fp32 values, then 16 fp32 sums of 16 values.
+// ACT_Q8 rewrites it in place as 256 codes followed by 8 XRec (one per
+// 32-value block).
+constexpr int XR_VALS = 1024;
+constexpr int XR_STRIDE = XR_VALS + 64;
+
+// Q8 activation record of one 32-value block, pre-scaled for the kernels:
+// dx = the fp16 scale widened to fp32; sdx = (sum of codes) * dx, and the
+// same for the first / second 16 codes.
+struct XRec {
+  float dx, sdx, sdx_lo, sdx_hi;
+};
+
+// Self-checking build (-DODI_GEMV_CHECKS): a failed index check records its
+// code and two values in err[1..3] (first failure wins), sets bit 30 of
+// err[0], and the guarded access is skipped.  Off in normal builds.
+#ifdef ODI_GEMV_CHECKS
+__device__ __forceinline__ bool gemv_check(bool ok, int* err, int code, long long x, long long y) {
+  if (!ok && err) {
+    atomicOr(err, 1 << 30);
+    if (atomicCAS(err + 1, 0, code) == 0) {
+      err[2] = (int)x;
+      err[3] = (int)y;
+    }
+  }
+  return ok;
+}
+#define GCHK(cond, code, x, y) gemv_check((cond), a.err, (code), (long long)(x), (long long)(y))
+#else
+#define GCHK(cond, code, x, y) true
+#endif
 
 // Exact int -> float for |v| < 2^22 with two full-rate ops.
 __device__ __forceinline__ float i2f(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }
@@ -49,401 +81,584 @@ template <int B>
 __device__ __forceinline__ float byte_magic(uint32_t w) {
   return __int_as_float(__byte_perm(w, 0x4Bu, 0x4550u | B));
 }
+// d * (byte B of w), exactly rounded, in two ops: fma(d, 2^23 + b, -d*2^23).
+template <int B>
+__device__ __forceinline__ float scale_byte(float d, float nd23, uint32_t w) {
+  return fmaf(d, byte_magic<B>(w), nd23);
+}
 
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
 }
 
-__device__ __forceinline__ int owner_of(int u, int P, int U) {
-  return (int)(((int64_t)(u + 1) * P - 1) / U);
-}
-
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ float4 lds128f(const uint8_t* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ uint32_t ldsu16(const uint8_t* p) {
   return *reinterpret_cast<const unsigned short*>(p);
 }
 __device__ __forceinline__ float h2f_lo(uint32_t w) { return h2f((uint16_t)(w & 0xFFFFu)); }
 __device__ __forceinline__ float h2f_hi(uint32_t w) { return h2f((uint16_t)(w >> 16)); }
 
-// ---------------------------------------------------------------------------
-// One lane's share of a unit: 4 groups of 16 codes (4 bytes per word) of one
-// row and one column quarter, with per-group scale A and min B
-// (value = A * code - B; Q8_0 codes are signed, B = 0).
-// Group g covers 16 consecutive columns starting at xoff(g) in the span and
-// uses half (g & 1) of activation record rec(g).
-// ---------------------------------------------------------------------------
-struct LaneCodes {
-  uint32_t cw[4][4];
-  float A[4];
-  float B[4];
-};
-
-// Bits s of each byte of h moved to bit 4 (s in 0..7).
-__device__ __forceinline__ uint32_t bit_to4(uint32_t h, int s) {
-  return (s <= 4 ? (h << (4 - s)) : (h >> (s - 4))) & 0x10101010u;
+// Signed x signed and unsigned x signed 4-way byte dot products.
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
-// Bits s, s+1 of each byte moved to bits 4, 5 (s even, 0..6).
-__device__ __forceinline__ uint32_t bits2_to4(uint32_t h, int s) {
-  return (s <= 4 ? (h << (4 - s)) : (h >> (s - 4))) & 0x30303030u;
+template <bool US>
+__device__ __forceinline__ int dot16(uint4 w, uint4 x, int acc) {
+  if (US) {
+    acc = dp4a_us(w.x, x.x, acc);
+    acc = dp4a_us(w.y, x.y, acc);
+    acc = dp4a_us(w.z, x.z, acc);
+    return dp4a_us(w.w, x.w, acc);
+  }
+  acc = dp4a_ss(w.x, x.x, acc);
+  acc = dp4a_ss(w.y, x.y, acc);
+  acc = dp4a_ss(w.z, x.z, acc);
+  return dp4a_ss(w.w, x.w, acc);
+}
+__device__ __forceinline__ uint4 and4(uint4 v, uint32_t m) { return make_uint4(v.x & m, v.y & m, v.z & m, v.w & m); }
+__device__ __forceinline__ uint4 shr4(uint4 v, int s) { return make_uint4(v.x >> s, v.y >> s, v.z >> s, v.w >> s); }
+__device__ __forceinline__ uint4 or4(uint4 a, uint4 b) { return make_uint4(a.x | b.x, a.y | b.y, a.z | b.z, a.w | b.w); }
+// bits s..s+nb-1 of every byte moved to bit 4 (mask m selects the result bits)
+__device__ __forceinline__ uint32_t mv4(uint32_t h, int s, uint32_t m) {
+  return (s <= 4 ? (h << (4 - s)) : (h >> (s - 4))) & m;
+}
+__device__ __forceinline__ uint4 mv4x4(uint4 h, int s, uint32_t m) {
+  return make_uint4(mv4(h.x, s, m), mv4(h.y, s, m), mv4(h.z, s, m), mv4(h.w, s, m));
 }
 
-template <int DT>
-struct QuarterMap {
-  // xoff: byte offset of group g's 16 activation codes in the 256-span
-  __device__ __forceinline__ static int xoff(int kq, int g) {
-    if (DT == Q6_K) {
-      const int h = kq >> 1, cl = kq & 1;
-      return 128 * h + 32 * cl + 16 * (g & 1) + 64 * (g >> 1);
-    }
-    return 64 * kq + 16 * g;
-  }
-  // record (32-value activation block) of group g
-  __device__ __forceinline__ static int rec(int kq, int g) {
-    if (DT == Q6_K) {
-      const int h = kq >> 1, cl = kq & 1;
-      return 4 * h + cl + 2 * (g >> 1);
-    }
-    return 2 * kq + (g >> 1);
-  }
-};
+// ---------------------------------------------------------------------------
+// Activation staging (all 128 consumer threads).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
 
-template <int DT>
-__device__ __forceinline__ void lane_codes(const uint8_t* __restrict__ st, int row, int kq, LaneCodes& lc) {
-  const uint8_t* sl = st + row * slice_bytes(DT);
-  if (DT == Q4_K || DT == Q5_K) {
-    const uint4 hd = lds128(sl);
-    const float d = h2f_lo(hd.x), dmin = h2f_hi(hd.x);
-    // 6-bit scales/mins of sub-blocks 0..3 (low) and 4..7 (high), one per byte
-    const uint32_t scv = kq < 2 ? (hd.y & 0x3F3F3F3Fu) : ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u));
-    const uint32_t mnv = kq < 2 ? (hd.z & 0x3F3F3F3Fu) : (((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u));
-    const int sh = 16 * (kq & 1);
-    lc.A[0] = lc.A[1] = d * i2f((scv >> sh) & 0xFF);
-    lc.A[2] = lc.A[3] = d * i2f((scv >> (sh + 8)) & 0xFF);
-    lc.B[0] = lc.B[1] = dmin * i2f((mnv >> sh) & 0xFF);
-    lc.B[2] = lc.B[3] = dmin * i2f((mnv >> (sh + 8)) & 0xFF);
-    const uint8_t* qs = sl + (DT == Q5_K ? 48 : 16) + 32 * kq;
-    const uint4 qa = lds128(qs), qb = lds128(qs + 16);
-    const uint32_t va[4] = {qa.x, qa.y, qa.z, qa.w}, vb[4] = {qb.x, qb.y, qb.z, qb.w};
+// 1. cp.async copies of the raw fp32 values of the chunk's spans for every
+//    token (16-byte copies when rows are 16-byte aligned, else 4-byte
+//    copies; columns past K are zero-filled).
+// 2. ACT_Q8: each 32-value block is quantised in place with the GGUF Q8_0
+//    quantiser's arithmetic (d = amax/127 in fp32, q = round-half-away(
+//    x * (1/d)), d kept as fp16): codes at [32*b, 32*b+32), XRec b at
+//    256 + 16*b.  ACT_F32: the sums of each 16 values go after the values.
+template <bool F32, int MT>
+__device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr) {
+  const int tid = threadIdx.x;  // 0..127
+  const int warp = tid >> 5, lane = tid & 31;
+  const bool vec = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+  const int nchunks = nsp * a.M * 64;
+  for (int c = tid; c < nchunks; c += NCW * 32) {
+    const int q = c & 63, jm = c >> 6;
+    const int m = jm % a.M, j = jm / a.M;
+    const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
+    const int64_t left = a.K - k;
+    const int nvalid = left <= 0 ? 0 : (left >= 4 ? 4 : (int)left);
+    const float* src = a.x + (int64_t)m * a.K + (nvalid ? k : 0);
+    uint8_t* dst = xr + (j * MT + m) * XR_STRIDE + 16 * q;
+    if (vec) {
+      cp_async16(dst, src, 4 * nvalid);
+    } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      lc.cw[0][i] = va[i] & 0x0F0F0F0Fu;
-      lc.cw[1][i] = vb[i] & 0x0F0F0F0Fu;
-      lc.cw[2][i] = (va[i] >> 4) & 0x0F0F0F0Fu;
-      lc.cw[3][i] = (vb[i] >> 4) & 0x0F0F0F0Fu;
+      for (int e = 0; e < 4; ++e) cp_async4(dst + 4 * e, src + (e < nvalid ? e : 0), e < nvalid ? 4 : 0);
     }
-    if (DT == Q5_K) {
-      const uint4 ha = lds128(sl + 16), hb = lds128(sl + 32);
-      const uint32_t wa[4] = {ha.x, ha.y, ha.z, ha.w}, wb[4] = {hb.x, hb.y, hb.z, hb.w};
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  consumer_sync();
+  // one warp per staged (span, token); lane = (block b = lane/4, 8 values)
+  const int b = lane >> 2, part = lane & 3;
+  for (int jm = warp; jm < nsp * MT; jm += NCW) {
+    if (jm % MT >= a.M) continue;  // uniform across the warp
+    uint8_t* rec = xr + jm * XR_STRIDE;
+    const float4 v0 = lds128f(rec + 4 * (32 * b + 8 * part));
+    const float4 v1 = lds128f(rec + 4 * (32 * b + 8 * part + 4));
+    if (F32) {
+      float s = ((v0.x + v0.y) + (v0.z + v0.w)) + ((v1.x + v1.y) + (v1.z + v1.w));
+      s += __shfl_xor_sync(0xffffffffu, s, 1);  // 16-value sums (parts 0-1, 2-3)
+      if ((part & 1) == 0) reinterpret_cast<float*>(rec + XR_VALS)[2 * b + (part >> 1)] = s;
+      continue;
+    }
+    float am = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
+                     fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    const float d = __fdiv_rn(am, 127.0f);
+    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    uint32_t packed[2] = {0u, 0u};
+    int s = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        lc.cw[0][i] |= bit_to4(wa[i], 2 * kq);
-        lc.cw[1][i] |= bit_to4(wb[i], 2 * kq);
-        lc.cw[2][i] |= bit_to4(wa[i], 2 * kq + 1);
-        lc.cw[3][i] |= bit_to4(wb[i], 2 * kq + 1);
+    for (int e = 0; e < 8; ++e) {
+      const int q = (int)roundf(__fmul_rn(vv[e], id));
+      s += q;
+      packed[e >> 2] |= (uint32_t)(q & 0xFF) << (8 * (e & 3));
+    }
+    const int s_half = s + __shfl_xor_sync(0xffffffffu, s, 1);        // 16 codes: parts 0-1 or 2-3
+    const int s_full = s_half + __shfl_xor_sync(0xffffffffu, s_half, 2);
+    const int s_hi = __shfl_sync(0xffffffffu, s_half, (lane & ~3) | 2);
+    __syncwarp();  // every lane has read its fp32 values before codes land on them
+    *reinterpret_cast<uint2*>(rec + 32 * b + 8 * part) = make_uint2(packed[0], packed[1]);
+    if (part == 0) {
+      const float dx = __half2float(__float2half_rn(d));
+      XRec r;
+      r.dx = dx;
+      r.sdx = __fmul_rn((float)s_full, dx);
+      r.sdx_lo = __fmul_rn((float)s_half, dx);
+      r.sdx_hi = __fmul_rn((float)s_hi, dx);
+      *reinterpret_cast<XRec*>(rec + 256 + 16 * b) = r;
+    }
+    __syncwarp();
+  }
+  consumer_sync();
+}
+
+// ---------------------------------------------------------------------------
+// ACT_Q8 units: one lane, one row, the whole 256-column span, MT tokens.
+// ---------------------------------------------------------------------------
+template <int MT>
+__device__ __forceinline__ void unit_q8_q4k(const uint8_t* __restrict__ sl, const uint8_t* __restrict__ xs, int M,
+                                            float (&acc)[MT], bool five) {
+  const uint4 hd = lds128(sl);
+  const float d = h2f_lo(hd.x), dmin = h2f_hi(hd.x);
+  const uint32_t scL = hd.y & 0x3F3F3F3Fu, mnL = hd.z & 0x3F3F3F3Fu;
+  const uint32_t scH = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+  const uint32_t mnH = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+  // Q4_K keeps the high nibbles in place (x16): their scales carry 1/16.
+  const float dh = five ? d : 0.0625f * d;
+  const float nd = -8388608.0f * d, ndh = -8388608.0f * dh, nm = -8388608.0f * dmin;
+  float A[8], B[8];
+  A[0] = scale_byte<0>(d, nd, scL);
+  A[1] = scale_byte<1>(dh, ndh, scL);
+  A[2] = scale_byte<2>(d, nd, scL);
+  A[3] = scale_byte<3>(dh, ndh, scL);
+  A[4] = scale_byte<0>(d, nd, scH);
+  A[5] = scale_byte<1>(dh, ndh, scH);
+  A[6] = scale_byte<2>(d, nd, scH);
+  A[7] = scale_byte<3>(dh, ndh, scH);
+  B[0] = scale_byte<0>(dmin, nm, mnL);
+  B[1] = scale_byte<1>(dmin, nm, mnL);
+  B[2] = scale_byte<2>(dmin, nm, mnL);
+  B[3] = scale_byte<3>(dmin, nm, mnL);
+  B[4] = scale_byte<0>(dmin, nm, mnH);
+  B[5] = scale_byte<1>(dmin, nm, mnH);
+  B[6] = scale_byte<2>(dmin, nm, mnH);
+  B[7] = scale_byte<3>(dmin, nm, mnH);
+  uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0;
+  if (five) {
+    h0 = lds128(sl + 16);
+    h1 = lds128(sl + 32);
+  }
+  const uint8_t* qs = sl + (five ? 48 : 16);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint4 q0 = lds128(qs + 32 * p), q1 = lds128(qs + 32 * p + 16);
+    uint4 l0 = and4(q0, 0x0F0F0F0Fu), l1 = and4(q1, 0x0F0F0F0Fu), u0, u1;
+    if (five) {
+      l0 = or4(l0, mv4x4(h0, 2 * p, 0x10101010u));
+      l1 = or4(l1, mv4x4(h1, 2 * p, 0x10101010u));
+      u0 = or4(and4(shr4(q0, 4), 0x0F0F0F0Fu), mv4x4(h0, 2 * p + 1, 0x10101010u));
+      u1 = or4(and4(shr4(q1, 4), 0x0F0F0F0Fu), mv4x4(h1, 2 * p + 1, 0x10101010u));
+    } else {
+      u0 = and4(q0, 0xF0F0F0F0u);
+      u1 = and4(q1, 0xF0F0F0F0u);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m < M) {
+        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint4 x0 = lds128(xr + 64 * p), x1 = lds128(xr + 64 * p + 16);
+        const uint4 x2 = lds128(xr + 64 * p + 32), x3 = lds128(xr + 64 * p + 48);
+        const float4 ra = lds128f(xr + 256 + 32 * p), rb = lds128f(xr + 256 + 32 * p + 16);
+        const int dl = dot16<false>(l1, x1, dot16<false>(l0, x0, 0));
+        const int du = five ? dot16<false>(u1, x3, dot16<false>(u0, x2, 0)) : dot16<true>(u1, x3, dot16<true>(u0, x2, 0));
+        float v = acc[m];
+        v = fmaf(i2f(dl), A[2 * p] * ra.x, v);
+        v = fmaf(-B[2 * p], ra.y, v);
+        v = fmaf(i2f(du), A[2 * p + 1] * rb.x, v);
+        v = fmaf(-B[2 * p + 1], rb.y, v);
+        acc[m] = v;
       }
     }
-  } else if (DT == Q6_K) {
-    const int h = kq >> 1, cl = kq & 1;
-    const uint4 a = lds128(sl + 16 + 64 * h + 32 * cl), b = lds128(sl + 16 + 64 * h + 32 * cl + 16);
-    const uint4 ha = lds128(sl + 144 + 32 * h), hb = lds128(sl + 144 + 32 * h + 16);
-    const uint32_t va[4] = {a.x, a.y, a.z, a.w}, vb[4] = {b.x, b.y, b.z, b.w};
-    const uint32_t wa[4] = {ha.x, ha.y, ha.z, ha.w}, wb[4] = {hb.x, hb.y, hb.z, hb.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      lc.cw[0][i] = (va[i] & 0x0F0F0F0Fu) | bits2_to4(wa[i], 2 * cl);
-      lc.cw[1][i] = (vb[i] & 0x0F0F0F0Fu) | bits2_to4(wb[i], 2 * cl);
-      lc.cw[2][i] = ((va[i] >> 4) & 0x0F0F0F0Fu) | bits2_to4(wa[i], 2 * cl + 4);
-      lc.cw[3][i] = ((vb[i] >> 4) & 0x0F0F0F0Fu) | bits2_to4(wb[i], 2 * cl + 4);
-    }
-    const float d = h2f((uint16_t)ldsu16(st + UNIT_ROWS * 208 + 2 * row));
-    const uint32_t s4 = ldsu16(sl + 8 * h + 2 * cl);      // int8 scales of sub-blocks sb, sb+1
-    const uint32_t s6 = ldsu16(sl + 8 * h + 2 * cl + 4);  // sb+4, sb+5
-    lc.A[0] = d * i2f((int)(signed char)(s4 & 0xFF));
-    lc.A[1] = d * i2f((int)(signed char)((s4 >> 8) & 0xFF));
-    lc.A[2] = d * i2f((int)(signed char)(s6 & 0xFF));
-    lc.A[3] = d * i2f((int)(signed char)((s6 >> 8) & 0xFF));
-#pragma unroll
-    for (int g = 0; g < 4; ++g) lc.B[g] = 32.0f * lc.A[g];
-  } else if (DT == Q8_0) {
-    const uint32_t dd = lds32(sl + 4 * kq);
-    lc.A[0] = lc.A[1] = h2f_lo(dd);
-    lc.A[2] = lc.A[3] = h2f_hi(dd);
-    lc.B[0] = lc.B[1] = lc.B[2] = lc.B[3] = 0.0f;
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const uint4 q = lds128(sl + 16 + 64 * kq + 16 * g);
-      lc.cw[g][0] = q.x; lc.cw[g][1] = q.y; lc.cw[g][2] = q.z; lc.cw[g][3] = q.w;
-    }
-  } else {  // Q4_0
-    const uint32_t dd = lds32(sl + 4 * kq);
-    lc.A[0] = lc.A[1] = h2f_lo(dd);
-    lc.A[2] = lc.A[3] = h2f_hi(dd);
-#pragma unroll
-    for (int g = 0; g < 4; ++g) lc.B[g] = 8.0f * lc.A[g];
-    const uint4 q0 = lds128(sl + 16 + 32 * kq), q1 = lds128(sl + 32 + 32 * kq);
-    const uint32_t v0[4] = {q0.x, q0.y, q0.z, q0.w}, v1[4] = {q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      lc.cw[0][i] = v0[i] & 0x0F0F0F0Fu;
-      lc.cw[1][i] = (v0[i] >> 4) & 0x0F0F0F0Fu;
-      lc.cw[2][i] = v1[i] & 0x0F0F0F0Fu;
-      lc.cw[3][i] = (v1[i] >> 4) & 0x0F0F0F0Fu;
-    }
   }
 }
 
-__device__ __forceinline__ int dot16(const uint32_t (&cw)[4], uint4 x, int acc) {
-  acc = __dp4a((int)cw[0], (int)x.x, acc);
-  acc = __dp4a((int)cw[1], (int)x.y, acc);
-  acc = __dp4a((int)cw[2], (int)x.z, acc);
-  acc = __dp4a((int)cw[3], (int)x.w, acc);
-  return acc;
-}
-
-// ---------------------------------------------------------------------------
-// ACT_Q8 unit.  Groups (0,1) and (2,3) share scale and activation block for
-// every type but Q6_K, so their integer dots are added before scaling.
-// ---------------------------------------------------------------------------
-template <int DT, int MT>
-__device__ __forceinline__ void unit_q8(const uint8_t* __restrict__ st, const uint8_t* __restrict__ xs, int M,
-                                        int row, int kq, float (&acc)[MT]) {
-  LaneCodes lc;
-  lane_codes<DT>(st, row, kq, lc);
+template <int MT>
+__device__ __forceinline__ void unit_q8_q6k(const uint8_t* __restrict__ sl, float d, const uint8_t* __restrict__ xs,
+                                            int M, float (&acc)[MT]) {
+  const uint4 scv = lds128(sl);  // 16 int8 scales
+  const uint32_t sw[4] = {scv.x ^ 0x80808080u, scv.y ^ 0x80808080u, scv.z ^ 0x80808080u, scv.w ^ 0x80808080u};
 #pragma unroll
-  for (int m = 0; m < MT; ++m) {
-    if (m < M) {
-      const uint8_t* xr = xs + m * ACT_Q8_BYTES;
-      float v = acc[m];
-      if (DT == Q6_K) {
-        const uint4 x0 = lds128(xr + QuarterMap<DT>::xoff(kq, 0)), x1 = lds128(xr + QuarterMap<DT>::xoff(kq, 1));
-        const uint4 x2 = lds128(xr + QuarterMap<DT>::xoff(kq, 2)), x3 = lds128(xr + QuarterMap<DT>::xoff(kq, 3));
-        const uint2 ra = *reinterpret_cast<const uint2*>(xr + 256 + 8 * QuarterMap<DT>::rec(kq, 0));
-        const uint2 rb = *reinterpret_cast<const uint2*>(xr + 256 + 8 * QuarterMap<DT>::rec(kq, 2));
-        const float dxa = __uint_as_float(ra.x), dxb = __uint_as_float(rb.x);
-        const int sa0 = (int)(short)(ra.y & 0xFFFFu), sa1 = (int)ra.y >> 16;
-        const int sb0 = (int)(short)(rb.y & 0xFFFFu), sb1 = (int)rb.y >> 16;
-        // (q - 32) . x = q . x - 32 * sum(x), exact in int32
-        const int d0 = dot16(lc.cw[0], x0, -32 * sa0), d1 = dot16(lc.cw[1], x1, -32 * sa1);
-        const int d2 = dot16(lc.cw[2], x2, -32 * sb0), d3 = dot16(lc.cw[3], x3, -32 * sb1);
-        v = fmaf(i2f(d0), lc.A[0] * dxa, v);
-        v = fmaf(i2f(d1), lc.A[1] * dxa, v);
-        v = fmaf(i2f(d2), lc.A[2] * dxb, v);
-        v = fmaf(i2f(d3), lc.A[3] * dxb, v);
-      } else {
-        const uint4 x0 = lds128(xr + 64 * kq), x1 = lds128(xr + 64 * kq + 16);
-        const uint4 x2 = lds128(xr + 64 * kq + 32), x3 = lds128(xr + 64 * kq + 48);
-        const uint4 rr = lds128(xr + 256 + 16 * kq);  // records 2kq, 2kq+1
-        const float dxa = __uint_as_float(rr.x), dxb = __uint_as_float(rr.z);
-        const int sa = (int)(short)(rr.y & 0xFFFFu) + ((int)rr.y >> 16);
-        const int sb = (int)(short)(rr.w & 0xFFFFu) + ((int)rr.w >> 16);
-        int da = DT == Q4_0 ? -8 * sa : 0, db = DT == Q4_0 ? -8 * sb : 0;
-        da = dot16(lc.cw[1], x1, dot16(lc.cw[0], x0, da));
-        db = dot16(lc.cw[3], x3, dot16(lc.cw[2], x2, db));
-        v = fmaf(i2f(da), lc.A[0] * dxa, v);
-        v = fmaf(i2f(db), lc.A[2] * dxb, v);
-        if (DT == Q4_K || DT == Q5_K) {
-          v = fmaf(-lc.B[0], i2f(sa) * dxa, v);
-          v = fmaf(-lc.B[2], i2f(sb) * dxb, v);
+  for (int h = 0; h < 2; ++h) {
+    const uint4 qh0 = lds128(sl + 144 + 32 * h), qh1 = lds128(sl + 144 + 32 * h + 16);
+#pragma unroll
+    for (int cl = 0; cl < 2; ++cl) {
+      const uint4 w0 = lds128(sl + 16 + 64 * h + 32 * cl), w1 = lds128(sl + 16 + 64 * h + 32 * cl + 16);
+      // codes 0..63: low nibbles -> column group c = cl, high nibbles -> c = cl + 2
+      const uint4 c0 = or4(and4(w0, 0x0F0F0F0Fu), mv4x4(qh0, 2 * cl, 0x30303030u));
+      const uint4 c1 = or4(and4(w1, 0x0F0F0F0Fu), mv4x4(qh1, 2 * cl, 0x30303030u));
+      const uint4 c2 = or4(and4(shr4(w0, 4), 0x0F0F0F0Fu), mv4x4(qh0, 2 * cl + 4, 0x30303030u));
+      const uint4 c3 = or4(and4(shr4(w1, 4), 0x0F0F0F0Fu), mv4x4(qh1, 2 * cl + 4, 0x30303030u));
+      const int sb = 8 * h + 2 * cl;  // sub-blocks sb, sb+1 (c0, c1) and sb+4, sb+5 (c2, c3)
+      // scale d * sc with sc signed: the byte sc ^ 0x80 is sc + 128, so
+      // magic - (2^23 + 128) is sc exactly
+      float A[4];
+      {
+        const uint32_t w = sw[sb >> 2];
+        const uint32_t w4 = sw[(sb + 4) >> 2];
+        const int o = sb & 3;  // 0 or 2
+        const float a0 = (o == 0 ? byte_magic<0>(w) : byte_magic<2>(w)) - 8388736.0f;
+        const float a1 = (o == 0 ? byte_magic<1>(w) : byte_magic<3>(w)) - 8388736.0f;
+        const float a2 = (o == 0 ? byte_magic<0>(w4) : byte_magic<2>(w4)) - 8388736.0f;
+        const float a3 = (o == 0 ? byte_magic<1>(w4) : byte_magic<3>(w4)) - 8388736.0f;
+        A[0] = d * a0;
+        A[1] = d * a1;
+        A[2] = d * a2;
+        A[3] = d * a3;
+      }
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        if (m < M) {
+          const uint8_t* xr = xs + m * XR_STRIDE;
+          const int xo = 128 * h + 32 * cl;
+          const uint4 x0 = lds128(xr + xo), x1 = lds128(xr + xo + 16);
+          const uint4 x2 = lds128(xr + xo + 64), x3 = lds128(xr + xo + 80);
+          const float4 ra = lds128f(xr + 256 + 16 * (4 * h + cl)), rb = lds128f(xr + 256 + 16 * (4 * h + cl + 2));
+          float v = acc[m];
+          // (q - 32) . x: integer dot, then -32 * A * sum(x) in fp32
+          v = fmaf(i2f(dot16<false>(c0, x0, 0)), A[0] * ra.x, v);
+          v = fmaf(-32.0f * A[0], ra.z, v);
+          v = fmaf(i2f(dot16<false>(c1, x1, 0)), A[1] * ra.x, v);
+          v = fmaf(-32.0f * A[1], ra.w, v);
+          v = fmaf(i2f(dot16<false>(c2, x2, 0)), A[2] * rb.x, v);
+          v = fmaf(-32.0f * A[2], rb.z, v);
+          v = fmaf(i2f(dot16<false>(c3, x3, 0)), A[3] * rb.x, v);
+          v = fmaf(-32.0f * A[3], rb.w, v);
+          acc[m] = v;
         }
       }
-      acc[m] = v;
+    }
+  }
+}
+
+template <int MT>
+__device__ __forceinline__ void unit_q8_q8_0(const uint8_t* __restrict__ sl, const uint8_t* __restrict__ xs, int M,
+                                             float (&acc)[MT]) {
+  const uint4 dv = lds128(sl);
+  const float dw[8] = {h2f_lo(dv.x), h2f_hi(dv.x), h2f_lo(dv.y), h2f_hi(dv.y),
+                       h2f_lo(dv.z), h2f_hi(dv.z), h2f_lo(dv.w), h2f_hi(dv.w)};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 q0 = lds128(sl + 16 + 32 * j), q1 = lds128(sl + 32 + 32 * j);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m < M) {
+        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
+        const float dx = *reinterpret_cast<const float*>(xr + 256 + 16 * j);
+        const int dd = dot16<false>(q1, x1, dot16<false>(q0, x0, 0));
+        acc[m] = fmaf(i2f(dd), dw[j] * dx, acc[m]);
+      }
+    }
+  }
+}
+
+template <int MT>
+__device__ __forceinline__ void unit_q8_q4_0(const uint8_t* __restrict__ sl, const uint8_t* __restrict__ xs, int M,
+                                             float (&acc)[MT]) {
+  const uint4 dv = lds128(sl);
+  const float dw[8] = {h2f_lo(dv.x), h2f_hi(dv.x), h2f_lo(dv.y), h2f_hi(dv.y),
+                       h2f_lo(dv.z), h2f_hi(dv.z), h2f_lo(dv.w), h2f_hi(dv.w)};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 q = lds128(sl + 16 + 16 * j);
+    const uint4 lo = and4(q, 0x0F0F0F0Fu), hi = and4(q, 0xF0F0F0F0u);  // hi kept x16
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m < M) {
+        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
+        const float2 r = *reinterpret_cast<const float2*>(xr + 256 + 16 * j);  // dx, sdx
+        // (q - 8) . x = lo . x0 + (hi . x1) / 16 - 8 * sum(x); the division is exact
+        const int dd = dot16<false>(lo, x0, 0) + (dot16<true>(hi, x1, 0) >> 4);
+        float v = fmaf(i2f(dd), dw[j] * r.x, acc[m]);
+        acc[m] = fmaf(-8.0f * dw[j], r.y, v);
+      }
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// ACT_F32 unit.
+// ACT_F32 units: 16 groups of 16 columns; value = A * code - B with integer
+// codes widened to fp32 exactly, then fp32 FMA against fp32 activations.
 // ---------------------------------------------------------------------------
+struct Group16 {
+  uint4 cw;  // 16 byte codes
+  float A, B;
+};
+
 template <int DT>
-__device__ __forceinline__ float dot16_f32(const uint32_t (&cw)[4], const float* __restrict__ x) {
+__device__ __forceinline__ Group16 group16(const uint8_t* __restrict__ sl, float tail_d, int g) {
+  Group16 G;
+  if (DT == Q4_K || DT == Q5_K) {
+    const int j = g >> 1, half = g & 1;  // sub-block j, 16-value half
+    const uint4 hd = lds128(sl);
+    const float d = h2f_lo(hd.x), dmin = h2f_hi(hd.x);
+    const uint8_t* s = sl + 4;
+    int sc, mn;
+    if (j < 4) {
+      sc = s[j] & 63;
+      mn = s[j + 4] & 63;
+    } else {
+      sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+      mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+    G.A = d * (float)sc;
+    G.B = dmin * (float)mn;
+    const uint8_t* qs = sl + (DT == Q5_K ? 48 : 16) + 32 * (j >> 1) + 16 * half;
+    const uint4 q = lds128(qs);
+    G.cw = (j & 1) ? and4(shr4(q, 4), 0x0F0F0F0Fu) : and4(q, 0x0F0F0F0Fu);
+    if (DT == Q5_K) G.cw = or4(G.cw, mv4x4(lds128(sl + 16 + 16 * half), j, 0x10101010u));
+  } else if (DT == Q6_K) {
+    // group g = 16 columns [16g, 16g+16): h = g/8, c = (g/2)&3, l0 = 16*(g&1)
+    const int h = g >> 3, c = (g >> 1) & 3, l0 = 16 * (g & 1);
+    const uint4 w = lds128(sl + 16 + 64 * h + 32 * (c & 1) + l0);
+    const uint4 qh = lds128(sl + 144 + 32 * h + l0);
+    G.cw = or4(and4(shr4(w, 4 * (c >> 1)), 0x0F0F0F0Fu), mv4x4(qh, 2 * c, 0x30303030u));
+    G.A = tail_d * (float)(int)(signed char)sl[g];
+    G.B = 32.0f * G.A;
+  } else if (DT == Q8_0) {
+    const int j = g >> 1;
+    G.cw = lds128(sl + 16 + 16 * g);
+    G.A = h2f((uint16_t)ldsu16(sl + 2 * j));
+    G.B = 0.0f;
+  } else {  // Q4_0: block j = g/2; low nibbles = values 0..15, high = 16..31
+    const int j = g >> 1;
+    const uint4 q = lds128(sl + 16 + 16 * j);
+    G.cw = (g & 1) ? and4(shr4(q, 4), 0x0F0F0F0Fu) : and4(q, 0x0F0F0F0Fu);
+    G.A = h2f((uint16_t)ldsu16(sl + 2 * j));
+    G.B = 8.0f * G.A;
+  }
+  return G;
+}
+
+template <int DT>
+__device__ __forceinline__ float dot16_f32(uint4 cw, const uint8_t* __restrict__ x) {
   // Q8_0 codes are signed: flip to q + 128 and remove that bias too.
   constexpr float bias = DT == Q8_0 ? 8388608.0f + 128.0f : 8388608.0f;
+  const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
   float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t w = DT == Q8_0 ? (cw[i] ^ 0x80808080u) : cw[i];
-    const float4 xv = *reinterpret_cast<const float4*>(x + 4 * i);
-    s0 = fmaf(xv.x, byte_magic<0>(w) - bias, s0);
-    s1 = fmaf(xv.y, byte_magic<1>(w) - bias, s1);
-    s0 = fmaf(xv.z, byte_magic<2>(w) - bias, s0);
-    s1 = fmaf(xv.w, byte_magic<3>(w) - bias, s1);
+    const uint32_t c = DT == Q8_0 ? (w[i] ^ 0x80808080u) : w[i];
+    const float4 xv = lds128f(x + 16 * i);
+    s0 = fmaf(xv.x, byte_magic<0>(c) - bias, s0);
+    s1 = fmaf(xv.y, byte_magic<1>(c) - bias, s1);
+    s0 = fmaf(xv.z, byte_magic<2>(c) - bias, s0);
+    s1 = fmaf(xv.w, byte_magic<3>(c) - bias, s1);
   }
   return s0 + s1;
 }
 
-__device__ __forceinline__ float sum16(const float* __restrict__ x) {
-  float s = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 v = *reinterpret_cast<const float4*>(x + 4 * i);
-    s += (v.x + v.y) + (v.z + v.w);
-  }
-  return s;
-}
-
 template <int DT, int MT>
-__device__ __forceinline__ void unit_f32(const uint8_t* __restrict__ st, const uint8_t* __restrict__ xs, int M,
-                                         int row, int kq, float (&acc)[MT]) {
-  LaneCodes lc;
-  lane_codes<DT>(st, row, kq, lc);
+__device__ __forceinline__ void unit_f32(const uint8_t* __restrict__ sl, float tail_d, const uint8_t* __restrict__ xs,
+                                         int M, float (&acc)[MT]) {
+#pragma unroll 2
+  for (int g = 0; g < 16; ++g) {
+    const Group16 G = group16<DT>(sl, tail_d, g);
 #pragma unroll
-  for (int m = 0; m < MT; ++m) {
-    if (m < M) {
-      const float* xr = reinterpret_cast<const float*>(xs + m * ACT_F32_BYTES);
-      float v = acc[m];
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const float* xg = xr + QuarterMap<DT>::xoff(kq, g);
-        v = fmaf(lc.A[g], dot16_f32<DT>(lc.cw[g], xg), v);
-        if (DT != Q8_0) v = fmaf(-lc.B[g], sum16(xg), v);
+    for (int m = 0; m < MT; ++m) {
+      if (m < M) {
+        const uint8_t* xr = xs + m * XR_STRIDE;
+        float v = fmaf(G.A, dot16_f32<DT>(G.cw, xr + 64 * g), acc[m]);
+        if (DT != Q8_0) v = fmaf(-G.B, reinterpret_cast<const float*>(xr + XR_VALS)[g], v);
+        acc[m] = v;
       }
-      acc[m] = v;
     }
   }
 }
 
+template <int DT, int MT, bool F32>
+__device__ __forceinline__ void unit(const uint8_t* __restrict__ st, int row, const uint8_t* __restrict__ xs, int M,
+                                     float (&acc)[MT]) {
+  const uint8_t* sl = st + row * slice_bytes(DT);
+  const float tail_d = DT == Q6_K ? h2f((uint16_t)ldsu16(st + UNIT_ROWS * 208 + 2 * row)) : 0.0f;
+  if (F32) {
+    unit_f32<DT, MT>(sl, tail_d, xs, M, acc);
+  } else if (DT == Q4_K) {
+    unit_q8_q4k<MT>(sl, xs, M, acc, false);
+  } else if (DT == Q5_K) {
+    unit_q8_q4k<MT>(sl, xs, M, acc, true);
+  } else if (DT == Q6_K) {
+    unit_q8_q6k<MT>(sl, tail_d, xs, M, acc);
+  } else if (DT == Q8_0) {
+    unit_q8_q8_0<MT>(sl, xs, M, acc);
+  } else {
+    unit_q8_q4_0<MT>(sl, xs, M, acc);
+  }
+}
+
 // ---------------------------------------------------------------------------
-// Row-tile flush: quarter sums -> tile sums -> y or fixup.
+// Cluster helpers (distributed shared memory).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem_f32(const float* local, int rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// Shared-memory layout of one CTA (offsets in bytes):
+//   [0, 1024)               mbarriers full[16], empty[16]
+//   red   [2][64][MT] fp32  the two unit-parity sums of each row
+//   part  [MT][64] fp32     this CTA's tile partial (read by rank 0 over DSMEM)
+//   xr    chunk x MT records of XR_STRIDE bytes: staged activations
+//   ring  stages x stage_bytes weight units
 template <int MT>
-__device__ __forceinline__ void flush_tile(const GemvArgs& a, const GemvPlan& pl, int g, bool whole, int c,
-                                           const float (&acc)[MT], int row, int kq, float* red,
-                                           volatile int* flag) {
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-    if (m < a.M) red[(kq * UNIT_ROWS + row) * MT + m] = acc[m];
-  consumer_sync();
-  const int tid = threadIdx.x;
-  const int c_lo = whole ? c : owner_of(g * pl.KB, pl.P, pl.U);
-  const int c_hi = whole ? c : owner_of((g + 1) * pl.KB - 1, pl.P, pl.U);
-  float* slot = a.partial + ((int64_t)g * pl.maxc + (c - c_lo)) * (UNIT_ROWS * MT);
-  for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
-    const int m = t >> 6, r = t & 63;
-    const float v = ((red[(0 * UNIT_ROWS + r) * MT + m] + red[(1 * UNIT_ROWS + r) * MT + m]) +
-                     red[(2 * UNIT_ROWS + r) * MT + m]) + red[(3 * UNIT_ROWS + r) * MT + m];
-    if (whole) {
-      const int64_t n = (int64_t)g * UNIT_ROWS + r;
-      if (n < a.N) a.y[(int64_t)m * a.N + n] = v;
-    } else {
-      slot[m * UNIT_ROWS + r] = v;
-    }
-  }
-  if (!whole) {
-    __threadfence();
-    consumer_sync();
-    if (tid == 0) {
-      __threadfence();
-      const int old = atomicAdd(&a.counters[g], 1);
-      const int last = old == (c_hi - c_lo);
-      if (last) atomicExch(&a.counters[g], 0);
-      *flag = last;
-    }
-    consumer_sync();
-    if (*flag) {
-      __threadfence();
-      const int nc = c_hi - c_lo + 1;
-      const float* base = a.partial + (int64_t)g * pl.maxc * (UNIT_ROWS * MT);
-      for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
-        const int m = t >> 6, r = t & 63;
-        const int64_t n = (int64_t)g * UNIT_ROWS + r;
-        float s = 0.0f;
-        for (int j = 0; j < nc; ++j) s += __ldcg(base + (int64_t)j * (UNIT_ROWS * MT) + m * UNIT_ROWS + r);
-        if (n < a.N) a.y[(int64_t)m * a.N + n] = s;
-      }
-    }
-  }
-  consumer_sync();  // red and flag are reused by the next flush
-}
+struct SmemMap {
+  static constexpr int red = BAR_BYTES;
+  static constexpr int part = red + 2 * UNIT_ROWS * MT * 4;
+  static constexpr int xr = (part + UNIT_ROWS * MT * 4 + 127) / 128 * 128;
+};
 
 // ---------------------------------------------------------------------------
-// The kernel.
+// The kernel: grid = G * C CTAs, clusters of C along x.
 // ---------------------------------------------------------------------------
 template <int DT, int MT, bool F32>
-__global__ void __launch_bounds__(NTHREADS, 2) qgemv_kernel(const GemvArgs a, const GemvPlan pl) {
+__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const GemvArgs a, const GemvPlan pl) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
-  volatile int* flag = reinterpret_cast<volatile int*>(smem + 512);
-  float* red = reinterpret_cast<float*>(smem + BAR_BYTES);
-  uint8_t* ring = smem + RING_OFFSET;
+  float* red = reinterpret_cast<float*>(smem + SmemMap<MT>::red);
+  float* part = reinterpret_cast<float*>(smem + SmemMap<MT>::part);
+  uint8_t* xr = smem + SmemMap<MT>::xr;
+  uint8_t* ring = xr + pl.xq_bytes;
   constexpr int UB = unit_bytes(DT);
-  constexpr int XB = F32 ? ACT_F32_BYTES : ACT_Q8_BYTES;
   const int S = pl.stages, SB = pl.stage_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x;
-  const int u0 = (int)((int64_t)pl.U * c / pl.P);
-  const int u1 = (int)((int64_t)pl.U * (c + 1) / pl.P);
+  const int g = blockIdx.x / pl.C, rank = blockIdx.x - g * pl.C;
+  const int kb0 = rank * pl.chunk;
+  const int nsp = min(pl.KB, kb0 + pl.chunk) - kb0;  // >= 1 by construction of the plan
+  const uint8_t* wsrc = a.w + ((int64_t)g * pl.KB + kb0) * UB;
+#ifdef ODI_GEMV_CHECKS
+  if (threadIdx.x == 0) {
+    uint32_t hw_rank = 0, hw_n = 1;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(hw_rank));
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(hw_n));
+    GCHK(g < pl.G && rank < pl.C && nsp >= 1 && kb0 + nsp <= pl.KB, 1, blockIdx.x, nsp);
+    GCHK((int)hw_rank == rank, 2, hw_rank, rank);
+    GCHK((int)hw_n == pl.C, 3, hw_n, pl.C);
+    GCHK(S >= 2 && S <= MAX_STAGES && (ring - smem) + S * SB <= pl.smem_bytes, 4, S, (ring - smem) + S * SB);
+    GCHK((xr - smem) + nsp * MT * XR_STRIDE <= (ring - smem), 5, nsp, pl.xq_bytes);
+  }
+#endif
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NCW);
+      mbar_init(&empty[s], 2);  // the two warps of a unit-parity pair
     }
     fence_mbar_init();
   }
   __syncthreads();
 
   if (warp == NCW) {
-    // ---------------- producer ----------------
+    // ---------------- producer: weights only, no dependency on earlier kernels
     if (lane == 0) {
-      const uint32_t xbytes = (uint32_t)a.M * XB;
-      // Fill the ring with weight units first: weights are not written by the
-      // kernels this one may overlap under programmatic dependent launch.
-      const int first = (u1 - u0) < S ? (u1 - u0) : S;
-      for (int i = 0; i < first; ++i) {
-        mbar_arrive_expect_tx(&full[i], UB + xbytes);
-        bulk_g2s(ring + i * SB, a.w + (int64_t)(u0 + i) * UB, UB, &full[i]);
-      }
-      pdl_wait();  // activation tiles are written by the previous kernel
-      for (int i = 0; i < first; ++i) {
-        const int kb = (u0 + i) % pl.KB;
-        bulk_g2s(ring + i * SB + UB, a.act + ((int64_t)kb * a.M_total + a.m0) * XB, xbytes, &full[i]);
-      }
-      int i = first;
-      for (int u = u0 + first; u < u1; ++u, ++i) {
-        const int s = i % S;
-        if (!mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, ERR_EMPTY_WAIT)) break;
-        uint8_t* st = ring + s * SB;
-        const int kb = u % pl.KB;
-        mbar_arrive_expect_tx(&full[s], UB + xbytes);
-        bulk_g2s(st, a.w + (int64_t)u * UB, UB, &full[s]);
-        bulk_g2s(st + UB, a.act + ((int64_t)kb * a.M_total + a.m0) * XB, xbytes, &full[s]);
-      }
       pdl_launch_dependents();
-      // Drain: every copy issued must land before the CTA may exit.
-      const int issued = i;
-      for (int s = 0; s < S && s < issued; ++s) {
-        const int last = s + S * ((issued - 1 - s) / S);
-        mbar_wait(&full[s], (last / S) & 1, a.err, ERR_DRAIN_WAIT);
+      const int first = nsp < S ? nsp : S;
+      for (int i = 0; i < first; ++i) {
+        mbar_arrive_expect_tx(&full[i], UB);
+        bulk_g2s(ring + i * SB, wsrc + (int64_t)i * UB, UB, &full[i]);
       }
+      int s = first % S;
+      uint32_t par = 0;
+      int i = first;
+      for (; i < nsp; ++i) {
+        if (s == 0) par = (uint32_t)(((i / S) - 1) & 1);
+        if (!mbar_wait(&empty[s], par, a.err, ERR_EMPTY_WAIT)) break;
+        if (!GCHK(s < S && (int64_t)g * pl.KB + kb0 + i < (int64_t)pl.G * pl.KB, 6, s, i)) break;
+        mbar_arrive_expect_tx(&full[s], UB);
+        bulk_g2s(ring + s * SB, wsrc + (int64_t)i * UB, UB, &full[s]);
+        if (++s == S) s = 0;
+      }
+      // Drain: every copy issued must land before the CTA may exit.
+      for (int t = 0; t < S && t < i; ++t) {
+        const int last = t + S * ((i - 1 - t) / S);
+        mbar_wait(&full[t], (last / S) & 1, a.err, ERR_DRAIN_WAIT);
+      }
+    }
+    __syncwarp();
+    if (pl.C > 1) {
+      cluster_sync_all();
+      cluster_sync_all();
     }
     return;
   }
 
-  // ---------------- consumers ----------------
+  // ---------------- consumers
+  pdl_wait();  // x is written by earlier kernels on the stream; y may be read by them
+  stage_acts<F32, MT>(a, kb0, nsp, xr);
+
   const int row = 32 * (warp & 1) + lane;
-  const int kq = warp >> 1;
+  const int up = warp >> 1;  // this warp takes units j = up, up + 2, ...
   float acc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
 
-  int i = 0;
-  for (int u = u0; u < u1; ++u, ++i) {
-    const int s = i % S;
-    if (!mbar_wait(&full[s], (i / S) & 1, a.err, ERR_FULL_WAIT)) break;
-    const uint8_t* st = ring + s * SB;
-    if (F32) unit_f32<DT, MT>(st, st + UB, a.M, row, kq, acc);
-    else unit_q8<DT, MT>(st, st + UB, a.M, row, kq, acc);
+  int s = up < S ? up : up - S;  // slot of unit j
+  uint32_t par = up < S ? 0u : 1u;
+  for (int j = up; j < nsp; j += 2) {
+    if (!mbar_wait(&full[s], par, a.err, ERR_FULL_WAIT)) break;
+    if (!GCHK(s >= 0 && s < S && j < nsp, 7, s, j)) break;
+    unit<DT, MT, F32>(ring + s * SB, row, xr + j * MT * XR_STRIDE, a.M, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    const int g = u / pl.KB, kb = u - g * pl.KB;
-    if (kb == pl.KB - 1 || u == u1 - 1) {
-      const bool whole = (u - kb >= u0) && (kb == pl.KB - 1);
-      flush_tile<MT>(a, pl, g, whole, c, acc, row, kq, red, flag);
-#pragma unroll
-      for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+    s += 2;
+    if (s >= S) {
+      s -= S;
+      par ^= 1u;
     }
+  }
+
+  // Tile reduction: unit parities (fixed order) -> CTA partial -> ranks (fixed order).
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+    if (m < a.M) red[(up * UNIT_ROWS + row) * MT + m] = acc[m];
+  consumer_sync();
+  const int tid = threadIdx.x;
+  for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
+    const int m = t >> 6, r = t & 63;
+    const float v = red[(0 * UNIT_ROWS + r) * MT + m] + red[(1 * UNIT_ROWS + r) * MT + m];
+    if (pl.C == 1) {
+      const int64_t n = (int64_t)g * UNIT_ROWS + r;
+      if (n < a.N) a.y[(int64_t)m * a.N + n] = v;
+    } else {
+      part[t] = v;
+    }
+  }
+  if (pl.C > 1) {
+    cluster_sync_all();  // every rank's partial is in its shared memory
+    if (rank == 0) {
+      for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
+        const int m = t >> 6, r = t & 63;
+        float v = part[t];
+        for (int q = 1; q < pl.C; ++q) v += ld_dsmem_f32(part + t, q);
+        const int64_t n = (int64_t)g * UNIT_ROWS + r;
+        if (n < a.N) a.y[(int64_t)m * a.N + n] = v;
+      }
+    }
+    cluster_sync_all();  // rank 0 is done reading: the other ranks may exit
   }
 }
 

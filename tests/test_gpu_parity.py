@@ -233,7 +233,9 @@ def test_matmul_multi_pass_tokens(cuda_lib, dt, M):
 # Llama-2-7B decode shapes (out x in) and the 4096 x 14336 headline shape.
 FULL = [(O.Q4_K, 4096, 14336), (O.Q4_K, 4096, 4096), (O.Q4_K, 11008, 4096), (O.Q8_0, 4096, 4096),
         (O.Q8_0, 4096, 11008), (O.Q6_K, 32000, 4096), (O.Q6_K, 4096, 11008), (O.Q4_0, 4096, 4096),
-        (O.Q5_K, 4096, 4096)]
+        (O.Q5_K, 4096, 4096),
+        # Llama-3-70B shapes (clusters of 2 with 16-span chunks, multi-wave grids)
+        (O.Q4_K, 128256, 8192), (O.Q4_K, 28672, 8192), (O.Q4_K, 8192, 28672)]
 
 
 @pytest.mark.parametrize("dt,N,K", FULL)
