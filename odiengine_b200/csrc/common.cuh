@@ -66,7 +66,7 @@ struct ActRec {
 // then the activation tiles.
 // ----------------------------------------------------------------------------
 constexpr int WS_HEADER = 256;
-enum : int { ERR_FULL_WAIT = 1, ERR_EMPTY_WAIT = 2, ERR_DRAIN_WAIT = 4 };
+enum : int { ERR_FULL_WAIT = 1, ERR_EMPTY_WAIT = 2, ERR_DRAIN_WAIT = 4, ERR_REDUCE_WAIT = 8 };
 
 // ~1 s at the B200's clock: far beyond any legitimate wait in these kernels.
 constexpr long long WAIT_BUDGET_CYCLES = 2000000000LL;

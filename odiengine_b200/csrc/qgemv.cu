@@ -50,10 +50,10 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
   }
   p.xq_bytes = (p.chunk * p.mt * XR_STRIDE + 127) / 128 * 128;
   p.stage_bytes = (unit_bytes(dt) + 127) / 128 * 128;
-  const int xr_off = p.mt == 1 ? SmemMap<1>::xr
-                     : p.mt == 2 ? SmemMap<2>::xr
-                     : p.mt == 4 ? SmemMap<4>::xr
-                                 : SmemMap<8>::xr;
+  const int xr_off = p.mt == 1 ? SmemMap<1>::xr(p.C)
+                     : p.mt == 2 ? SmemMap<2>::xr(p.C)
+                     : p.mt == 4 ? SmemMap<4>::xr(p.C)
+                                 : SmemMap<8>::xr(p.C);
   const int ring_off = xr_off + p.xq_bytes;
   int st = (SMEM_PER_CTA - ring_off) / p.stage_bytes;
   if (st > MAX_STAGES) st = MAX_STAGES;

@@ -154,20 +154,21 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
   const int tid = threadIdx.x;  // 0..127
   const int warp = tid >> 5, lane = tid & 31;
   const bool vec = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
-  const int nchunks = nsp * a.M * 64;
-  for (int c = tid; c < nchunks; c += NCW * 32) {
-    const int q = c & 63, jm = c >> 6;
-    const int m = jm % a.M, j = jm / a.M;
+  // 64 chunks per (span, token): threads 0-63 take even tokens, 64-127 odd
+  const int q = tid & 63;
+  for (int j = 0; j < nsp; ++j) {
     const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
     const int64_t left = a.K - k;
     const int nvalid = left <= 0 ? 0 : (left >= 4 ? 4 : (int)left);
-    const float* src = a.x + (int64_t)m * a.K + (nvalid ? k : 0);
-    uint8_t* dst = xr + (j * MT + m) * XR_STRIDE + 16 * q;
-    if (vec) {
-      cp_async16(dst, src, 4 * nvalid);
-    } else {
+    for (int m = tid >> 6; m < a.M; m += 2) {
+      const float* src = a.x + (int64_t)m * a.K + (nvalid ? k : 0);
+      uint8_t* dst = xr + (j * MT + m) * XR_STRIDE + 16 * q;
+      if (vec) {
+        cp_async16(dst, src, 4 * nvalid);
+      } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) cp_async4(dst + 4 * e, src + (e < nvalid ? e : 0), e < nvalid ? 4 : 0);
+        for (int e = 0; e < 4; ++e) cp_async4(dst + 4 * e, src + (e < nvalid ? e : 0), e < nvalid ? 4 : 0);
+      }
     }
   }
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
@@ -507,28 +508,63 @@ __device__ __forceinline__ void unit(const uint8_t* __restrict__ st, int row, co
 // ---------------------------------------------------------------------------
 // Cluster helpers (distributed shared memory).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float ld_dsmem_f32(const float* local, int rank) {
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, int rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
+  return remote;
+}
+__device__ __forceinline__ void st_dsmem_f32(uint32_t remote, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (clock64() - t0 > WAIT_BUDGET_CYCLES) {
+      if (err) atomicOr(err, code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
 }
 
-// Shared-memory layout of one CTA (offsets in bytes):
-//   [0, 1024)               mbarriers full[16], empty[16]
+// Shared-memory layout of one CTA (offsets in bytes; the host plan holds
+// xr_off and ring_off):
+//   [0, 512)                mbarriers full[16], empty[16]
+//   [512, 520)              reduction mbarrier (rank 0 of a cluster)
 //   red   [2][64][MT] fp32  the two unit-parity sums of each row
-//   part  [MT][64] fp32     this CTA's tile partial (read by rank 0 over DSMEM)
+//   part  [C][MT*64] fp32   tile partials; rank 0 receives those of the other
+//                           ranks here over distributed shared memory
 //   xr    chunk x MT records of XR_STRIDE bytes: staged activations
 //   ring  stages x stage_bytes weight units
 template <int MT>
 struct SmemMap {
+  static constexpr int redbar = 512;
   static constexpr int red = BAR_BYTES;
   static constexpr int part = red + 2 * UNIT_ROWS * MT * 4;
-  static constexpr int xr = (part + UNIT_ROWS * MT * 4 + 127) / 128 * 128;
+  static constexpr int xr(int C) { return (part + C * UNIT_ROWS * MT * 4 + 127) / 128 * 128; }
 };
 
 // ---------------------------------------------------------------------------
@@ -539,9 +575,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
+  uint64_t* redbar = reinterpret_cast<uint64_t*>(smem + SmemMap<MT>::redbar);
   float* red = reinterpret_cast<float*>(smem + SmemMap<MT>::red);
   float* part = reinterpret_cast<float*>(smem + SmemMap<MT>::part);
-  uint8_t* xr = smem + SmemMap<MT>::xr;
+  uint8_t* xr = smem + SmemMap<MT>::xr(pl.C);
   uint8_t* ring = xr + pl.xq_bytes;
   constexpr int UB = unit_bytes(DT);
   const int S = pl.stages, SB = pl.stage_bytes;
@@ -558,7 +595,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     GCHK(g < pl.G && rank < pl.C && nsp >= 1 && kb0 + nsp <= pl.KB, 1, blockIdx.x, nsp);
     GCHK((int)hw_rank == rank, 2, hw_rank, rank);
     GCHK((int)hw_n == pl.C, 3, hw_n, pl.C);
-    GCHK(S >= 2 && S <= MAX_STAGES && (ring - smem) + S * SB <= pl.smem_bytes, 4, S, (ring - smem) + S * SB);
+    GCHK(S >= 2 && S <= MAX_STAGES && (S & 1) == 0 && (ring - smem) + S * SB <= pl.smem_bytes, 4, S,
+         (ring - smem) + S * SB);
     GCHK((xr - smem) + nsp * MT * XR_STRIDE <= (ring - smem), 5, nsp, pl.xq_bytes);
   }
 #endif
@@ -568,9 +606,14 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 2);  // the two warps of a unit-parity pair
     }
+    // rank 0 receives one arrival per consumer thread of every other rank
+    if (pl.C > 1) mbar_init(redbar, (pl.C - 1) * NCW * 32);
     fence_mbar_init();
   }
   __syncthreads();
+  // Cluster barrier, split: arrive now, wait only before the first remote
+  // access (rank 0's reduction mbarrier is initialised before its arrive).
+  if (pl.C > 1) cluster_arrive();
 
   if (warp == NCW) {
     // ---------------- producer: weights only, no dependency on earlier kernels
@@ -599,10 +642,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
       }
     }
     __syncwarp();
-    if (pl.C > 1) {
-      cluster_sync_all();
-      cluster_sync_all();
-    }
+    if (pl.C > 1) cluster_wait();
     return;
   }
 
@@ -616,8 +656,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
 
-  int s = up < S ? up : up - S;  // slot of unit j
-  uint32_t par = up < S ? 0u : 1u;
+  int s = up;  // slot of unit j (S is even: each pair owns the slots of its parity)
+  uint32_t par = 0u;
   for (int j = up; j < nsp; j += 2) {
     if (!mbar_wait(&full[s], par, a.err, ERR_FULL_WAIT)) break;
     if (!GCHK(s >= 0 && s < S && j < nsp, 7, s, j)) break;
@@ -631,34 +671,41 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     }
   }
 
-  // Tile reduction: unit parities (fixed order) -> CTA partial -> ranks (fixed order).
+  // Tile reduction: unit parities (fixed order) -> CTA partial -> ranks (fixed
+  // order).  Ranks other than 0 push their partial into rank 0's shared
+  // memory and signal its reduction mbarrier; rank 0 waits, adds, writes y.
 #pragma unroll
   for (int m = 0; m < MT; ++m)
     if (m < a.M) red[(up * UNIT_ROWS + row) * MT + m] = acc[m];
   consumer_sync();
   const int tid = threadIdx.x;
+  if (pl.C > 1) cluster_wait();
   for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
     const int m = t >> 6, r = t & 63;
     const float v = red[(0 * UNIT_ROWS + r) * MT + m] + red[(1 * UNIT_ROWS + r) * MT + m];
     if (pl.C == 1) {
       const int64_t n = (int64_t)g * UNIT_ROWS + r;
       if (n < a.N) a.y[(int64_t)m * a.N + n] = v;
-    } else {
+    } else if (rank == 0) {
       part[t] = v;
+    } else {
+      st_dsmem_f32(dsmem_addr(part + rank * UNIT_ROWS * MT + t, 0), v);
     }
   }
   if (pl.C > 1) {
-    cluster_sync_all();  // every rank's partial is in its shared memory
-    if (rank == 0) {
+    if (rank != 0) {
+      mbar_arrive_remote(dsmem_addr(redbar, 0));  // releases this thread's pushes
+    } else {
+      mbar_wait_cluster(redbar, 0, a.err, ERR_REDUCE_WAIT);
+      consumer_sync();  // rank 0's own partial, written by other threads
       for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
         const int m = t >> 6, r = t & 63;
         float v = part[t];
-        for (int q = 1; q < pl.C; ++q) v += ld_dsmem_f32(part + t, q);
+        for (int q = 1; q < pl.C; ++q) v += part[q * UNIT_ROWS * MT + t];
         const int64_t n = (int64_t)g * UNIT_ROWS + r;
         if (n < a.N) a.y[(int64_t)m * a.N + n] = v;
       }
     }
-    cluster_sync_all();  // rank 0 is done reading: the other ranks may exit
   }
 }
 
