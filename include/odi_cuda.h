@@ -171,6 +171,40 @@ int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t 
 int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
                          int act_mode, void* stream);
 
+/* Size of the static device array behind odi_cuda_matmul_host_noalloc. */
+#define ODI_CUDA_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* The product of odi_cuda_matmul_host, for callers that must not allocate
+ * device memory once they are running.  No counterpart in the reference.
+ *
+ * Who needs it: an engine that reserves HBM for its weights and KV cache up
+ * front cannot have a later cudaMalloc fail or carve into that reservation;
+ * a process whose device memory belongs to another allocator's pool must
+ * not allocate behind that pool's back; a decode loop cannot afford the
+ * device-wide synchronisation that cudaMalloc / cudaFree may cause.
+ * odi_cuda_matmul_host grows a per-device buffer with cudaMalloc whenever it
+ * meets a larger M; this call allocates nothing.  It stages x, y and the
+ * kernels' error word in one static device array of
+ * ODI_CUDA_NOALLOC_SCRATCH_BYTES per GPU, part of the library's device image:
+ * every GPU that loads the library holds that array until the process exits.
+ * (The weight itself is uploaded beforehand, at load time, by
+ * odi_cuda_weight_upload.)
+ *
+ * Limit: 256 + round_up(M*K*4, 256) + M*N*4 <= ODI_CUDA_NOALLOC_SCRATCH_BYTES
+ * (M=1 fits any N up to about two million); a larger call returns
+ * ODI_CUDA_ERR_INVALID_ARGUMENT and runs nothing.
+ *
+ * The first call on a device, with that device current, looks up the
+ * array's device address; make that first call before any stream capture on
+ * the device.  All calls share the one array per device: each call clears
+ * the error word (the only part that must start at zero) and overwrites the
+ * x and y regions.  Calls whose GPU work overlaps -- e.g. two host threads
+ * on two streams of the same device -- race on the array and corrupt each
+ * other's results, so serialise them.  Synchronous: returns once h_y holds
+ * the result; ODI_CUDA_ERR_OPERATION_FAILED if a kernel wait gave up. */
+int odi_cuda_matmul_host_noalloc(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
+                                 int act_mode, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

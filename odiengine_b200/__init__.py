@@ -70,7 +70,12 @@ SIGNATURES = {
     "odi_cuda_workspace_status": (_int, [_vp, ctypes.POINTER(_int), _vp]),
     "odi_cuda_dequantize": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
     "odi_cuda_matmul_host": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
+    "odi_cuda_matmul_host_noalloc": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
 }
+
+# ODI_CUDA_NOALLOC_SCRATCH_BYTES (include/odi_cuda.h): the static device
+# array behind odi_cuda_matmul_host_noalloc.
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 _lib = None
 

@@ -333,3 +333,83 @@ extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, 
   CK(cudaStreamSynchronize(s), "sync");
   return ODI_CUDA_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Host-buffer matmul that allocates nothing (odi_cuda_matmul_host_noalloc).
+//
+// For callers that may not allocate device memory while running (HBM
+// reserved up front, memory owned by another allocator's pool, or a decode
+// loop that cannot take cudaMalloc's synchronisation).  Instead of the
+// cudaMalloc-grown arena above, x, y and the error word live in one static
+// device array per GPU, held from module load until the process exits:
+//   [0, 256)                    error word (must be zero when a product starts;
+//                               cleared by every call)
+//   [256, 256 + rx)             x, M*K fp32     (rx = M*K*4 rounded up to 256)
+//   [256 + rx, ... + M*N*4)     y, M*N fp32
+// Every call shares the array; calls whose GPU work overlaps race on it.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ODI_CUDA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_dev[64];  // device address of the array, per device
+
+// The array's name is a host-side stand-in in host code; the device address
+// comes from cudaGetSymbolAddress, looked up once per device with that
+// device current (the first call on each device does it).
+int noalloc_scratch(int dev, unsigned char** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_dev[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (static scratch)");
+    g_noalloc_dev[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_dev[dev];
+  return ODI_CUDA_OK;
+}
+}  // namespace
+
+extern "C" int odi_cuda_matmul_host_noalloc(const odi_cuda_weight* w, const float* h_x, float* h_y,
+                                            int64_t M, int act_mode, void* stream) {
+  if (!w || !h_x || !h_y) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  if (M < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M");
+  if (M == 0) return ODI_CUDA_OK;
+  if (act_mode != ODI_CUDA_ACT_Q8 && act_mode != ODI_CUDA_ACT_F32)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "unknown act_mode %d", act_mode);
+  const int64_t cap = (int64_t)ODI_CUDA_NOALLOC_SCRATCH_BYTES;
+  const int64_t per_token = 4 * (w->K + w->N);
+  bool fits = M <= (cap - WS_HEADER) / per_token;  // bounds M before any product can overflow
+  int64_t x_off = WS_HEADER, y_off = 0, need = 0;
+  if (fits) {
+    y_off = x_off + (M * w->K * 4 + 255) / 256 * 256;
+    need = y_off + M * w->N * 4;
+    fits = need <= cap;
+  }
+  if (!fits)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT,
+                "odi_cuda_matmul_host_noalloc: M=%lld tokens of K=%lld inputs and N=%lld outputs exceed its "
+                "static scratch of %lld bytes (needs 256 + round_up(M*K*4, 256) + M*N*4); use "
+                "odi_cuda_matmul_host or fewer tokens per call",
+                (long long)M, (long long)w->K, (long long)w->N, (long long)cap);
+  int dev = 0;
+  CK(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(ODI_CUDA_ERR_INVALID_STATE, "device %d out of range", dev);
+  if (dev != w->device) return fail(ODI_CUDA_ERR_INVALID_STATE, "weight lives on device %d, current is %d", w->device, dev);
+  unsigned char* scr = nullptr;
+  int rc = noalloc_scratch(dev, &scr);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  float* d_x = reinterpret_cast<float*>(scr + x_off);
+  float* d_y = reinterpret_cast<float*>(scr + y_off);
+  CK(cudaMemsetAsync(scr, 0, sizeof(int), s), "clear error word");
+  CK(cudaMemcpyAsync(d_x, h_x, (size_t)(M * w->K) * sizeof(float), cudaMemcpyHostToDevice, s), "H2D x");
+  rc = odi_cuda_matmul(w->dtype, w->data, d_x, d_y, M, w->N, w->K, act_mode, scr, WS_HEADER, 0, stream);
+  if (rc) return rc;
+  CK(cudaMemcpyAsync(h_y, d_y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
+  int err = 0;
+  CK(cudaMemcpyAsync(&err, scr, sizeof(int), cudaMemcpyDeviceToHost, s), "read error word");
+  CK(cudaStreamSynchronize(s), "sync");
+  if (err) return fail(ODI_CUDA_ERR_OPERATION_FAILED, "a kernel wait gave up (error word 0x%x)", err);
+  return ODI_CUDA_OK;
+}
