@@ -5,8 +5,9 @@ Headline workload: Q4_K weight, 4096 output rows x 14336 inputs, M = 1 token,
 the shape the decode-GEMV target is quoted on.  One step = one pass over a
 ring of R distinct weight copies (R * 33 MB > 4 x the 126 MB L2, so every
 GEMV streams its weights from HBM), each copy with its own activation row:
-per copy one activation-quantise kernel and one GEMV kernel, replayed from a
-CUDA graph with programmatic dependent launch.
+per copy one GEMV kernel (the Q8_0 activation quantisation is fused into its
+shared-memory stage), replayed from a CUDA graph with programmatic dependent
+launch.
 
 Reported (one JSON line on rank 0):
   value       whole-job algorithmic GB/s (weights + x + y bytes / time)
@@ -439,11 +440,14 @@ def run_ours(args, rank, world, local_rank):
 
 def traffic_per_launch():
     """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "qgemv_q4k_4096x14336_m1.json")
+    import re
+
+    path = os.path.join(ROOT, "profiles", "qgemv_q4k_4096x14336_m1.md")
     try:
         with open(path) as f:
-            return json.load(f).get("dram_bytes_per_launch")
-    except Exception:
+            m = re.search(r"^dram_bytes_per_launch = (\d+)", f.read(), re.M)
+        return int(m.group(1)) if m else None
+    except OSError:
         return None
 
 
