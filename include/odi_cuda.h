@@ -171,6 +171,12 @@ int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t 
 int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
                          int act_mode, void* stream);
 
+/* Host-buffer form of Backend::dequantize (backend.hpp:111;
+ * cpu_backend.cpp:625-648) for an uploaded weight: h_out receives N*K fp32
+ * values in block order ([N][K]).  Synchronous; uses a temporary device
+ * buffer of N*K*4 bytes. */
+int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* stream);
+
 /* Size of the static device array behind odi_cuda_matmul_host_noalloc. */
 #define ODI_CUDA_NOALLOC_SCRATCH_BYTES (8u << 20)
 

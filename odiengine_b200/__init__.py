@@ -71,6 +71,7 @@ SIGNATURES = {
     "odi_cuda_dequantize": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
     "odi_cuda_matmul_host": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "odi_cuda_matmul_host_noalloc": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
+    "odi_cuda_dequantize_host": (_int, [_vp, _vp, _vp]),
 }
 
 # ODI_CUDA_NOALLOC_SCRATCH_BYTES (include/odi_cuda.h): the static device

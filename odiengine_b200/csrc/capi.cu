@@ -334,6 +334,23 @@ extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, 
   return ODI_CUDA_OK;
 }
 
+extern "C" int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* stream) {
+  if (!w || !h_out) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  int dev = 0;
+  CK(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != w->device) return fail(ODI_CUDA_ERR_INVALID_STATE, "weight lives on device %d, current is %d", w->device, dev);
+  const size_t bytes = (size_t)(w->N * w->K) * sizeof(float);
+  float* d_out = nullptr;
+  CK(cudaMalloc(&d_out, bytes), "cudaMalloc (dequantize output)");
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = launch_dequant(w->dtype, w->data, d_out, w->N, w->K, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(h_out, d_out, bytes, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(d_out);
+  if (e != cudaSuccess) return cuda_fail(e, "dequantize_host");
+  return ODI_CUDA_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Host-buffer matmul that allocates nothing (odi_cuda_matmul_host_noalloc).
 //

@@ -1,0 +1,127 @@
+// backend_c.cpp -- a C facade over odi::Backend objects: the reference's
+// CPUBackend and this project's CUDABackend, driven through the same
+// Backend calls (matmul, dequantize, sync, the metadata queries).  Tensors
+// are passed as (pointer, dtype, ndim, shape) and wrapped in non-owning
+// odi::Tensor views (tensor.hpp:50), the way Context hands the backend its
+// scratch and the GGUF weight views.
+//
+// Every function catches what the backend throws and returns 1 with the
+// message in odi_be_last_error(); 0 on success.
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+#include "cuda_backend.hpp"
+
+namespace {
+thread_local std::string t_err;
+
+int caught(const char* what) {
+  t_err = what;
+  return 1;
+}
+
+std::vector<int64_t> dims(int ndim, const int64_t* shape) { return std::vector<int64_t>(shape, shape + ndim); }
+
+odi::Tensor view(const void* p, int dtype, int ndim, const int64_t* shape) {
+  return odi::Tensor(const_cast<void*>(p), dims(ndim, shape), (odi_dtype_t)dtype);
+}
+}  // namespace
+
+extern "C" {
+
+const char* odi_be_last_error(void) { return t_err.c_str(); }
+
+// kind: ODI_BACKEND_CPU (1) or ODI_BACKEND_CUDA (4).  act_mode (CUDA only):
+// ODI_CUDA_ACT_Q8 or ODI_CUDA_ACT_F32.  NULL on failure.
+void* odi_be_create(int kind, int num_threads, int device, int act_mode) {
+  try {
+    if (kind == ODI_BACKEND_CPU) return static_cast<odi::Backend*>(new odi::CPUBackend(num_threads));
+    if (kind == ODI_BACKEND_CUDA)
+      return static_cast<odi::Backend*>(new odi::CUDABackend(
+          num_threads, device,
+          act_mode == ODI_CUDA_ACT_F32 ? odi::CUDABackend::ActMode::F32 : odi::CUDABackend::ActMode::Q8));
+    t_err = "unknown backend kind " + std::to_string(kind);
+  } catch (const std::exception& e) {
+    caught(e.what());
+  }
+  return nullptr;
+}
+
+void odi_be_destroy(void* be) { delete static_cast<odi::Backend*>(be); }
+
+int odi_be_matmul(void* be, void* out, int out_ndim, const int64_t* out_shape, const void* a, int a_dtype,
+                  int a_ndim, const int64_t* a_shape, const void* b, int b_dtype, int b_ndim,
+                  const int64_t* b_shape) {
+  try {
+    odi::Tensor o = view(out, ODI_DTYPE_F32, out_ndim, out_shape);
+    static_cast<odi::Backend*>(be)->matmul(o, view(a, a_dtype, a_ndim, a_shape), view(b, b_dtype, b_ndim, b_shape));
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_quantized_matmul(void* be, void* out, int out_ndim, const int64_t* out_shape, const void* a,
+                            int a_ndim, const int64_t* a_shape, const void* b, int b_dtype, int b_ndim,
+                            const int64_t* b_shape) {
+  try {
+    odi::Tensor o = view(out, ODI_DTYPE_F32, out_ndim, out_shape);
+    static_cast<odi::Backend*>(be)->quantized_matmul(o, view(a, ODI_DTYPE_F32, a_ndim, a_shape),
+                                                    view(b, b_dtype, b_ndim, b_shape));
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_dequantize(void* be, float* out, const void* x, int x_dtype, int x_ndim, const int64_t* x_shape) {
+  try {
+    odi::Tensor xv = view(x, x_dtype, x_ndim, x_shape);
+    const int64_t n = xv.numel();
+    odi::Tensor o(out, {n}, ODI_DTYPE_F32);
+    static_cast<odi::Backend*>(be)->dequantize(o, xv);
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_sync(void* be) {
+  try {
+    static_cast<odi::Backend*>(be)->sync();
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_supports_dtype(void* be, int dtype) {
+  return static_cast<odi::Backend*>(be)->supports_dtype((odi_dtype_t)dtype) ? 1 : 0;
+}
+
+// type(), name(), device_info(), used_memory(), available_memory().
+int odi_be_info(void* be, int* type, char* name, size_t name_len, char* info, size_t info_len, size_t* used,
+                size_t* avail) {
+  try {
+    auto* b = static_cast<odi::Backend*>(be);
+    if (type) *type = (int)b->type();
+    if (name && name_len) std::snprintf(name, name_len, "%s", b->name().c_str());
+    if (info && info_len) std::snprintf(info, info_len, "%s", b->device_info().c_str());
+    if (used) *used = b->used_memory();
+    if (avail) *avail = b->available_memory();
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+// Weights held in HBM by a CUDABackend; -1 for any other backend.
+int64_t odi_be_cached_weights(void* be) {
+  auto* c = dynamic_cast<odi::CUDABackend*>(static_cast<odi::Backend*>(be));
+  return c ? (int64_t)c->cached_weights() : -1;
+}
+
+}  // extern "C"

@@ -1,0 +1,167 @@
+// cuda_backend.cpp -- odi::CUDABackend (see cuda_backend.hpp).
+#include "cuda_backend.hpp"
+
+#include <cstdlib>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+namespace odi {
+
+namespace {
+
+[[noreturn]] void raise(const char* what, int rc) {
+  std::string msg = what;
+  msg += ": ";
+  const char* e = odi_cuda_last_error();
+  msg += (e && *e) ? e : "error";
+  msg += " (status " + std::to_string(rc) + ")";
+  throw std::runtime_error(msg);
+}
+
+void ck(int rc, const char* what) {
+  if (rc != ODI_CUDA_OK) raise(what, rc);
+}
+
+CUDABackend::ActMode act_from_env() {
+  const char* v = std::getenv("ODI_CUDA_ACT");
+  if (v && (std::strcmp(v, "f32") == 0 || std::strcmp(v, "F32") == 0)) return CUDABackend::ActMode::F32;
+  return CUDABackend::ActMode::Q8;
+}
+
+// The device this host thread last bound; CUDA's current device is per thread.
+thread_local int t_bound_device = -1;
+
+}  // namespace
+
+CUDABackend::CUDABackend(int num_threads, int device) : CUDABackend(num_threads, device, act_from_env()) {}
+
+CUDABackend::CUDABackend(int num_threads, int device, ActMode act)
+    : CPUBackend(num_threads), device_(device), act_(act) {
+  ck(odi_cuda_init(device), "CUDABackend");
+  t_bound_device = device;
+}
+
+CUDABackend::~CUDABackend() {
+  try {
+    release_weights();
+  } catch (...) {
+  }
+}
+
+void CUDABackend::bind_device() const {
+  if (t_bound_device != device_) {
+    ck(odi_cuda_init(device_), "CUDABackend: bind device");
+    t_bound_device = device_;
+  }
+}
+
+std::string CUDABackend::device_info() const {
+  bind_device();
+  char buf[256] = {};
+  ck(odi_cuda_device_info(buf, sizeof buf), "device_info");
+  return buf;
+}
+
+size_t CUDABackend::available_memory() const {
+  bind_device();
+  size_t free_b = 0, total_b = 0;
+  ck(odi_cuda_memory_info(&free_b, &total_b), "available_memory");
+  return free_b;
+}
+
+size_t CUDABackend::used_memory() const {
+  std::lock_guard<std::mutex> lk(mu_);
+  return weight_bytes_;
+}
+
+size_t CUDABackend::cached_weights() const {
+  std::lock_guard<std::mutex> lk(mu_);
+  return weights_.size();
+}
+
+bool CUDABackend::supports_dtype(odi_dtype_t dtype) const {
+  // fp32 runs through the inherited CPU code; the quantized types listed in
+  // odi_cuda_supports_dtype run on the GPU.
+  return dtype == ODI_DTYPE_F32 || odi_cuda_supports_dtype(dtype) == 1 || CPUBackend::supports_dtype(dtype);
+}
+
+odi_cuda_weight* CUDABackend::weight_for(const Tensor& b, int64_t N, int64_t K) {
+  const Key key{b.data(), (int)b.dtype(), N, K};
+  std::lock_guard<std::mutex> lk(mu_);
+  auto it = weights_.find(key);
+  if (it != weights_.end()) return it->second;
+  odi_cuda_weight* w = nullptr;
+  ck(odi_cuda_weight_upload(b.data(), (int)b.dtype(), N, K, &w), "weight upload");
+  weights_.emplace(key, w);
+  weight_bytes_ += (size_t)odi_cuda_tiled_bytes((int)b.dtype(), N, K);
+  return w;
+}
+
+void CUDABackend::release_weights() {
+  std::lock_guard<std::mutex> lk(mu_);
+  int first_rc = ODI_CUDA_OK;
+  for (auto& kv : weights_) {
+    int rc = odi_cuda_weight_free(kv.second);
+    if (rc != ODI_CUDA_OK && first_rc == ODI_CUDA_OK) first_rc = rc;
+  }
+  weights_.clear();
+  weight_bytes_ = 0;
+  ck(first_rc, "release_weights");
+}
+
+// Shape rules and messages follow CPUBackend::matmul (cpu_backend.cpp:177-227):
+// M = a.shape(-2) (1 for a vector), K = a.shape(-1), N = b.shape(-1), and K
+// must equal b.shape(-2) (b.shape(0) for a vector b).  Leading batch
+// dimensions of `a` are not iterated, exactly as there.
+void CUDABackend::matmul(Tensor& out, const Tensor& a, const Tensor& b) {
+  if (!dtype_is_quantized(b.dtype()) || odi_cuda_supports_dtype(b.dtype()) != 1) {
+    // fp32 x fp32, and the legacy Q4_1 / Q5_0 / Q5_1 block types, keep the
+    // CPU backend's implementation.
+    CPUBackend::matmul(out, a, b);
+    return;
+  }
+  if (a.ndim() < 1 || b.ndim() < 1) throw std::runtime_error("matmul: invalid tensor dimensions");
+  int64_t M = a.ndim() >= 2 ? a.shape(-2) : 1;
+  const int64_t K = a.shape(-1);
+  int64_t N = b.shape(-1);
+  if (b.ndim() == 1) {
+    N = 1;
+    if (K != b.shape(0)) throw std::runtime_error("matmul: dimension mismatch");
+  } else if (K != b.shape(-2)) {
+    throw std::runtime_error("matmul: dimension mismatch");
+  }
+  if (a.dtype() != ODI_DTYPE_F32) throw std::runtime_error("matmul: quantized weights require F32 activations");
+  if (!out.data() || !a.data() || !b.data()) throw std::runtime_error("matmul: null tensor data");
+  bind_device();
+  odi_cuda_weight* w = weight_for(b, N, K);
+  ck(odi_cuda_matmul_host(w, a.data_ptr<float>(), out.data_ptr<float>(), M, (int)act_, nullptr), "matmul");
+}
+
+void CUDABackend::quantized_matmul(Tensor& out, const Tensor& a, const Tensor& b_quant) {
+  matmul(out, a, b_quant);  // as cpu_backend.cpp:650-653
+}
+
+// Block order = element order [N][K], n = x.numel() values (cpu_backend.cpp:625-648).
+// A weight tensor has shape [K, N] (K the contiguous dimension); a 1-D
+// tensor is one row.
+void CUDABackend::dequantize(Tensor& out, const Tensor& x) {
+  if (odi_cuda_supports_dtype(x.dtype()) != 1) {
+    CPUBackend::dequantize(out, x);
+    return;
+  }
+  if (!out.data() || !x.data()) throw std::runtime_error("dequantize: null tensor data");
+  const int64_t K = x.ndim() >= 2 ? x.shape(0) : x.numel();
+  if (K <= 0 || x.numel() % K) throw std::runtime_error("dequantize: invalid shape");
+  const int64_t N = x.numel() / K;
+  bind_device();
+  odi_cuda_weight* w = weight_for(x, N, K);
+  ck(odi_cuda_dequantize_host(w, out.data_ptr<float>(), nullptr), "dequantize");
+}
+
+void CUDABackend::sync() {
+  bind_device();
+  ck(odi_cuda_sync(nullptr), "sync");
+}
+
+}  // namespace odi

@@ -1,0 +1,89 @@
+// cuda_backend.hpp -- odi::CUDABackend, the reference engine's Backend with
+// its quantized matrix product on the B200 (through include/odi_cuda.h).
+//
+// Drop-in for the factory slot left at src/compute/cpu/cpu_backend.cpp:1011-1013
+// (`case ODI_BACKEND_CUDA: // TODO: return std::make_unique<CUDABackend>();`).
+// Compiles against the reference tree: it includes its compute/backend.hpp
+// and compute/cpu/cpu_backend.hpp.
+//
+// What runs where:
+//   matmul / quantized_matmul with a quantized `b` (backend.hpp:38, 114;
+//     cpu_backend.cpp:177-227): on the GPU.  The weight's packed GGUF blocks
+//     are uploaded once and kept in HBM in the tiled layout, keyed by the
+//     host address of the blocks (the GGUF mmap view, valid while the Model
+//     lives, gguf_parser.cpp:614-628), dtype and shape; activations are
+//     copied in and the result copied out on every call, so `out` is ready
+//     when matmul returns, as Context expects (context.cpp:76-78).
+//   dequantize of a supported quantized tensor (backend.hpp:111): on the GPU.
+//   Everything else (element-wise ops, norms, attention, fp32 x fp32
+//   matmul) is the CPU backend's, inherited unchanged.
+//
+// Errors keep the reference's convention: a failure throws
+// std::runtime_error (cpu_backend.cpp:180,192,195,201,226); the message is
+// the library's odi_cuda_last_error() text.
+#pragma once
+
+#include <cstdint>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+
+#include "compute/cpu/cpu_backend.hpp"
+#include "odi_cuda.h"
+
+namespace odi {
+
+class CUDABackend : public CPUBackend {
+ public:
+  // Activation arithmetic of the quantized product.
+  //   Q8  : activations quantised to Q8_0 (the gguf definition), integer block
+  //         dots, fp32 scales -- the decode hot path.
+  //   F32 : fp32 activations times the exactly widened codes, fp32 sums --
+  //         the reference's own arithmetic.
+  enum class ActMode { Q8 = ODI_CUDA_ACT_Q8, F32 = ODI_CUDA_ACT_F32 };
+
+  // Throws std::runtime_error when `device` is not a usable sm_100 GPU.
+  // The environment variable ODI_CUDA_ACT=f32 selects ActMode::F32 when
+  // `act` is not given explicitly through the second constructor.
+  explicit CUDABackend(int num_threads = 0, int device = 0);
+  CUDABackend(int num_threads, int device, ActMode act);
+  ~CUDABackend() override;
+
+  CUDABackend(const CUDABackend&) = delete;
+  CUDABackend& operator=(const CUDABackend&) = delete;
+
+  odi_backend_type_t type() const override { return ODI_BACKEND_CUDA; }
+  std::string name() const override { return "CUDA"; }
+  std::string device_info() const override;
+  size_t available_memory() const override;
+  size_t used_memory() const override;
+  bool supports_dtype(odi_dtype_t dtype) const override;
+
+  void matmul(Tensor& out, const Tensor& a, const Tensor& b) override;
+  void quantized_matmul(Tensor& out, const Tensor& a, const Tensor& b_quant) override;
+  void dequantize(Tensor& out, const Tensor& x) override;
+  void sync() override;
+
+  // Drops every cached device copy of a weight (e.g. after unloading a model
+  // whose mmap address may be reused).
+  void release_weights();
+
+  // Number of weights currently held in HBM, and their bytes.
+  size_t cached_weights() const;
+
+  ActMode act_mode() const { return act_; }
+
+ private:
+  using Key = std::tuple<const void*, int, int64_t, int64_t>;
+  odi_cuda_weight* weight_for(const Tensor& b, int64_t N, int64_t K);
+  void bind_device() const;
+
+  int device_ = 0;
+  ActMode act_ = ActMode::Q8;
+  mutable std::mutex mu_;
+  std::map<Key, odi_cuda_weight*> weights_;
+  size_t weight_bytes_ = 0;
+};
+
+}  // namespace odi
