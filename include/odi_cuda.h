@@ -48,11 +48,20 @@ enum {
  *   ODI_CUDA_ACT_Q8  -- activations are quantised to Q8_0 first (bit-exact
  *                       with the GGUF Q8_0 quantiser) and dotted against the
  *                       weight codes in integer arithmetic; fp32 block scales.
+ *                       Streaming GEMV, 8 tokens per launch (decode).
  *   ODI_CUDA_ACT_F32 -- fp32 activations times the fp32-decoded weights, the
  *                       arithmetic of the reference's matmul_q4_0 /
  *                       matmul_q8_0 (cpu_backend.cpp:786-854) up to
- *                       summation order. */
-enum { ODI_CUDA_ACT_Q8 = 0, ODI_CUDA_ACT_F32 = 1 };
+ *                       summation order.  Streaming GEMV.
+ *   ODI_CUDA_ACT_F16 -- tensor cores (tcgen05): weights decoded to fp16
+ *                       (fp16(d*sc) * q - fp16(dmin*m)), activations rounded
+ *                       to fp16, exact products, fp32 sums (prefill).  For
+ *                       the dtypes odi_cuda_tc_supported accepts.
+ *   ODI_CUDA_ACT_AUTO -- ODI_CUDA_ACT_F16 when M >= ODI_CUDA_TC_MIN_TOKENS
+ *                       and the dtype has a tensor-core path, else
+ *                       ODI_CUDA_ACT_Q8. */
+enum { ODI_CUDA_ACT_Q8 = 0, ODI_CUDA_ACT_F32 = 1, ODI_CUDA_ACT_F16 = 2, ODI_CUDA_ACT_AUTO = 3 };
+#define ODI_CUDA_TC_MIN_TOKENS 64
 
 /* Flags for odi_cuda_matmul. */
 enum {
@@ -140,8 +149,13 @@ int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t 
 /* --- the quantized matrix product ------------------------------------------ */
 
 /* Device scratch needed by odi_cuda_matmul: 256 bytes holding the device
- * error word (activations are staged on chip, never in global memory). */
+ * error word for the streaming GEMV (activations are staged on chip, never
+ * in global memory); the tensor-core path adds its fp16 activation tiles
+ * (1024 + ceil(M/128)*128 * ceil(K/256)*256 * 2 bytes). */
 size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode);
+
+/* 1 if `dtype` has the tensor-core (ODI_CUDA_ACT_F16) path, else 0. */
+int odi_cuda_tc_supported(int dtype);
 
 /* y[M, N] = x[M, K] . dequant(W)^T in fp32 -- Backend::matmul /
  * quantized_matmul (backend.hpp:38, 114) with a = x, b = W.
@@ -196,9 +210,10 @@ int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* strea
  * (The weight itself is uploaded beforehand, at load time, by
  * odi_cuda_weight_upload.)
  *
- * Limit: 256 + round_up(M*K*4, 256) + M*N*4 <= ODI_CUDA_NOALLOC_SCRATCH_BYTES
- * (M=1 fits any N up to about two million); a larger call returns
- * ODI_CUDA_ERR_INVALID_ARGUMENT and runs nothing.
+ * Limit: round_up(W, 256) + round_up(M*K*4, 256) + M*N*4 <=
+ * ODI_CUDA_NOALLOC_SCRATCH_BYTES, W = odi_cuda_matmul_workspace_bytes (256
+ * on the streaming GEMV, so M=1 fits any N up to about two million); a
+ * larger call returns ODI_CUDA_ERR_INVALID_ARGUMENT and runs nothing.
  *
  * The first call on a device, with that device current, looks up the
  * array's device address; make that first call before any stream capture on

@@ -37,6 +37,9 @@ BLOCK_BYTES = {ODI_DTYPE_Q8_0: 34, ODI_DTYPE_Q4_0: 18, ODI_DTYPE_Q4_K: 144, ODI_
 
 ACT_Q8 = 0
 ACT_F32 = 1
+ACT_F16 = 2
+ACT_AUTO = 3
+TC_MIN_TOKENS = 64
 FLAG_PDL = 1
 
 # odi_error_t values (include/odi/odi_error.h:11-48)
@@ -72,6 +75,7 @@ SIGNATURES = {
     "odi_cuda_matmul_host": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "odi_cuda_matmul_host_noalloc": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "odi_cuda_dequantize_host": (_int, [_vp, _vp, _vp]),
+    "odi_cuda_tc_supported": (_int, [_int]),
 }
 
 # ODI_CUDA_NOALLOC_SCRATCH_BYTES (include/odi_cuda.h): the static device

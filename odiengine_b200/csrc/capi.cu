@@ -52,6 +52,20 @@ int num_sms_current() {
   return sms[dev];
 }
 
+// ODI_CUDA_ACT_AUTO resolved for this call; -1 for an unknown mode.
+int resolve_act_mode(int dt, int64_t M, int act_mode) {
+  switch (act_mode) {
+    case ODI_CUDA_ACT_Q8:
+    case ODI_CUDA_ACT_F32:
+    case ODI_CUDA_ACT_F16:
+      return act_mode;
+    case ODI_CUDA_ACT_AUTO:
+      return (tc_supported(dt) && M >= ODI_CUDA_TC_MIN_TOKENS) ? ODI_CUDA_ACT_F16 : ODI_CUDA_ACT_Q8;
+    default:
+      return -1;
+  }
+}
+
 int check_shape(int dt, int64_t N, int64_t K) {
   if (!dtype_ok(dt)) return fail(ODI_CUDA_ERR_UNSUPPORTED_DTYPE, "dtype %d is not supported by the CUDA backend", dt);
   if (N < 1 || K < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid weight shape N=%lld K=%lld", (long long)N, (long long)K);
@@ -218,9 +232,12 @@ int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t 
   return ODI_CUDA_OK;
 }
 
+int odi_cuda_tc_supported(int dtype) { return tc_supported(dtype) ? 1 : 0; }
+
 size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode) {
-  (void)act_mode;
   if (!dtype_ok(dtype) || M < 1 || N < 1 || K < 1) return 0;
+  if (resolve_act_mode(dtype, M, act_mode) == ODI_CUDA_ACT_F16)
+    return (size_t)(TC_X16_OFFSET + tc_x16_bytes(M, K));  // error word + fp16 activation tiles
   return WS_HEADER;  // the device error word; activations are staged on chip
 }
 
@@ -231,16 +248,34 @@ int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d
   if (rc) return rc;
   if (M < 0 || M > (1 << 20)) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M=%lld", (long long)M);
   if (M == 0) return ODI_CUDA_OK;
-  if (act_mode != ODI_CUDA_ACT_Q8 && act_mode != ODI_CUDA_ACT_F32)
-    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "unknown act_mode %d", act_mode);
+  const int mode = resolve_act_mode(dtype, M, act_mode);
+  if (mode < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "unknown act_mode %d", act_mode);
+  if (mode == ODI_CUDA_ACT_F16 && !tc_supported(dtype))
+    return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "dtype %d has no tensor-core path (ODI_CUDA_ACT_F16)", dtype);
   if (!d_w_tiled || !d_x || !d_y || !d_workspace) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
   if (((uintptr_t)d_w_tiled | (uintptr_t)d_workspace) & 15)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight and workspace must be 16-byte aligned");
-  if (workspace_bytes < WS_HEADER)
-    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %d bytes", workspace_bytes, WS_HEADER);
-  const bool f32 = act_mode == ODI_CUDA_ACT_F32;
-  const bool pdl = (flags & ODI_CUDA_FLAG_PDL) != 0;
+  const size_t need = odi_cuda_matmul_workspace_bytes(dtype, M, N, K, mode);
+  if (workspace_bytes < need)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
   cudaStream_t s = (cudaStream_t)stream;
+  if (mode == ODI_CUDA_ACT_F16) {
+    const int bn = tc_block_n((int)M);
+    TcArgs t;
+    t.w = (const uint8_t*)d_w_tiled;
+    t.x16 = (const uint8_t*)d_workspace + TC_X16_OFFSET;
+    t.y = d_y;
+    t.err = (int*)d_workspace;
+    t.N = N;
+    t.M = (int)M;
+    t.M_pad = (int)((M + bn - 1) / bn * bn);
+    t.KB = (int)((K + UNIT_COLS - 1) / UNIT_COLS);
+    CK(launch_act_pack_f16(d_x, t.M, K, t.M_pad, (uint8_t*)d_workspace + TC_X16_OFFSET, s), "act_pack_f16 launch");
+    CK(launch_qgemm_tc(dtype, t, s), "qgemm_tc launch");
+    return ODI_CUDA_OK;
+  }
+  const bool f32 = mode == ODI_CUDA_ACT_F32;
+  const bool pdl = (flags & ODI_CUDA_FLAG_PDL) != 0;
   const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
   if (plan.C == 0)
     return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
@@ -359,10 +394,12 @@ extern "C" int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, 
 // loop that cannot take cudaMalloc's synchronisation).  Instead of the
 // cudaMalloc-grown arena above, x, y and the error word live in one static
 // device array per GPU, held from module load until the process exits:
-//   [0, 256)                    error word (must be zero when a product starts;
-//                               cleared by every call)
-//   [256, 256 + rx)             x, M*K fp32     (rx = M*K*4 rounded up to 256)
-//   [256 + rx, ... + M*N*4)     y, M*N fp32
+//   [0, ws)                     the product's workspace: the error word first
+//                               (must be zero when a product starts; cleared by
+//                               every call), then, on the tensor-core path, the
+//                               fp16 activation tiles; ws rounded up to 256 = rw
+//   [rw, rw + rx)               x, M*K fp32     (rx = M*K*4 rounded up to 256)
+//   [rw + rx, ... + M*N*4)      y, M*N fp32
 // Every call shares the array; calls whose GPU work overlaps race on it.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char g_noalloc_scratch[ODI_CUDA_NOALLOC_SCRATCH_BYTES];
@@ -392,22 +429,25 @@ extern "C" int odi_cuda_matmul_host_noalloc(const odi_cuda_weight* w, const floa
   if (!w || !h_x || !h_y) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
   if (M < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M");
   if (M == 0) return ODI_CUDA_OK;
-  if (act_mode != ODI_CUDA_ACT_Q8 && act_mode != ODI_CUDA_ACT_F32)
+  if (resolve_act_mode(w->dtype, M, act_mode) < 0)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "unknown act_mode %d", act_mode);
   const int64_t cap = (int64_t)ODI_CUDA_NOALLOC_SCRATCH_BYTES;
   const int64_t per_token = 4 * (w->K + w->N);
   bool fits = M <= (cap - WS_HEADER) / per_token;  // bounds M before any product can overflow
-  int64_t x_off = WS_HEADER, y_off = 0, need = 0;
+  int64_t ws = 0, x_off = 0, y_off = 0, need = 0;
   if (fits) {
+    // the workspace (error word first), then x, then y
+    ws = (int64_t)odi_cuda_matmul_workspace_bytes(w->dtype, M, w->N, w->K, act_mode);
+    x_off = (ws + 255) / 256 * 256;
     y_off = x_off + (M * w->K * 4 + 255) / 256 * 256;
     need = y_off + M * w->N * 4;
-    fits = need <= cap;
+    fits = ws > 0 && need <= cap;
   }
   if (!fits)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT,
                 "odi_cuda_matmul_host_noalloc: M=%lld tokens of K=%lld inputs and N=%lld outputs exceed its "
-                "static scratch of %lld bytes (needs 256 + round_up(M*K*4, 256) + M*N*4); use "
-                "odi_cuda_matmul_host or fewer tokens per call",
+                "static scratch of %lld bytes (needs round_up(workspace, 256) + round_up(M*K*4, 256) + M*N*4); "
+                "use odi_cuda_matmul_host or fewer tokens per call",
                 (long long)M, (long long)w->K, (long long)w->N, (long long)cap);
   int dev = 0;
   CK(cudaGetDevice(&dev), "cudaGetDevice");
@@ -421,7 +461,7 @@ extern "C" int odi_cuda_matmul_host_noalloc(const odi_cuda_weight* w, const floa
   float* d_y = reinterpret_cast<float*>(scr + y_off);
   CK(cudaMemsetAsync(scr, 0, sizeof(int), s), "clear error word");
   CK(cudaMemcpyAsync(d_x, h_x, (size_t)(M * w->K) * sizeof(float), cudaMemcpyHostToDevice, s), "H2D x");
-  rc = odi_cuda_matmul(w->dtype, w->data, d_x, d_y, M, w->N, w->K, act_mode, scr, WS_HEADER, 0, stream);
+  rc = odi_cuda_matmul(w->dtype, w->data, d_x, d_y, M, w->N, w->K, act_mode, scr, (size_t)ws, 0, stream);
   if (rc) return rc;
   CK(cudaMemcpyAsync(h_y, d_y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
   int err = 0;

@@ -43,4 +43,22 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
 cudaError_t launch_gemv(int dt, bool f32act, const GemvPlan& plan, const GemvArgs& a, bool pdl,
                         cudaStream_t s);
 
+// Prefill-shaped GEMM on the tensor cores (qgemm_tc.cu).  Weights decoded to
+// fp16 in shared memory, activations packed to fp16 operand tiles in the
+// workspace by launch_act_pack_f16, fp32 accumulation in tensor memory.
+struct TcArgs {
+  const uint8_t* w;    // tiled weight
+  const uint8_t* x16;  // packed fp16 activation tiles (tc_x16_bytes)
+  float* y;            // [M][N] fp32
+  int* err;            // device error word
+  int64_t N;
+  int M, M_pad, KB;    // tokens, tokens rounded up to the block, 256-column spans
+};
+constexpr int TC_X16_OFFSET = 1024;  // packed activations start here in the workspace
+bool tc_supported(int dt);
+int tc_block_n(int M);
+int64_t tc_x16_bytes(int64_t M, int64_t K);
+cudaError_t launch_act_pack_f16(const float* x, int M, int64_t K, int M_pad, uint8_t* x16, cudaStream_t s);
+cudaError_t launch_qgemm_tc(int dt, const TcArgs& a, cudaStream_t s);
+
 }  // namespace odi_cuda

@@ -65,6 +65,8 @@ def lib():
         L.orc_quantize_act_planes.argtypes = [_vp, _i64, _i64, _vp, _vp]
         L.orc_matmul_q8act.argtypes = [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]
         L.orc_fp32_bound.argtypes = [ctypes.c_int, _vp, _vp, _i64, _i64, _i64, _vp]
+        L.orc_term_magnitude.argtypes = [ctypes.c_int, _vp, _i64, _i64, _vp]
+        L.orc_block_factors.argtypes = [ctypes.c_int, _vp, _i64, _i64, _vp, _vp, _vp]
         L.orc_tiled_bytes.restype = _i64
         L.orc_tiled_bytes.argtypes = [ctypes.c_int, _i64, _i64]
         L.orc_unit_bytes.restype = _i64
@@ -189,6 +191,69 @@ def fp32_bound(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int) -> np.ndar
     if rc:
         raise ValueError(f"orc_fp32_bound failed ({rc})")
     return bound
+
+
+def term_magnitude(dtype: int, blocks: np.ndarray, N: int, K: int) -> np.ndarray:
+    """|A_g*q| + |B_g| per weight element ([N, K]; >= |w|): the scale of the
+    error of decoding a weight to fp16 from fp16-rounded factors."""
+    out = np.zeros((N, K), dtype=np.float32)
+    rc = lib().orc_term_magnitude(dtype, _p(np.ascontiguousarray(blocks)), N, K, _p(out))
+    if rc:
+        raise ValueError(f"orc_term_magnitude failed ({rc})")
+    return out
+
+
+def decode_f16(dtype: int, blocks: np.ndarray, N: int, K: int) -> np.ndarray:
+    """The fp16 weights the tensor-core path decodes ([N, K] float16):
+    rne16(q * rne16(A) - rne16(B)) with value = A*q - B, one rounding of the
+    exact result (an IEEE fp16 fma), A and B rounded from fp32."""
+    A = np.zeros((N, K), dtype=np.float32)
+    B = np.zeros((N, K), dtype=np.float32)
+    q = np.zeros((N, K), dtype=np.int32)
+    rc = lib().orc_block_factors(dtype, _p(np.ascontiguousarray(blocks)), N, K, _p(A), _p(B), _p(q))
+    if rc:
+        raise ValueError(f"orc_block_factors failed ({rc})")
+    a16 = A.astype(np.float16).astype(np.float64)
+    b16 = B.astype(np.float16).astype(np.float64)
+    return (q.astype(np.float64) * a16 - b16).astype(np.float16)
+
+
+def matmul_f16(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int):
+    """Restatement of the tensor-core product: fp16 activations times
+    decode_f16 weights summed exactly (float64), and the fp32-summation
+    bound 2 (K + 16) 2^-24 sum |x16 w16| that any summation order meets."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    x16 = x.astype(np.float16).astype(np.float64)
+    w16 = decode_f16(dtype, blocks, N, K).astype(np.float64)
+    y = x16 @ w16.T
+    bound = 2.0 * (K + 16) * 2.0 ** -24 * (np.abs(x16) @ np.abs(w16).T)
+    return y, bound
+
+
+def f16_bound(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int) -> np.ndarray:
+    """Bound on |y - y_exact| for the tensor-core path (fp16 weights decoded
+    as fp16(A)*q - fp16(B) in one fp16 fma, fp16-rounded activations, exact
+    products, fp32 sums in any order), per output [M, N]:
+
+        1.01 * (2^-10 * S_T + 2^-11 * S_W) + 2 (K + 16) 2^-24 * 1.01 * S_T
+        + 2^-20 * sum|x| + 2^-24 * sum|w|
+
+    S_T = sum_k |x_k| T_k (T = term_magnitude), S_W = sum_k |x_k| |w_k|.
+    The first term: |fp16 w - w| <= 2^-11 (T + |w|) + 2^-21 and
+    |fp16 x - x| <= 2^-11 |x| + 2^-25 (round to nearest, subnormals
+    included); the second: fp32 reassociation of K terms of size
+    <= 1.01 |x| T; the last two: the absolute (subnormal) parts."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    ax = np.abs(x).astype(np.float64)
+    T = term_magnitude(dtype, blocks, N, K).astype(np.float64)
+    W = np.abs(dequantize(dtype, blocks, N, K)).astype(np.float64)
+    S_T = ax @ T.T
+    S_W = ax @ W.T
+    u = 2.0 ** -24
+    return (1.01 * (2.0 ** -10 * S_T + 2.0 ** -11 * S_W) + 2.0 * (K + 16) * u * 1.01 * S_T
+            + 2.0 ** -20 * ax.sum(1)[:, None] + u * W.sum(1)[None, :])
 
 
 def tiled_bytes(dtype: int, N: int, K: int) -> int:

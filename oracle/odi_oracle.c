@@ -604,6 +604,51 @@ static void block_codes(int dtype, const uint8_t* blk, wcodes* c) {
   }
 }
 
+/* Per-element term magnitude T = |A_g * q| + |B_g| of the decomposition
+ * value = A_g * q - B_g above (>= |value|; = |value| without a min term).
+ * Rounding the two factors to fp16 before combining them errs by at most
+ * 2^-11 * T per factor, so T is the scale of the fp16 decoding error of the
+ * tensor-core path.  out is [N][K]. */
+int orc_term_magnitude(int dtype, const void* blocks, int64_t N, int64_t K, float* out) {
+  if (!supported(dtype) || N < 0 || K < 0) return -1;
+  int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
+  int64_t nb = (K + be - 1) / be;
+  wcodes c;
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t b = 0; b < nb; ++b) {
+      block_codes(dtype, (const uint8_t*)blocks + (n * nb + b) * bb, &c);
+      for (int j = 0; j < be && b * be + j < K; ++j) {
+        int g = j / c.gsize;
+        float t = fabsf(c.A[g] * (float)c.q[j]) + (c.has_min ? fabsf(c.B[g]) : 0.0f);
+        out[n * K + b * be + j] = t;
+      }
+    }
+  }
+  return 0;
+}
+
+/* Per-element factors of value = A * q - B (A, B fp32 as computed from the
+ * block's fp16 fields; B = 0 without a min term).  Out arrays are [N][K]. */
+int orc_block_factors(int dtype, const void* blocks, int64_t N, int64_t K, float* A, float* B, int32_t* q) {
+  if (!supported(dtype) || N < 0 || K < 0) return -1;
+  int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
+  int64_t nb = (K + be - 1) / be;
+  wcodes c;
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t b = 0; b < nb; ++b) {
+      block_codes(dtype, (const uint8_t*)blocks + (n * nb + b) * bb, &c);
+      for (int j = 0; j < be && b * be + j < K; ++j) {
+        int g = j / c.gsize;
+        int64_t o = n * K + b * be + j;
+        A[o] = c.A[g];
+        B[o] = c.has_min ? c.B[g] : 0.0f;
+        q[o] = c.q[j];
+      }
+    }
+  }
+  return 0;
+}
+
 int orc_matmul_q8act(int dtype, float* out, const float* a, const void* b, int64_t M, int64_t K,
                      int64_t N, float* bound, float* mag_out) {
   if (!supported(dtype) || M < 0 || N < 0 || K < 0) return -1;

@@ -90,6 +90,12 @@ void orc_quantize_act_planes(const float* x, int64_t M, int64_t K, int8_t* xq, v
  * dequantised weights: sum_b 0.5625*d_x,b*sum|w| plus fp32 rounding terms.
  * If mag != NULL, mag[m*N+n] receives sum of |scaled block terms|, the
  * magnitude that bounds fp32 reordering error of the Q8 product itself. */
+/* |A_g*q| + |B_g| per element ([N][K]): scale of fp16 decoding errors. */
+int orc_term_magnitude(int dtype, const void* blocks, int64_t N, int64_t K, float* out);
+
+/* value = A*q - B per element ([N][K] each). */
+int orc_block_factors(int dtype, const void* blocks, int64_t N, int64_t K, float* A, float* B, int32_t* q);
+
 int orc_matmul_q8act(int dtype, float* out, const float* a, const void* b,
                      int64_t M, int64_t K, int64_t N, float* bound, float* mag);
 
