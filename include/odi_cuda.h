@@ -151,7 +151,7 @@ int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t 
 /* Device scratch needed by odi_cuda_matmul: 256 bytes holding the device
  * error word for the streaming GEMV (activations are staged on chip, never
  * in global memory); the tensor-core path adds its fp16 activation tiles
- * (1024 + ceil(M/128)*128 * ceil(K/256)*256 * 2 bytes). */
+ * (1024 + ceil(M/256)*256 * ceil(K/256)*256 * 2 bytes). */
 size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode);
 
 /* 1 if `dtype` has the tensor-core (ODI_CUDA_ACT_F16) path, else 0. */

@@ -52,13 +52,13 @@ struct TcArgs {
   float* y;            // [M][N] fp32
   int* err;            // device error word
   int64_t N;
-  int M, M_pad, KB;    // tokens, tokens rounded up to the block, 256-column spans
+  int M, M_pad, KB;    // tokens, tokens rounded up to 256 (packed rows), 256-column spans
 };
 constexpr int TC_X16_OFFSET = 1024;  // packed activations start here in the workspace
 bool tc_supported(int dt);
-int tc_block_n(int M);
+int tc_block_n(int64_t M, int64_t N, int num_sms);
 int64_t tc_x16_bytes(int64_t M, int64_t K);
 cudaError_t launch_act_pack_f16(const float* x, int M, int64_t K, int M_pad, uint8_t* x16, cudaStream_t s);
-cudaError_t launch_qgemm_tc(int dt, const TcArgs& a, cudaStream_t s);
+cudaError_t launch_qgemm_tc(int dt, int bn, const TcArgs& a, cudaStream_t s);
 
 }  // namespace odi_cuda

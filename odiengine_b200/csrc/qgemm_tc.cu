@@ -13,11 +13,13 @@
 //   warp 1     allocates TMEM; one lane issues tcgen05.mma (kind::f16,
 //              M=128, N=BN, K=16; four per k-block) and tcgen05.commit
 //              releases the shared-memory stages it has read.
-//   warps 2-5  decode: thread r owns weight row r; per k-block it writes the
-//              row's 64 fp16 weights (128 bytes) into the K-major
-//              128-byte-swizzled operand tile, then fences the writes for
-//              the tensor core's async proxy.  At the end they read the
-//              accumulators back (tcgen05.ld) and write y.
+//   warps 2-9  decode: thread (h, r) owns half h of weight row r; per
+//              k-block it writes 32 of the row's 64 fp16 weights (64 of its
+//              128 bytes) into the K-major 128-byte-swizzled operand tile,
+//              then fences the writes for the tensor core's async proxy.
+//              At the end they read the accumulators back (tcgen05.ld, two
+//              warps per 32-lane quarter, half of the columns each) and
+//              write y.
 //
 // Operand tiles (A = weights, B = activations) use the canonical K-major
 // SWIZZLE_128B layout: rows of 64 fp16 (128 B), 8-row atoms of 1024 B
@@ -41,7 +43,8 @@ namespace tc {
 constexpr int BM = 128;            // weight rows per CTA (UMMA M)
 constexpr int BK = 64;             // k-block: one 128-byte swizzle row of fp16
 constexpr int KBS = UNIT_COLS / BK;  // k-blocks per 256-column span (4)
-constexpr int NTHREADS = 192;
+constexpr int NDEC = 256;          // decode threads: 2 per weight row
+constexpr int NTHREADS = 64 + NDEC;
 constexpr int A_STAGE = BM * BK * 2;  // 16 KB
 constexpr int ERR_TC_WAIT = 16;
 
@@ -51,7 +54,7 @@ struct Cfg {
   static constexpr int RAW = 2 * UB;                    // two 64-row units
   static constexpr int RAW_STAGE = (RAW + 1023) / 1024 * 1024;
   static constexpr int B_STAGE = BN * BK * 2;
-  static constexpr int SA = 4, SB = 4;
+  static constexpr int SA = 4, SB = BN >= 256 ? 3 : 4;
   static constexpr int RS = (BN >= 256 || UB > 10000) ? 2 : 3;
   static constexpr int A_OFF = 0;
   static constexpr int B_OFF = A_OFF + SA * A_STAGE;
@@ -136,9 +139,10 @@ __device__ __forceinline__ uint4 chunk_q4(uint32_t w0, uint32_t w1, __half2 s, _
   return o;
 }
 
-// Q4_K: one k-block (64 values = sub-blocks 2j and 2j+1) of one row into its
-// swizzled 128-byte operand row.
-__device__ __forceinline__ void decode_q4k_kblock(const uint8_t* sl, int j, uint8_t* arow, int sw) {
+// Q4_K: half h of one k-block (64 values = sub-blocks 2j and 2j+1; h = 0 the
+// low nibbles = sub-block 2j = chunks 0-3, h = 1 the high nibbles = sub-block
+// 2j+1 = chunks 4-7) of one row into its swizzled 128-byte operand row.
+__device__ __forceinline__ void decode_q4k_kblock(const uint8_t* sl, int j, int h, uint8_t* arow, int sw) {
   const uint4 hd = ld128s(sl);
   const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
   const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
@@ -146,36 +150,34 @@ __device__ __forceinline__ void decode_q4k_kblock(const uint8_t* sl, int j, uint
   const uint32_t scL = hd.y & 0x3F3F3F3Fu, mnL = hd.z & 0x3F3F3F3Fu;
   const uint32_t scH = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
   const uint32_t mnH = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
-  const int b0 = 2 * j, b1 = 2 * j + 1;
-  const uint32_t sc0 = ((b0 < 4 ? scL : scH) >> (8 * (b0 & 3))) & 0xFFu;
-  const uint32_t sc1 = ((b1 < 4 ? scL : scH) >> (8 * (b1 & 3))) & 0xFFu;
-  const uint32_t m0 = ((b0 < 4 ? mnL : mnH) >> (8 * (b0 & 3))) & 0xFFu;
-  const uint32_t m1 = ((b1 < 4 ? mnL : mnH) >> (8 * (b1 & 3))) & 0xFFu;
-  const __half2 s0 = __float2half2_rn(d * (float)sc0), s1 = __float2half2_rn(d * (float)sc1);
-  const __half2 n0 = __float2half2_rn(-(dmin * (float)m0)), n1 = __float2half2_rn(-(dmin * (float)m1));
+  const int b = 2 * j + h;
+  const uint32_t sc = ((b < 4 ? scL : scH) >> (8 * (b & 3))) & 0xFFu;
+  const uint32_t mn = ((b < 4 ? mnL : mnH) >> (8 * (b & 3))) & 0xFFu;
+  const __half2 s = __float2half2_rn(d * (float)sc);
+  const __half2 n = __float2half2_rn(-(dmin * (float)mn));
   const uint4 qa = ld128s(sl + 16 + 32 * j), qb = ld128s(sl + 32 + 32 * j);
   const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    st128s(arow + ((c ^ sw) << 4), chunk_q4<false>(q[2 * c], q[2 * c + 1], s0, n0));
-    st128s(arow + (((c + 4) ^ sw) << 4), chunk_q4<true>(q[2 * c], q[2 * c + 1], s1, n1));
+    const uint4 o = h ? chunk_q4<true>(q[2 * c], q[2 * c + 1], s, n) : chunk_q4<false>(q[2 * c], q[2 * c + 1], s, n);
+    st128s(arow + (((c + 4 * h) ^ sw) << 4), o);
   }
 }
 
-// Q6_K: one k-block of one row.  Slice = scales[16], ql[128], qh[64]; d from
+// Q6_K: half h of one k-block of one row.  Slice = scales[16], ql[128], qh[64]; d from
 // the unit's tail plane.  k-block kb = half (kb >> 1), quarter groups
 // g0 = 2*(kb & 1) and g0+1 of that half; group g of a half takes the
 // (g >> 1 ? high : low) nibbles of ql[(g & 1) * 32 + l] and bits 2g..2g+1 of
 // qh[l], l = 0..31; value = d * sc[8*half + 2g + l/16] * (q - 32).
-__device__ __forceinline__ void decode_q6k_kblock(const uint8_t* sl, float d, int kb, uint8_t* arow, int sw) {
+__device__ __forceinline__ void decode_q6k_kblock(const uint8_t* sl, float d, int kb, int h, uint8_t* arow, int sw) {
   const int half = kb >> 1, g0 = 2 * (kb & 1);
   const uint8_t* ql = sl + 16 + 64 * half;
   const uint8_t* qh = sl + 144 + 32 * half;
   const uint4 scv = ld128s(sl);
   const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
   const __half2 k1056 = __float2half2_rn(1056.0f);
-#pragma unroll
-  for (int gg = 0; gg < 2; ++gg) {
+  {
+    const int gg = h;  // decode half h = quarter group g0 + h (chunks 4h .. 4h+3)
     const int g = g0 + gg;
     const uint8_t* qlp = ql + (g & 1) * 32;
     const bool hi = (g >> 1) != 0;
@@ -237,10 +239,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (tid == 0) {
     for (int i = 0; i < C::RS; ++i) {
       mbar_init(&full_r[i], 1);
-      mbar_init(&empty_r[i], 128);
+      mbar_init(&empty_r[i], NDEC);
     }
     for (int i = 0; i < C::SA; ++i) {
-      mbar_init(&full_a[i], 128);
+      mbar_init(&full_a[i], NDEC);
       mbar_init(&empty_a[i], 1);
     }
     for (int i = 0; i < C::SB; ++i) {
@@ -307,8 +309,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mma_commit(accum);  // arrives once every MMA issued above has completed
     }
   } else {
-    // ---------------- decode + epilogue (warps 2-5) ----------------
-    const int r = tid - 64;  // weight row within the CTA
+    // ---------------- decode + epilogue (warps 2-9) ----------------
+    const int r = (tid - 64) & (BM - 1);  // weight row within the CTA
+    const int h = (tid - 64) >> 7;        // half of the row's k-block
     const int u = r >> 6, sl_i = r & 63;
     uint8_t* arow0 = a_st + (r >> 3) * 1024 + (r & 7) * 128;
     const int sw = r & 7;
@@ -327,24 +330,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         uint8_t* arow = arow0 + as * A_STAGE;
         if (!live) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) st128s(arow + (c << 4), make_uint4(0, 0, 0, 0));
+          for (int c = 0; c < 4; ++c) st128s(arow + ((c + 4 * h) << 4), make_uint4(0, 0, 0, 0));
         } else if (DT == Q4_K) {
-          decode_q4k_kblock(sl, q, arow, sw);
+          decode_q4k_kblock(sl, q, h, arow, sw);
         } else if (DT == Q6_K) {
-          decode_q6k_kblock(sl, d6, q, arow, sw);
+          decode_q6k_kblock(sl, d6, q, h, arow, sw);
         }
         fence_async_smem();
         mbar_arrive(&full_a[as]);
       }
       mbar_arrive(&empty_r[rs]);
     }
-    // epilogue: accumulator row = TMEM lane 32 * (warp % 4) + lane
+    // epilogue: accumulator row = TMEM lane 32 * (warp % 4) + lane; the two
+    // warps of a quarter take half of the columns each
     if (mbar_wait(accum, 0, err, ERR_TC_WAIT)) {
       tc_fence_after();
       const int quarter = warp & 3;
+      const int chalf = (warp - 2) >> 2;
       const int64_t row = (int64_t)blockIdx.x * BM + quarter * 32 + lane;
 #pragma unroll 1
-      for (int c = 0; c < BN / 16; ++c) {
+      for (int c = chalf * (BN / 32); c < (chalf + 1) * (BN / 32); ++c) {
         float v[16];
         tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 16), v);
         if (row < N) {
@@ -404,7 +409,7 @@ static cudaError_t launch_tc(const TcArgs& a, cudaStream_t s) {
     attr_set[dev] = true;
   }
   const int G = (int)((a.N + UNIT_ROWS - 1) / UNIT_ROWS);
-  dim3 grid((G + 1) / 2, a.M_pad / BN);
+  dim3 grid((G + 1) / 2, (a.M + BN - 1) / BN);
   kern<<<grid, NTHREADS, C::SMEM, s>>>(a.w, a.x16, a.y, a.err, a.N, a.M, a.M_pad, G, a.KB);
   return cudaGetLastError();
 }
@@ -413,11 +418,31 @@ static cudaError_t launch_tc(const TcArgs& a, cudaStream_t s) {
 
 bool tc_supported(int dt) { return dt == Q4_K || dt == Q6_K; }
 
-int tc_block_n(int M) { (void)M; return 128; }
+// Token block (UMMA N) for M tokens against N weight rows on num_sms SMs,
+// one CTA per SM: estimated time = waves x per-k-block cost, where a
+// k-block costs about max(BN, 160) token-columns (the decode of the
+// 128 x 64 weight block bounds small BN).
+int tc_block_n(int64_t M, int64_t N, int num_sms) {
+  const int64_t rowtiles = (N + tc::BM - 1) / tc::BM;
+  const int sms = num_sms > 0 ? num_sms : 148;
+  int best = 128;
+  double best_t = 1e300;
+  for (int bn = 128; bn <= 256; bn *= 2) {
+    const int64_t tiles = rowtiles * ((M + bn - 1) / bn);
+    const double waves = (double)((tiles + sms - 1) / sms);
+    const double t = waves * (bn > 160 ? bn : 160);
+    if (t < best_t) {
+      best_t = t;
+      best = bn;
+    }
+  }
+  return best;
+}
 
+// Packed activations: tokens padded to a multiple of 256 (any block), K to
+// whole 256-column spans.
 int64_t tc_x16_bytes(int64_t M, int64_t K) {
-  const int bn = tc_block_n((int)M);
-  const int64_t M_pad = (M + bn - 1) / bn * bn;
+  const int64_t M_pad = (M + 255) / 256 * 256;
   const int64_t nkb = (K + UNIT_COLS - 1) / UNIT_COLS * tc::KBS;
   return nkb * M_pad * tc::BK * 2;
 }
@@ -431,12 +456,17 @@ cudaError_t launch_act_pack_f16(const float* x, int M, int64_t K, int M_pad, uin
   return cudaGetLastError();
 }
 
-cudaError_t launch_qgemm_tc(int dt, const TcArgs& a, cudaStream_t s) {
+template <int BN>
+static cudaError_t launch_bn(int dt, const TcArgs& a, cudaStream_t s) {
   switch (dt) {
-    case Q4_K: return tc::launch_tc<Q4_K, 128>(a, s);
-    case Q6_K: return tc::launch_tc<Q6_K, 128>(a, s);
+    case Q4_K: return tc::launch_tc<Q4_K, BN>(a, s);
+    case Q6_K: return tc::launch_tc<Q6_K, BN>(a, s);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_qgemm_tc(int dt, int bn, const TcArgs& a, cudaStream_t s) {
+  return bn == 256 ? launch_bn<256>(dt, a, s) : launch_bn<128>(dt, a, s);
 }
 
 }  // namespace odi_cuda
