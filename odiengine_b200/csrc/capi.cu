@@ -260,7 +260,7 @@ int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
   cudaStream_t s = (cudaStream_t)stream;
   if (mode == ODI_CUDA_ACT_F16) {
-    const int bn = tc_block_n(M, N, num_sms_current());
+    const TcPlan plan = make_tc_plan(M, N, K, num_sms_current());
     TcArgs t;
     t.w = (const uint8_t*)d_w_tiled;
     t.x16 = (const uint8_t*)d_workspace + TC_X16_OFFSET;
@@ -271,7 +271,7 @@ int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d
     t.M_pad = (int)((M + 255) / 256 * 256);
     t.KB = (int)((K + UNIT_COLS - 1) / UNIT_COLS);
     CK(launch_act_pack_f16(d_x, t.M, K, t.M_pad, (uint8_t*)d_workspace + TC_X16_OFFSET, s), "act_pack_f16 launch");
-    CK(launch_qgemm_tc(dtype, bn, t, s), "qgemm_tc launch");
+    CK(launch_qgemm_tc(dtype, plan, t, s), "qgemm_tc launch");
     return ODI_CUDA_OK;
   }
   const bool f32 = mode == ODI_CUDA_ACT_F32;

@@ -56,9 +56,14 @@ struct TcArgs {
 };
 constexpr int TC_X16_OFFSET = 1024;  // packed activations start here in the workspace
 bool tc_supported(int dt);
-int tc_block_n(int64_t M, int64_t N, int num_sms);
+struct TcPlan {
+  int BN;     // tokens per CTA (UMMA N): 32, 64, 128 or 256
+  int C;      // K split: CTAs per cluster, each with `chunk` spans
+  int chunk;
+};
+TcPlan make_tc_plan(int64_t M, int64_t N, int64_t K, int num_sms);
 int64_t tc_x16_bytes(int64_t M, int64_t K);
 cudaError_t launch_act_pack_f16(const float* x, int M, int64_t K, int M_pad, uint8_t* x16, cudaStream_t s);
-cudaError_t launch_qgemm_tc(int dt, int bn, const TcArgs& a, cudaStream_t s);
+cudaError_t launch_qgemm_tc(int dt, const TcPlan& p, const TcArgs& a, cudaStream_t s);
 
 }  // namespace odi_cuda

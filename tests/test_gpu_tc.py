@@ -6,8 +6,10 @@ Two checks per output element:
         |y - y16| <= 2 (K + 16) 2^-24 sum |x16 w16|     (fp32 summation order)
   * vs the exact real product of the GGUF weights (the reference's matmul up
     to fp32 rounding), oracle.f16_bound (fp16 rounding of both operands).
-At the full prefill shapes the reference is computed for a sample of weight
-rows (rows are independent outputs).
+At the full prefill and batched-decode shapes the reference is computed for
+a sample of weight rows (rows are independent outputs).  The shapes cover
+every token block (32, 64, 128, 256) and K splits of 1, 2, 4 and 8 CTAs
+(cluster reduce-scatter through distributed shared memory).
 """
 import numpy as np
 import pytest
@@ -53,7 +55,8 @@ def _check(dt, x, blocks, N, y, rows=None):
 
 @pytest.mark.parametrize("dt", TC)
 @pytest.mark.parametrize("N,K,M", [(128, 256, 64), (256, 1024, 128), (200, 512, 130), (64, 768, 1),
-                                   (1000, 2048, 300)])
+                                   (1000, 2048, 300), (512, 4096, 16), (4096, 4096, 8), (330, 7936, 40),
+                                   (384, 1024, 64)])
 def test_tc_small(cuda_lib, dt, N, K, M):
     b = O.quantize(dt, O.seeded_weights(N, K, seed=N))
     x = O.seeded_acts(M, K, seed=K)
@@ -62,7 +65,8 @@ def test_tc_small(cuda_lib, dt, N, K, M):
 
 
 @pytest.mark.parametrize("dt", TC)
-@pytest.mark.parametrize("N,K,M", [(14336, 4096, 512), (4096, 14336, 512), (14336, 4096, 2048)])
+@pytest.mark.parametrize("N,K,M", [(14336, 4096, 512), (4096, 14336, 512), (14336, 4096, 2048),
+                                   (4096, 14336, 2048), (28672, 8192, 32), (8192, 28672, 32)])
 def test_tc_prefill_shapes(cuda_lib, dt, N, K, M):
     b = O.quantize(dt, O.seeded_weights(N, K, seed=0))
     x = O.seeded_acts(M, K, seed=1)
