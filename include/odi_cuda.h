@@ -61,7 +61,9 @@ enum {
  *                       and the dtype has a tensor-core path, else
  *                       ODI_CUDA_ACT_Q8. */
 enum { ODI_CUDA_ACT_Q8 = 0, ODI_CUDA_ACT_F32 = 1, ODI_CUDA_ACT_F16 = 2, ODI_CUDA_ACT_AUTO = 3 };
-#define ODI_CUDA_TC_MIN_TOKENS 64
+/* From 9 tokens the streaming GEMV needs a second pass over the weight,
+ * and the tensor-core path is faster on every measured decode shape. */
+#define ODI_CUDA_TC_MIN_TOKENS 9
 
 /* Flags for odi_cuda_matmul. */
 enum {

@@ -39,7 +39,7 @@ ACT_Q8 = 0
 ACT_F32 = 1
 ACT_F16 = 2
 ACT_AUTO = 3
-TC_MIN_TOKENS = 64
+TC_MIN_TOKENS = 9  # ODI_CUDA_TC_MIN_TOKENS
 FLAG_PDL = 1
 
 # odi_error_t values (include/odi/odi_error.h:11-48)

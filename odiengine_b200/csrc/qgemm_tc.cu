@@ -616,8 +616,10 @@ bool tc_supported(int dt) { return dt == Q4_K || dt == Q6_K; }
 // Work plan: token block BN (the UMMA N) and the K split C (cluster size).
 // Estimated time = the CTAs one SM must run (ceil(tiles / SMs)) x the cost
 // of one CTA: (spans + 2 for the prologue and epilogue + BN/64 for the
-// reduce-scatter when K is split) x 4 k-blocks x max(BN, 160) token-columns
-// (the decode of the 128 x 64 weight block bounds small BN).
+// reduce-scatter when K is split) x 4 atoms x the cost of one 64-column
+// atom in cycles, the larger of the tensor work (about 2.93 * BN at the
+// measured rate), the issuing thread (about 95 per MMA, 4 per atom, plus
+// about 200 per stage of KSUB atoms) and the decode (about 300).
 TcPlan make_tc_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
   const int64_t rowtiles = (N + tc::BM - 1) / tc::BM;
   const int KB = (int)((K + UNIT_COLS - 1) / UNIT_COLS);
@@ -634,8 +636,12 @@ TcPlan make_tc_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
       if (ceff != c) continue;  // every rank needs at least one span
       const int64_t tiles = rowtiles * ((M + bn - 1) / bn) * ceff;
       const double per_sm = (double)((tiles + sms - 1) / sms);
+      const int ksub = bn <= 32 ? 4 : (bn <= 128 ? 2 : 1);
+      double atom = 2.93 * bn;
+      if (atom < 380.0 + 200.0 / ksub) atom = 380.0 + 200.0 / ksub;
+      if (atom < 300.0) atom = 300.0;
       // a K split adds the reduce-scatter of the 128 x BN partial tile
-      double t = per_sm * (chunk + 2 + (ceff > 1 ? bn / 64.0 : 0.0)) * 4.0 * (bn > 160 ? bn : 160);
+      const double t = per_sm * (chunk + 2 + (ceff > 1 ? bn / 64.0 : 0.0)) * 4.0 * atom;
       if (t < best_t) {
         best_t = t;
         best = TcPlan{bn, ceff, chunk};

@@ -35,14 +35,13 @@ extern "C" {
 const char* odi_be_last_error(void) { return t_err.c_str(); }
 
 // kind: ODI_BACKEND_CPU (1) or ODI_BACKEND_CUDA (4).  act_mode (CUDA only):
-// ODI_CUDA_ACT_Q8 or ODI_CUDA_ACT_F32.  NULL on failure.
+// an ODI_CUDA_ACT_* value.  NULL on failure.
 void* odi_be_create(int kind, int num_threads, int device, int act_mode) {
   try {
     if (kind == ODI_BACKEND_CPU) return static_cast<odi::Backend*>(new odi::CPUBackend(num_threads));
     if (kind == ODI_BACKEND_CUDA)
-      return static_cast<odi::Backend*>(new odi::CUDABackend(
-          num_threads, device,
-          act_mode == ODI_CUDA_ACT_F32 ? odi::CUDABackend::ActMode::F32 : odi::CUDABackend::ActMode::Q8));
+      return static_cast<odi::Backend*>(
+          new odi::CUDABackend(num_threads, device, static_cast<odi::CUDABackend::ActMode>(act_mode)));
     t_err = "unknown backend kind " + std::to_string(kind);
   } catch (const std::exception& e) {
     caught(e.what());

@@ -25,8 +25,11 @@ void ck(int rc, const char* what) {
 
 CUDABackend::ActMode act_from_env() {
   const char* v = std::getenv("ODI_CUDA_ACT");
-  if (v && (std::strcmp(v, "f32") == 0 || std::strcmp(v, "F32") == 0)) return CUDABackend::ActMode::F32;
-  return CUDABackend::ActMode::Q8;
+  if (!v) return CUDABackend::ActMode::AUTO;
+  if (std::strcmp(v, "f32") == 0 || std::strcmp(v, "F32") == 0) return CUDABackend::ActMode::F32;
+  if (std::strcmp(v, "q8") == 0 || std::strcmp(v, "Q8") == 0) return CUDABackend::ActMode::Q8;
+  if (std::strcmp(v, "f16") == 0 || std::strcmp(v, "F16") == 0) return CUDABackend::ActMode::F16;
+  return CUDABackend::ActMode::AUTO;
 }
 
 // The device this host thread last bound; CUDA's current device is per thread.

@@ -37,15 +37,19 @@ namespace odi {
 class CUDABackend : public CPUBackend {
  public:
   // Activation arithmetic of the quantized product.
-  //   Q8  : activations quantised to Q8_0 (the gguf definition), integer block
-  //         dots, fp32 scales -- the decode hot path.
-  //   F32 : fp32 activations times the exactly widened codes, fp32 sums --
-  //         the reference's own arithmetic.
-  enum class ActMode { Q8 = ODI_CUDA_ACT_Q8, F32 = ODI_CUDA_ACT_F32 };
+  //   Q8   : activations quantised to Q8_0 (the gguf definition), integer
+  //          block dots, fp32 scales -- the decode GEMV.
+  //   F32  : fp32 activations times the exactly widened codes, fp32 sums --
+  //          the reference's own arithmetic.
+  //   F16  : tensor cores, fp16-decoded weights and fp16 activations, fp32
+  //          sums -- prefill.
+  //   AUTO : F16 from ODI_CUDA_TC_MIN_TOKENS tokens on (dtypes with a
+  //          tensor-core path), else Q8.
+  enum class ActMode { Q8 = ODI_CUDA_ACT_Q8, F32 = ODI_CUDA_ACT_F32, F16 = ODI_CUDA_ACT_F16, AUTO = ODI_CUDA_ACT_AUTO };
 
   // Throws std::runtime_error when `device` is not a usable sm_100 GPU.
-  // The environment variable ODI_CUDA_ACT=f32 selects ActMode::F32 when
-  // `act` is not given explicitly through the second constructor.
+  // Without an explicit mode the environment variable ODI_CUDA_ACT (q8, f32,
+  // f16 or auto) selects it; the default is AUTO.
   explicit CUDABackend(int num_threads = 0, int device = 0);
   CUDABackend(int num_threads, int device, ActMode act);
   ~CUDABackend() override;
@@ -80,7 +84,7 @@ class CUDABackend : public CPUBackend {
   void bind_device() const;
 
   int device_ = 0;
-  ActMode act_ = ActMode::Q8;
+  ActMode act_ = ActMode::AUTO;
   mutable std::mutex mu_;
   std::map<Key, odi_cuda_weight*> weights_;
   size_t weight_bytes_ = 0;

@@ -218,6 +218,28 @@ def test_cuda_backend_matmul(cuda_backends, dt, N, K, M):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+def test_cuda_backend_auto_mode(cuda_lib, dt):
+    """The default (AUTO) backend: tensor cores from 9 tokens for the dtypes
+    that have them, else the Q8 GEMV."""
+    need_adapter()
+    be = Backend(BACKEND_CUDA, act_mode=3)
+    try:
+        N, K = 320, 2048
+        b = weight(dt, N, K, seed=21)
+        for M in (1, 8, 9, 40):
+            x = O.seeded_acts(M, K, seed=M)
+            y = be.matmul(np.full((M, N), np.nan, np.float32), x, b, dt, (K, N))
+            if M >= 9 and dt in (O.Q4_K, O.Q6_K):
+                y16, b16 = O.matmul_f16(dt, x, b, N)
+                assert (np.abs(y.astype(np.float64) - y16) <= b16 + 1e-30).all()
+            else:
+                _check_q8(dt, x, b, N, y)
+    finally:
+        be.close()
+
+
+@pytest.mark.gpu
 def test_cuda_backend_matches_cpu_backend_and_errors(cuda_backends):
     q8, f32 = cuda_backends
     cpu = Backend(BACKEND_CPU)
