@@ -252,6 +252,24 @@ class DeviceWeight:
     def data_ptr(self) -> int:
         return lib().odi_cuda_weight_data(self.handle)
 
+    def matmul(self, x, y=None, act_mode: int = None, flags: int = 0, stream=None):
+        """y[M, N] = x[M, K] . W^T for device fp32 tensors (asynchronous on
+        `stream`); the workspace is cached on the weight and grown on demand."""
+        import torch
+
+        if act_mode is None:
+            act_mode = ACT_AUTO
+        M = x.shape[0]
+        if y is None:
+            y = torch.empty((M, self.N), dtype=torch.float32, device=x.device)
+        need = workspace_bytes(self.dtype, M, self.N, self.K, act_mode)
+        ws = getattr(self, "_ws", None)
+        if ws is None or ws.numel() < need or ws.device != x.device:
+            ws = self._ws = new_workspace(need, x.device)
+        check(lib().odi_cuda_matmul(self.dtype, self.data_ptr, _ptr(x), _ptr(y), M, self.N, self.K, act_mode,
+                                    _ptr(ws), ws.numel(), flags, _stream(stream)))
+        return y
+
     def free(self) -> None:
         if self.handle:
             check(lib().odi_cuda_weight_free(self.handle))
