@@ -220,7 +220,7 @@ def _one_port_gemv(nthreads):
 METRIC = "Q4_K decode GEMV HBM GB/s (4096x14336, M=1)"
 
 
-def workload_config(R, world):
+def workload_config(R, world, gather="fused"):
     return {
         "workload": f"Q4_K GEMV {N_ROWS}x{K_COLS} (out x in), M={M_TOK}; a step = {SWEEPS} passes over a "
                     f"ring of {R} weight copies",
@@ -228,7 +228,9 @@ def workload_config(R, world):
         "ring_copies": R, "l2": "inputs larger than L2: each step streams the whole ring "
                                  f"({R} x {q4k_bytes(N_ROWS, K_COLS) / 1e6:.1f} MB > 126 MB L2)",
         "act_mode": "q8 (activations quantised to Q8_0, int8 dp4a dots, fp32 scales)",
-        "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+        "parallelism": (f"row-shard x{world}, gathered by the GEMV epilogue (NVLink peer stores + arrival "
+                        f"counters)" if gather == "fused" else f"row-shard x{world} + NCCL all-gather")
+        if world > 1 else "single GPU",
     }
 
 
@@ -269,7 +271,8 @@ def run_ours(args, rank, world, local_rank):
         gen.manual_seed(7 + rank)
         xs = [torch.empty((M, K), dtype=torch.float32, device=dev).normal_(0.0, 1.0, generator=gen) for _ in range(R)]
         ys = [torch.zeros((M, N), dtype=torch.float32, device=dev) for _ in range(R)]
-        gathered = [torch.zeros((world, M, N), dtype=torch.float32, device=dev) for _ in range(R)] if world > 1 else None
+        gathered = [torch.zeros((world * M, N), dtype=torch.float32, device=dev) for _ in range(R)] \
+            if world > 1 else None
     stream.synchronize()
     ws_bytes = ob.workspace_bytes(dt, M, N, K, ob.ACT_Q8)
     ws = ob.new_workspace(ws_bytes, dev)
@@ -286,15 +289,41 @@ def run_ours(args, rank, world, local_rank):
         return 0
 
     pg = None
+    fused = world > 1 and args.gather == "fused"
     if world > 1:
         import torch.distributed as dist
 
         pg = dist.group.WORLD
+    if fused:
+        # Row shards gathered by the GEMV itself: each rank's GEMV stores its
+        # slice into every rank's buffer for that ring copy (NVLink peer
+        # stores) and bumps per-rank arrival counters; a one-block kernel
+        # waits for all ranks (bounded) before the next product.
+        from odiengine_b200.sharded import SymmetricBuffer
+
+        obytes = M * N * world * 4
+        sym = SymmetricBuffer(256 + R * obytes, pg)
+        own = sym.ptrs[rank]
+        inc = (ctypes.c_uint64 * world)(*([L.odi_cuda_scatter_signals(dt, M, N, K, ob.ACT_Q8)] * world))
+        scatters = []
+        for r in range(R):
+            sc = ob.Scatter()
+            for p in range(world):
+                sc.out[p] = sym.ptrs[p] + 256 + r * obytes
+                sc.counters[p] = sym.ptrs[p]
+            sc.nranks, sc.rank, sc.row0, sc.ld = world, rank, rank * N, N * world
+            scatters.append(sc)
 
     def step_body(flags=ob.FLAG_PDL, gemv_only=False):
         # one product = one kernel (activation quantisation is fused in);
-        # gemv_only leaves out the multi-GPU all-gathers
+        # gemv_only leaves out the multi-GPU gathers
         for r in range(R):
+            if fused and not gemv_only:
+                ob.check(L.odi_cuda_matmul_scatter(dt, weights[r].data_ptr(), xs[r].data_ptr(), M, N, K, ob.ACT_Q8,
+                                                   ws.data_ptr(), ws.numel(), flags, ctypes.byref(scatters[r]),
+                                                   s_ptr))
+                ob.check(L.odi_cuda_wait_peers(own, own + 64, inc, world, ws.data_ptr(), s_ptr))
+                continue
             ob.check(L.odi_cuda_matmul(dt, weights[r].data_ptr(), xs[r].data_ptr(), ys[r].data_ptr(), M, N, K,
                                        ob.ACT_Q8, ws.data_ptr(), ws.numel(), flags, s_ptr))
             if world > 1 and not gemv_only:
@@ -422,7 +451,7 @@ def run_ours(args, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "q4_k weights x q8_0 activations (int8 dp4a, fp32 accumulate)", "data": "synthetic",
-            "config": workload_config(R, world),
+            "config": workload_config(R, world, args.gather),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(),
                          "kernel": "qgemv_kernel<Q4_K,1,false>", "us_per_launch": round(us_gemv, 3),
@@ -431,10 +460,20 @@ def run_ours(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "reference_cpu_config1": ref_cfg1,
             "clocks": clk.summary(),
-            "gpu_launches": args.steps * SWEEPS * R,
+            "gpu_launches": args.steps * SWEEPS * R * (2 if fused else 1),
         }
         print(json.dumps(line), flush=True)
     del g_step, g_gemv
+    if fused:
+        torch.cuda.synchronize()
+        st = ob.workspace_status(ws)
+        if st:
+            raise RuntimeError(f"peer wait gave up (error word {st:#x})")
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[local_rank])
+        sym.close()
     return 0
 
 
@@ -460,6 +499,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="small case for ncu: 3 products, no timing")
+    ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
+                    help="N > 1: gather the row shards from the GEMV epilogue (fused) or with ncclAllGather")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

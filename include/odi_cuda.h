@@ -193,6 +193,60 @@ int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y,
  * buffer of N*K*4 bytes. */
 int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* stream);
 
+/* --- row-sharded product with the all-gather fused into the GEMV ------------ */
+
+/* A weight sharded by output rows over nranks GPUs (one process each): rank
+ * r holds rows [row0, row0 + N) of the full ld-row weight.  Instead of a
+ * GEMV followed by an all-gather of the slices (ncclAllGather), each rank's
+ * GEMV stores its slice straight into every rank's gathered output buffer
+ * (peer stores over NVLink); the last CTA of each launch then adds one
+ * arrival to its slot [rank] of every rank's counter array (release, system
+ * scope).  The workspace's first 256 bytes hold the launch's completion
+ * count: zero at start, left zero by every launch that completes.
+ *   out[p]      : rank p's gathered output, [M][ld] fp32 (own rank included)
+ *   counters[p] : rank p's arrival counters, nranks uint64 (zero at start)
+ * Peer addresses come from odi_cuda_sym_alloc / odi_cuda_ipc_open.  No TMA
+ * and no multicast: plain stores and system-scope atomics. */
+#define ODI_CUDA_MAX_PEERS 8
+#define ODI_CUDA_IPC_HANDLE_BYTES 64
+typedef struct odi_cuda_scatter {
+  float* out[ODI_CUDA_MAX_PEERS];
+  unsigned long long* counters[ODI_CUDA_MAX_PEERS];
+  int nranks;
+  int rank;
+  int64_t row0;
+  int64_t ld;
+} odi_cuda_scatter;
+
+/* Arrivals one odi_cuda_matmul_scatter call of this shard shape adds to
+ * its slot on every rank (one per launch: ceil(M / tokens per pass)); -1 if
+ * the shape / mode has no fused path (the tensor-core modes). */
+int64_t odi_cuda_scatter_signals(int dtype, int64_t M, int64_t N, int64_t K, int act_mode);
+
+/* The GEMV of odi_cuda_matmul on this rank's shard (N = shard rows), with
+ * the output scattered as described above.  ACT_Q8 / ACT_F32 (and AUTO
+ * below ODI_CUDA_TC_MIN_TOKENS).  Asynchronous on `stream`. */
+int odi_cuda_matmul_scatter(int dtype, const void* d_w_tiled, const float* d_x, int64_t M, int64_t N,
+                            int64_t K, int act_mode, void* d_workspace, size_t workspace_bytes, int flags,
+                            const odi_cuda_scatter* sc, void* stream);
+
+/* Before using the gathered output: waits (one small kernel on `stream`)
+ * until every source rank p's counter reached d_consumed[p] +
+ * increments[p] (increments = odi_cuda_scatter_signals of rank p's shard),
+ * then advances d_consumed.  d_counters / d_consumed are this rank's own
+ * arrays (nranks uint64, zero at start).  Bounded: a rank that never
+ * arrives sets the workspace error word (see odi_cuda_workspace_status). */
+int odi_cuda_wait_peers(const unsigned long long* d_counters, unsigned long long* d_consumed,
+                        const unsigned long long* increments, int nranks, void* d_workspace, void* stream);
+
+/* Zeroed device buffer for sharing with other processes: *d_ptr and the
+ * ODI_CUDA_IPC_HANDLE_BYTES-byte handle to pass to the other ranks. */
+int odi_cuda_sym_alloc(size_t bytes, void** d_ptr, void* ipc_handle);
+int odi_cuda_sym_free(void* d_ptr);
+/* Map another rank's buffer (handle from its odi_cuda_sym_alloc). */
+int odi_cuda_ipc_open(const void* ipc_handle, void** d_ptr);
+int odi_cuda_ipc_close(void* d_ptr);
+
 /* Size of the static device array behind odi_cuda_matmul_host_noalloc. */
 #define ODI_CUDA_NOALLOC_SCRATCH_BYTES (8u << 20)
 

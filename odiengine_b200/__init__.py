@@ -76,11 +76,29 @@ SIGNATURES = {
     "odi_cuda_matmul_host_noalloc": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "odi_cuda_dequantize_host": (_int, [_vp, _vp, _vp]),
     "odi_cuda_tc_supported": (_int, [_int]),
+    "odi_cuda_scatter_signals": (_i64, [_int, _i64, _i64, _i64, _int]),
+    "odi_cuda_matmul_scatter": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp, _vp]),
+    "odi_cuda_wait_peers": (_int, [_vp, _vp, _vp, _int, _vp, _vp]),
+    "odi_cuda_sym_alloc": (_int, [_sz, ctypes.POINTER(_vp), _vp]),
+    "odi_cuda_sym_free": (_int, [_vp]),
+    "odi_cuda_ipc_open": (_int, [_vp, ctypes.POINTER(_vp)]),
+    "odi_cuda_ipc_close": (_int, [_vp]),
 }
 
 # ODI_CUDA_NOALLOC_SCRATCH_BYTES (include/odi_cuda.h): the static device
 # array behind odi_cuda_matmul_host_noalloc.
 NOALLOC_SCRATCH_BYTES = 8 << 20
+
+MAX_PEERS = 8  # ODI_CUDA_MAX_PEERS
+IPC_HANDLE_BYTES = 64  # ODI_CUDA_IPC_HANDLE_BYTES
+
+
+class Scatter(ctypes.Structure):
+    """odi_cuda_scatter (include/odi_cuda.h)."""
+
+    _fields_ = [("out", ctypes.c_void_p * MAX_PEERS), ("counters", ctypes.c_void_p * MAX_PEERS),
+                ("nranks", ctypes.c_int), ("rank", ctypes.c_int), ("row0", ctypes.c_int64), ("ld", ctypes.c_int64)]
+
 
 _lib = None
 
@@ -252,6 +270,14 @@ class DeviceWeight:
     def data_ptr(self) -> int:
         return lib().odi_cuda_weight_data(self.handle)
 
+    def _ws_for(self, M: int, act_mode: int, device):
+        """The weight's cached workspace, grown to what M tokens need."""
+        need = workspace_bytes(self.dtype, M, self.N, self.K, act_mode)
+        ws = getattr(self, "_ws", None)
+        if ws is None or ws.numel() < need or ws.device != device:
+            ws = self._ws = new_workspace(need, device)
+        return ws
+
     def matmul(self, x, y=None, act_mode: int = None, flags: int = 0, stream=None):
         """y[M, N] = x[M, K] . W^T for device fp32 tensors (asynchronous on
         `stream`); the workspace is cached on the weight and grown on demand."""
@@ -262,10 +288,7 @@ class DeviceWeight:
         M = x.shape[0]
         if y is None:
             y = torch.empty((M, self.N), dtype=torch.float32, device=x.device)
-        need = workspace_bytes(self.dtype, M, self.N, self.K, act_mode)
-        ws = getattr(self, "_ws", None)
-        if ws is None or ws.numel() < need or ws.device != x.device:
-            ws = self._ws = new_workspace(need, x.device)
+        ws = self._ws_for(M, act_mode, x.device)
         check(lib().odi_cuda_matmul(self.dtype, self.data_ptr, _ptr(x), _ptr(y), M, self.N, self.K, act_mode,
                                     _ptr(ws), ws.numel(), flags, _stream(stream)))
         return y

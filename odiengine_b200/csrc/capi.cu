@@ -76,6 +76,34 @@ int check_shape(int dt, int64_t N, int64_t K) {
   return ODI_CUDA_OK;
 }
 
+// The streaming GEMV over M tokens: one launch per pass of plan.mt tokens.
+// With `sc`, each pass scatters its rows into every rank's gathered buffer.
+int run_gemv(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N, int64_t K,
+             bool f32, int* err, bool pdl, cudaStream_t s, const GemvScatter* sc) {
+  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
+  if (plan.C == 0)
+    return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
+  for (int64_t m0 = 0; m0 < M; m0 += plan.mt) {
+    GemvArgs a;
+    a.w = (const uint8_t*)d_w_tiled;
+    a.x = d_x + m0 * K;
+    a.y = d_y ? d_y + m0 * N : nullptr;
+    a.err = err;
+    a.N = N;
+    a.K = K;
+    a.M = (int)((M - m0) < plan.mt ? (M - m0) : plan.mt);
+    a.sc = GemvScatter{};
+    if (sc) {
+      a.sc = *sc;
+      for (int p = 0; p < sc->n; ++p) a.sc.out[p] = sc->out[p] + m0 * sc->ld;
+      a.sc.done = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(err) + WS_DONE_OFFSET);
+      a.sc.writers = plan.G;
+    }
+    CK(launch_gemv(dtype, f32, plan, a, pdl, s), "qgemv launch");
+  }
+  return ODI_CUDA_OK;
+}
+
 }  // namespace
 
 struct odi_cuda_weight {
@@ -276,21 +304,7 @@ int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d
   }
   const bool f32 = mode == ODI_CUDA_ACT_F32;
   const bool pdl = (flags & ODI_CUDA_FLAG_PDL) != 0;
-  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
-  if (plan.C == 0)
-    return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
-  for (int64_t m0 = 0; m0 < M; m0 += plan.mt) {
-    GemvArgs a;
-    a.w = (const uint8_t*)d_w_tiled;
-    a.x = d_x + m0 * K;
-    a.y = d_y + m0 * N;
-    a.err = (int*)d_workspace;
-    a.N = N;
-    a.K = K;
-    a.M = (int)((M - m0) < plan.mt ? (M - m0) : plan.mt);
-    CK(launch_gemv(dtype, f32, plan, a, pdl, s), "qgemv launch");
-  }
-  return ODI_CUDA_OK;
+  return run_gemv(dtype, d_w_tiled, d_x, d_y, M, N, K, f32, (int*)d_workspace, pdl, s, nullptr);
 }
 
 int odi_cuda_workspace_status(void* d_workspace, int* status, void* stream) {
@@ -310,6 +324,105 @@ int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t 
   if (rc) return rc;
   if (!d_w_tiled || !d_out) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
   CK(launch_dequant(dtype, d_w_tiled, d_out, N, K, (cudaStream_t)stream), "dequantize");
+  return ODI_CUDA_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Row-shard scatter: the all-gather of a row-sharded product fused into the
+// GEMV (peer stores over NVLink), symmetric buffers shared by IPC handles.
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int64_t odi_cuda_scatter_signals(int dtype, int64_t M, int64_t N, int64_t K, int act_mode) {
+  if (!dtype_ok(dtype) || M < 1 || N < 1 || K < 1) return -1;
+  const int mode = resolve_act_mode(dtype, M, act_mode);
+  if (mode != ODI_CUDA_ACT_Q8 && mode != ODI_CUDA_ACT_F32) return -1;
+  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), mode == ODI_CUDA_ACT_F32, num_sms_current());
+  if (plan.C == 0) return -1;
+  return (M + plan.mt - 1) / plan.mt;  // one arrival per launch (pass)
+}
+
+int odi_cuda_matmul_scatter(int dtype, const void* d_w_tiled, const float* d_x, int64_t M, int64_t N, int64_t K,
+                            int act_mode, void* d_workspace, size_t workspace_bytes, int flags,
+                            const odi_cuda_scatter* sc, void* stream) {
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (M < 1 || M > (1 << 20)) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M=%lld", (long long)M);
+  const int mode = resolve_act_mode(dtype, M, act_mode);
+  if (mode != ODI_CUDA_ACT_Q8 && mode != ODI_CUDA_ACT_F32)
+    return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "the fused scatter runs on the streaming GEMV (ACT_Q8 / ACT_F32)");
+  if (!sc || sc->nranks < 1 || sc->nranks > MAX_PEERS || sc->rank < 0 || sc->rank >= sc->nranks)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid scatter description");
+  if (sc->row0 < 0 || sc->row0 + N > sc->ld)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "shard rows [%lld, %lld) outside the %lld gathered rows",
+                (long long)sc->row0, (long long)(sc->row0 + N), (long long)sc->ld);
+  for (int p = 0; p < sc->nranks; ++p)
+    if (!sc->out[p] || !sc->counters[p]) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null peer buffer %d", p);
+  if (!d_w_tiled || !d_x || !d_workspace) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  if (((uintptr_t)d_w_tiled | (uintptr_t)d_workspace) & 15)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight and workspace must be 16-byte aligned");
+  if (workspace_bytes < WS_HEADER) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small");
+  GemvScatter g{};
+  for (int p = 0; p < sc->nranks; ++p) {
+    g.out[p] = sc->out[p];
+    g.cnt[p] = sc->counters[p];
+  }
+  g.n = sc->nranks;
+  g.src = sc->rank;
+  g.row0 = sc->row0;
+  g.ld = sc->ld;
+  return run_gemv(dtype, d_w_tiled, d_x, nullptr, M, N, K, mode == ODI_CUDA_ACT_F32, (int*)d_workspace,
+                  (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, &g);
+}
+
+int odi_cuda_wait_peers(const unsigned long long* d_counters, unsigned long long* d_consumed,
+                        const unsigned long long* increments, int nranks, void* d_workspace, void* stream) {
+  if (!d_counters || !d_consumed || !increments || !d_workspace)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  if (nranks < 1 || nranks > MAX_PEERS) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid nranks %d", nranks);
+  PeerWait w{};
+  for (int p = 0; p < nranks; ++p) w.inc[p] = increments[p];
+  w.n = nranks;
+  CK(launch_wait_peers(d_counters, d_consumed, w, (int*)d_workspace, (cudaStream_t)stream), "wait_peers launch");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_sym_alloc(size_t bytes, void** d_ptr, void* ipc_handle) {
+  if (!d_ptr || !ipc_handle || bytes == 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  *d_ptr = nullptr;
+  void* p = nullptr;
+  CK(cudaMalloc(&p, bytes), "cudaMalloc (symmetric buffer)");
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "symmetric buffer");
+  }
+  static_assert(sizeof(h) <= ODI_CUDA_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(ipc_handle, &h, sizeof h);
+  *d_ptr = p;
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_sym_free(void* d_ptr) {
+  if (d_ptr) CK(cudaFree(d_ptr), "cudaFree (symmetric buffer)");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_ipc_open(const void* ipc_handle, void** d_ptr) {
+  if (!ipc_handle || !d_ptr) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof h);
+  *d_ptr = nullptr;
+  CK(cudaIpcOpenMemHandle(d_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_ipc_close(void* d_ptr) {
+  if (d_ptr) CK(cudaIpcCloseMemHandle(d_ptr), "cudaIpcCloseMemHandle");
   return ODI_CUDA_OK;
 }
 

@@ -29,6 +29,21 @@ struct GemvPlan {
   int mt;            // tokens per pass (template instantiation)
 };
 
+// Output scatter of a row shard into every rank's gathered buffer (the
+// all-gather of a row-sharded product, fused into the GEMV epilogue).  With
+// n == 0 the product is written to GemvArgs::y as usual.
+constexpr int MAX_PEERS = 8;
+struct GemvScatter {
+  float* out[MAX_PEERS];                 // rank p's gathered output [M][ld] (own rank included)
+  unsigned long long* cnt[MAX_PEERS];    // rank p's arrival counters; this rank adds to [src]
+  int n;                                 // ranks; 0 = no scatter
+  int src;                               // this rank
+  int64_t row0, ld;                      // first row of this shard in the full output, full rows
+  unsigned* done;                        // local completion count of the launch (workspace, zero)
+  int writers;                           // CTAs of the launch that write outputs (one per row tile)
+};
+constexpr int WS_DONE_OFFSET = 64;       // byte offset of GemvScatter::done in the workspace
+
 struct GemvArgs {
   const uint8_t* w;   // tiled weight
   const float* x;     // activations of this pass [M][K] fp32, row stride K
@@ -36,12 +51,23 @@ struct GemvArgs {
   int* err;           // device error word
   int64_t N, K;
   int M;              // tokens in this pass (<= mt)
+  GemvScatter sc;     // row offset of this pass's tokens is folded into sc.out
 };
 
 // Plan for dtype / tokens / fp32-activation mode on a device with num_sms SMs.
 GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms);
 cudaError_t launch_gemv(int dt, bool f32act, const GemvPlan& plan, const GemvArgs& a, bool pdl,
                         cudaStream_t s);
+
+// Peer signalling (peer.cu): wait until every source rank's counter has
+// advanced by inc[src] past what this rank consumed, then consume.
+constexpr int ERR_PEER_WAIT = 32;
+struct PeerWait {
+  unsigned long long inc[MAX_PEERS];
+  int n;
+};
+cudaError_t launch_wait_peers(const unsigned long long* cnt, unsigned long long* consumed, const PeerWait& w,
+                              int* err, cudaStream_t s);
 
 // Prefill-shaped GEMM on the tensor cores (qgemm_tc.cu).  Weights decoded to
 // fp16 in shared memory, activations packed to fp16 operand tiles in the

@@ -567,6 +567,35 @@ struct SmemMap {
   static constexpr int xr(int C) { return (part + C * UNIT_ROWS * MT * 4 + 127) / 128 * 128; }
 };
 
+// One output element: to y, or -- for a row shard -- to every rank's gathered
+// buffer (plain stores; peers' buffers are reached over NVLink).
+__device__ __forceinline__ void store_out(const GemvArgs& a, int m, int64_t n, float v) {
+  if (a.sc.n == 0) {
+    a.y[(int64_t)m * a.N + n] = v;
+    return;
+  }
+  const int64_t off = (int64_t)m * a.sc.ld + a.sc.row0 + n;
+  for (int p = 0; p < a.sc.n; ++p) a.sc.out[p][off] = v;
+}
+
+// After this CTA's output stores (consumer_sync between), one thread per
+// writing CTA: the CTA's stores are ordered before its arrival on the
+// launch's local completion count (GPU scope); the last of the
+// sc.writers writing CTAs then makes every observed store visible
+// system-wide, resets the count for the next launch and adds one arrival to
+// this rank's counter on every rank (release, system scope) -- one remote
+// signal per launch, not one per CTA.
+__device__ __forceinline__ void signal_peers(const GemvArgs& a) {
+  if (a.sc.n == 0) return;
+  __threadfence();
+  const unsigned prev = atomicAdd(a.sc.done, 1u);
+  if (prev != (unsigned)a.sc.writers - 1) return;
+  __threadfence_system();
+  *a.sc.done = 0u;
+  for (int p = 0; p < a.sc.n; ++p)
+    asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(a.sc.cnt[p] + a.sc.src) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // The kernel: grid = G * C CTAs, clusters of C along x.
 // ---------------------------------------------------------------------------
@@ -685,7 +714,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     const float v = red[(0 * UNIT_ROWS + r) * MT + m] + red[(1 * UNIT_ROWS + r) * MT + m];
     if (pl.C == 1) {
       const int64_t n = (int64_t)g * UNIT_ROWS + r;
-      if (n < a.N) a.y[(int64_t)m * a.N + n] = v;
+      if (n < a.N) store_out(a, m, n, v);
     } else if (rank == 0) {
       part[t] = v;
     } else {
@@ -703,9 +732,16 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
         float v = part[t];
         for (int q = 1; q < pl.C; ++q) v += part[q * UNIT_ROWS * MT + t];
         const int64_t n = (int64_t)g * UNIT_ROWS + r;
-        if (n < a.N) a.y[(int64_t)m * a.N + n] = v;
+        if (n < a.N) store_out(a, m, n, v);
+      }
+      if (a.sc.n) {
+        consumer_sync();
+        if (tid == 0) signal_peers(a);
       }
     }
+  } else if (a.sc.n) {
+    consumer_sync();
+    if (tid == 0) signal_peers(a);
   }
 }
 

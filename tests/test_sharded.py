@@ -7,7 +7,9 @@ bit (rows are independent, so sharding changes no arithmetic), for even and
 ragged N and for M = 1 and M > 1 (the rank-major permute).
 GPU: with two or more devices, two NCCL ranks run the CUDA product on their
 shards and must reproduce the single-GPU result up to fp32 summation order
-(the work split depends on the shard's row count).
+(the work split depends on the shard's row count); the fused scatter (peer
+stores from the GEMV epilogue, arrival counters, bounded wait) must equal
+the NCCL all-gather bit for bit over repeated calls.
 """
 import os
 import socket
@@ -114,6 +116,20 @@ def _gpu_worker(rank, world, port, out_q):
             y = w.matmul(x, act_mode=mode)
             torch.cuda.synchronize()
             res.append(y.cpu().numpy())
+        # fused scatter (GEMV epilogue stores to every rank + counters) must
+        # give exactly the NCCL all-gather result, call after call
+        fused_ok = []
+        for dt, N, K, M in [(O.Q4_K, 1024, 2048, 1), (O.Q6_K, 1000, 1024, 4), (O.Q4_K, 130, 512, 8)]:
+            b = O.quantize(dt, O.seeded_weights(N, K, seed=3))
+            wn = RowShardedWeight(dt, N, K).load(b)
+            wf = RowShardedWeight(dt, N, K, fused=True).load(b)
+            for call in range(4):
+                x = torch.from_numpy(O.seeded_acts(M, K, seed=10 + call)).cuda()
+                yn = wn.matmul(x, act_mode=ob.ACT_Q8).cpu()
+                yf = wf.matmul(x, act_mode=ob.ACT_Q8).cpu()
+                fused_ok.append(bool(torch.equal(yn, yf)))
+            wf.sym.close()
+        res.append(fused_ok)
         if rank == 0:
             out_q.put(res)
     finally:
@@ -139,6 +155,8 @@ def test_sharded_two_gpus_match_one():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    assert all(got[-1]), got[-1]
+    got = got[:-1]
     ob.init(0)
     torch.cuda.set_device(0)
     for (dt, N, K, M, mode), y in zip([(O.Q4_K, 1024, 2048, 1, ob.ACT_Q8), (O.Q4_K, 1000, 2048, 32, ob.ACT_AUTO),
