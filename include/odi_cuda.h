@@ -193,6 +193,60 @@ int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y,
  * buffer of N*K*4 bytes. */
 int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* stream);
 
+/* --- decode step: the non-matmul operations of Context::forward ------------- */
+
+/* Device-resident decode state: the next input token, its position (KV
+ * slot) and the number of tokens generated.  Every decode operation reads
+ * it from device memory and odi_cuda_argmax advances it, so one step can be
+ * captured in a CUDA graph and replayed token after token. */
+typedef struct odi_cuda_decode_state {
+  int32_t token;
+  int32_t pos;
+  int32_t step;
+  int32_t reserved;
+} odi_cuda_decode_state;
+
+/* x[E] = table[token] (Backend::embedding, cpu_backend.cpp:610-619; table
+ * fp32 [vocab][E], an out-of-range token reads row 0). */
+int odi_cuda_embed(const float* d_table, int64_t vocab, int64_t E, const odi_cuda_decode_state* d_state, float* d_x,
+                   void* stream);
+
+/* y = x / sqrt(mean(x^2) + eps) * w per row of n (Backend::rms_norm,
+ * cpu_backend.cpp:388-414).  y may alias x. */
+int odi_cuda_rms_norm(const float* d_x, const float* d_w, float* d_y, int64_t rows, int64_t n, float eps,
+                      void* stream);
+
+/* Rotary embedding of q [heads][head_dim] and k [kv_heads][head_dim] at the
+ * state's pos (pairs i, i + head_dim/2, freq = theta^(-2i/head_dim):
+ * Backend::rope, cpu_backend.cpp:500-539), then k and v appended to the fp16
+ * caches [kv_heads][ctx][head_dim] at pos (context.cpp:205-214).
+ * head_dim 64 or 128; pos >= ctx writes nothing. */
+int odi_cuda_rope_kv(float* d_q, float* d_k, const float* d_v, void* d_kcache, void* d_vcache,
+                     const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,
+                     float theta, void* stream);
+
+/* Attention of one query token over cache positions 0..pos (fp16 K, V;
+ * fp32 scores and softmax), out [heads][head_dim] (Backend::attention,
+ * cpu_backend.cpp:541-608, with the causal limit taken at the query's
+ * absolute position).  Grouped-query heads share kv head h / (heads /
+ * kv_heads).  Needs odi_cuda_attention_scratch_bytes of device scratch. */
+size_t odi_cuda_attention_scratch_bytes(int heads, int head_dim, int ctx);
+int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void* d_vcache, float* d_out,
+                              const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,
+                              float scale, void* d_scratch, size_t scratch_bytes, void* stream);
+
+/* out[F] = silu(gate) * up with gate_up = [gate F | up F] (context.cpp:272-275). */
+int odi_cuda_silu_mul(const float* d_gate_up, float* d_out, int64_t F, void* stream);
+
+/* x += d (the residual adds of context.cpp:124, 130). */
+int odi_cuda_add(float* d_x, const float* d_d, int64_t n, void* stream);
+
+/* Greedy next token (first index of the largest logit): sets state.token,
+ * stores it at d_record[state.step] when step < record_len, then advances
+ * step and pos. */
+int odi_cuda_argmax(const float* d_logits, int64_t V, odi_cuda_decode_state* d_state, int32_t* d_record,
+                    int record_len, void* stream);
+
 /* --- row-sharded product with the all-gather fused into the GEMV ------------ */
 
 /* A weight sharded by output rows over nranks GPUs (one process each): rank

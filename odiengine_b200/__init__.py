@@ -76,6 +76,15 @@ SIGNATURES = {
     "odi_cuda_matmul_host_noalloc": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "odi_cuda_dequantize_host": (_int, [_vp, _vp, _vp]),
     "odi_cuda_tc_supported": (_int, [_int]),
+    "odi_cuda_embed": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "odi_cuda_rms_norm": (_int, [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
+    "odi_cuda_rope_kv": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, ctypes.c_float, _vp]),
+    "odi_cuda_attention_scratch_bytes": (_sz, [_int, _int, _int]),
+    "odi_cuda_attention_decode": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, ctypes.c_float, _vp, _sz,
+                                         _vp]),
+    "odi_cuda_silu_mul": (_int, [_vp, _vp, _i64, _vp]),
+    "odi_cuda_add": (_int, [_vp, _vp, _i64, _vp]),
+    "odi_cuda_argmax": (_int, [_vp, _i64, _vp, _vp, _int, _vp]),
     "odi_cuda_scatter_signals": (_i64, [_int, _i64, _i64, _i64, _int]),
     "odi_cuda_matmul_scatter": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp, _vp]),
     "odi_cuda_wait_peers": (_int, [_vp, _vp, _vp, _int, _vp, _vp]),
@@ -264,10 +273,24 @@ class DeviceWeight:
         h = ctypes.c_void_p()
         check(lib().odi_cuda_weight_upload(buf.ctypes.data_as(ctypes.c_void_p), w.dtype, w.N, w.K, ctypes.byref(h)))
         self.handle = h
+        self.tiled = None
         self.dtype, self.N, self.K = w.dtype, w.N, w.K
+
+    @classmethod
+    def from_tiled(cls, dtype: int, N: int, K: int, tiled) -> "DeviceWeight":
+        """Wrap a device uint8 tensor already in the tiled layout (e.g. made by
+        quantize_weight + repack on the device); the tensor is kept alive."""
+        if tiled.numel() != tiled_bytes(dtype, N, K):
+            raise ValueError("tiled tensor size does not match the shape")
+        self = cls.__new__(cls)
+        self.handle, self.tiled = None, tiled
+        self.dtype, self.N, self.K = dtype, N, K
+        return self
 
     @property
     def data_ptr(self) -> int:
+        if self.tiled is not None:
+            return self.tiled.data_ptr()
         return lib().odi_cuda_weight_data(self.handle)
 
     def _ws_for(self, M: int, act_mode: int, device):
@@ -294,7 +317,8 @@ class DeviceWeight:
         return y
 
     def free(self) -> None:
-        if self.handle:
+        self.tiled = None
+        if getattr(self, "handle", None):
             check(lib().odi_cuda_weight_free(self.handle))
             self.handle = None
 

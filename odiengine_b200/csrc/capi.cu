@@ -330,6 +330,88 @@ int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t 
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// Decode-step operations (the non-matmul half of Context::forward).
+// ---------------------------------------------------------------------------
+static_assert(sizeof(odi_cuda_decode_state) == sizeof(DecodeState), "decode state layout");
+
+extern "C" {
+
+int odi_cuda_embed(const float* d_table, int64_t vocab, int64_t E, const odi_cuda_decode_state* d_state, float* d_x,
+                   void* stream) {
+  if (!d_table || !d_state || !d_x || vocab < 1 || E < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "embed: bad argument");
+  CK(launch_embed(d_table, vocab, E, reinterpret_cast<const DecodeState*>(d_state), d_x, (cudaStream_t)stream),
+     "embed launch");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_rms_norm(const float* d_x, const float* d_w, float* d_y, int64_t rows, int64_t n, float eps,
+                      void* stream) {
+  if (!d_x || !d_w || !d_y || rows < 1 || rows > 65535 || n < 1)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "rms_norm: bad argument");
+  CK(launch_rms_norm(d_x, d_w, d_y, rows, n, eps, (cudaStream_t)stream), "rms_norm launch");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_rope_kv(float* d_q, float* d_k, const float* d_v, void* d_kcache, void* d_vcache,
+                     const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,
+                     float theta, void* stream) {
+  if (!d_q || !d_k || !d_v || !d_kcache || !d_vcache || !d_state)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "rope_kv: null argument");
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads || (head_dim != 64 && head_dim != 128) || ctx < 1)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "rope_kv: heads %d / kv_heads %d / head_dim %d / ctx %d", heads,
+                kv_heads, head_dim, ctx);
+  CK(launch_rope_kv(d_q, d_k, d_v, (__half*)d_kcache, (__half*)d_vcache, reinterpret_cast<const DecodeState*>(d_state),
+                    heads, kv_heads, head_dim, ctx, theta, (cudaStream_t)stream),
+     "rope_kv launch");
+  return ODI_CUDA_OK;
+}
+
+size_t odi_cuda_attention_scratch_bytes(int heads, int head_dim, int ctx) {
+  if (heads < 1 || head_dim < 1 || ctx < 1) return 0;
+  return (size_t)heads * attention_chunks(ctx) * (head_dim + 2) * sizeof(float);
+}
+
+int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void* d_vcache, float* d_out,
+                              const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,
+                              float scale, void* d_scratch, size_t scratch_bytes, void* stream) {
+  if (!d_q || !d_kcache || !d_vcache || !d_out || !d_state || !d_scratch)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: null argument");
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads || (head_dim != 64 && head_dim != 128) || ctx < 1)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: heads %d / kv_heads %d / head_dim %d", heads, kv_heads,
+                head_dim);
+  if (scratch_bytes < odi_cuda_attention_scratch_bytes(heads, head_dim, ctx))
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: scratch too small");
+  CK(launch_attention(d_q, (const __half*)d_kcache, (const __half*)d_vcache, d_out, (float*)d_scratch,
+                      reinterpret_cast<const DecodeState*>(d_state), heads, kv_heads, head_dim, ctx, scale,
+                      (cudaStream_t)stream),
+     "attention launch");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_silu_mul(const float* d_gate_up, float* d_out, int64_t F, void* stream) {
+  if (!d_gate_up || !d_out || F < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "silu_mul: bad argument");
+  CK(launch_silu_mul(d_gate_up, d_out, F, (cudaStream_t)stream), "silu_mul launch");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_add(float* d_x, const float* d_d, int64_t n, void* stream) {
+  if (!d_x || !d_d || n < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "add: bad argument");
+  CK(launch_add(d_x, d_d, n, (cudaStream_t)stream), "add launch");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_argmax(const float* d_logits, int64_t V, odi_cuda_decode_state* d_state, int32_t* d_record,
+                    int record_len, void* stream) {
+  if (!d_logits || !d_state || V < 1 || V > 0x7ffffffe) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "argmax: bad argument");
+  CK(launch_argmax(d_logits, V, reinterpret_cast<DecodeState*>(d_state), d_record, d_record ? record_len : 0,
+                   (cudaStream_t)stream),
+     "argmax launch");
+  return ODI_CUDA_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
 // Row-shard scatter: the all-gather of a row-sharded product fused into the
 // GEMV (peer stores over NVLink), symmetric buffers shared by IPC handles.
 // ---------------------------------------------------------------------------

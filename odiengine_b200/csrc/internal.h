@@ -69,6 +69,30 @@ struct PeerWait {
 cudaError_t launch_wait_peers(const unsigned long long* cnt, unsigned long long* consumed, const PeerWait& w,
                               int* err, cudaStream_t s);
 
+// Decode-step kernels (decode_ops.cu).  The token and position live on the
+// device; argmax advances them, so one captured graph serves every step.
+struct DecodeState {
+  int token;  // input token of the next step
+  int pos;    // its position (KV slot)
+  int step;   // tokens generated so far (index into the token record)
+  int reserved;
+};
+constexpr int ATT_CHUNK = 256;  // positions per CTA in the attention's first pass
+int attention_chunks(int ctx);
+cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x,
+                         cudaStream_t s);
+cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,
+                            cudaStream_t s);
+cudaError_t launch_rope_kv(float* q, float* k, const float* v, __half* kc, __half* vc, const DecodeState* st,
+                           int heads, int kv_heads, int hd, int ctx, float theta, cudaStream_t s);
+cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, float* o, float* part,
+                             const DecodeState* st, int heads, int kv_heads, int hd, int ctx, float scale,
+                             cudaStream_t s);
+cudaError_t launch_silu_mul(const float* gu, float* a, int64_t F, cudaStream_t s);
+cudaError_t launch_add(float* x, const float* d, int64_t n, cudaStream_t s);
+cudaError_t launch_argmax(const float* logits, int64_t V, DecodeState* st, int* record, int record_len,
+                          cudaStream_t s);
+
 // Prefill-shaped GEMM on the tensor cores (qgemm_tc.cu).  Weights decoded to
 // fp16 in shared memory, activations packed to fp16 operand tiles in the
 // workspace by launch_act_pack_f16, fp32 accumulation in tensor memory.

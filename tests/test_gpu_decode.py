@@ -1,0 +1,226 @@
+"""Device decode step (odiengine_b200.decode, csrc/decode_ops.cu) against the
+oracle's float64 restatement of the reference forward pass (oracle/llama.py).
+
+Per operation (tolerances written per test):
+  embed, add                exact
+  rms_norm                  |dy| <= 1e-5 |y| + 1e-6         (fp32 sum of squares)
+  rope                      |d| <= 2e-5 (|q| + 1)            (fp32 angle, sincosf)
+  fp16 KV append            bit-exact: fp16(rotated k), fp16(v)
+  attention (GQA, 2 chunks) |d| <= 1e-4 max|v|               (fp32 softmax, fp16 K/V)
+  silu_mul                  |d| <= 1e-6 |y| + 1e-7
+  argmax                    exact, ties -> lowest index; state advanced
+End to end (tiny Llama, 2 layers, GQA): logits within 2e-3 of their scale
+with fp32 GEMVs (ACT_F32) and within 6e-2 with Q8 activations; greedy
+tokens equal wherever the oracle's top-2 gap exceeds that tolerance; a
+replayed CUDA graph reproduces the eager steps exactly.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from oracle.llama import LlamaRef, rms_norm, rope
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dtype=None):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda() if dtype is None else \
+        torch.from_numpy(np.ascontiguousarray(a)).to(dtype).cuda()
+
+
+def _state(token, pos, step=0):
+    import torch
+
+    return torch.tensor([token, pos, step, 0], dtype=torch.int32, device="cuda")
+
+
+def test_embed_and_add(cuda_lib):
+    import torch
+
+    L = cuda_lib.lib()
+    rng = np.random.default_rng(0)
+    table = rng.standard_normal((50, 96)).astype(np.float32)
+    x = torch.zeros(96, device="cuda")
+    st = _state(37, 0)
+    td = _t(table)
+    cuda_lib.check(L.odi_cuda_embed(td.data_ptr(), 50, 96, st.data_ptr(), x.data_ptr(), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(x.cpu().numpy(), table[37])
+    d = rng.standard_normal(96).astype(np.float32)
+    dd = _t(d)
+    cuda_lib.check(L.odi_cuda_add(x.data_ptr(), dd.data_ptr(), 96, None))
+    torch.cuda.synchronize()
+    assert np.array_equal(x.cpu().numpy(), table[37] + d)
+
+
+@pytest.mark.parametrize("n", [96, 4096, 5000])
+def test_rms_norm(cuda_lib, n):
+    import torch
+
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal((3, n)).astype(np.float32)
+    w = (1 + 0.02 * rng.standard_normal(n)).astype(np.float32)
+    y = torch.zeros((3, n), device="cuda")
+    xd, wd = _t(x), _t(w)
+    cuda_lib.check(cuda_lib.lib().odi_cuda_rms_norm(xd.data_ptr(), wd.data_ptr(), y.data_ptr(), 3, n, 1e-5, None))
+    torch.cuda.synchronize()
+    ref = np.stack([rms_norm(x[i], w, 1e-5) for i in range(3)])
+    assert (np.abs(y.cpu().numpy() - ref) <= 1e-5 * np.abs(ref) + 1e-6).all()
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_rope_kv_append(cuda_lib, hd):
+    import torch
+
+    H, KV, ctx, pos = 8, 2, 40, 29
+    rng = np.random.default_rng(hd)
+    q = rng.standard_normal((H, hd)).astype(np.float32)
+    k = rng.standard_normal((KV, hd)).astype(np.float32)
+    v = rng.standard_normal((KV, hd)).astype(np.float32)
+    qd, kd, vd = _t(q), _t(k), _t(v)
+    kc = torch.zeros((KV, ctx, hd), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    st = _state(0, pos)
+    cuda_lib.check(cuda_lib.lib().odi_cuda_rope_kv(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kc.data_ptr(),
+                                                   vc.data_ptr(), st.data_ptr(), H, KV, hd, ctx, 10000.0, None))
+    torch.cuda.synchronize()
+    qr = rope(q.astype(np.float64), pos, 10000.0)
+    kr = rope(k.astype(np.float64), pos, 10000.0)
+    assert (np.abs(qd.cpu().numpy() - qr) <= 2e-5 * (np.abs(qr) + 1)).all()
+    kg = kd.cpu().numpy()
+    assert (np.abs(kg - kr) <= 2e-5 * (np.abs(kr) + 1)).all()
+    kcn, vcn = kc.cpu().numpy(), vc.cpu().numpy()
+    assert np.array_equal(kcn[:, pos], kg.astype(np.float16))
+    assert np.array_equal(vcn[:, pos], v.astype(np.float16))
+    assert not kcn[:, :pos].any() and not kcn[:, pos + 1:].any()
+
+
+@pytest.mark.parametrize("hd,H,KV,pos", [(128, 8, 2, 300), (64, 4, 4, 0), (128, 32, 32, 2047)])
+def test_attention_decode(cuda_lib, hd, H, KV, pos):
+    import torch
+
+    ctx = max(pos + 1, 64)
+    rng = np.random.default_rng(pos + hd)
+    q = rng.standard_normal((H, hd)).astype(np.float32)
+    kc = rng.standard_normal((KV, ctx, hd)).astype(np.float16)
+    vc = rng.standard_normal((KV, ctx, hd)).astype(np.float16)
+    L = cuda_lib.lib()
+    sb = L.odi_cuda_attention_scratch_bytes(H, hd, ctx)
+    scratch = torch.zeros(sb // 4 + 1, device="cuda")
+    out = torch.zeros((H, hd), device="cuda")
+    st = _state(0, pos)
+    scale = 1.0 / np.sqrt(hd)
+    qd, kd, vd = _t(q), _t(kc), _t(vc)
+    cuda_lib.check(L.odi_cuda_attention_decode(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(),
+                                               st.data_ptr(), H, KV, hd, ctx, scale, scratch.data_ptr(), sb, None))
+    torch.cuda.synchronize()
+    ref = np.zeros((H, hd))
+    for h in range(H):
+        kh = h // (H // KV)
+        s = kc[kh, : pos + 1].astype(np.float64) @ q[h].astype(np.float64) * scale
+        p = np.exp(s - s.max())
+        ref[h] = (p / p.sum()) @ vc[kh, : pos + 1].astype(np.float64)
+    assert (np.abs(out.cpu().numpy() - ref) <= 1e-4 * np.abs(vc).max()).all()
+
+
+def test_silu_mul(cuda_lib):
+    import torch
+
+    F = 11008
+    gu = np.random.default_rng(1).standard_normal(2 * F).astype(np.float32) * 4
+    a = torch.zeros(F, device="cuda")
+    gd = _t(gu)
+    cuda_lib.check(cuda_lib.lib().odi_cuda_silu_mul(gd.data_ptr(), a.data_ptr(), F, None))
+    torch.cuda.synchronize()
+    g, u = gu[:F].astype(np.float64), gu[F:].astype(np.float64)
+    ref = g / (1 + np.exp(-g)) * u
+    assert (np.abs(a.cpu().numpy() - ref) <= 1e-6 * np.abs(ref) + 1e-7).all()
+
+
+def test_argmax_ties_and_state(cuda_lib):
+    import torch
+
+    V = 32000
+    lg = np.random.default_rng(2).standard_normal(V).astype(np.float32)
+    lg[12345] = lg[777] = 9.0  # a tie: the first index wins
+    st = _state(5, 10, 3)
+    rec = torch.full((8,), -1, dtype=torch.int32, device="cuda")
+    ld = _t(lg)
+    cuda_lib.check(cuda_lib.lib().odi_cuda_argmax(ld.data_ptr(), V, st.data_ptr(), rec.data_ptr(), 8, None))
+    torch.cuda.synchronize()
+    assert st.cpu().tolist() == [777, 11, 4, 0]
+    assert rec.cpu().tolist()[3] == 777
+
+
+# --------------------------------------------------------------------------
+# end to end, tiny Llama
+# --------------------------------------------------------------------------
+def _tiny(act_mode):
+    from odiengine_b200.decode import LlamaConfig
+
+    return LlamaConfig(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1000, ctx=64,
+                       act_mode=act_mode)
+
+
+def _oracle_weights(ob, cfg, mw):
+    def deq(dw):
+        blocks = ob.unpack(dw.dtype, dw.tiled, dw.N, dw.K).cpu().numpy()
+        return O.dequantize(dw.dtype, blocks, dw.N, dw.K).astype(np.float64)
+
+    W = {"token_embd": mw.token_embd.cpu().numpy().astype(np.float64),
+         "out_norm": mw.out_norm.cpu().numpy(), "output": deq(mw.output)}
+    for l, lw in enumerate(mw.layers):
+        W[f"attn_norm.{l}"] = lw.attn_norm.cpu().numpy()
+        W[f"ffn_norm.{l}"] = lw.ffn_norm.cpu().numpy()
+        W[f"wqkv.{l}"] = deq(lw.wqkv)
+        W[f"wo.{l}"] = deq(lw.wo)
+        W[f"wgu.{l}"] = deq(lw.wgu)
+        W[f"wdown.{l}"] = deq(lw.wdown)
+    return W
+
+
+@pytest.mark.parametrize("act_mode,tol", [(1, 2e-3), (0, 6e-2)], ids=["f32", "q8"])
+def test_tiny_model_matches_oracle(cuda_lib, act_mode, tol):
+    from odiengine_b200.decode import DecodeModel, seeded_model
+
+    cfg = _tiny(act_mode)
+    mw = seeded_model(cfg, seed=7)
+    dm = DecodeModel(cfg, mw)
+    ref = LlamaRef(cfg, _oracle_weights(cuda_lib, cfg, mw))
+    prompt = [5, 17, 999, 3, 250]
+    dm.prefill(prompt[:-1])
+    for p, t in enumerate(prompt[:-1]):
+        ref.step(t, p)
+    dm.reset(prompt[-1], len(prompt) - 1)
+    token, pos = prompt[-1], len(prompt) - 1
+    for _ in range(6):
+        lr = ref.step(token, pos)
+        got = dm.generate(1)[0]
+        lg = dm.logits.cpu().numpy().astype(np.float64)
+        scale = np.abs(lr).max()
+        assert (np.abs(lg - lr) <= tol * scale).all(), np.abs(lg - lr).max() / scale
+        top2 = np.sort(lr)[-2:]
+        if top2[1] - top2[0] > 2 * tol * scale:
+            assert got == int(np.argmax(lr))
+        token, pos = got, pos + 1
+
+
+def test_graph_replay_equals_eager(cuda_lib):
+    from odiengine_b200.decode import DecodeModel, seeded_model
+
+    cfg = _tiny(0)
+    mw = seeded_model(cfg, seed=9)
+    a = DecodeModel(cfg, mw)
+    b = DecodeModel(cfg, mw)
+    for m in (a, b):
+        m.reset(11, 0)
+    eager = a.generate(12)
+    b.generate(1)  # one eager step first (sets kernel attributes), then restart and capture
+    b.clear_cache()
+    b.reset(11, 0)
+    b.capture()
+    b.clear_cache()
+    b.reset(11, 0)
+    assert b.generate(12) == eager
