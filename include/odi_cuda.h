@@ -171,6 +171,25 @@ int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d
                     int64_t N, int64_t K, int act_mode, void* d_workspace,
                     size_t workspace_bytes, int flags, void* stream);
 
+/* Operations fused into the streaming GEMV of odi_cuda_matmul (decode
+ * step): the activation row is RMS-normalised first (Backend::rms_norm,
+ * cpu_backend.cpp:388-414: x / sqrt(mean(x^2) + eps) * norm_weight), or is
+ * silu(gate) * up of a [gate K | up K] row (the SwiGLU of context.cpp:
+ * 272-275; x rows then hold 2K values); the product is added to y
+ * (the residual add of context.cpp:124, 130) instead of stored. */
+typedef struct odi_cuda_matmul_opts {
+  const float* norm_weight;  /* K weights, or NULL */
+  float norm_eps;
+  int swiglu;                /* exclusive with norm_weight */
+  int accumulate;
+} odi_cuda_matmul_opts;
+
+/* odi_cuda_matmul with the operations above (ACT_Q8 / ACT_F32, and AUTO
+ * below ODI_CUDA_TC_MIN_TOKENS); opts == NULL is odi_cuda_matmul. */
+int odi_cuda_matmul_fused(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M,
+                          int64_t N, int64_t K, int act_mode, void* d_workspace, size_t workspace_bytes,
+                          int flags, const odi_cuda_matmul_opts* opts, void* stream);
+
 /* Reads and clears the device-side error word of a workspace (kernel waits
  * that gave up set it).  Synchronises `stream`.  *status = 0 when clean. */
 int odi_cuda_workspace_status(void* d_workspace, int* status, void* stream);

@@ -70,6 +70,7 @@ SIGNATURES = {
     "odi_cuda_quantize_q8_0": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "odi_cuda_matmul_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _int]),
     "odi_cuda_matmul": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp]),
+    "odi_cuda_matmul_fused": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp, _vp]),
     "odi_cuda_workspace_status": (_int, [_vp, ctypes.POINTER(_int), _vp]),
     "odi_cuda_dequantize": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
     "odi_cuda_matmul_host": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
@@ -100,6 +101,13 @@ NOALLOC_SCRATCH_BYTES = 8 << 20
 
 MAX_PEERS = 8  # ODI_CUDA_MAX_PEERS
 IPC_HANDLE_BYTES = 64  # ODI_CUDA_IPC_HANDLE_BYTES
+
+
+class MatmulOpts(ctypes.Structure):
+    """odi_cuda_matmul_opts (include/odi_cuda.h)."""
+
+    _fields_ = [("norm_weight", ctypes.c_void_p), ("norm_eps", ctypes.c_float), ("swiglu", ctypes.c_int),
+                ("accumulate", ctypes.c_int)]
 
 
 class Scatter(ctypes.Structure):

@@ -79,18 +79,21 @@ int check_shape(int dt, int64_t N, int64_t K) {
 // The streaming GEMV over M tokens: one launch per pass of plan.mt tokens.
 // With `sc`, each pass scatters its rows into every rank's gathered buffer.
 int run_gemv(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N, int64_t K,
-             bool f32, int* err, bool pdl, cudaStream_t s, const GemvScatter* sc) {
+             bool f32, int* err, bool pdl, cudaStream_t s, const GemvScatter* sc, const GemvFuse* fu = nullptr) {
+  const int64_t ldx = (fu && fu->swiglu) ? 2 * K : K;
   const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
   if (plan.C == 0)
     return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
   for (int64_t m0 = 0; m0 < M; m0 += plan.mt) {
     GemvArgs a;
     a.w = (const uint8_t*)d_w_tiled;
-    a.x = d_x + m0 * K;
+    a.x = d_x + m0 * ldx;
     a.y = d_y ? d_y + m0 * N : nullptr;
     a.err = err;
     a.N = N;
     a.K = K;
+    a.ldx = ldx;
+    a.fu = fu ? *fu : GemvFuse{};
     a.M = (int)((M - m0) < plan.mt ? (M - m0) : plan.mt);
     a.sc = GemvScatter{};
     if (sc) {
@@ -305,6 +308,32 @@ int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d
   const bool f32 = mode == ODI_CUDA_ACT_F32;
   const bool pdl = (flags & ODI_CUDA_FLAG_PDL) != 0;
   return run_gemv(dtype, d_w_tiled, d_x, d_y, M, N, K, f32, (int*)d_workspace, pdl, s, nullptr);
+}
+
+int odi_cuda_matmul_fused(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N,
+                          int64_t K, int act_mode, void* d_workspace, size_t workspace_bytes, int flags,
+                          const odi_cuda_matmul_opts* opts, void* stream) {
+  if (!opts) return odi_cuda_matmul(dtype, d_w_tiled, d_x, d_y, M, N, K, act_mode, d_workspace, workspace_bytes,
+                                    flags, stream);
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (M < 1 || M > (1 << 20)) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M=%lld", (long long)M);
+  const int mode = resolve_act_mode(dtype, M, act_mode);
+  if (mode != ODI_CUDA_ACT_Q8 && mode != ODI_CUDA_ACT_F32)
+    return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "fused prologues / epilogues run on the streaming GEMV (ACT_Q8 / ACT_F32)");
+  if (opts->norm_weight && opts->swiglu)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "norm_weight and swiglu are exclusive");
+  if (!d_w_tiled || !d_x || !d_y || !d_workspace) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  if (((uintptr_t)d_w_tiled | (uintptr_t)d_workspace) & 15)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight and workspace must be 16-byte aligned");
+  if (workspace_bytes < WS_HEADER) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small");
+  GemvFuse fu{};
+  fu.norm_w = opts->norm_weight;
+  fu.eps = opts->norm_eps;
+  fu.swiglu = opts->swiglu ? 1 : 0;
+  fu.accumulate = opts->accumulate ? 1 : 0;
+  return run_gemv(dtype, d_w_tiled, d_x, d_y, M, N, K, mode == ODI_CUDA_ACT_F32, (int*)d_workspace,
+                  (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, nullptr, &fu);
 }
 
 int odi_cuda_workspace_status(void* d_workspace, int* status, void* stream) {

@@ -96,17 +96,20 @@ __global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, con
 }
 
 // Flash decoding, pass 1: CTA (h, c) covers positions [c*ATT_CHUNK, +ATT_CHUNK)
-// of kv_len = pos + 1; its 8 warps take 32 positions each.  Lane l holds
-// dims [l*HD/32, +HD/32) of q and of its running output; per position the
-// warp loads k_j and v_j coalesced (HD halves each), reduces the dot across
-// lanes and updates an online softmax (running max m, sum l, output acc).
-// The CTA folds its warps and writes (m, l, acc[HD]) for the chunk.
+// of kv_len = pos + 1; its 8 warps take PW = ATT_CHUNK/8 positions each.
+// Lane l holds dims [l*HD/32, +HD/32) of q and of its running output.  A
+// warp first loads all PW positions' k and v (coalesced: each position is
+// HD contiguous halves), so the loads are in flight together, then reduces
+// the PW dots across lanes and folds them into an online softmax (running
+// max m, sum l, output acc).  The CTA folds its warps and writes
+// (m, l, acc[HD]) for the chunk.
 template <int HD>
 __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
                                                            const __half* __restrict__ vc, float* __restrict__ part,
                                                            const DecodeState* st, int heads, int kv_heads, int ctx,
                                                            int nch, float scale) {
-  constexpr int DPL = HD / 32;  // dims per lane
+  constexpr int DPL = HD / 32;         // dims per lane
+  constexpr int PW = ATT_CHUNK / 8;    // positions per warp
   __shared__ float sm[8], sl[8], sacc[8][HD];
   const int h = blockIdx.x, c = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -120,31 +123,53 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
   float m = -INFINITY, l = 0.f, acc[DPL];
 #pragma unroll
   for (int e = 0; e < DPL; ++e) acc[e] = 0.f;
-  const int j0 = c * ATT_CHUNK + warp * (ATT_CHUNK / 8);
-  const int j1 = min(kv_len, j0 + ATT_CHUNK / 8);
-  for (int j = j0; j < j1; ++j) {
-    float kf[DPL], vf[DPL];
-    const __half* kp = kb + (int64_t)j * HD + lane * DPL;
-    const __half* vp = vb + (int64_t)j * HD + lane * DPL;
+  const int j0 = c * ATT_CHUNK + warp * PW;
+  const int nj = max(0, min(kv_len - j0, PW));
+  __half2 kr[PW][DPL / 2], vr[PW][DPL / 2];
 #pragma unroll
-    for (int e = 0; e < DPL; e += 2) {
-      const float2 kk = __half22float2(*reinterpret_cast<const __half2*>(kp + e));
-      const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(vp + e));
-      kf[e] = kk.x;
-      kf[e + 1] = kk.y;
-      vf[e] = vv.x;
-      vf[e + 1] = vv.y;
+  for (int t = 0; t < PW; ++t) {
+    if (t < nj) {
+      const __half2* kp = reinterpret_cast<const __half2*>(kb + (int64_t)(j0 + t) * HD + lane * DPL);
+      const __half2* vp = reinterpret_cast<const __half2*>(vb + (int64_t)(j0 + t) * HD + lane * DPL);
+#pragma unroll
+      for (int e = 0; e < DPL / 2; ++e) {
+        kr[t][e] = kp[e];
+        vr[t][e] = vp[e];
+      }
     }
+  }
+  float sc[PW];
+#pragma unroll
+  for (int t = 0; t < PW; ++t) {
     float d = 0.f;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) d = fmaf(qr[e], kf[e], d);
-    const float s = warp_sum(d);
-    const float mn = fmaxf(m, s);
-    const float corr = expf(m - mn), p = expf(s - mn);
-    l = l * corr + p;
+    for (int e = 0; e < DPL / 2; ++e) {
+      const float2 kk = __half22float2(kr[t][e]);
+      d = fmaf(qr[2 * e], kk.x, d);
+      d = fmaf(qr[2 * e + 1], kk.y, d);
+    }
+    sc[t] = d;
+  }
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) acc[e] = fmaf(p, vf[e], acc[e] * corr);
-    m = mn;
+  for (int o = 16; o; o >>= 1) {
+#pragma unroll
+    for (int t = 0; t < PW; ++t) sc[t] += __shfl_xor_sync(0xffffffffu, sc[t], o);
+  }
+#pragma unroll
+  for (int t = 0; t < PW; ++t) {
+    if (t < nj) {
+      const float s = sc[t];
+      const float mn = fmaxf(m, s);
+      const float corr = expf(m - mn), p = expf(s - mn);
+      l = l * corr + p;
+#pragma unroll
+      for (int e = 0; e < DPL / 2; ++e) {
+        const float2 vv = __half22float2(vr[t][e]);
+        acc[2 * e] = fmaf(p, vv.x, acc[2 * e] * corr);
+        acc[2 * e + 1] = fmaf(p, vv.y, acc[2 * e + 1] * corr);
+      }
+      m = mn;
+    }
   }
   if (lane == 0) {
     sm[warp] = m;

@@ -44,14 +44,26 @@ struct GemvScatter {
 };
 constexpr int WS_DONE_OFFSET = 64;       // byte offset of GemvScatter::done in the workspace
 
+// Transforms fused into the GEMV (decode step): the activation row is first
+// RMS-normalised (norm_w) or is silu(gate) * up of a [gate K | up K] row
+// (swiglu); the result is added to y (accumulate) instead of stored.
+struct GemvFuse {
+  const float* norm_w;  // non-null: x <- x / sqrt(mean(x^2) + eps) * norm_w, per token over K
+  float eps;
+  int swiglu;           // x rows are [gate | up], 2K values
+  int accumulate;       // y += product
+};
+
 struct GemvArgs {
   const uint8_t* w;   // tiled weight
-  const float* x;     // activations of this pass [M][K] fp32, row stride K
+  const float* x;     // activations of this pass [M][ldx] fp32
   float* y;           // outputs of this pass [M][N] fp32, row stride N
   int* err;           // device error word
   int64_t N, K;
+  int64_t ldx;        // row stride of x (K, or 2K for swiglu)
   int M;              // tokens in this pass (<= mt)
   GemvScatter sc;     // row offset of this pass's tokens is folded into sc.out
+  GemvFuse fu;
 };
 
 // Plan for dtype / tokens / fp32-activation mode on a device with num_sms SMs.
@@ -77,7 +89,7 @@ struct DecodeState {
   int step;   // tokens generated so far (index into the token record)
   int reserved;
 };
-constexpr int ATT_CHUNK = 256;  // positions per CTA in the attention's first pass
+constexpr int ATT_CHUNK = 64;  // positions per CTA in the attention's first pass (8 per warp)
 int attention_chunks(int ctx);
 cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x,
                          cudaStream_t s);

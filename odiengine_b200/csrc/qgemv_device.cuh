@@ -149,29 +149,83 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_by
 //    quantiser's arithmetic (d = amax/127 in fp32, q = round-half-away(
 //    x * (1/d)), d kept as fp16): codes at [32*b, 32*b+32), XRec b at
 //    256 + 16*b.  ACT_F32: the sums of each 16 values go after the values.
+// Fused prologues (GemvFuse), applied to the staged fp32 values before the
+// quantisation: SwiGLU builds silu(gate) * up with plain loads; RMSNorm
+// first reduces sum(x^2) over the whole row of every token of the pass
+// (the CTA reads the row once; the weights stream meanwhile) and then
+// scales the staged chunk by rms * norm_w.
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+template <int MT>
+__device__ __forceinline__ void row_rms(const GemvArgs& a, float* rms_out /* smem [MT] */, float* red /* smem */) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int m = 0; m < a.M; ++m) {
+    const float* xm = a.x + (int64_t)m * a.ldx;
+    float s = 0.f;
+    for (int64_t k = tid; k < a.K; k += NCW * 32) s = fmaf(xm[k], xm[k], s);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp * MT + m] = s;
+  }
+  consumer_sync();
+  if (tid < a.M) {
+    const float s = (red[0 * MT + tid] + red[1 * MT + tid]) + (red[2 * MT + tid] + red[3 * MT + tid]);
+    rms_out[tid] = 1.0f / sqrtf(s / (float)a.K + a.fu.eps);
+  }
+  consumer_sync();
+}
+
 template <bool F32, int MT>
-__device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr) {
+__device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr,
+                                           float* __restrict__ fuse_smem) {
   const int tid = threadIdx.x;  // 0..127
   const int warp = tid >> 5, lane = tid & 31;
-  const bool vec = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+  const bool vec = (a.K & 3) == 0 && (a.ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
   // 64 chunks per (span, token): threads 0-63 take even tokens, 64-127 odd
   const int q = tid & 63;
-  for (int j = 0; j < nsp; ++j) {
-    const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
-    const int64_t left = a.K - k;
-    const int nvalid = left <= 0 ? 0 : (left >= 4 ? 4 : (int)left);
-    for (int m = tid >> 6; m < a.M; m += 2) {
-      const float* src = a.x + (int64_t)m * a.K + (nvalid ? k : 0);
-      uint8_t* dst = xr + (j * MT + m) * XR_STRIDE + 16 * q;
-      if (vec) {
-        cp_async16(dst, src, 4 * nvalid);
-      } else {
+  if (a.fu.swiglu) {
+    for (int j = 0; j < nsp; ++j) {
+      const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
+      for (int m = tid >> 6; m < a.M; m += 2) {
+        const float* g = a.x + (int64_t)m * a.ldx;
+        float* dst = reinterpret_cast<float*>(xr + (j * MT + m) * XR_STRIDE + 16 * q);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) cp_async4(dst + 4 * e, src + (e < nvalid ? e : 0), e < nvalid ? 4 : 0);
+        for (int e = 0; e < 4; ++e) dst[e] = k + e < a.K ? silu_f(g[k + e]) * g[a.K + k + e] : 0.0f;
+      }
+    }
+  } else {
+    for (int j = 0; j < nsp; ++j) {
+      const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
+      const int64_t left = a.K - k;
+      const int nvalid = left <= 0 ? 0 : (left >= 4 ? 4 : (int)left);
+      for (int m = tid >> 6; m < a.M; m += 2) {
+        const float* src = a.x + (int64_t)m * a.ldx + (nvalid ? k : 0);
+        uint8_t* dst = xr + (j * MT + m) * XR_STRIDE + 16 * q;
+        if (vec) {
+          cp_async16(dst, src, 4 * nvalid);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) cp_async4(dst + 4 * e, src + (e < nvalid ? e : 0), e < nvalid ? 4 : 0);
+        }
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (a.fu.norm_w) row_rms<MT>(a, fuse_smem, fuse_smem + MT);  // overlaps the copies
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (a.fu.norm_w) {
+      // scale this thread's own staged 4-value chunks
+      for (int j = 0; j < nsp; ++j) {
+        const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
+        for (int m = tid >> 6; m < a.M; m += 2) {
+          float* v = reinterpret_cast<float*>(xr + (j * MT + m) * XR_STRIDE + 16 * q);
+          const float r = fuse_smem[m];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (k + e < a.K) v[e] = v[e] * r * a.fu.norm_w[k + e];
+        }
       }
     }
   }
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   consumer_sync();
   // one warp per staged (span, token); lane = (block b = lane/4, 8 values)
   const int b = lane >> 2, part = lane & 3;
@@ -562,6 +616,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 template <int MT>
 struct SmemMap {
   static constexpr int redbar = 512;
+  static constexpr int fuse = 768;  // GemvFuse scratch: rms[MT], partial sums[4][MT]
   static constexpr int red = BAR_BYTES;
   static constexpr int part = red + 2 * UNIT_ROWS * MT * 4;
   static constexpr int xr(int C) { return (part + C * UNIT_ROWS * MT * 4 + 127) / 128 * 128; }
@@ -571,7 +626,8 @@ struct SmemMap {
 // buffer (plain stores; peers' buffers are reached over NVLink).
 __device__ __forceinline__ void store_out(const GemvArgs& a, int m, int64_t n, float v) {
   if (a.sc.n == 0) {
-    a.y[(int64_t)m * a.N + n] = v;
+    float* p = a.y + (int64_t)m * a.N + n;
+    *p = a.fu.accumulate ? *p + v : v;
     return;
   }
   const int64_t off = (int64_t)m * a.sc.ld + a.sc.row0 + n;
@@ -677,7 +733,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
 
   // ---------------- consumers
   pdl_wait();  // x is written by earlier kernels on the stream; y may be read by them
-  stage_acts<F32, MT>(a, kb0, nsp, xr);
+  stage_acts<F32, MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
 
   const int row = 32 * (warp & 1) + lane;
   const int up = warp >> 1;  // this warp takes units j = up, up + 2, ...

@@ -132,10 +132,14 @@ class DecodeModel:
     forward pass (embed .. argmax) on ``stream``; ``capture()`` records it as
     a CUDA graph that ``generate`` replays."""
 
-    def __init__(self, cfg: LlamaConfig, weights: ModelWeights, device=None, max_record: int = 4096):
+    def __init__(self, cfg: LlamaConfig, weights: ModelWeights, device=None, max_record: int = 4096,
+                 fused: bool = True):
         import torch
 
         self.cfg, self.w = cfg, weights
+        # fused: RMSNorm, SwiGLU and the residual adds run inside the GEMVs
+        # (odi_cuda_matmul_fused); otherwise as separate kernels
+        self.fused = fused
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         dev, f32 = self.device, torch.float32
         E, F, H, hd = cfg.hidden, cfg.ffn, cfg.heads, cfg.head_dim
@@ -172,7 +176,46 @@ class DecodeModel:
         check(lib().odi_cuda_matmul(dw.dtype, dw.data_ptr, _ptr(x), _ptr(y), 1, dw.N, dw.K, self.cfg.act_mode,
                                     _ptr(ws), ws.numel(), FLAG_PDL, s))
 
+    def _gemv_fused(self, dw: DeviceWeight, x, y, s, norm=None, swiglu=False, accumulate=False):
+        from . import MatmulOpts
+
+        o = MatmulOpts(_ptr(norm) if norm is not None else None, self.cfg.eps, 1 if swiglu else 0,
+                       1 if accumulate else 0)
+        ws = dw._ws
+        check(lib().odi_cuda_matmul_fused(dw.dtype, dw.data_ptr, _ptr(x), _ptr(y), 1, dw.N, dw.K, self.cfg.act_mode,
+                                          _ptr(ws), ws.numel(), FLAG_PDL, ctypes.byref(o), s))
+
     def step(self) -> None:
+        if self.fused:
+            self._step_fused()
+        else:
+            self._step_unfused()
+
+    def _step_fused(self) -> None:
+        """7 launches per layer: QKV GEMV (RMSNorm fused), rope + KV append,
+        attention (2), O GEMV (+= x), gate|up GEMV (RMSNorm fused), down GEMV
+        (SwiGLU fused, += x)."""
+        cfg, L, s = self.cfg, lib(), self.stream.cuda_stream
+        H, KV, hd = cfg.heads, cfg.kv_heads, cfg.head_dim
+        st = _ptr(self.state)
+        q = _ptr(self.qkv)
+        k = q + H * hd * 4
+        v = k + KV * hd * 4
+        scale = 1.0 / math.sqrt(hd)
+        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, cfg.hidden, st, _ptr(self.x), s))
+        for li, lw in enumerate(self.w.layers):
+            kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
+            self._gemv_fused(lw.wqkv, self.x, self.qkv, s, norm=lw.attn_norm)
+            check(L.odi_cuda_rope_kv(q, k, v, kc, vc, st, H, KV, hd, cfg.ctx, cfg.theta, s))
+            check(L.odi_cuda_attention_decode(q, kc, vc, _ptr(self.attn), st, H, KV, hd, cfg.ctx, scale,
+                                              _ptr(self.att_scratch), self.att_scratch.numel() * 4, s))
+            self._gemv_fused(lw.wo, self.attn, self.x, s, accumulate=True)
+            self._gemv_fused(lw.wgu, self.x, self.gu, s, norm=lw.ffn_norm)
+            self._gemv_fused(lw.wdown, self.gu, self.x, s, swiglu=True, accumulate=True)
+        self._gemv_fused(self.w.output, self.x, self.logits, s, norm=self.w.out_norm)
+        check(L.odi_cuda_argmax(_ptr(self.logits), cfg.vocab, st, _ptr(self.record), self.max_record, s))
+
+    def _step_unfused(self) -> None:
         cfg, L, s = self.cfg, lib(), self.stream.cuda_stream
         E, F, H, KV, hd = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim
         st = _ptr(self.state)
@@ -200,6 +243,8 @@ class DecodeModel:
         check(L.odi_cuda_argmax(_ptr(self.logits), cfg.vocab, st, _ptr(self.record), self.max_record, s))
 
     def launches_per_step(self) -> int:
+        if self.fused:
+            return 1 + 7 * self.cfg.layers + 2  # embed, per layer, output GEMV + argmax
         return 1 + 11 * self.cfg.layers + 3  # embed, per layer, final norm + output GEMV + argmax
 
     def capture(self) -> None:

@@ -9,8 +9,9 @@ Per operation (tolerances written per test):
   attention (GQA, 2 chunks) |d| <= 1e-4 max|v|               (fp32 softmax, fp16 K/V)
   silu_mul                  |d| <= 1e-6 |y| + 1e-7
   argmax                    exact, ties -> lowest index; state advanced
-End to end (tiny Llama, 2 layers, GQA): logits within 2e-3 of their scale
-with fp32 GEMVs (ACT_F32) and within 6e-2 with Q8 activations; greedy
+End to end (tiny Llama, 2 layers, GQA), with RMSNorm / SwiGLU / residual
+adds fused into the GEMVs and as separate kernels: logits within 2e-3 of
+their scale with fp32 GEMVs (ACT_F32) and within 6e-2 with Q8 activations; greedy
 tokens equal wherever the oracle's top-2 gap exceeds that tolerance; a
 replayed CUDA graph reproduces the eager steps exactly.
 """
@@ -181,13 +182,14 @@ def _oracle_weights(ob, cfg, mw):
     return W
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "separate"])
 @pytest.mark.parametrize("act_mode,tol", [(1, 2e-3), (0, 6e-2)], ids=["f32", "q8"])
-def test_tiny_model_matches_oracle(cuda_lib, act_mode, tol):
+def test_tiny_model_matches_oracle(cuda_lib, act_mode, tol, fused):
     from odiengine_b200.decode import DecodeModel, seeded_model
 
     cfg = _tiny(act_mode)
     mw = seeded_model(cfg, seed=7)
-    dm = DecodeModel(cfg, mw)
+    dm = DecodeModel(cfg, mw, fused=fused)
     ref = LlamaRef(cfg, _oracle_weights(cuda_lib, cfg, mw))
     prompt = [5, 17, 999, 3, 250]
     dm.prefill(prompt[:-1])
@@ -224,3 +226,56 @@ def test_graph_replay_equals_eager(cuda_lib):
     b.clear_cache()
     b.reset(11, 0)
     assert b.generate(12) == eager
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K, O.Q8_0])
+@pytest.mark.parametrize("mode", [0, 1], ids=["q8", "f32"])
+def test_matmul_fused_ops(cuda_lib, dt, mode):
+    """odi_cuda_matmul_fused: RMSNorm prologue, SwiGLU prologue, accumulate
+    epilogue, against float64 compositions of the separate operations.
+    Tolerance: fp32 GEMV 1e-4 * (|W| @ |a|); Q8 GEMV adds the activation
+    quantisation bound of the oracle (0.5625 d_x sum|w| per block)."""
+    import ctypes
+
+    import torch
+
+    ob = cuda_lib
+    N, K, M = 320, 2048, 2
+    rng = np.random.default_rng(dt + mode)
+    b = O.quantize(dt, O.seeded_weights(N, K, seed=dt))
+    W = O.dequantize(dt, b, N, K).astype(np.float64)
+    dw = ob.DeviceWeight(ob.QuantWeight(dt, (K, N), b))
+    ws = dw._ws_for(M, mode, torch.device("cuda"))
+
+    def run(x, y, opts):
+        xd = _t(x)
+        ob.check(ob.lib().odi_cuda_matmul_fused(dt, dw.data_ptr, xd.data_ptr(), y.data_ptr(), M, N, K, mode,
+                                                ws.data_ptr(), ws.numel(), 0, ctypes.byref(opts), None))
+        torch.cuda.synchronize()
+        assert ob.workspace_status(ws) == 0
+        return y.cpu().numpy().astype(np.float64)
+
+    def tol(a):
+        t = 1e-4 * (np.abs(a) @ np.abs(W).T)
+        if mode == 0:
+            _, bact = O.matmul_q8act(dt, a.astype(np.float32), b, N)
+            t = t + bact
+        return t
+
+    # RMSNorm prologue
+    x = rng.standard_normal((M, K)).astype(np.float32) * 3
+    nw = (1 + 0.02 * rng.standard_normal(K)).astype(np.float32)
+    nwd = _t(nw)
+    y = run(x, torch.zeros((M, N), device="cuda"), ob.MatmulOpts(nwd.data_ptr(), 1e-5, 0, 0))
+    h = np.stack([rms_norm(x[i], nw, 1e-5) for i in range(M)])
+    assert (np.abs(y - h @ W.T) <= tol(h)).all()
+    # SwiGLU prologue (x rows are [gate | up])
+    gu = rng.standard_normal((M, 2 * K)).astype(np.float32)
+    y = run(gu, torch.zeros((M, N), device="cuda"), ob.MatmulOpts(None, 0.0, 1, 0))
+    g, u = gu[:, :K].astype(np.float64), gu[:, K:].astype(np.float64)
+    a = g / (1 + np.exp(-g)) * u
+    assert (np.abs(y - a @ W.T) <= tol(a)).all()
+    # accumulate epilogue
+    y0 = rng.standard_normal((M, N)).astype(np.float32)
+    y = run(x, _t(y0), ob.MatmulOpts(None, 0.0, 0, 1))
+    assert (np.abs(y - (y0 + x.astype(np.float64) @ W.T)) <= tol(x.astype(np.float64)) + 1e-6 * np.abs(y0)).all()
