@@ -182,6 +182,14 @@ typedef struct odi_cuda_matmul_opts {
   float norm_eps;
   int swiglu;                /* exclusive with norm_weight */
   int accumulate;
+  /* RMSNorm from partial sums instead of a pass over x: norm_ssq holds
+   * norm_ssq_count sums of squares per token (e.g. out_ssq of the GEMV, or
+   * the ssq of odi_cuda_embed, that wrote x).  NULL: sum x itself. */
+  const float* norm_ssq;
+  int norm_ssq_count;
+  /* If non-NULL: the sum of squares of the stored y of every 64-row tile,
+   * [M][ceil(N / 64)] -- what the next GEMV's RMSNorm needs. */
+  float* out_ssq;
 } odi_cuda_matmul_opts;
 
 /* odi_cuda_matmul with the operations above (ACT_Q8 / ACT_F32, and AUTO
@@ -226,9 +234,11 @@ typedef struct odi_cuda_decode_state {
 } odi_cuda_decode_state;
 
 /* x[E] = table[token] (Backend::embedding, cpu_backend.cpp:610-619; table
- * fp32 [vocab][E], an out-of-range token reads row 0). */
+ * fp32 [vocab][E], an out-of-range token reads row 0).  d_ssq (or NULL):
+ * the sum of squares of every 64 values, ceil(E / 64) floats, for a fused
+ * RMSNorm (odi_cuda_matmul_opts.norm_ssq). */
 int odi_cuda_embed(const float* d_table, int64_t vocab, int64_t E, const odi_cuda_decode_state* d_state, float* d_x,
-                   void* stream);
+                   float* d_ssq, void* stream);
 
 /* y = x / sqrt(mean(x^2) + eps) * w per row of n (Backend::rms_norm,
  * cpu_backend.cpp:388-414).  y may alias x. */

@@ -332,6 +332,11 @@ int odi_cuda_matmul_fused(int dtype, const void* d_w_tiled, const float* d_x, fl
   fu.eps = opts->norm_eps;
   fu.swiglu = opts->swiglu ? 1 : 0;
   fu.accumulate = opts->accumulate ? 1 : 0;
+  if (opts->norm_ssq && opts->norm_ssq_count < 1)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "norm_ssq_count must be positive");
+  fu.ssq_in = opts->norm_ssq;
+  fu.ssq_n = opts->norm_ssq_count;
+  fu.ssq_out = opts->out_ssq;
   return run_gemv(dtype, d_w_tiled, d_x, d_y, M, N, K, mode == ODI_CUDA_ACT_F32, (int*)d_workspace,
                   (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, nullptr, &fu);
 }
@@ -366,9 +371,9 @@ static_assert(sizeof(odi_cuda_decode_state) == sizeof(DecodeState), "decode stat
 extern "C" {
 
 int odi_cuda_embed(const float* d_table, int64_t vocab, int64_t E, const odi_cuda_decode_state* d_state, float* d_x,
-                   void* stream) {
+                   float* d_ssq, void* stream) {
   if (!d_table || !d_state || !d_x || vocab < 1 || E < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "embed: bad argument");
-  CK(launch_embed(d_table, vocab, E, reinterpret_cast<const DecodeState*>(d_state), d_x, (cudaStream_t)stream),
+  CK(launch_embed(d_table, vocab, E, reinterpret_cast<const DecodeState*>(d_state), d_x, d_ssq, (cudaStream_t)stream),
      "embed launch");
   return ODI_CUDA_OK;
 }

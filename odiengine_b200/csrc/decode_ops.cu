@@ -31,13 +31,22 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// One CTA of 64 threads per 64 values; with ssq, each CTA also leaves the
+// sum of squares of its values (the slot a fused RMSNorm reads).
 __global__ void embed_kernel(const float* __restrict__ table, const DecodeState* st, float* __restrict__ x,
-                             int64_t E, int64_t vocab) {
+                             float* __restrict__ ssq, int64_t E, int64_t vocab) {
+  __shared__ float red[2];
   int tok = st->token;
   if (tok < 0 || tok >= vocab) tok = 0;  // out-of-range ids are rejected on the host; never read outside
-  const float* row = table + (int64_t)tok * E;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < E; i += (int64_t)gridDim.x * blockDim.x)
-    x[i] = row[i];
+  const int64_t i = blockIdx.x * 64ll + threadIdx.x;
+  const float v = i < E ? table[(int64_t)tok * E + i] : 0.f;
+  if (i < E) x[i] = v;
+  if (ssq) {
+    const float s = warp_sum(v * v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) ssq[blockIdx.x] = red[0] + red[1];
+  }
 }
 
 // One CTA per row.
@@ -293,9 +302,9 @@ static int grid_for(int64_t n, int threads) {
   return (int)(b < 1 ? 1 : b);
 }
 
-cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x,
+cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x, float* ssq,
                          cudaStream_t s) {
-  embed_kernel<<<grid_for(E, 256), 256, 0, s>>>(table, st, x, E, vocab);
+  embed_kernel<<<(unsigned)((E + 63) / 64), 64, 0, s>>>(table, st, x, ssq, E, vocab);
   return cudaGetLastError();
 }
 

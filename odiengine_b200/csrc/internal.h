@@ -52,6 +52,9 @@ struct GemvFuse {
   float eps;
   int swiglu;           // x rows are [gate | up], 2K values
   int accumulate;       // y += product
+  const float* ssq_in;  // norm: sums of squares of x in ssq_n slots per token (else summed from x)
+  int ssq_n;
+  float* ssq_out;       // sums of squares of the stored y, one slot per 64-row tile: [M][G]
 };
 
 struct GemvArgs {
@@ -91,7 +94,7 @@ struct DecodeState {
 };
 constexpr int ATT_CHUNK = 64;  // positions per CTA in the attention's first pass (8 per warp)
 int attention_chunks(int ctx);
-cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x,
+cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x, float* ssq,
                          cudaStream_t s);
 cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,
                             cudaStream_t s);

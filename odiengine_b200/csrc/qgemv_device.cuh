@@ -160,9 +160,14 @@ template <int MT>
 __device__ __forceinline__ void row_rms(const GemvArgs& a, float* rms_out /* smem [MT] */, float* red /* smem */) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   for (int m = 0; m < a.M; ++m) {
-    const float* xm = a.x + (int64_t)m * a.ldx;
     float s = 0.f;
-    for (int64_t k = tid; k < a.K; k += NCW * 32) s = fmaf(xm[k], xm[k], s);
+    if (a.fu.ssq_in) {  // the producer of x left its sums of squares in slots
+      const float* sq = a.fu.ssq_in + (int64_t)m * a.fu.ssq_n;
+      for (int i = tid; i < a.fu.ssq_n; i += NCW * 32) s += sq[i];
+    } else {
+      const float* xm = a.x + (int64_t)m * a.ldx;
+      for (int64_t k = tid; k < a.K; k += NCW * 32) s = fmaf(xm[k], xm[k], s);
+    }
 #pragma unroll
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (lane == 0) red[warp * MT + m] = s;
@@ -624,14 +629,27 @@ struct SmemMap {
 
 // One output element: to y, or -- for a row shard -- to every rank's gathered
 // buffer (plain stores; peers' buffers are reached over NVLink).
-__device__ __forceinline__ void store_out(const GemvArgs& a, int m, int64_t n, float v) {
+__device__ __forceinline__ float store_out(const GemvArgs& a, int m, int64_t n, float v) {
   if (a.sc.n == 0) {
     float* p = a.y + (int64_t)m * a.N + n;
-    *p = a.fu.accumulate ? *p + v : v;
-    return;
+    const float nv = a.fu.accumulate ? *p + v : v;
+    *p = nv;
+    return nv;
   }
   const int64_t off = (int64_t)m * a.sc.ld + a.sc.row0 + n;
   for (int p = 0; p < a.sc.n; ++p) a.sc.out[p][off] = v;
+  return v;
+}
+
+// ssq_out: the squares of this tile's stored values were left at buf[r*rs +
+// m*ms]; one thread per token adds the 64 rows in order into slot g.
+__device__ __forceinline__ void write_ssq(const GemvArgs& a, const float* buf, int rs, int ms, int g, int G) {
+  const int tid = threadIdx.x;
+  if (tid < a.M) {
+    float s = 0.f;
+    for (int r = 0; r < UNIT_ROWS; ++r) s += buf[r * rs + tid * ms];
+    a.fu.ssq_out[(int64_t)tid * G + g] = s;
+  }
 }
 
 // After this CTA's output stores (consumer_sync between), one thread per
@@ -770,12 +788,17 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     const float v = red[(0 * UNIT_ROWS + r) * MT + m] + red[(1 * UNIT_ROWS + r) * MT + m];
     if (pl.C == 1) {
       const int64_t n = (int64_t)g * UNIT_ROWS + r;
-      if (n < a.N) store_out(a, m, n, v);
+      const float nv = n < a.N ? store_out(a, m, n, v) : 0.f;
+      if (a.fu.ssq_out) red[(0 * UNIT_ROWS + r) * MT + m] = nv * nv;  // the slot this thread just read
     } else if (rank == 0) {
       part[t] = v;
     } else {
       st_dsmem_f32(dsmem_addr(part + rank * UNIT_ROWS * MT + t, 0), v);
     }
+  }
+  if (pl.C == 1 && a.fu.ssq_out) {
+    consumer_sync();
+    write_ssq(a, red, MT, 1, g, pl.G);
   }
   if (pl.C > 1) {
     if (rank != 0) {
@@ -788,7 +811,12 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
         float v = part[t];
         for (int q = 1; q < pl.C; ++q) v += part[q * UNIT_ROWS * MT + t];
         const int64_t n = (int64_t)g * UNIT_ROWS + r;
-        if (n < a.N) store_out(a, m, n, v);
+        const float nv = n < a.N ? store_out(a, m, n, v) : 0.f;
+        if (a.fu.ssq_out) part[t] = nv * nv;  // the slot this thread just read
+      }
+      if (a.fu.ssq_out) {
+        consumer_sync();
+        write_ssq(a, part, 1, UNIT_ROWS, g, pl.G);
       }
       if (a.sc.n) {
         consumer_sync();

@@ -151,6 +151,10 @@ class DecodeModel:
         self.gu = torch.zeros(2 * F, dtype=f32, device=dev)
         self.a = torch.zeros(F, dtype=f32, device=dev)
         self.logits = torch.zeros(cfg.vocab, dtype=f32, device=dev)
+        # sums of squares of x per 64 values, left by x's writer (embed or a
+        # residual GEMV) for the next fused RMSNorm
+        self.ssq_slots = (E + 63) // 64
+        self.ssq = torch.zeros(self.ssq_slots, dtype=f32, device=dev)
         self.kc = torch.zeros((cfg.layers, cfg.kv_heads, cfg.ctx, hd), dtype=torch.float16, device=dev)
         self.vc = torch.zeros_like(self.kc)
         sb = lib().odi_cuda_attention_scratch_bytes(H, hd, cfg.ctx)
@@ -177,10 +181,14 @@ class DecodeModel:
                                     _ptr(ws), ws.numel(), FLAG_PDL, s))
 
     def _gemv_fused(self, dw: DeviceWeight, x, y, s, norm=None, swiglu=False, accumulate=False):
+        """norm: RMSNorm of x from the sums of squares its writer left in
+        self.ssq; accumulate: y += product, leaving y's sums of squares."""
         from . import MatmulOpts
 
+        ssq = _ptr(self.ssq)
         o = MatmulOpts(_ptr(norm) if norm is not None else None, self.cfg.eps, 1 if swiglu else 0,
-                       1 if accumulate else 0)
+                       1 if accumulate else 0, ssq if norm is not None else None, self.ssq_slots,
+                       ssq if accumulate else None)
         ws = dw._ws
         check(lib().odi_cuda_matmul_fused(dw.dtype, dw.data_ptr, _ptr(x), _ptr(y), 1, dw.N, dw.K, self.cfg.act_mode,
                                           _ptr(ws), ws.numel(), FLAG_PDL, ctypes.byref(o), s))
@@ -202,7 +210,7 @@ class DecodeModel:
         k = q + H * hd * 4
         v = k + KV * hd * 4
         scale = 1.0 / math.sqrt(hd)
-        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, cfg.hidden, st, _ptr(self.x), s))
+        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, cfg.hidden, st, _ptr(self.x), _ptr(self.ssq), s))
         for li, lw in enumerate(self.w.layers):
             kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
             self._gemv_fused(lw.wqkv, self.x, self.qkv, s, norm=lw.attn_norm)
@@ -223,7 +231,7 @@ class DecodeModel:
         k = q + H * hd * 4
         v = k + KV * hd * 4
         scale = 1.0 / math.sqrt(hd)
-        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, E, st, _ptr(self.x), s))
+        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, E, st, _ptr(self.x), None, s))
         for li, lw in enumerate(self.w.layers):
             kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
             check(L.odi_cuda_rms_norm(_ptr(self.x), _ptr(lw.attn_norm), _ptr(self.h), 1, E, cfg.eps, s))

@@ -46,9 +46,11 @@ def test_embed_and_add(cuda_lib):
     x = torch.zeros(96, device="cuda")
     st = _state(37, 0)
     td = _t(table)
-    cuda_lib.check(L.odi_cuda_embed(td.data_ptr(), 50, 96, st.data_ptr(), x.data_ptr(), None))
+    ssq = torch.zeros(2, device="cuda")
+    cuda_lib.check(L.odi_cuda_embed(td.data_ptr(), 50, 96, st.data_ptr(), x.data_ptr(), ssq.data_ptr(), None))
     torch.cuda.synchronize()
     assert np.array_equal(x.cpu().numpy(), table[37])
+    assert np.allclose(ssq.cpu().numpy(), [np.sum(table[37][:64] ** 2), np.sum(table[37][64:] ** 2)], rtol=1e-5)
     d = rng.standard_normal(96).astype(np.float32)
     dd = _t(d)
     cuda_lib.check(L.odi_cuda_add(x.data_ptr(), dd.data_ptr(), 96, None))
@@ -279,3 +281,43 @@ def test_matmul_fused_ops(cuda_lib, dt, mode):
     y0 = rng.standard_normal((M, N)).astype(np.float32)
     y = run(x, _t(y0), ob.MatmulOpts(None, 0.0, 0, 1))
     assert (np.abs(y - (y0 + x.astype(np.float64) @ W.T)) <= tol(x.astype(np.float64)) + 1e-6 * np.abs(y0)).all()
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
+def test_matmul_fused_ssq_slots(cuda_lib, dt):
+    """The residual GEMV leaves per-64-row sums of squares of the stored y
+    (out_ssq); a norm GEMV fed those slots (norm_ssq) equals one that sums x
+    itself, up to the order of the sum of squares."""
+    import ctypes
+
+    import torch
+
+    ob = cuda_lib
+    N, K, M = 4096, 4096, 1
+    rng = np.random.default_rng(dt)
+    b = O.quantize(dt, O.seeded_weights(N, K, seed=dt))
+    dw = ob.DeviceWeight(ob.QuantWeight(dt, (K, N), b))
+    ws = dw._ws_for(M, 1, torch.device("cuda"))
+    x = _t(rng.standard_normal((M, K)).astype(np.float32))
+    y = _t(rng.standard_normal((M, N)).astype(np.float32))
+    slots = torch.zeros((M, N // 64), device="cuda")
+    ob.check(ob.lib().odi_cuda_matmul_fused(dt, dw.data_ptr, x.data_ptr(), y.data_ptr(), M, N, K, 1, ws.data_ptr(),
+                                            ws.numel(), 0, ctypes.byref(ob.MatmulOpts(None, 0.0, 0, 1, None, 0,
+                                                                                      slots.data_ptr())), None))
+    torch.cuda.synchronize()
+    yn = y.cpu().numpy().astype(np.float64)
+    ref = (yn.reshape(M, N // 64, 64) ** 2).sum(-1)
+    assert np.allclose(slots.cpu().numpy(), ref, rtol=1e-5)
+    # RMSNorm of y from the slots vs from y itself
+    nw = _t((1 + 0.02 * rng.standard_normal(N)).astype(np.float32))
+    out_a = torch.zeros((M, K), device="cuda")
+    out_b = torch.zeros((M, K), device="cuda")
+    dw2 = ob.DeviceWeight(ob.QuantWeight(dt, (N, K), O.quantize(dt, O.seeded_weights(K, N, seed=3))))
+    ws2 = dw2._ws_for(M, 1, torch.device("cuda"))
+    for out, opts in ((out_a, ob.MatmulOpts(nw.data_ptr(), 1e-5, 0, 0, slots.data_ptr(), N // 64, None)),
+                      (out_b, ob.MatmulOpts(nw.data_ptr(), 1e-5, 0, 0, None, 0, None))):
+        ob.check(ob.lib().odi_cuda_matmul_fused(dt, dw2.data_ptr, y.data_ptr(), out.data_ptr(), M, K, N, 1,
+                                                ws2.data_ptr(), ws2.numel(), 0, ctypes.byref(opts), None))
+    torch.cuda.synchronize()
+    a, bb = out_a.cpu().numpy(), out_b.cpu().numpy()
+    assert np.allclose(a, bb, rtol=1e-4, atol=1e-4 * np.abs(bb).max())
