@@ -10,7 +10,7 @@ static int tokens_per_pass(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 
 // GPU when there are few tiles (decode shapes), at the cost of one
 // distributed-shared-memory reduction per tile.  Estimated time in units of
 // one span, per CTA slot: waves * (chunk + 1) (+ half a CTA of tail when the
-// grid needs more than one wave) (+ the reduction).
+// grid needs more than one wave) (+ the reduction and cluster cost).
 GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms) {
   GemvPlan p{};
   p.G = (int)((N + UNIT_ROWS - 1) / UNIT_ROWS);
@@ -30,7 +30,10 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
       const double waves = ctas / slots;
       double t = (waves > 1.0 ? waves : 1.0) * (chunk + 1);
       if (waves > 1.0) t += 0.5 * (chunk + 1);
-      if (ceff > 1) t += 0.5;
+      // the cluster reduction, and the scheduling of larger clusters, cost
+      // 0.5 + 0.25 * log2(C) spans (fitted to measured C = 1..8 timings of
+      // the 7B and 70B decode shapes)
+      if (ceff > 1) t += 0.5 + 0.25 * (ceff >= 8 ? 3 : ceff >= 4 ? 2 : 1);
       if (t < best) {
         best = t;
         bestC = ceff;
