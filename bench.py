@@ -18,6 +18,13 @@ Reported (one JSON line on rank 0):
               measured HBM copy bandwidth in MEASURED_PEAKS.json
   cpu_baseline the oracle's restatement of the reference loop on the host
               cores (the reference itself throws on Q4_K), bounded sample
+  decode_7b   (1 GPU) the second half of the metric: tokens/s of greedy
+              decode of a Llama-2-7B-shaped Q4_K/Q6_K model with 2048 prompt
+              tokens in the fp16 KV cache, 256 timed steps (CUDA events
+              around graph replays), its HBM roofline (weights + mean KV
+              bytes per token), an end-to-end figure through
+              DecodeModel.generate and a host-core sample of the same
+              token's matrix products
 
 Multi-GPU (torchrun, N > 1): weak scaling by output-row sharding -- every
 rank holds a 4096-row shard of each weight (the full matrix has 4096*N
@@ -198,6 +205,12 @@ def run_reference(args, rank):
                                    "reference block loop; CPUBackend::matmul throws for K-quants)"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_decode:
+        t_cpu, sample = cpu_decode_sample(nthreads)
+        line["decode_7b"] = {"metric": "7B-shape Q4_K decode tokens/s (1 sequence, greedy)",
+                             "value": round(1.0 / t_cpu, 4), "unit": "tokens/s",
+                             "cpu_baseline": {"value": round(1.0 / t_cpu, 4), "unit": "tokens/s",
+                                              "cores": nthreads, "kind": "port", "sample": sample}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -445,6 +458,11 @@ def run_ours(args, rank, world, local_rank):
                         "threads_used": r1[2], "kind": "reference",
                         "sample": "unmodified CPUBackend::matmul, Q4_0 4096x4096 M=1 (config 1)"}
 
+    decode = None
+    if world == 1 and not args.no_decode:
+        del g_step, g_gemv
+        decode = run_decode(args, local_rank)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -461,9 +479,11 @@ def run_ours(args, rank, world, local_rank):
             "reference_cpu_config1": ref_cfg1,
             "clocks": clk.summary(),
             "gpu_launches": args.steps * SWEEPS * R * (2 if fused else 1),
+            "decode_7b": decode,
         }
         print(json.dumps(line), flush=True)
-    del g_step, g_gemv
+    if decode is None:
+        del g_step, g_gemv
     if fused:
         torch.cuda.synchronize()
         st = ob.workspace_status(ws)
@@ -475,6 +495,133 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier(device_ids=[local_rank])
         sym.close()
     return 0
+
+
+DEC_PROMPT, DEC_GEN = 2048, 256
+
+
+def run_decode(args, local_rank):
+    """7B-shape decode (Llama-2-7B shape: 32 layers, hidden 4096, 32 heads of
+    128, ffn 11008, vocab 32000; Q4_K attention and gate/up, Q6_K down and
+    output, seeded N(0, 0.02) weights quantised on the device; fp16 KV
+    cache).  The KV cache is filled from 2048 seeded random prompt tokens,
+    then DEC_GEN greedy steps are timed: each step is one replay of the
+    captured decode graph (embed .. argmax, token and position advanced on
+    the device)."""
+    import torch
+
+    from odiengine_b200.decode import DecodeModel, LlamaConfig, seeded_model
+
+    dev = torch.device("cuda", local_rank)
+    P, G = DEC_PROMPT, DEC_GEN
+    cfg = LlamaConfig(ctx=P + G + 8)
+    t0 = time.perf_counter()
+    mw = seeded_model(cfg, seed=0, device=dev)
+    torch.cuda.synchronize()
+    t_build = time.perf_counter() - t0
+    dm = DecodeModel(cfg, mw, device=dev)
+    dm.reset(1, 0)
+    dm.generate(1)  # one eager step (kernel attributes), then the graph
+    dm.clear_cache()
+    dm.reset(1, 0)
+    dm.capture()
+    gen = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (P,), generator=gen).tolist()
+    dm.clear_cache()
+    t0 = time.perf_counter()
+    dm.prefill(prompt)
+    t_prefill = time.perf_counter() - t0
+
+    def from_prompt_end():
+        # the last prompt token again at its own position: its argmax is the
+        # first generated token
+        dm.reset(prompt[-1], P - 1)
+        dm.stream.synchronize()
+
+    from_prompt_end()
+    dm.generate(max(3, args.warmup))
+    from_prompt_end()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        clk.wait_first_sample()
+        e0.record(dm.stream)
+        with torch.cuda.stream(dm.stream):
+            for _ in range(G):
+                dm.graph.replay()
+        e1.record(dm.stream)
+        dm.stream.synchronize()
+    ms_tok = e0.elapsed_time(e1) / G
+    toks = dm.record[:G].cpu().tolist()
+    # end to end: the same G steps through DecodeModel.generate (host call,
+    # graph replays, the G tokens read back to the host), wall clock
+    from_prompt_end()
+    t0 = time.perf_counter()
+    toks2 = dm.generate(G)
+    el = time.perf_counter() - t0
+    assert toks2 == toks, "decode is not deterministic"
+    wb = cfg.weight_bytes()
+    kvb = cfg.kv_bytes(P + G // 2)  # mean cache length read per step
+    bytes_tok = wb + kvb
+    peak, peak_kind = measured_peak()
+    achieved = bytes_tok / (ms_tok * 1e-3) / 1e9
+    res = {
+        "metric": "7B-shape Q4_K decode tokens/s (1 sequence, greedy)", "value": round(1e3 / ms_tok, 2),
+        "unit": "tokens/s", "ms_per_token": round(ms_tok, 4), "higher_is_better": True,
+        "config": {"workload": f"Llama-2-7B-shape decode, {P} prompt tokens in the fp16 KV cache, then {G} greedy "
+                               "steps", "layers": cfg.layers, "hidden": cfg.hidden, "heads": cfg.heads,
+                   "head_dim": cfg.head_dim, "ffn": cfg.ffn, "vocab": cfg.vocab,
+                   "weights": "Q4_K attention + gate/up, Q6_K down + output, seeded N(0, 0.02)",
+                   "l2": "inputs larger than L2: each step streams 4.1 GB of weights"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "bytes_per_token": bytes_tok,
+                     "weight_bytes": wb, "kv_bytes_mean": kvb, "peak_kind": peak_kind},
+        "e2e": {"value": round(G / el, 2), "unit": "tokens/s", "h2d_bytes_per_step": round(16 / G, 4),
+                "d2h_bytes_per_step": 4,
+                "call": "DecodeModel.generate from the prompt's end (16-byte state written once, graph replays, "
+                        "the tokens read back at the end)"},
+        "gpu_launches_per_token": dm.launches_per_step(),
+        "prefill_s": round(t_prefill, 2), "build_s": round(t_build, 2),
+        "first_tokens": toks[:8], "clocks": clk.summary(),
+        "cpu_baseline": None,
+    }
+    if not args.no_cpu:
+        nth = os.cpu_count() or 1
+        t_cpu, sample = cpu_decode_sample(nth)
+        res["cpu_baseline"] = {"value": round(1.0 / t_cpu, 4), "unit": "tokens/s", "cores": nth, "kind": "port",
+                               "sample": sample}
+    del dm, mw
+    torch.cuda.synchronize()
+    return res
+
+
+def cpu_decode_sample(nthreads: int, reps: int = 3):
+    """Host-core time of one 7B-shape decode token's matrix products: the
+    oracle restatement of the reference loop (the reference's CPUBackend
+    throws on K-quants) on one layer's four products (Q4_K QKV 12288x4096,
+    O 4096x4096, gate|up 22016x4096; Q6_K down 4096x11008) times 32 layers,
+    plus the Q6_K 32000x4096 output product.  Attention, norms and the
+    elementwise ops are left out, so this overstates the CPU's speed.
+    Returns (seconds per token, sample description)."""
+    import oracle as O
+
+    shapes = [(O.Q4_K, 12288, 4096), (O.Q4_K, 4096, 4096), (O.Q4_K, 22016, 4096), (O.Q6_K, 4096, 11008)]
+    out = (O.Q6_K, 32000, 4096)
+
+    def best_time(dt, N, K):
+        b = O.quantize(dt, O.seeded_weights(N, K, seed=0))
+        x = O.seeded_acts(1, K, seed=1)
+        O.matmul_ref(dt, x, b, N, nthreads)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            O.matmul_ref(dt, x, b, N, nthreads)
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    layer = sum(best_time(*sh) for sh in shapes)
+    t = 32 * layer + best_time(*out)
+    return t, (f"one layer's 4 products + the output product, best of {reps}, scaled to 32 layers; "
+               f"{nthreads} threads; oracle restatement of the reference loop; matrix products only")
 
 
 def traffic_per_launch():
@@ -498,6 +645,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="leave out the 7B-shape decode tokens/s")
     ap.add_argument("--profile", action="store_true", help="small case for ncu: 3 products, no timing")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="N > 1: gather the row shards from the GEMV epilogue (fused) or with ncclAllGather")

@@ -258,7 +258,11 @@ int odi_cuda_rope_kv(float* d_q, float* d_k, const float* d_v, void* d_kcache, v
  * fp32 scores and softmax), out [heads][head_dim] (Backend::attention,
  * cpu_backend.cpp:541-608, with the causal limit taken at the query's
  * absolute position).  Grouped-query heads share kv head h / (heads /
- * kv_heads).  Needs odi_cuda_attention_scratch_bytes of device scratch. */
+ * kv_heads).  One launch: the last CTA of each head folds the chunks.
+ * Needs odi_cuda_attention_scratch_bytes of 16-byte aligned device scratch,
+ * zero-filled before its first use; each call leaves its per-head arrival
+ * counters zero again, so one scratch serves every layer and step (calls on
+ * one stream only). */
 size_t odi_cuda_attention_scratch_bytes(int heads, int head_dim, int ctx);
 int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void* d_vcache, float* d_out,
                               const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,

@@ -402,7 +402,7 @@ int odi_cuda_rope_kv(float* d_q, float* d_k, const float* d_v, void* d_kcache, v
 
 size_t odi_cuda_attention_scratch_bytes(int heads, int head_dim, int ctx) {
   if (heads < 1 || head_dim < 1 || ctx < 1) return 0;
-  return (size_t)heads * attention_chunks(ctx) * (head_dim + 2) * sizeof(float);
+  return attention_scratch(heads, head_dim, ctx);
 }
 
 int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void* d_vcache, float* d_out,
@@ -415,7 +415,9 @@ int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void
                 head_dim);
   if (scratch_bytes < odi_cuda_attention_scratch_bytes(heads, head_dim, ctx))
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: scratch too small");
-  CK(launch_attention(d_q, (const __half*)d_kcache, (const __half*)d_vcache, d_out, (float*)d_scratch,
+  if (reinterpret_cast<uintptr_t>(d_scratch) & 15)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: scratch not 16-byte aligned");
+  CK(launch_attention(d_q, (const __half*)d_kcache, (const __half*)d_vcache, d_out, d_scratch,
                       reinterpret_cast<const DecodeState*>(d_state), heads, kv_heads, head_dim, ctx, scale,
                       (cudaStream_t)stream),
      "attention launch");

@@ -36,6 +36,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void embed_kernel(const float* __restrict__ table, const DecodeState* st, float* __restrict__ x,
                              float* __restrict__ ssq, int64_t E, int64_t vocab) {
   __shared__ float red[2];
+  pdl_launch_dependents();
+  pdl_wait();
   int tok = st->token;
   if (tok < 0 || tok >= vocab) tok = 0;  // out-of-range ids are rejected on the host; never read outside
   const int64_t i = blockIdx.x * 64ll + threadIdx.x;
@@ -53,6 +55,8 @@ __global__ void embed_kernel(const float* __restrict__ table, const DecodeState*
 __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
                                 int64_t n, float eps) {
   __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const float* xr = x + blockIdx.x * n;
   float* yr = y + blockIdx.x * n;
   float s = 0.f;
@@ -74,6 +78,8 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
 __global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v,
                                __half* __restrict__ kc, __half* __restrict__ vc, const DecodeState* st, int heads,
                                int kv_heads, int hd, int ctx, float theta) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int pos = st->pos;
   if (pos < 0 || pos >= ctx) return;  // the host keeps pos < ctx; never write outside the cache
   const int i = threadIdx.x, half = hd >> 1;
@@ -104,22 +110,28 @@ __global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, con
   }
 }
 
-// Flash decoding, pass 1: CTA (h, c) covers positions [c*ATT_CHUNK, +ATT_CHUNK)
-// of kv_len = pos + 1; its 8 warps take PW = ATT_CHUNK/8 positions each.
-// Lane l holds dims [l*HD/32, +HD/32) of q and of its running output.  A
-// warp first loads all PW positions' k and v (coalesced: each position is
-// HD contiguous halves), so the loads are in flight together, then reduces
-// the PW dots across lanes and folds them into an online softmax (running
-// max m, sum l, output acc).  The CTA folds its warps and writes
-// (m, l, acc[HD]) for the chunk.
+// Flash decoding in one launch.  CTA (h, c) covers positions
+// [c*ATT_CHUNK, +ATT_CHUNK) of kv_len = pos + 1; its 8 warps take
+// PW = ATT_CHUNK/8 positions each.  Lane l holds dims [l*HD/32, +HD/32) of q
+// and of its running output.  A warp first loads all PW positions' k and v
+// (coalesced: each position is HD contiguous halves), so the loads are in
+// flight together, then reduces the PW dots across lanes and folds them into
+// an online softmax (running max m, sum l, output acc).  The CTA folds its
+// warps and writes (m, l, acc[HD]) for the chunk.  The last CTA of head h
+// to finish (arrival counter cnt[h]) folds the chunks in chunk order and
+// writes the head's output, then zeroes cnt[h] for the next launch.
 template <int HD>
-__global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
-                                                           const __half* __restrict__ vc, float* __restrict__ part,
-                                                           const DecodeState* st, int heads, int kv_heads, int ctx,
-                                                           int nch, float scale) {
+__global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
+                                                   const __half* __restrict__ vc, float* __restrict__ o,
+                                                   float* __restrict__ part, int* __restrict__ cnt,
+                                                   const DecodeState* st, int heads, int kv_heads, int ctx,
+                                                   int nch, float scale) {
   constexpr int DPL = HD / 32;         // dims per lane
   constexpr int PW = ATT_CHUNK / 8;    // positions per warp
   __shared__ float sm[8], sl[8], sacc[8][HD];
+  __shared__ int is_last;
+  pdl_launch_dependents();
+  pdl_wait();  // q and the cache are written by the kernels before
   const int h = blockIdx.x, c = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv_len = min(st->pos + 1, ctx);
@@ -204,30 +216,34 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     out[0] = M;
     out[1] = L;
   }
-}
-
-// Pass 2: one CTA per head folds the chunks of kv_len.
-template <int HD>
-__global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ o, const DecodeState* st,
-                                    int ctx, int nch) {
-  const int h = blockIdx.x, d = threadIdx.x;
-  const int kv_len = min(st->pos + 1, ctx);
+  // every writer's partial is visible device-wide before the arrival
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(&cnt[h], 1) == nch - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
   const int nc = (kv_len + ATT_CHUNK - 1) / ATT_CHUNK;
   const float* p = part + (int64_t)h * nch * (HD + 2);
-  float M = -INFINITY;
-  for (int c = 0; c < nc; ++c) M = fmaxf(M, p[c * (HD + 2)]);
-  float L = 0.f, a = 0.f;
-  for (int c = 0; c < nc; ++c) {
-    const float mc = p[c * (HD + 2)];
-    if (mc == -INFINITY) continue;
-    const float f = expf(mc - M);
-    L += p[c * (HD + 2) + 1] * f;
-    a += p[c * (HD + 2) + 2 + d] * f;
+  float Mx = -INFINITY;
+  for (int cc = 0; cc < nc; ++cc) Mx = fmaxf(Mx, __ldcg(p + cc * (HD + 2)));
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float L = 0.f, a = 0.f;
+    for (int cc = 0; cc < nc; ++cc) {
+      const float mc = __ldcg(p + cc * (HD + 2));
+      if (mc == -INFINITY) continue;
+      const float f = expf(mc - Mx);
+      L += __ldcg(p + cc * (HD + 2) + 1) * f;
+      a += __ldcg(p + cc * (HD + 2) + 2 + d) * f;
+    }
+    o[(int64_t)h * HD + d] = a / L;
   }
-  if (d < HD) o[(int64_t)h * HD + d] = a / L;
+  if (threadIdx.x == 0) cnt[h] = 0;
 }
 
 __global__ void silu_mul_kernel(const float* __restrict__ gu, float* __restrict__ a, int64_t F) {
+  pdl_launch_dependents();
+  pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < F; i += (int64_t)gridDim.x * blockDim.x) {
     const float g = gu[i];
     a[i] = g / (1.0f + expf(-g)) * gu[F + i];
@@ -235,6 +251,8 @@ __global__ void silu_mul_kernel(const float* __restrict__ gu, float* __restrict_
 }
 
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ d, int64_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     x[i] += d[i];
 }
@@ -245,6 +263,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
                                                       int* __restrict__ record, int record_len) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_launch_dependents();
+  pdl_wait();
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
@@ -296,6 +316,25 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
 
 namespace odi_cuda {
 
+// Every kernel here triggers its dependents on entry and waits for the
+// kernels before it (griddepcontrol) before touching global memory, so all
+// are launched with programmatic stream serialisation: the next kernel (a
+// GEMV streaming its weights) may start while this one runs.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 static int grid_for(int64_t n, int threads) {
   int64_t b = (n + threads - 1) / threads;
   if (b > 148 * 8) b = 148 * 8;
@@ -304,54 +343,53 @@ static int grid_for(int64_t n, int threads) {
 
 cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x, float* ssq,
                          cudaStream_t s) {
-  embed_kernel<<<(unsigned)((E + 63) / 64), 64, 0, s>>>(table, st, x, ssq, E, vocab);
-  return cudaGetLastError();
+  return launch_pdl(embed_kernel, dim3((unsigned)((E + 63) / 64)), dim3(64), s, table, st, x, ssq, E, vocab);
 }
 
 cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,
                             cudaStream_t s) {
-  rms_norm_kernel<<<(unsigned)rows, 512, 0, s>>>(x, w, y, n, eps);
-  return cudaGetLastError();
+  return launch_pdl(rms_norm_kernel, dim3((unsigned)rows), dim3(512), s, x, w, y, n, eps);
 }
 
 cudaError_t launch_rope_kv(float* q, float* k, const float* v, __half* kc, __half* vc, const DecodeState* st,
                            int heads, int kv_heads, int hd, int ctx, float theta, cudaStream_t s) {
-  rope_kv_kernel<<<heads + kv_heads, hd / 2, 0, s>>>(q, k, v, kc, vc, st, heads, kv_heads, hd, ctx, theta);
-  return cudaGetLastError();
+  return launch_pdl(rope_kv_kernel, dim3(heads + kv_heads), dim3(hd / 2), s, q, k, v, kc, vc, st, heads, kv_heads,
+                    hd, ctx, theta);
 }
 
 int attention_chunks(int ctx) { return (ctx + ATT_CHUNK - 1) / ATT_CHUNK; }
 
-cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, float* o, float* part,
+size_t attention_scratch(int heads, int hd, int ctx) {
+  return att_part_offset(heads) + (size_t)heads * attention_chunks(ctx) * (hd + 2) * sizeof(float);
+}
+
+cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, float* o, void* scratch,
                              const DecodeState* st, int heads, int kv_heads, int hd, int ctx, float scale,
                              cudaStream_t s) {
   const int nch = attention_chunks(ctx);
-  if (hd == 128) {
-    attn_partial_kernel<128><<<dim3(heads, nch), 256, 0, s>>>(q, kc, vc, part, st, heads, kv_heads, ctx, nch, scale);
-    attn_combine_kernel<128><<<heads, 128, 0, s>>>(part, o, st, ctx, nch);
-  } else if (hd == 64) {
-    attn_partial_kernel<64><<<dim3(heads, nch), 256, 0, s>>>(q, kc, vc, part, st, heads, kv_heads, ctx, nch, scale);
-    attn_combine_kernel<64><<<heads, 64, 0, s>>>(part, o, st, ctx, nch);
-  } else {
-    return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  int* cnt = static_cast<int*>(scratch);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + att_part_offset(heads));
+  const dim3 grid(heads, nch);
+  if (hd == 128)
+    return launch_pdl(attn_kernel<128>, grid, dim3(256), s, q, kc, vc, o, part, cnt, st, heads, kv_heads, ctx, nch,
+                      scale);
+  if (hd == 64)
+    return launch_pdl(attn_kernel<64>, grid, dim3(256), s, q, kc, vc, o, part, cnt, st, heads, kv_heads, ctx, nch,
+                      scale);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_silu_mul(const float* gu, float* a, int64_t F, cudaStream_t s) {
-  silu_mul_kernel<<<grid_for(F, 256), 256, 0, s>>>(gu, a, F);
-  return cudaGetLastError();
+  return launch_pdl(silu_mul_kernel, dim3(grid_for(F, 256)), dim3(256), s, gu, a, F);
 }
 
 cudaError_t launch_add(float* x, const float* d, int64_t n, cudaStream_t s) {
-  add_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, d, n);
-  return cudaGetLastError();
+  return launch_pdl(add_kernel, dim3(grid_for(n, 256)), dim3(256), s, x, d, n);
 }
 
 cudaError_t launch_argmax(const float* logits, int64_t V, DecodeState* st, int* record, int record_len,
                           cudaStream_t s) {
-  argmax_kernel<<<1, 1024, 0, s>>>(logits, V, st, record, record_len);
-  return cudaGetLastError();
+  return launch_pdl(argmax_kernel, dim3(1), dim3(1024), s, logits, V, st, record, record_len);
 }
 
 }  // namespace odi_cuda

@@ -24,7 +24,7 @@ struct GemvPlan {
   int chunk;         // spans per CTA
   int stages;        // weight ring depth
   int stage_bytes;   // one unit, 128-aligned
-  int xq_bytes;      // per-warp staged activations: chunk * mt * (80 | 256)
+  int xq_bytes;      // staged activations: chunk * mt records, 128-aligned
   int smem_bytes;    // dynamic shared memory per CTA
   int mt;            // tokens per pass (template instantiation)
 };
@@ -94,13 +94,17 @@ struct DecodeState {
 };
 constexpr int ATT_CHUNK = 64;  // positions per CTA in the attention's first pass (8 per warp)
 int attention_chunks(int ctx);
+// attention scratch: per-head arrival counters (zero between launches), then
+// the per-chunk partials [heads][chunks][hd + 2] fp32
+inline size_t att_part_offset(int heads) { return ((size_t)heads * sizeof(int) + 255) / 256 * 256; }
+size_t attention_scratch(int heads, int hd, int ctx);
 cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x, float* ssq,
                          cudaStream_t s);
 cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,
                             cudaStream_t s);
 cudaError_t launch_rope_kv(float* q, float* k, const float* v, __half* kc, __half* vc, const DecodeState* st,
                            int heads, int kv_heads, int hd, int ctx, float theta, cudaStream_t s);
-cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, float* o, float* part,
+cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, float* o, void* scratch,
                              const DecodeState* st, int heads, int kv_heads, int hd, int ctx, float scale,
                              cudaStream_t s);
 cudaError_t launch_silu_mul(const float* gu, float* a, int64_t F, cudaStream_t s);

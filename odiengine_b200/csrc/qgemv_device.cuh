@@ -150,10 +150,10 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_by
 //    x * (1/d)), d kept as fp16): codes at [32*b, 32*b+32), XRec b at
 //    256 + 16*b.  ACT_F32: the sums of each 16 values go after the values.
 // Fused prologues (GemvFuse), applied to the staged fp32 values before the
-// quantisation: SwiGLU builds silu(gate) * up with plain loads; RMSNorm
-// first reduces sum(x^2) over the whole row of every token of the pass
-// (the CTA reads the row once; the weights stream meanwhile) and then
-// scales the staged chunk by rms * norm_w.
+// quantisation: SwiGLU builds silu(gate) * up from the staged gate and up
+// halves; RMSNorm reduces sum(x^2) of every token of the pass -- from the
+// sums of squares x's writer left in slots, else over the whole row -- while
+// the copies are in flight, then scales the staged chunk by rms * norm_w.
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 template <int MT>
@@ -180,65 +180,92 @@ __device__ __forceinline__ void row_rms(const GemvArgs& a, float* rms_out /* sme
   consumer_sync();
 }
 
+// Four fp32 values (nvalid of them real, the rest zero-filled) by cp.async.
+__device__ __forceinline__ void copy4(uint8_t* dst, const float* src, int nvalid, bool vec) {
+  if (vec) {
+    cp_async16(dst, src, 4 * nvalid);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) cp_async4(dst + 4 * e, src + (e < nvalid ? e : 0), e < nvalid ? 4 : 0);
+  }
+}
+
+// The prologue's second input for the 8 values [k, k+8) a lane quantises:
+// the up half of record r's token (SwiGLU) or the norm weights (RMSNorm),
+// read from L2 (ld.global.cg), zero past K.
+__device__ __forceinline__ void prologue8(const GemvArgs& a, int kb0, int r, int off, float4& e0, float4& e1) {
+  const int j = r / a.M, m = r - j * a.M;
+  const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + off;
+  const float* p = a.fu.swiglu ? a.x + (int64_t)m * a.ldx + a.K : a.fu.norm_w;
+  if (k + 8 <= a.K && (reinterpret_cast<uintptr_t>(p + k) & 15) == 0) {
+    e0 = __ldcg(reinterpret_cast<const float4*>(p + k));
+    e1 = __ldcg(reinterpret_cast<const float4*>(p + k + 4));
+  } else {
+    float t[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t[e] = k + e < a.K ? __ldcg(p + k + e) : 0.f;
+    e0 = make_float4(t[0], t[1], t[2], t[3]);
+    e1 = make_float4(t[4], t[5], t[6], t[7]);
+  }
+}
+
+// Staging: x (or the gate half of a SwiGLU input) of every span of the chunk
+// by cp.async in one group, so it costs one memory round trip whatever the
+// chunk length.  The RMSNorm sum of squares is reduced while the copies fly.
+// Then one warp per staged (span, token) applies the prologue -- its second
+// input read one record ahead, so its latency overlaps the previous record
+// -- and quantises.
 template <bool F32, int MT>
 __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr,
                                            float* __restrict__ fuse_smem) {
   const int tid = threadIdx.x;  // 0..127
   const int warp = tid >> 5, lane = tid & 31;
   const bool vec = (a.K & 3) == 0 && (a.ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
-  // 64 chunks per (span, token): threads 0-63 take even tokens, 64-127 odd
+  // 64 chunks of 4 values per (span, token): threads 0-63 take even tokens, 64-127 odd
   const int q = tid & 63;
-  if (a.fu.swiglu) {
-    for (int j = 0; j < nsp; ++j) {
-      const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
-      for (int m = tid >> 6; m < a.M; m += 2) {
-        const float* g = a.x + (int64_t)m * a.ldx;
-        float* dst = reinterpret_cast<float*>(xr + (j * MT + m) * XR_STRIDE + 16 * q);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) dst[e] = k + e < a.K ? silu_f(g[k + e]) * g[a.K + k + e] : 0.0f;
-      }
-    }
-  } else {
-    for (int j = 0; j < nsp; ++j) {
-      const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
-      const int64_t left = a.K - k;
-      const int nvalid = left <= 0 ? 0 : (left >= 4 ? 4 : (int)left);
-      for (int m = tid >> 6; m < a.M; m += 2) {
-        const float* src = a.x + (int64_t)m * a.ldx + (nvalid ? k : 0);
-        uint8_t* dst = xr + (j * MT + m) * XR_STRIDE + 16 * q;
-        if (vec) {
-          cp_async16(dst, src, 4 * nvalid);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) cp_async4(dst + 4 * e, src + (e < nvalid ? e : 0), e < nvalid ? 4 : 0);
-        }
-      }
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    if (a.fu.norm_w) row_rms<MT>(a, fuse_smem, fuse_smem + MT);  // overlaps the copies
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (a.fu.norm_w) {
-      // scale this thread's own staged 4-value chunks
-      for (int j = 0; j < nsp; ++j) {
-        const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
-        for (int m = tid >> 6; m < a.M; m += 2) {
-          float* v = reinterpret_cast<float*>(xr + (j * MT + m) * XR_STRIDE + 16 * q);
-          const float r = fuse_smem[m];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (k + e < a.K) v[e] = v[e] * r * a.fu.norm_w[k + e];
-        }
-      }
-    }
+  for (int j = 0; j < nsp; ++j) {
+    const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + 4 * q;
+    const int64_t left = a.K - k;
+    const int nvalid = left <= 0 ? 0 : (left >= 4 ? 4 : (int)left);
+    for (int m = tid >> 6; m < a.M; m += 2)
+      copy4(xr + (j * MT + m) * XR_STRIDE + 16 * q, a.x + (int64_t)m * a.ldx + (nvalid ? k : 0), nvalid, vec);
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (a.fu.norm_w) row_rms<MT>(a, fuse_smem, fuse_smem + MT);  // overlaps the copies
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   consumer_sync();
-  // one warp per staged (span, token); lane = (block b = lane/4, 8 values)
+  // lane = (block b = lane/4, 8 values)
   const int b = lane >> 2, part = lane & 3;
-  for (int jm = warp; jm < nsp * MT; jm += NCW) {
-    if (jm % MT >= a.M) continue;  // uniform across the warp
-    uint8_t* rec = xr + jm * XR_STRIDE;
-    const float4 v0 = lds128f(rec + 4 * (32 * b + 8 * part));
-    const float4 v1 = lds128f(rec + 4 * (32 * b + 8 * part + 4));
+  const int off = 32 * b + 8 * part;
+  const int nrec = nsp * a.M;
+  const bool pro = a.fu.swiglu || a.fu.norm_w;
+  float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0;
+  if (pro && warp < nrec) prologue8(a, kb0, warp, off, n0, n1);
+  for (int r = warp; r < nrec; r += NCW) {
+    const int j = r / a.M, m = r - j * a.M;
+    uint8_t* rec = xr + (j * MT + m) * XR_STRIDE;
+    float4 v0 = lds128f(rec + 4 * off);
+    float4 v1 = lds128f(rec + 4 * (off + 4));
+    if (pro) {
+      const float4 e0 = n0, e1 = n1;
+      if (r + NCW < nrec) prologue8(a, kb0, r + NCW, off, n0, n1);
+      float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      const float ee[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+      if (a.fu.swiglu) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vv[e] = silu_f(vv[e]) * ee[e];  // past K: silu(0) * 0
+      } else {
+        const float rr = fuse_smem[m];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vv[e] = vv[e] * rr * ee[e];
+      }
+      v0 = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      v1 = make_float4(vv[4], vv[5], vv[6], vv[7]);
+      if (F32) {  // the fp32 dot reads the staged values
+        *reinterpret_cast<float4*>(rec + 4 * off) = v0;
+        *reinterpret_cast<float4*>(rec + 4 * (off + 4)) = v1;
+      }
+    }
     if (F32) {
       float s = ((v0.x + v0.y) + (v0.z + v0.w)) + ((v1.x + v1.y) + (v1.z + v1.w));
       s += __shfl_xor_sync(0xffffffffu, s, 1);  // 16-value sums (parts 0-1, 2-3)
@@ -256,9 +283,9 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
     int s = 0;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const int q = (int)roundf(__fmul_rn(vv[e], id));
-      s += q;
-      packed[e >> 2] |= (uint32_t)(q & 0xFF) << (8 * (e & 3));
+      const int qq = (int)roundf(__fmul_rn(vv[e], id));
+      s += qq;
+      packed[e >> 2] |= (uint32_t)(qq & 0xFF) << (8 * (e & 3));
     }
     const int s_half = s + __shfl_xor_sync(0xffffffffu, s, 1);        // 16 codes: parts 0-1 or 2-3
     const int s_full = s_half + __shfl_xor_sync(0xffffffffu, s_half, 2);
@@ -267,12 +294,12 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
     *reinterpret_cast<uint2*>(rec + 32 * b + 8 * part) = make_uint2(packed[0], packed[1]);
     if (part == 0) {
       const float dx = __half2float(__float2half_rn(d));
-      XRec r;
-      r.dx = dx;
-      r.sdx = __fmul_rn((float)s_full, dx);
-      r.sdx_lo = __fmul_rn((float)s_half, dx);
-      r.sdx_hi = __fmul_rn((float)s_hi, dx);
-      *reinterpret_cast<XRec*>(rec + 256 + 16 * b) = r;
+      XRec rq;
+      rq.dx = dx;
+      rq.sdx = __fmul_rn((float)s_full, dx);
+      rq.sdx_lo = __fmul_rn((float)s_half, dx);
+      rq.sdx_hi = __fmul_rn((float)s_hi, dx);
+      *reinterpret_cast<XRec*>(rec + 256 + 16 * b) = rq;
     }
     __syncwarp();
   }
@@ -720,6 +747,13 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
 
   if (warp == NCW) {
     // ---------------- producer: weights only, no dependency on earlier kernels
+    if (lane != 0 && a.fu.norm_w) {
+      // the RMSNorm weights are constant too: into L2 for the prologue
+      const int64_t k0 = (int64_t)kb0 * UNIT_COLS;
+      const int64_t kn = min((int64_t)a.K, k0 + (int64_t)nsp * UNIT_COLS);
+      for (int64_t k = k0 + 32 * (lane - 1); k < kn; k += 32 * 31)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.fu.norm_w + k));
+    }
     if (lane == 0) {
       pdl_launch_dependents();
       const int first = nsp < S ? nsp : S;

@@ -200,8 +200,8 @@ class DecodeModel:
             self._step_unfused()
 
     def _step_fused(self) -> None:
-        """7 launches per layer: QKV GEMV (RMSNorm fused), rope + KV append,
-        attention (2), O GEMV (+= x), gate|up GEMV (RMSNorm fused), down GEMV
+        """6 launches per layer: QKV GEMV (RMSNorm fused), rope + KV append,
+        attention, O GEMV (+= x), gate|up GEMV (RMSNorm fused), down GEMV
         (SwiGLU fused, += x)."""
         cfg, L, s = self.cfg, lib(), self.stream.cuda_stream
         H, KV, hd = cfg.heads, cfg.kv_heads, cfg.head_dim
@@ -252,8 +252,8 @@ class DecodeModel:
 
     def launches_per_step(self) -> int:
         if self.fused:
-            return 1 + 7 * self.cfg.layers + 2  # embed, per layer, output GEMV + argmax
-        return 1 + 11 * self.cfg.layers + 3  # embed, per layer, final norm + output GEMV + argmax
+            return 1 + 6 * self.cfg.layers + 2  # embed, per layer, output GEMV + argmax
+        return 1 + 10 * self.cfg.layers + 3  # embed, per layer, final norm + output GEMV + argmax
 
     def capture(self) -> None:
         """Record one step as a CUDA graph (after one eager step has run)."""

@@ -126,6 +126,24 @@ def test_attention_decode(cuda_lib, hd, H, KV, pos):
         p = np.exp(s - s.max())
         ref[h] = (p / p.sum()) @ vc[kh, : pos + 1].astype(np.float64)
     assert (np.abs(out.cpu().numpy() - ref) <= 1e-4 * np.abs(vc).max()).all()
+    # the per-head arrival counters are left zero: the same scratch serves
+    # the next calls, here at every earlier position of a short sweep
+    first = out.cpu().numpy().copy()
+    for p2 in sorted({0, pos // 3, pos}):
+        st2 = _state(0, p2)
+        cuda_lib.check(L.odi_cuda_attention_decode(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(),
+                                                   st2.data_ptr(), H, KV, hd, ctx, scale, scratch.data_ptr(), sb,
+                                                   None))
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for h in range(H):
+            kh = h // (H // KV)
+            s = kc[kh, : p2 + 1].astype(np.float64) @ q[h].astype(np.float64) * scale
+            p = np.exp(s - s.max())
+            r = (p / p.sum()) @ vc[kh, : p2 + 1].astype(np.float64)
+            assert (np.abs(got[h] - r) <= 1e-4 * np.abs(vc).max()).all(), (p2, h)
+    assert np.array_equal(got, first)  # the sweep ends at pos: same result as the first call
+    assert not scratch[: H].any()  # counters (the first H ints) are zero again
 
 
 def test_silu_mul(cuda_lib):
