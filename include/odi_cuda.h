@@ -258,15 +258,30 @@ int odi_cuda_rope_kv(float* d_q, float* d_k, const float* d_v, void* d_kcache, v
  * fp32 scores and softmax), out [heads][head_dim] (Backend::attention,
  * cpu_backend.cpp:541-608, with the causal limit taken at the query's
  * absolute position).  Grouped-query heads share kv head h / (heads /
- * kv_heads).  One launch: the last CTA of each head folds the chunks.
- * Needs odi_cuda_attention_scratch_bytes of 16-byte aligned device scratch,
- * zero-filled before its first use; each call leaves its per-head arrival
- * counters zero again, so one scratch serves every layer and step (calls on
- * one stream only). */
+ * kv_heads); 1, 2, 4 or 8 query heads per kv head.  One launch: K and V
+ * are streamed by bulk copies, split over about two CTAs per SM, and the
+ * last CTA of each kv head folds the splits.  The caches must be 16-byte
+ * aligned.  Needs odi_cuda_attention_scratch_bytes of 16-byte aligned
+ * device scratch, zero-filled before its first use; each call leaves its
+ * arrival counters zero again, so one scratch serves every layer and step
+ * (calls on one stream only).  The scratch's first int is an error word
+ * (odi_cuda_workspace_status reads it): non-zero if a bounded wait of the
+ * kernel gave up. */
 size_t odi_cuda_attention_scratch_bytes(int heads, int head_dim, int ctx);
 int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void* d_vcache, float* d_out,
                               const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,
                               float scale, void* d_scratch, size_t scratch_bytes, void* stream);
+
+/* odi_cuda_rope_kv followed by odi_cuda_attention_decode, in one launch:
+ * q [heads][head_dim], k and v [kv_heads][head_dim] are this step's raw
+ * projections (q is rotated in registers and left unchanged in memory);
+ * the rotated k and v are written as fp16 into the caches at the state's
+ * pos (nothing is written when pos >= ctx).  Same results as the two calls;
+ * same scratch and alignment rules as odi_cuda_attention_decode. */
+int odi_cuda_rope_attention(const float* d_q, const float* d_k, const float* d_v, void* d_kcache, void* d_vcache,
+                            float* d_out, const odi_cuda_decode_state* d_state, int heads, int kv_heads,
+                            int head_dim, int ctx, float theta, float scale, void* d_scratch, size_t scratch_bytes,
+                            void* stream);
 
 /* out[F] = silu(gate) * up with gate_up = [gate F | up F] (context.cpp:272-275). */
 int odi_cuda_silu_mul(const float* d_gate_up, float* d_out, int64_t F, void* stream);

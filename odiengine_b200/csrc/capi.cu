@@ -405,23 +405,57 @@ size_t odi_cuda_attention_scratch_bytes(int heads, int head_dim, int ctx) {
   return attention_scratch(heads, head_dim, ctx);
 }
 
-int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void* d_vcache, float* d_out,
-                              const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,
-                              float scale, void* d_scratch, size_t scratch_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+int attention_common(const float* d_q, const void* d_kcache, const void* d_vcache, float* d_out,
+                     const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,
+                     float scale, void* d_scratch, size_t scratch_bytes, const AttRope& rp, void* stream) {
   if (!d_q || !d_kcache || !d_vcache || !d_out || !d_state || !d_scratch)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: null argument");
   if (heads < 1 || kv_heads < 1 || heads % kv_heads || (head_dim != 64 && head_dim != 128) || ctx < 1)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: heads %d / kv_heads %d / head_dim %d", heads, kv_heads,
                 head_dim);
+  {
+    const int grp = heads / kv_heads;
+    if (grp != 1 && grp != 2 && grp != 4 && grp != 8)
+      return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "attention: %d query heads per kv head (1, 2, 4 or 8 supported)",
+                  grp);
+  }
+  if (reinterpret_cast<uintptr_t>(d_kcache) & 15 || reinterpret_cast<uintptr_t>(d_vcache) & 15)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: caches must be 16-byte aligned");
   if (scratch_bytes < odi_cuda_attention_scratch_bytes(heads, head_dim, ctx))
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: scratch too small");
   if (reinterpret_cast<uintptr_t>(d_scratch) & 15)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "attention: scratch not 16-byte aligned");
   CK(launch_attention(d_q, (const __half*)d_kcache, (const __half*)d_vcache, d_out, d_scratch,
-                      reinterpret_cast<const DecodeState*>(d_state), heads, kv_heads, head_dim, ctx, scale,
+                      reinterpret_cast<const DecodeState*>(d_state), heads, kv_heads, head_dim, ctx, scale, rp,
                       (cudaStream_t)stream),
      "attention launch");
   return ODI_CUDA_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void* d_vcache, float* d_out,
+                              const odi_cuda_decode_state* d_state, int heads, int kv_heads, int head_dim, int ctx,
+                              float scale, void* d_scratch, size_t scratch_bytes, void* stream) {
+  return attention_common(d_q, d_kcache, d_vcache, d_out, d_state, heads, kv_heads, head_dim, ctx, scale, d_scratch,
+                          scratch_bytes, AttRope{}, stream);
+}
+
+int odi_cuda_rope_attention(const float* d_q, const float* d_k, const float* d_v, void* d_kcache, void* d_vcache,
+                            float* d_out, const odi_cuda_decode_state* d_state, int heads, int kv_heads,
+                            int head_dim, int ctx, float theta, float scale, void* d_scratch, size_t scratch_bytes,
+                            void* stream) {
+  if (!d_k || !d_v) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "rope_attention: null k or v");
+  AttRope rp;
+  rp.k = d_k;
+  rp.v = d_v;
+  rp.theta = theta;
+  return attention_common(d_q, d_kcache, d_vcache, d_out, d_state, heads, kv_heads, head_dim, ctx, scale, d_scratch,
+                          scratch_bytes, rp, stream);
 }
 
 int odi_cuda_silu_mul(const float* d_gate_up, float* d_out, int64_t F, void* stream) {

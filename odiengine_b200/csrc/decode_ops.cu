@@ -110,135 +110,289 @@ __global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, con
   }
 }
 
-// Flash decoding in one launch.  CTA (h, c) covers positions
-// [c*ATT_CHUNK, +ATT_CHUNK) of kv_len = pos + 1; its 8 warps take
-// PW = ATT_CHUNK/8 positions each.  Lane l holds dims [l*HD/32, +HD/32) of q
-// and of its running output.  A warp first loads all PW positions' k and v
-// (coalesced: each position is HD contiguous halves), so the loads are in
-// flight together, then reduces the PW dots across lanes and folds them into
-// an online softmax (running max m, sum l, output acc).  The CTA folds its
-// warps and writes (m, l, acc[HD]) for the chunk.  The last CTA of head h
-// to finish (arrival counter cnt[h]) folds the chunks in chunk order and
-// writes the head's output, then zeroes cnt[h] for the next launch.
-template <int HD>
-__global__ void __launch_bounds__(256) attn_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
-                                                   const __half* __restrict__ vc, float* __restrict__ o,
-                                                   float* __restrict__ part, int* __restrict__ cnt,
-                                                   const DecodeState* st, int heads, int kv_heads, int ctx,
-                                                   int nch, float scale) {
-  constexpr int DPL = HD / 32;         // dims per lane
-  constexpr int PW = ATT_CHUNK / 8;    // positions per warp
-  __shared__ float sm[8], sl[8], sacc[8][HD];
+// Flash decoding in one launch, streamed by the bulk-copy engine.
+// CTA (kvh, split) serves the G = heads / kv_heads query heads of kv head
+// kvh over the 64-position chunks c = split, split + nsplit, ... of
+// kv_len = pos + 1.  Thread 0 streams each chunk's K and V tiles (64 x HD
+// fp16 each, contiguous in the [kv_head][ctx][HD] cache) into a two-stage
+// shared-memory ring with cp.async.bulk (no multicast), completing on an
+// mbarrier; the four warps take 16 positions each.  Scores: lane l holds
+// dims [l*HD/32, +HD/32) of q; the 16 partial dots are summed across lanes
+// by a halving butterfly (16 shuffles), after which lanes 2t and 2t+1 hold
+// position t's score.  Online softmax per warp and head (running max m,
+// sum l, output acc), then the CTA folds its warps and writes (m, l,
+// acc[HD]) per head for its split.  The last CTA of kv head kvh to finish
+// (arrival counter) folds the splits in split order, writes the heads'
+// outputs and zeroes its counter for the next launch.
+// With rope (the rope_kv step fused in): q, k and v are this step's raw
+// projections; every CTA rotates q in registers (the arithmetic of
+// rope_kv_kernel), and the CTA whose chunk holds pos writes the rotated k and
+// v as fp16 into its shared K / V tiles (after the chunk landed) and into the
+// caches, for the steps after.
+// Every mbarrier wait is bounded: a wait that gives up sets the error word,
+// the CTA stops consuming (the decision is made uniform by a CTA-wide vote),
+// drains its copies in flight and still arrives, so counters stay balanced.
+constexpr int ATT_STAGES = 2;
+constexpr int ATT_THREADS = 128;
+
+template <int HD, int G>
+constexpr int att_smem_bytes() {
+  return ATT_STAGES * 2 * ATT_CHUNK * HD * 2 + 4 * G * (HD + 2) * 4 + ATT_STAGES * 8;
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restrict__ q,
+                                                           const __half* __restrict__ kc,
+                                                           const __half* __restrict__ vc, float* __restrict__ o,
+                                                           float* __restrict__ part, int* __restrict__ cnt,
+                                                           int* __restrict__ err, const DecodeState* st, int ctx,
+                                                           int nsplit, float scale, const float* __restrict__ kraw,
+                                                           const float* __restrict__ vraw, float theta, int rope,
+                                                           __half* __restrict__ kcw, __half* __restrict__ vcw) {
+  constexpr int DPL = HD / 32;           // dims per lane
+  constexpr int TILE = ATT_CHUNK * HD;   // halves per K (or V) tile
+  constexpr int PW = ATT_CHUNK / 4;      // positions per warp per chunk (16)
+  extern __shared__ __align__(128) uint8_t att_smem[];
+  __half* tiles = reinterpret_cast<__half*>(att_smem);  // [stage][K | V][TILE]
+  float* fold = reinterpret_cast<float*>(att_smem + ATT_STAGES * 2 * TILE * 2);  // [4][G][HD + 2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(fold + 4 * G * (HD + 2));
   __shared__ int is_last;
   pdl_launch_dependents();
   pdl_wait();  // q and the cache are written by the kernels before
-  const int h = blockIdx.x, c = blockIdx.y;
+  const int kvh = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv_len = min(st->pos + 1, ctx);
-  const int kvh = h / (heads / kv_heads);
+  const int nc = kv_len > 0 ? (kv_len + ATT_CHUNK - 1) / ATT_CHUNK : 0;
+  const int nmine = split < nc ? (nc - 1 - split) / nsplit + 1 : 0;
   const __half* kb = kc + (int64_t)kvh * ctx * HD;
   const __half* vb = vc + (int64_t)kvh * ctx * HD;
-  float qr[DPL];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) qr[e] = q[(int64_t)h * HD + lane * DPL + e] * scale;
-  float m = -INFINITY, l = 0.f, acc[DPL];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) acc[e] = 0.f;
-  const int j0 = c * ATT_CHUNK + warp * PW;
-  const int nj = max(0, min(kv_len - j0, PW));
-  __half2 kr[PW][DPL / 2], vr[PW][DPL / 2];
-#pragma unroll
-  for (int t = 0; t < PW; ++t) {
-    if (t < nj) {
-      const __half2* kp = reinterpret_cast<const __half2*>(kb + (int64_t)(j0 + t) * HD + lane * DPL);
-      const __half2* vp = reinterpret_cast<const __half2*>(vb + (int64_t)(j0 + t) * HD + lane * DPL);
-#pragma unroll
-      for (int e = 0; e < DPL / 2; ++e) {
-        kr[t][e] = kp[e];
-        vr[t][e] = vp[e];
-      }
-    }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ATT_STAGES; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
   }
-  float sc[PW];
-#pragma unroll
-  for (int t = 0; t < PW; ++t) {
-    float d = 0.f;
-#pragma unroll
-    for (int e = 0; e < DPL / 2; ++e) {
-      const float2 kk = __half22float2(kr[t][e]);
-      d = fmaf(qr[2 * e], kk.x, d);
-      d = fmaf(qr[2 * e + 1], kk.y, d);
-    }
-    sc[t] = d;
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-#pragma unroll
-    for (int t = 0; t < PW; ++t) sc[t] += __shfl_xor_sync(0xffffffffu, sc[t], o);
-  }
-#pragma unroll
-  for (int t = 0; t < PW; ++t) {
-    if (t < nj) {
-      const float s = sc[t];
-      const float mn = fmaxf(m, s);
-      const float corr = expf(m - mn), p = expf(s - mn);
-      l = l * corr + p;
-#pragma unroll
-      for (int e = 0; e < DPL / 2; ++e) {
-        const float2 vv = __half22float2(vr[t][e]);
-        acc[2 * e] = fmaf(p, vv.x, acc[2 * e] * corr);
-        acc[2 * e + 1] = fmaf(p, vv.y, acc[2 * e + 1] * corr);
-      }
-      m = mn;
-    }
-  }
-  if (lane == 0) {
-    sm[warp] = m;
-    sl[warp] = l;
-  }
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) sacc[warp][lane * DPL + e] = acc[e];
   __syncthreads();
-  float M = -INFINITY;
+  int issued = 0;
+  auto issue = [&](int i) {  // thread 0: chunk i of this CTA into stage i % ATT_STAGES
+    const int p0 = (split + i * nsplit) * ATT_CHUNK;
+    const int n = min(ATT_CHUNK, kv_len - p0);
+    const uint32_t bytes = (uint32_t)n * HD * 2;
+    const int s = i % ATT_STAGES;
+    mbar_arrive_expect_tx(&full[s], 2 * bytes);
+    bulk_g2s(tiles + (2 * s) * TILE, kb + (int64_t)p0 * HD, bytes, &full[s]);
+    bulk_g2s(tiles + (2 * s + 1) * TILE, vb + (int64_t)p0 * HD, bytes, &full[s]);
+  };
+  if (threadIdx.x == 0)
+    for (; issued < nmine && issued < ATT_STAGES; ++issued) issue(issued);
+
+  constexpr int HALF = HD / 2;
+  const int pos = st->pos;
+  const bool rot = rope && pos >= 0 && pos < ctx;
+  // rotary angles of this lane's dims (pair index d mod HD/2), as rope_kv_kernel
+  float rsn[DPL], rcs[DPL];
 #pragma unroll
-  for (int w = 0; w < 8; ++w) M = fmaxf(M, sm[w]);
-  float* out = part + ((int64_t)h * nch + c) * (HD + 2);
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    float a = 0.f;
-    for (int w = 0; w < 8; ++w)
-      if (sm[w] != -INFINITY) a += sacc[w][d] * expf(sm[w] - M);
-    out[2 + d] = a;
+  for (int e = 0; e < DPL; ++e) {
+    rsn[e] = 0.f;
+    rcs[e] = 1.f;
+    if (rot) {
+      const int pi = (lane * DPL + e) % HALF;
+      const float freq = 1.0f / powf(theta, 2.0f * (float)pi / (float)HD);
+      sincosf((float)pos * freq, &rsn[e], &rcs[e]);
+    }
+  }
+  const bool lower = lane * DPL < HALF;  // partner dims d + HD/2 live on lane ^ 16
+  float qr[G][DPL], acc[G][DPL], m[G], l[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+      float v = q[(int64_t)(kvh * G + g) * HD + lane * DPL + e];
+      if (rot) {
+        const float pv = __shfl_xor_sync(0xffffffffu, v, 16);
+        v = lower ? v * rcs[e] - pv * rsn[e] : pv * rsn[e] + v * rcs[e];
+      }
+      qr[g][e] = v * scale;
+      acc[g][e] = 0.f;
+    }
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+  }
+  // the CTA whose chunks include pos appends this step's k and v: its local
+  // chunk index, and each of the first HD/2 threads' rotated pair
+  const int cpos = rot ? pos / ATT_CHUNK : -1;
+  const int ipos = (rot && cpos % nsplit == split) ? cpos / nsplit : -1;
+  __half k0h = __float2half_rn(0.f), k1h = k0h, v0h = k0h, v1h = k0h;
+  if (ipos >= 0 && threadIdx.x < HALF) {
+    const int t = threadIdx.x;
+    const float freq = 1.0f / powf(theta, 2.0f * (float)t / (float)HD);
+    float sn, cs;
+    sincosf((float)pos * freq, &sn, &cs);
+    const float k0 = kraw[(int64_t)kvh * HD + t], k1 = kraw[(int64_t)kvh * HD + t + HALF];
+    k0h = __float2half_rn(k0 * cs - k1 * sn);
+    k1h = __float2half_rn(k0 * sn + k1 * cs);
+    v0h = __float2half_rn(vraw[(int64_t)kvh * HD + t]);
+    v1h = __float2half_rn(vraw[(int64_t)kvh * HD + t + HALF]);
+  }
+  const int pidx = (lane >> 1) & 15;  // the position whose score this lane ends with
+  int i = 0;
+  for (; i < nmine; ++i) {
+    const int s = i % ATT_STAGES;
+    const bool ok = mbar_wait(&full[s], (uint32_t)(i / ATT_STAGES) & 1u, err, ERR_FULL_WAIT);
+    if (__syncthreads_or(!ok)) break;  // uniform: every thread stops at the same chunk
+    const int p0 = (split + i * nsplit) * ATT_CHUNK;
+    if (i == ipos) {  // this step's k and v: into the landed tiles and the caches
+      if (threadIdx.x < HALF) {
+        const int t = threadIdx.x, row = pos - p0;
+        __half* kt = tiles + (2 * s) * TILE + row * HD;
+        __half* vt = kt + TILE;
+        kt[t] = k0h;
+        kt[t + HALF] = k1h;
+        vt[t] = v0h;
+        vt[t + HALF] = v1h;
+        __half* kg = kcw + ((int64_t)kvh * ctx + pos) * HD;
+        __half* vg = vcw + ((int64_t)kvh * ctx + pos) * HD;
+        kg[t] = k0h;
+        kg[t + HALF] = k1h;
+        vg[t] = v0h;
+        vg[t + HALF] = v1h;
+      }
+      __syncthreads();
+    }
+    const __half* Ks = tiles + (2 * s) * TILE + warp * PW * HD + lane * DPL;
+    const __half* Vs = Ks + TILE;
+    const int nvalid = min(PW, kv_len - p0 - warp * PW);  // this warp's positions in the chunk
+    if (nvalid > 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float sc[PW];
+#pragma unroll
+        for (int t = 0; t < PW; ++t) {
+          float d = 0.f;
+#pragma unroll
+          for (int e = 0; e < DPL / 2; ++e) {
+            const float2 kk = __half22float2(reinterpret_cast<const __half2*>(Ks + t * HD)[e]);
+            d = fmaf(qr[g][2 * e], kk.x, d);
+            d = fmaf(qr[g][2 * e + 1], kk.y, d);
+          }
+          sc[t] = d;
+        }
+        // halving butterfly: 16 positions x 32 lanes -> position pidx on lanes 2*pidx, 2*pidx + 1
+#pragma unroll
+        for (int w = 16, n = PW / 2; n >= 1; w >>= 1, n >>= 1) {
+          const bool up = lane & w;
+#pragma unroll
+          for (int t = 0; t < n; ++t) {
+            const float send = up ? sc[t] : sc[t + n];
+            const float keep = up ? sc[t + n] : sc[t];
+            sc[t] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+          }
+        }
+        const float sfull = sc[0] + __shfl_xor_sync(0xffffffffu, sc[0], 1);
+        const bool valid = pidx < nvalid;
+        const float sv = valid ? sfull : -INFINITY;
+        float mx = sv;
+#pragma unroll
+        for (int w = 16; w; w >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, w));
+        const float mn = fmaxf(m[g], mx);  // finite: nvalid > 0
+        const float corr = expf(m[g] - mn);
+        const float pv = valid ? expf(sv - mn) : 0.f;
+        float ps = (lane & 1) ? 0.f : pv;
+#pragma unroll
+        for (int w = 16; w; w >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, w);
+        l[g] = l[g] * corr + ps;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[g][e] *= corr;
+        for (int t = 0; t < nvalid; ++t) {  // rows past the chunk's end hold stale data: not read
+          const float pt = __shfl_sync(0xffffffffu, pv, 2 * t);
+#pragma unroll
+          for (int e = 0; e < DPL / 2; ++e) {
+            const float2 vv = __half22float2(reinterpret_cast<const __half2*>(Vs + t * HD)[e]);
+            acc[g][2 * e] = fmaf(pt, vv.x, acc[g][2 * e]);
+            acc[g][2 * e + 1] = fmaf(pt, vv.y, acc[g][2 * e + 1]);
+          }
+        }
+        m[g] = mn;
+      }
+    }
+    __syncthreads();  // every warp is done with stage s
+    if (threadIdx.x == 0 && issued < nmine) issue(issued++);
   }
   if (threadIdx.x == 0) {
-    float L = 0.f;
-    for (int w = 0; w < 8; ++w)
-      if (sm[w] != -INFINITY) L += sl[w] * expf(sm[w] - M);
-    out[0] = M;
-    out[1] = L;
+    // copies still in flight (only after a wait gave up) land before the CTA may exit
+    for (int j = i; j < issued; ++j)
+      mbar_wait(&full[j % ATT_STAGES], (uint32_t)(j / ATT_STAGES) & 1u, err, ERR_DRAIN_WAIT);
+  }
+  // fold the four warps, per head
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float* f = fold + (warp * G + g) * (HD + 2);
+    if (lane == 0) {
+      f[0] = m[g];
+      f[1] = l[g];
+    }
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) f[2 + lane * DPL + e] = acc[g][e];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * HD; idx += ATT_THREADS) {
+    const int g = idx / HD, d = idx - g * HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, fold[(w * G + g) * (HD + 2)]);
+    float a = 0.f, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float* f = fold + (w * G + g) * (HD + 2);
+      if (f[0] != -INFINITY) {
+        const float sc = expf(f[0] - M);
+        a += f[2 + d] * sc;
+        L += f[1] * sc;
+      }
+    }
+    float* out = part + ((int64_t)(kvh * G + g) * nsplit + split) * (HD + 2);
+    out[2 + d] = a;
+    if (d == 0) {
+      out[0] = M;
+      out[1] = L;
+    }
   }
   // every writer's partial is visible device-wide before the arrival
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(&cnt[h], 1) == nch - 1;
+  if (threadIdx.x == 0) is_last = atomicAdd(&cnt[kvh], 1) == nsplit - 1;
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  const int nc = (kv_len + ATT_CHUNK - 1) / ATT_CHUNK;
-  const float* p = part + (int64_t)h * nch * (HD + 2);
-  float Mx = -INFINITY;
-  for (int cc = 0; cc < nc; ++cc) Mx = fmaxf(Mx, __ldcg(p + cc * (HD + 2)));
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    float L = 0.f, a = 0.f;
-    for (int cc = 0; cc < nc; ++cc) {
-      const float mc = __ldcg(p + cc * (HD + 2));
-      if (mc == -INFINITY) continue;
-      const float f = expf(mc - Mx);
-      L += __ldcg(p + cc * (HD + 2) + 1) * f;
-      a += __ldcg(p + cc * (HD + 2) + 2 + d) * f;
+  // Online merge of the splits in split order; the partials of up to 16
+  // splits are loaded together, so the merge costs one L2 round trip per 16.
+  constexpr int SB = 16;
+  for (int idx = threadIdx.x; idx < G * HD; idx += ATT_THREADS) {
+    const int g = idx / HD, d = idx - g * HD;
+    const int h = kvh * G + g;
+    const float* p = part + (int64_t)h * nsplit * (HD + 2);
+    float M = -INFINITY, L = 0.f, a = 0.f;
+    for (int s0 = 0; s0 < nsplit; s0 += SB) {
+      float mc[SB], lc[SB], ac[SB];
+#pragma unroll
+      for (int u = 0; u < SB; ++u) {
+        const bool in = s0 + u < nsplit;
+        const float* ps = p + (s0 + u) * (HD + 2);
+        mc[u] = in ? __ldcg(ps) : -INFINITY;
+        lc[u] = in ? __ldcg(ps + 1) : 0.f;
+        ac[u] = in ? __ldcg(ps + 2 + d) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < SB; ++u) {
+        if (mc[u] == -INFINITY) continue;
+        const float mn = fmaxf(M, mc[u]);
+        const float fo = expf(M - mn), fn = expf(mc[u] - mn);
+        L = L * fo + lc[u] * fn;
+        a = a * fo + ac[u] * fn;
+        M = mn;
+      }
     }
-    o[(int64_t)h * HD + d] = a / L;
+    o[(int64_t)h * HD + d] = L > 0.f ? a / L : 0.f;
   }
-  if (threadIdx.x == 0) cnt[h] = 0;
+  if (threadIdx.x == 0) cnt[kvh] = 0;
 }
 
 __global__ void silu_mul_kernel(const float* __restrict__ gu, float* __restrict__ a, int64_t F) {
@@ -321,11 +475,12 @@ namespace odi_cuda {
 // are launched with programmatic stream serialisation: the next kernel (a
 // GEMV streaming its weights) may start while this one runs.
 template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+static cudaError_t launch_pdl_smem(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                   Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -333,6 +488,11 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cud
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  return launch_pdl_smem(kern, grid, block, 0, s, args...);
 }
 
 static int grid_for(int64_t n, int threads) {
@@ -363,19 +523,61 @@ size_t attention_scratch(int heads, int hd, int ctx) {
   return att_part_offset(heads) + (size_t)heads * attention_chunks(ctx) * (hd + 2) * sizeof(float);
 }
 
+// Splits per kv head: about two CTAs per SM in all (the ring takes 64 KB of
+// shared memory, so a streaming GEMV CTA still fits beside two of them),
+// never more than the context's chunks.
+int attention_splits(int kv_heads, int ctx, int num_sms) {
+  const int want = (2 * num_sms + kv_heads / 2) / kv_heads;
+  const int nch = attention_chunks(ctx);
+  return want < 1 ? 1 : want > nch ? nch : want;
+}
+
+template <int HD, int G>
+static cudaError_t launch_att_t(const float* q, const __half* kc, const __half* vc, float* o, void* scratch,
+                                const DecodeState* st, int heads, int kv_heads, int ctx, float scale,
+                                const AttRope& rp, cudaStream_t s) {
+  auto kern = attn_kernel<HD, G>;
+  constexpr int smem = att_smem_bytes<HD, G>();
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int nsplit = attention_splits(kv_heads, ctx, sms);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  int* err = reinterpret_cast<int*>(base);
+  int* cnt = reinterpret_cast<int*>(base + ATT_CNT_OFFSET);
+  float* part = reinterpret_cast<float*>(base + att_part_offset(heads));
+  return launch_pdl_smem(kern, dim3(kv_heads, nsplit), dim3(ATT_THREADS), smem, s, q, kc, vc, o, part, cnt, err, st,
+                         ctx, nsplit, scale, rp.k, rp.v, rp.theta, rp.k ? 1 : 0, const_cast<__half*>(kc),
+                         const_cast<__half*>(vc));
+}
+
+template <int HD>
+static cudaError_t launch_att_hd(const float* q, const __half* kc, const __half* vc, float* o, void* scratch,
+                                 const DecodeState* st, int heads, int kv_heads, int ctx, float scale,
+                                 const AttRope& rp, cudaStream_t s) {
+  switch (heads / kv_heads) {
+    case 1: return launch_att_t<HD, 1>(q, kc, vc, o, scratch, st, heads, kv_heads, ctx, scale, rp, s);
+    case 2: return launch_att_t<HD, 2>(q, kc, vc, o, scratch, st, heads, kv_heads, ctx, scale, rp, s);
+    case 4: return launch_att_t<HD, 4>(q, kc, vc, o, scratch, st, heads, kv_heads, ctx, scale, rp, s);
+    case 8: return launch_att_t<HD, 8>(q, kc, vc, o, scratch, st, heads, kv_heads, ctx, scale, rp, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, float* o, void* scratch,
                              const DecodeState* st, int heads, int kv_heads, int hd, int ctx, float scale,
-                             cudaStream_t s) {
-  const int nch = attention_chunks(ctx);
-  int* cnt = static_cast<int*>(scratch);
-  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + att_part_offset(heads));
-  const dim3 grid(heads, nch);
-  if (hd == 128)
-    return launch_pdl(attn_kernel<128>, grid, dim3(256), s, q, kc, vc, o, part, cnt, st, heads, kv_heads, ctx, nch,
-                      scale);
-  if (hd == 64)
-    return launch_pdl(attn_kernel<64>, grid, dim3(256), s, q, kc, vc, o, part, cnt, st, heads, kv_heads, ctx, nch,
-                      scale);
+                             const AttRope& rp, cudaStream_t s) {
+  if (hd == 128) return launch_att_hd<128>(q, kc, vc, o, scratch, st, heads, kv_heads, ctx, scale, rp, s);
+  if (hd == 64) return launch_att_hd<64>(q, kc, vc, o, scratch, st, heads, kv_heads, ctx, scale, rp, s);
   return cudaErrorInvalidValue;
 }
 

@@ -94,19 +94,29 @@ struct DecodeState {
 };
 constexpr int ATT_CHUNK = 64;  // positions per CTA in the attention's first pass (8 per warp)
 int attention_chunks(int ctx);
-// attention scratch: per-head arrival counters (zero between launches), then
-// the per-chunk partials [heads][chunks][hd + 2] fp32
-inline size_t att_part_offset(int heads) { return ((size_t)heads * sizeof(int) + 255) / 256 * 256; }
+// attention scratch: the error word (int at 0), per-kv-head arrival counters
+// from byte 16 (zero between launches), then the per-split partials
+// [heads][splits][hd + 2] fp32 from the next 256-byte boundary
+constexpr int ATT_CNT_OFFSET = 16;
+inline size_t att_part_offset(int heads) { return (ATT_CNT_OFFSET + (size_t)heads * sizeof(int) + 255) / 256 * 256; }
 size_t attention_scratch(int heads, int hd, int ctx);
+int attention_splits(int kv_heads, int ctx, int num_sms);
 cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x, float* ssq,
                          cudaStream_t s);
 cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,
                             cudaStream_t s);
 cudaError_t launch_rope_kv(float* q, float* k, const float* v, __half* kc, __half* vc, const DecodeState* st,
                            int heads, int kv_heads, int hd, int ctx, float theta, cudaStream_t s);
+// rope_kv fused into the attention: this step's raw k and v (k == nullptr:
+// q is already rotated and the caches already hold pos)
+struct AttRope {
+  const float* k = nullptr;
+  const float* v = nullptr;
+  float theta = 0.f;
+};
 cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, float* o, void* scratch,
                              const DecodeState* st, int heads, int kv_heads, int hd, int ctx, float scale,
-                             cudaStream_t s);
+                             const AttRope& rp, cudaStream_t s);
 cudaError_t launch_silu_mul(const float* gu, float* a, int64_t F, cudaStream_t s);
 cudaError_t launch_add(float* x, const float* d, int64_t n, cudaStream_t s);
 cudaError_t launch_argmax(const float* logits, int64_t V, DecodeState* st, int* record, int record_len,

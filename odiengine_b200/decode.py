@@ -170,9 +170,34 @@ class DecodeModel:
             for dw in (lw.wqkv, lw.wo, lw.wgu, lw.wdown):
                 dw._ws_for(1, cfg.act_mode, dev)
         self.w.output._ws_for(1, cfg.act_mode, dev)
+        # error words of every kernel with bounded waits (the GEMV workspaces'
+        # and the attention scratch's first int), gathered in one read
+        words = [self.att_scratch.view(torch.int32)[:1]]
+        for lw in self.w.layers:
+            for dw in (lw.wqkv, lw.wo, lw.wgu, lw.wdown):
+                words.append(dw._ws.view(torch.int32)[:1])
+        words.append(self.w.output._ws.view(torch.int32)[:1])
+        self._err_words = words
         # the buffers and the weights were filled on the current stream: the
         # model's own stream must not run ahead of those fills
         self.stream.wait_stream(torch.cuda.current_stream(dev))
+
+    def status(self) -> int:
+        """OR of the device error words (0: no bounded wait gave up)."""
+        import torch
+
+        self.stream.synchronize()
+        with torch.cuda.stream(self.stream):
+            words = torch.cat(self._err_words).cpu().tolist()
+        v = 0
+        for x in words:
+            v |= x
+        return v
+
+    def _check_status(self) -> None:
+        st = self.status()
+        if st:
+            raise RuntimeError(f"decode step: a bounded device wait gave up (error word {st:#x})")
 
     # ---- one step ----------------------------------------------------------
     def _gemv(self, dw: DeviceWeight, x, y, s):
@@ -200,9 +225,9 @@ class DecodeModel:
             self._step_unfused()
 
     def _step_fused(self) -> None:
-        """6 launches per layer: QKV GEMV (RMSNorm fused), rope + KV append,
-        attention, O GEMV (+= x), gate|up GEMV (RMSNorm fused), down GEMV
-        (SwiGLU fused, += x)."""
+        """5 launches per layer: QKV GEMV (RMSNorm fused), attention (rope and
+        the KV append fused), O GEMV (+= x), gate|up GEMV (RMSNorm fused),
+        down GEMV (SwiGLU fused, += x)."""
         cfg, L, s = self.cfg, lib(), self.stream.cuda_stream
         H, KV, hd = cfg.heads, cfg.kv_heads, cfg.head_dim
         st = _ptr(self.state)
@@ -214,9 +239,8 @@ class DecodeModel:
         for li, lw in enumerate(self.w.layers):
             kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
             self._gemv_fused(lw.wqkv, self.x, self.qkv, s, norm=lw.attn_norm)
-            check(L.odi_cuda_rope_kv(q, k, v, kc, vc, st, H, KV, hd, cfg.ctx, cfg.theta, s))
-            check(L.odi_cuda_attention_decode(q, kc, vc, _ptr(self.attn), st, H, KV, hd, cfg.ctx, scale,
-                                              _ptr(self.att_scratch), self.att_scratch.numel() * 4, s))
+            check(L.odi_cuda_rope_attention(q, k, v, kc, vc, _ptr(self.attn), st, H, KV, hd, cfg.ctx, cfg.theta,
+                                            scale, _ptr(self.att_scratch), self.att_scratch.numel() * 4, s))
             self._gemv_fused(lw.wo, self.attn, self.x, s, accumulate=True)
             self._gemv_fused(lw.wgu, self.x, self.gu, s, norm=lw.ffn_norm)
             self._gemv_fused(lw.wdown, self.gu, self.x, s, swiglu=True, accumulate=True)
@@ -252,7 +276,7 @@ class DecodeModel:
 
     def launches_per_step(self) -> int:
         if self.fused:
-            return 1 + 6 * self.cfg.layers + 2  # embed, per layer, output GEMV + argmax
+            return 1 + 5 * self.cfg.layers + 2  # embed, per layer, output GEMV + argmax
         return 1 + 10 * self.cfg.layers + 3  # embed, per layer, final norm + output GEMV + argmax
 
     def capture(self) -> None:
@@ -308,7 +332,7 @@ class DecodeModel:
             with torch.cuda.stream(self.stream):
                 self.state.copy_(host[i], non_blocking=True)
             self._run()
-        self.stream.synchronize()
+        self._check_status()
 
     def generate(self, n: int) -> list:
         """n greedy steps from the current state; returns the n tokens."""
@@ -321,5 +345,5 @@ class DecodeModel:
         start = int(cur[2])
         for _ in range(n):
             self._run()
-        self.stream.synchronize()
+        self._check_status()
         return self.record[start:start + n].cpu().tolist()

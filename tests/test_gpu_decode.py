@@ -100,7 +100,8 @@ def test_rope_kv_append(cuda_lib, hd):
     assert not kcn[:, :pos].any() and not kcn[:, pos + 1:].any()
 
 
-@pytest.mark.parametrize("hd,H,KV,pos", [(128, 8, 2, 300), (64, 4, 4, 0), (128, 32, 32, 2047)])
+@pytest.mark.parametrize("hd,H,KV,pos", [(128, 8, 2, 300), (64, 4, 4, 0), (128, 32, 32, 2047), (128, 64, 8, 1500),
+                                        (64, 8, 4, 77), (128, 32, 32, 63), (128, 32, 32, 64)])
 def test_attention_decode(cuda_lib, hd, H, KV, pos):
     import torch
 
@@ -143,7 +144,72 @@ def test_attention_decode(cuda_lib, hd, H, KV, pos):
             r = (p / p.sum()) @ vc[kh, : p2 + 1].astype(np.float64)
             assert (np.abs(got[h] - r) <= 1e-4 * np.abs(vc).max()).all(), (p2, h)
     assert np.array_equal(got, first)  # the sweep ends at pos: same result as the first call
-    assert not scratch[: H].any()  # counters (the first H ints) are zero again
+    words = scratch.view(torch.int32)
+    assert int(words[0]) == 0  # error word: no bounded wait gave up
+    assert not words[4: 4 + KV].any()  # arrival counters (from byte 16) are zero again
+
+
+@pytest.mark.parametrize("hd,H,KV,pos,ctx", [(128, 32, 32, 2047, 2048), (128, 64, 8, 1000, 1100), (64, 8, 4, 0, 64),
+                                            (128, 8, 2, 129, 256), (128, 8, 8, 300, 300)])
+def test_rope_attention_equals_two_calls(cuda_lib, hd, H, KV, pos, ctx):
+    """The fused rope + KV append + attention gives the results of
+    odi_cuda_rope_kv then odi_cuda_attention_decode, bit for bit (pos >= ctx:
+    nothing appended, q not rotated, in both)."""
+    import torch
+
+    L = cuda_lib.lib()
+    rng = np.random.default_rng(pos + 7 * hd + H)
+    q = rng.standard_normal((H, hd)).astype(np.float32)
+    k = rng.standard_normal((KV, hd)).astype(np.float32)
+    v = rng.standard_normal((KV, hd)).astype(np.float32)
+    kc0 = rng.standard_normal((KV, ctx, hd)).astype(np.float16)
+    vc0 = rng.standard_normal((KV, ctx, hd)).astype(np.float16)
+    sb = L.odi_cuda_attention_scratch_bytes(H, hd, ctx)
+    st = _state(0, pos)
+    scale = 1.0 / np.sqrt(hd)
+    theta = 10000.0
+    outs = []
+    for fused in (False, True):
+        qd, kd, vd = _t(q), _t(k), _t(v)
+        kc, vc = _t(kc0), _t(vc0)
+        scratch = torch.zeros(sb // 4 + 1, device="cuda")
+        out = torch.zeros((H, hd), device="cuda")
+        if fused:
+            cuda_lib.check(L.odi_cuda_rope_attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kc.data_ptr(),
+                                                     vc.data_ptr(), out.data_ptr(), st.data_ptr(), H, KV, hd, ctx,
+                                                     theta, scale, scratch.data_ptr(), sb, None))
+        else:
+            cuda_lib.check(L.odi_cuda_rope_kv(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kc.data_ptr(),
+                                              vc.data_ptr(), st.data_ptr(), H, KV, hd, ctx, theta, None))
+            cuda_lib.check(L.odi_cuda_attention_decode(qd.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(),
+                                                       st.data_ptr(), H, KV, hd, ctx, scale, scratch.data_ptr(), sb,
+                                                       None))
+        torch.cuda.synchronize()
+        assert int(scratch.view(torch.int32)[0]) == 0
+        outs.append((out.cpu().numpy(), kc.cpu().numpy(), vc.cpu().numpy(), qd.cpu().numpy()))
+    (o1, k1, v1, q1), (o2, k2, v2, q2) = outs
+    assert np.array_equal(o1, o2)
+    assert np.array_equal(k1, k2) and np.array_equal(v1, v2)
+    assert np.array_equal(q2, q)  # the fused call leaves q as it was
+    if pos < ctx:
+        assert not np.array_equal(k2[:, pos], kc0[:, pos])  # this step's k was appended
+
+
+def test_attention_group_unsupported(cuda_lib):
+    import torch
+
+    L = cuda_lib.lib()
+    H, KV, hd, ctx = 12, 4, 64, 64  # three query heads per kv head
+    sb = L.odi_cuda_attention_scratch_bytes(H, hd, ctx)
+    scratch = torch.zeros(sb // 4 + 1, device="cuda")
+    q = torch.zeros((H, hd), device="cuda")
+    kc = torch.zeros((KV, ctx, hd), dtype=torch.float16, device="cuda")
+    out = torch.zeros((H, hd), device="cuda")
+    st = _state(0, 5)
+    rc = L.odi_cuda_attention_decode(q.data_ptr(), kc.data_ptr(), kc.data_ptr(), out.data_ptr(), st.data_ptr(), H,
+                                     KV, hd, ctx, 0.125, scratch.data_ptr(), sb, None)
+    assert rc == 4  # ODI_CUDA_ERR_NOT_IMPLEMENTED
+    assert b"query heads per kv head" in L.odi_cuda_last_error()
 
 
 def test_silu_mul(cuda_lib):
@@ -246,6 +312,7 @@ def test_graph_replay_equals_eager(cuda_lib):
     b.clear_cache()
     b.reset(11, 0)
     assert b.generate(12) == eager
+    assert a.status() == 0 and b.status() == 0  # no bounded device wait gave up
 
 
 @pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K, O.Q8_0])
