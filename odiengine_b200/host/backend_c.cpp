@@ -10,10 +10,12 @@
 #include <cstdio>
 #include <cstring>
 #include <exception>
+#include <memory>
 #include <string>
 #include <vector>
 
 #include "cuda_backend.hpp"
+#include "format/gguf_parser.hpp"
 
 namespace {
 thread_local std::string t_err;
@@ -118,6 +120,57 @@ int odi_be_info(void* be, int* type, char* name, size_t name_len, char* info, si
 }
 
 // Weights held in HBM by a CUDABackend; -1 for any other backend.
+// GGUF files through the reference's own parser (gguf_parser.cpp): open
+// (memory-mapped, as Model::Model does), the tensor views Context gets
+// from Model::get_tensor, close.  NULL / non-zero on failure.
+void* odi_be_gguf_open(const char* path) {
+  try {
+    std::unique_ptr<odi::GGUFFile> f = odi::GGUFFile::open(path, true);
+    if (!f) {
+      t_err = std::string("GGUFFile::open failed for ") + (path ? path : "(null)");
+      return nullptr;
+    }
+    return f.release();
+  } catch (const std::exception& e) {
+    caught(e.what());
+  }
+  return nullptr;
+}
+
+void odi_be_gguf_close(void* f) { delete static_cast<odi::GGUFFile*>(f); }
+
+int64_t odi_be_gguf_tensor_count(void* f) { return (int64_t) static_cast<odi::GGUFFile*>(f)->tensor_count(); }
+
+// The view of tensor `name`: data pointer into the mapping, odi dtype, ndim
+// and up to 4 dims (GGUF order).
+int odi_be_gguf_tensor(void* f, const char* name, const void** data, int* dtype, int* ndim, int64_t* shape) {
+  try {
+    const odi::Tensor t = static_cast<odi::GGUFFile*>(f)->load_tensor(name);
+    if (!t.is_valid()) return caught((std::string("no tensor ") + name).c_str());
+    if (t.ndim() > 4) return caught("tensor has more than 4 dimensions");
+    *data = t.data();
+    *dtype = (int)t.dtype();
+    *ndim = (int)t.ndim();
+    for (int i = 0; i < (int)t.ndim(); ++i) shape[i] = t.shape(i);
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+// The loader hook on a CUDA backend: CUDABackend::upload_model(file).
+int odi_be_upload_model(void* be, void* f, int64_t* n_uploaded) {
+  try {
+    auto* cuda = dynamic_cast<odi::CUDABackend*>(static_cast<odi::Backend*>(be));
+    if (!cuda) return caught("upload_model: not a CUDA backend");
+    const size_t n = cuda->upload_model(*static_cast<odi::GGUFFile*>(f));
+    if (n_uploaded) *n_uploaded = (int64_t)n;
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
 int64_t odi_be_cached_weights(void* be) {
   auto* c = dynamic_cast<odi::CUDABackend*>(static_cast<odi::Backend*>(be));
   return c ? (int64_t)c->cached_weights() : -1;

@@ -1,6 +1,8 @@
 // cuda_backend.cpp -- odi::CUDABackend (see cuda_backend.hpp).
 #include "cuda_backend.hpp"
 
+#include "format/gguf_parser.hpp"
+
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
@@ -99,6 +101,22 @@ odi_cuda_weight* CUDABackend::weight_for(const Tensor& b, int64_t N, int64_t K) 
   weights_.emplace(key, w);
   weight_bytes_ += (size_t)odi_cuda_tiled_bytes((int)b.dtype(), N, K);
   return w;
+}
+
+size_t CUDABackend::upload_model(const GGUFFile& file) {
+  bind_device();
+  size_t n = 0;
+  for (const std::string& name : file.tensor_names()) {
+    const Tensor t = file.load_tensor(name);
+    if (!t.is_valid() || t.ndim() != 2 || !dtype_is_quantized(t.dtype()) || odi_cuda_supports_dtype(t.dtype()) != 1)
+      continue;
+    // a weight view is [K, N] (GGUF dims, K contiguous), as matmul reads b
+    const int64_t K = t.shape(0), N = t.shape(1);
+    const size_t before = cached_weights();
+    weight_for(t, N, K);
+    if (cached_weights() > before) ++n;
+  }
+  return n;
 }
 
 void CUDABackend::release_weights() {

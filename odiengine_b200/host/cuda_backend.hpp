@@ -34,6 +34,8 @@
 
 namespace odi {
 
+class GGUFFile;
+
 class CUDABackend : public CPUBackend {
  public:
   // Activation arithmetic of the quantized product.
@@ -68,6 +70,17 @@ class CUDABackend : public CPUBackend {
   void quantized_matmul(Tensor& out, const Tensor& a, const Tensor& b_quant) override;
   void dequantize(Tensor& out, const Tensor& x) override;
   void sync() override;
+
+  // The loader hook, for Model::Model right after GGUFFile::open
+  // (src/core/model.cpp:26-29): every 2-D tensor of the file whose dtype this
+  // backend computes on the GPU is uploaded now, once, as its GGUF blocks
+  // repacked in HBM, under the key matmul looks up (the GGUF view's host
+  // address, dtype and shape; load_tensor returns the same view each time,
+  // gguf_parser.cpp:614-628).  The first forward pass then finds every weight
+  // resident.  Tensors already resident are skipped.  Returns the number
+  // uploaded by this call; throws std::runtime_error if an upload fails.
+  // The file must outlive the backend's use of its weights.
+  size_t upload_model(const GGUFFile& file);
 
   // Drops every cached device copy of a weight (e.g. after unloading a model
   // whose mmap address may be reused).

@@ -35,6 +35,12 @@ FACADE = {
     "odi_be_info": (_int, [_vp, ctypes.POINTER(_int), ctypes.c_char_p, _sz, ctypes.c_char_p, _sz,
                            ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
     "odi_be_cached_weights": (_i64, [_vp]),
+    "odi_be_gguf_open": (_vp, [ctypes.c_char_p]),
+    "odi_be_gguf_close": (None, [_vp]),
+    "odi_be_gguf_tensor_count": (_i64, [_vp]),
+    "odi_be_gguf_tensor": (_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(_int), ctypes.POINTER(_int),
+                                  _shape]),
+    "odi_be_upload_model": (_int, [_vp, _vp, ctypes.POINTER(_i64)]),
 }
 
 
