@@ -17,8 +17,13 @@
  * invertible (odi_cuda_unpack).
  *
  * dtype ids are odi_dtype_t values (include/odi/odi_types.h:32-49):
- *   ODI_DTYPE_Q8_0 = 6, ODI_DTYPE_Q4_0 = 7, ODI_DTYPE_Q4_K = 11,
+ *   ODI_DTYPE_Q8_0 = 6, ODI_DTYPE_Q4_0 = 7, ODI_DTYPE_Q4_1 = 8,
+ *   ODI_DTYPE_Q5_0 = 9, ODI_DTYPE_Q5_1 = 10, ODI_DTYPE_Q4_K = 11,
  *   ODI_DTYPE_Q5_K = 12, ODI_DTYPE_Q6_K = 13.
+ * Q4_1 / Q5_0 / Q5_1 give the product their block format defines
+ * (cpu_backend.cpp:704-767 decode); the reference CPU backend's
+ * dequantize + matmul_f32 fallback for them reads the weight transposed
+ * (cpu_backend.cpp:211-216) and is not reproduced.
  */
 #ifndef ODI_CUDA_H
 #define ODI_CUDA_H
@@ -92,8 +97,8 @@ int odi_cuda_device_info(char* buf, size_t len);
 /* Backend::available_memory / used_memory (backend.hpp:26-27). */
 int odi_cuda_memory_info(size_t* free_bytes, size_t* total_bytes);
 
-/* Backend::supports_dtype (backend.hpp:30): 1 for Q8_0, Q4_0, Q4_K, Q5_K,
- * Q6_K, else 0. */
+/* Backend::supports_dtype (backend.hpp:30): 1 for Q8_0, Q4_0, Q4_1, Q5_0,
+ * Q5_1, Q4_K, Q5_K, Q6_K, else 0. */
 int odi_cuda_supports_dtype(int dtype);
 
 /* Message for the last non-zero status returned on this thread
@@ -133,7 +138,8 @@ const void* odi_cuda_weight_data(const odi_cuda_weight* w);
 int odi_cuda_weight_shape(const odi_cuda_weight* w, int* dtype, int64_t* N, int64_t* K);
 
 /* fp32 weights [N, K] (device) -> GGUF blocks [N][ceil(K/block)] (device).
- * Q4_0 / Q8_0 are byte-identical to the GGUF quantisers; Q4_K / Q5_K / Q6_K
+ * Q4_0 / Q8_0 / Q4_1 / Q5_0 / Q5_1 are byte-identical to the GGUF quantisers
+ * (gguf 0.19.0); Q4_K / Q5_K / Q6_K
  * use this library's own quantisers of the GGML formats.  The reference has
  * no quantiser (Tensor::to throws for quantized dtypes, tensor.cpp:654-656);
  * this brings fp32 checkpoints and synthetic models up on the device. */

@@ -24,16 +24,19 @@ LIB_PATH = os.path.join(HERE, "libodi_cuda.so")
 ODI_DTYPE_F32 = 0
 ODI_DTYPE_Q8_0 = 6
 ODI_DTYPE_Q4_0 = 7
+ODI_DTYPE_Q4_1 = 8
+ODI_DTYPE_Q5_0 = 9
+ODI_DTYPE_Q5_1 = 10
 ODI_DTYPE_Q4_K = 11
 ODI_DTYPE_Q5_K = 12
 ODI_DTYPE_Q6_K = 13
-DTYPE_NAMES = {ODI_DTYPE_Q8_0: "Q8_0", ODI_DTYPE_Q4_0: "Q4_0", ODI_DTYPE_Q4_K: "Q4_K",
-               ODI_DTYPE_Q5_K: "Q5_K", ODI_DTYPE_Q6_K: "Q6_K"}
+DTYPE_NAMES = {ODI_DTYPE_Q8_0: "Q8_0", ODI_DTYPE_Q4_0: "Q4_0", ODI_DTYPE_Q4_1: "Q4_1", ODI_DTYPE_Q5_0: "Q5_0",
+               ODI_DTYPE_Q5_1: "Q5_1", ODI_DTYPE_Q4_K: "Q4_K", ODI_DTYPE_Q5_K: "Q5_K", ODI_DTYPE_Q6_K: "Q6_K"}
 DTYPES = {v: k for k, v in DTYPE_NAMES.items()}
-BLOCK_ELEMS = {ODI_DTYPE_Q8_0: 32, ODI_DTYPE_Q4_0: 32, ODI_DTYPE_Q4_K: 256, ODI_DTYPE_Q5_K: 256,
-               ODI_DTYPE_Q6_K: 256}
-BLOCK_BYTES = {ODI_DTYPE_Q8_0: 34, ODI_DTYPE_Q4_0: 18, ODI_DTYPE_Q4_K: 144, ODI_DTYPE_Q5_K: 176,
-               ODI_DTYPE_Q6_K: 210}
+BLOCK_ELEMS = {ODI_DTYPE_Q8_0: 32, ODI_DTYPE_Q4_0: 32, ODI_DTYPE_Q4_1: 32, ODI_DTYPE_Q5_0: 32, ODI_DTYPE_Q5_1: 32,
+               ODI_DTYPE_Q4_K: 256, ODI_DTYPE_Q5_K: 256, ODI_DTYPE_Q6_K: 256}
+BLOCK_BYTES = {ODI_DTYPE_Q8_0: 34, ODI_DTYPE_Q4_0: 18, ODI_DTYPE_Q4_1: 20, ODI_DTYPE_Q5_0: 22, ODI_DTYPE_Q5_1: 24,
+               ODI_DTYPE_Q4_K: 144, ODI_DTYPE_Q5_K: 176, ODI_DTYPE_Q6_K: 210}
 
 ACT_Q8 = 0
 ACT_F32 = 1

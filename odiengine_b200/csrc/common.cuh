@@ -10,13 +10,19 @@
 namespace odi_cuda {
 
 // odi_dtype_t ids (include/odi/odi_types.h:32-49).
-enum DType : int { Q8_0 = 6, Q4_0 = 7, Q4_K = 11, Q5_K = 12, Q6_K = 13 };
+enum DType : int { Q8_0 = 6, Q4_0 = 7, Q4_1 = 8, Q5_0 = 9, Q5_1 = 10, Q4_K = 11, Q5_K = 12, Q6_K = 13 };
 
 // ----------------------------------------------------------------------------
 // Tiled weight layout.  A unit = 64 output rows x 256 input columns.  Each
 // unit is 64 row slices of SLICE bytes followed by a tail plane:
 //   Q4_0 slice 144 B: d[8] fp16, qs[8][16]           (8 GGUF blocks)
 //   Q8_0 slice 272 B: d[8] fp16, qs[8][32]           (8 GGUF blocks)
+//   Q4_1 slice 176 B: d[8], m[8] fp16, qs[8][16], 16 B pad
+//   Q5_0 slice 176 B: d[8] fp16, qh[8][4], qs[8][16]
+//   Q5_1 slice 208 B: d[8], m[8] fp16, qh[8][4], qs[8][16], 16 B pad
+//     (the 32-value block types keep their fields field-major over the 8
+//     blocks of a span; the pads make every slice stride an odd multiple of
+//     16 B, so 128-bit loads of 8 consecutive rows hit distinct banks)
 //   Q4_K slice 144 B: the GGUF super-block verbatim  (d, dmin, scales[12], qs[128])
 //   Q5_K slice 176 B: the GGUF super-block verbatim  (d, dmin, scales[12], qh[32], qs[128])
 //   Q6_K slice 208 B: scales[16], ql[128], qh[64]; tail plane d[64] fp16
@@ -27,18 +33,33 @@ constexpr int UNIT_ROWS = 64;
 constexpr int UNIT_COLS = 256;
 
 __host__ __device__ constexpr int slice_bytes(int dt) {
-  return dt == Q4_0 ? 144 : dt == Q8_0 ? 272 : dt == Q4_K ? 144 : dt == Q5_K ? 176 : dt == Q6_K ? 208 : 0;
+  return dt == Q4_0 ? 144 : dt == Q8_0 ? 272 : dt == Q4_1 ? 176 : dt == Q5_0 ? 176 : dt == Q5_1 ? 208
+       : dt == Q4_K ? 144 : dt == Q5_K ? 176 : dt == Q6_K ? 208 : 0;
 }
+// The 32-value block types: fields of a GGUF block [d][m][qh][qs] (m and qh
+// where the type has them) and their field-major places in a slice.
+__host__ __device__ constexpr bool is_block32(int dt) {
+  return dt == Q4_0 || dt == Q8_0 || dt == Q4_1 || dt == Q5_0 || dt == Q5_1;
+}
+__host__ __device__ constexpr bool has_min(int dt) { return dt == Q4_1 || dt == Q5_1; }
+__host__ __device__ constexpr bool has_qh(int dt) { return dt == Q5_0 || dt == Q5_1; }
+__host__ __device__ constexpr int qs_bytes(int dt) { return dt == Q8_0 ? 32 : 16; }
+__host__ __device__ constexpr int blk_qh(int dt) { return has_min(dt) ? 4 : 2; }
+__host__ __device__ constexpr int blk_qs(int dt) { return 2 + (has_min(dt) ? 2 : 0) + (has_qh(dt) ? 4 : 0); }
+__host__ __device__ constexpr int sl_m(int) { return 16; }
+__host__ __device__ constexpr int sl_qh(int dt) { return 16 + (has_min(dt) ? 16 : 0); }
+__host__ __device__ constexpr int sl_qs(int dt) { return sl_qh(dt) + (has_qh(dt) ? 32 : 0); }
 __host__ __device__ constexpr int unit_bytes(int dt) {
   return slice_bytes(dt) * UNIT_ROWS + (dt == Q6_K ? 2 * UNIT_ROWS : 0);
 }
 __host__ __device__ constexpr int block_elems(int dt) {
-  return (dt == Q4_0 || dt == Q8_0) ? 32 : (dt == Q4_K || dt == Q5_K || dt == Q6_K) ? 256 : 0;
+  return is_block32(dt) ? 32 : (dt == Q4_K || dt == Q5_K || dt == Q6_K) ? 256 : 0;
 }
 __host__ __device__ constexpr int block_bytes(int dt) {
-  return dt == Q4_0 ? 18 : dt == Q8_0 ? 34 : dt == Q4_K ? 144 : dt == Q5_K ? 176 : dt == Q6_K ? 210 : 0;
+  return dt == Q4_0 ? 18 : dt == Q8_0 ? 34 : dt == Q4_1 ? 20 : dt == Q5_0 ? 22 : dt == Q5_1 ? 24
+       : dt == Q4_K ? 144 : dt == Q5_K ? 176 : dt == Q6_K ? 210 : 0;
 }
-inline bool dtype_ok(int dt) { return dt == Q4_0 || dt == Q8_0 || dt == Q4_K || dt == Q5_K || dt == Q6_K; }
+inline bool dtype_ok(int dt) { return is_block32(dt) || dt == Q4_K || dt == Q5_K || dt == Q6_K; }
 
 // ----------------------------------------------------------------------------
 // Activation tile layout (device scratch written by the activation kernels).

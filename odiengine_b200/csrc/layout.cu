@@ -29,16 +29,23 @@ __device__ __forceinline__ int64_t tiled_src(int dt, int64_t idx, int64_t N, int
     if (o < 144) return blk + (o - 16);
     return blk + 128 + (o - 144);
   }
-  // Q4_0 / Q8_0: 8 blocks of 32 per span
+  // 32-value block types: 8 blocks per span, fields field-major in the slice
   const int64_t nb_row = (K + 31) / 32;
-  const int qb = bb - 2;
   int j, t;
-  if (o < 16) {
+  if (o < 16) {  // d
     j = o >> 1;
     t = o & 1;
-  } else {
-    j = (o - 16) / qb;
-    t = 2 + (o - 16) - j * qb;
+  } else if (has_min(dt) && o < sl_qh(dt)) {  // m
+    j = (o - 16) >> 1;
+    t = 2 + ((o - 16) & 1);
+  } else if (has_qh(dt) && o < sl_qs(dt)) {  // qh
+    j = (o - sl_qh(dt)) >> 2;
+    t = blk_qh(dt) + ((o - sl_qh(dt)) & 3);
+  } else {  // qs, then the pad
+    const int q = o - sl_qs(dt), qb = qs_bytes(dt);
+    j = q / qb;
+    if (j >= 8) return -1;
+    t = blk_qs(dt) + (q - j * qb);
   }
   const int64_t b = kb * 8 + j;
   if (b >= nb_row) return -1;
@@ -56,11 +63,14 @@ __device__ __forceinline__ int64_t gguf_dst(int dt, int64_t idx, int64_t K, int6
   const int t = (int)(rb - b * bb);
   const int64_t g = n / UNIT_ROWS;
   const int r = (int)(n - g * UNIT_ROWS);
-  if (dt == Q4_0 || dt == Q8_0) {
+  if (is_block32(dt)) {
     const int64_t kb = b >> 3;
     const int j = (int)(b & 7);
     const int64_t base = (g * KB + kb) * ub + (int64_t)r * sb;
-    return t < 2 ? base + 2 * j + t : base + 16 + (int64_t)(bb - 2) * j + (t - 2);
+    if (t < 2) return base + 2 * j + t;
+    if (has_min(dt) && t < 4) return base + sl_m(dt) + 2 * j + (t - 2);
+    if (has_qh(dt) && t < blk_qs(dt)) return base + sl_qh(dt) + 4 * j + (t - blk_qh(dt));
+    return base + sl_qs(dt) + (int64_t)qs_bytes(dt) * j + (t - blk_qs(dt));
   }
   const int64_t ubase = (g * KB + b) * ub;
   const int64_t base = ubase + (int64_t)r * sb;
@@ -92,8 +102,10 @@ __global__ void unpack_kernel(int dt, const uint8_t* __restrict__ tiled, uint8_t
 __device__ __forceinline__ uint16_t ld16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
 
 // Decode element (n, k) from the tiled layout in the reference / gguf
-// arithmetic: Q4_0 (q-8)*d, Q8_0 q*d, Q4_K/Q5_K (d*sc)*q - dmin*m,
-// Q6_K (d*sc)*(q-32).
+// arithmetic: Q4_0 (q-8)*d, Q8_0 q*d, Q4_1 / Q5_1 q*d + m, Q5_0 (q-16)*d
+// (cpu_backend.cpp:704-767; each operation rounded, as gguf's float32
+// numpy and the reference built without contraction), Q4_K/Q5_K
+// (d*sc)*q - dmin*m, Q6_K (d*sc)*(q-32).
 __device__ float decode_tiled(int dt, const uint8_t* __restrict__ w, int64_t n, int64_t k, int64_t KB) {
   const int ub = unit_bytes(dt), sb = slice_bytes(dt);
   const int64_t g = n / UNIT_ROWS, kb = k / UNIT_COLS;
@@ -110,6 +122,19 @@ __device__ float decode_tiled(int dt, const uint8_t* __restrict__ w, int64_t n, 
   if (dt == Q8_0) {
     const int j = e >> 5, l = e & 31;
     return (float)(int8_t)sl[16 + 32 * j + l] * h2f(ld16(sl + 2 * j));
+  }
+  if (dt == Q4_1 || dt == Q5_0 || dt == Q5_1) {
+    const int j = e >> 5, l = e & 31;
+    const float d = h2f(ld16(sl + 2 * j));
+    const uint8_t byte = sl[sl_qs(dt) + 16 * j + (l & 15)];
+    int q = l < 16 ? (byte & 15) : (byte >> 4);
+    if (has_qh(dt)) {
+      const uint8_t* h = sl + sl_qh(dt) + 4 * j;
+      const uint32_t qh = (uint32_t)h[0] | ((uint32_t)h[1] << 8) | ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+      q |= (int)((qh >> l) & 1u) << 4;
+    }
+    if (dt == Q5_0) return __fmul_rn((float)(q - 16), d);
+    return __fadd_rn(__fmul_rn((float)q, d), h2f(ld16(sl + sl_m(dt) + 2 * j)));
   }
   if (dt == Q4_K || dt == Q5_K) {
     const float d = h2f(ld16(sl)), dmin = h2f(ld16(sl + 2));

@@ -126,6 +126,9 @@ static cudaError_t launch_dt(int dt, const GemvPlan& pl, const GemvArgs& a, bool
   switch (dt) {
     case Q4_0: return launch_mt<Q4_0, F32>(pl, a, pdl, s);
     case Q8_0: return launch_mt<Q8_0, F32>(pl, a, pdl, s);
+    case Q4_1: return launch_mt<Q4_1, F32>(pl, a, pdl, s);
+    case Q5_0: return launch_mt<Q5_0, F32>(pl, a, pdl, s);
+    case Q5_1: return launch_mt<Q5_1, F32>(pl, a, pdl, s);
     case Q4_K: return launch_mt<Q4_K, F32>(pl, a, pdl, s);
     case Q5_K: return launch_mt<Q5_K, F32>(pl, a, pdl, s);
     case Q6_K: return launch_mt<Q6_K, F32>(pl, a, pdl, s);

@@ -481,6 +481,70 @@ __device__ __forceinline__ void unit_q8_q4_0(const uint8_t* __restrict__ sl, con
   }
 }
 
+// Bits 0..3 of h to bit 4 of bytes 0..3: the fifth bits of four 5-bit codes
+// (the multiply places copies of h at bits 0, 7, 14, 21; no carries).
+__device__ __forceinline__ uint32_t bit4_spread(uint32_t h) { return (((h & 0xFu) * 0x00204081u) << 4) & 0x10101010u; }
+// The fifth bits of 16 codes: bits base..base+15 of a block's qh word.
+__device__ __forceinline__ uint4 fifth_bits16(uint32_t qh, int base) {
+  return make_uint4(bit4_spread(qh >> base), bit4_spread(qh >> (base + 4)), bit4_spread(qh >> (base + 8)),
+                    bit4_spread(qh >> (base + 12)));
+}
+
+// Q4_1, Q5_0, Q5_1 (32-value blocks, cpu_backend.cpp:704-767): per block
+// value = d * q + m (Q4_1, Q5_1) or d * (q - 16) (Q5_0), q the 4- or 5-bit
+// code.  The integer dot of the codes with the int8 activations is exact;
+// the min (or the -16 offset) folds into the block's sum of activation
+// codes: sum((d q + m) x) = d dx sum(q xq) + m sdx.
+template <int DT, int MT>
+__device__ __forceinline__ void unit_q8_legacy(const uint8_t* __restrict__ sl, const uint8_t* __restrict__ xs,
+                                               int M, float (&acc)[MT]) {
+  constexpr bool FIVE = has_qh(DT), MIN = has_min(DT);
+  const uint4 dv = lds128(sl);
+  const float dw[8] = {h2f_lo(dv.x), h2f_hi(dv.x), h2f_lo(dv.y), h2f_hi(dv.y),
+                       h2f_lo(dv.z), h2f_hi(dv.z), h2f_lo(dv.w), h2f_hi(dv.w)};
+  float bw[8];  // the additive term per block: m, or -16 d
+  if (MIN) {
+    const uint4 mv = lds128(sl + sl_m(DT));
+    const float t[8] = {h2f_lo(mv.x), h2f_hi(mv.x), h2f_lo(mv.y), h2f_hi(mv.y),
+                        h2f_lo(mv.z), h2f_hi(mv.z), h2f_lo(mv.w), h2f_hi(mv.w)};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bw[j] = t[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bw[j] = -16.0f * dw[j];
+  }
+  uint32_t qhw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (FIVE) {
+    const uint4 h0 = lds128(sl + sl_qh(DT)), h1 = lds128(sl + sl_qh(DT) + 16);
+    qhw[0] = h0.x; qhw[1] = h0.y; qhw[2] = h0.z; qhw[3] = h0.w;
+    qhw[4] = h1.x; qhw[5] = h1.y; qhw[6] = h1.z; qhw[7] = h1.w;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 q = lds128(sl + sl_qs(DT) + 16 * j);
+    uint4 lo, hi;
+    if (FIVE) {
+      lo = or4(and4(q, 0x0F0F0F0Fu), fifth_bits16(qhw[j], 0));
+      hi = or4(and4(shr4(q, 4), 0x0F0F0F0Fu), fifth_bits16(qhw[j], 16));
+    } else {
+      lo = and4(q, 0x0F0F0F0Fu);
+      hi = and4(q, 0xF0F0F0F0u);  // kept x16
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m < M) {
+        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
+        const float2 r = *reinterpret_cast<const float2*>(xr + 256 + 16 * j);  // dx, sdx
+        const int dd = FIVE ? dot16<false>(lo, x0, dot16<false>(hi, x1, 0))
+                            : dot16<false>(lo, x0, 0) + (dot16<true>(hi, x1, 0) >> 4);  // exact division
+        float v = fmaf(i2f(dd), dw[j] * r.x, acc[m]);
+        acc[m] = fmaf(bw[j], r.y, v);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // ACT_F32 units: 16 groups of 16 columns; value = A * code - B with integer
 // codes widened to fp32 exactly, then fp32 FMA against fp32 activations.
@@ -525,6 +589,15 @@ __device__ __forceinline__ Group16 group16(const uint8_t* __restrict__ sl, float
     G.cw = lds128(sl + 16 + 16 * g);
     G.A = h2f((uint16_t)ldsu16(sl + 2 * j));
     G.B = 0.0f;
+  } else if (DT == Q4_1 || DT == Q5_0 || DT == Q5_1) {
+    // block j = g/2: low nibbles = values 0..15, high = 16..31; value = A q - B
+    const int j = g >> 1;
+    const uint4 q = lds128(sl + sl_qs(DT) + 16 * j);
+    G.cw = (g & 1) ? and4(shr4(q, 4), 0x0F0F0F0Fu) : and4(q, 0x0F0F0F0Fu);
+    if (has_qh(DT))
+      G.cw = or4(G.cw, fifth_bits16(*reinterpret_cast<const uint32_t*>(sl + sl_qh(DT) + 4 * j), 16 * (g & 1)));
+    G.A = h2f((uint16_t)ldsu16(sl + 2 * j));
+    G.B = DT == Q5_0 ? 16.0f * G.A : -h2f((uint16_t)ldsu16(sl + sl_m(DT) + 2 * j));
   } else {  // Q4_0: block j = g/2; low nibbles = values 0..15, high = 16..31
     const int j = g >> 1;
     const uint4 q = lds128(sl + 16 + 16 * j);
@@ -586,6 +659,8 @@ __device__ __forceinline__ void unit(const uint8_t* __restrict__ st, int row, co
     unit_q8_q6k<MT>(sl, tail_d, xs, M, acc);
   } else if (DT == Q8_0) {
     unit_q8_q8_0<MT>(sl, xs, M, acc);
+  } else if (DT == Q4_1 || DT == Q5_0 || DT == Q5_1) {
+    unit_q8_legacy<DT, MT>(sl, xs, M, acc);
   } else {
     unit_q8_q4_0<MT>(sl, xs, M, acc);
   }

@@ -6,9 +6,14 @@
 // GPU so synthetic models (and fp32 checkpoints) can be brought up without a
 // host round trip.  One thread per block, IEEE fp32 with no contraction, so
 // the bytes are identical to the CPU quantisers:
-//   Q4_0, Q8_0 -- the GGUF quantisers (gguf 0.19.0 Q4_0 / Q8_0):
+//   Q4_0, Q8_0, Q4_1, Q5_0, Q5_1 -- the GGUF quantisers (gguf 0.19.0):
 //     Q4_0: m = signed value of largest |x| (first), d = m / -8,
 //           q = min(15, trunc(x / d + 8.5)); Q8_0: d = amax / 127, q = round(x / d)
+//     Q4_1 / Q5_1: d = (max - min) / 15 (31), q = min(15 (31), trunc((x - min) / d + 0.5)),
+//           d and min stored as fp16
+//     Q5_0: as Q4_0 with d = m / -16, q = min(31, trunc(x / d + 16.5))
+//     (the fifth bits of Q5_0 / Q5_1 packed little-endian into qh, element
+//     j at bit j)
 //   Q4_K, Q5_K, Q6_K -- this project's own quantisers of the GGML formats:
 //     Q4_K/Q5_K: per 32 values scale = (max - min<=0) / levels, min = -min;
 //       6-bit codes of scale / d and min / dmin with d = max scale / 63,
@@ -49,6 +54,50 @@ __device__ void q8_0_block(const float* x, uint8_t* blk) {
   const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
   st16(blk, f2h_bits(d));
   for (int j = 0; j < 32; ++j) blk[2 + j] = (uint8_t)(int8_t)(int)roundf(__fmul_rn(x[j], id));
+}
+
+// Q4_1 (levels 15) and Q5_1 (levels 31): block [d][m][qh (Q5_1)][qs].
+__device__ void qmin_block(const float* x, uint8_t* blk, int levels) {
+  float mx = x[0], mn = x[0];
+  for (int j = 1; j < 32; ++j) {
+    mx = fmaxf(mx, x[j]);
+    mn = fminf(mn, x[j]);
+  }
+  const float d = __fdiv_rn(__fsub_rn(mx, mn), (float)levels);
+  const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+  st16(blk, f2h_bits(d));
+  st16(blk + 2, f2h_bits(mn));
+  uint8_t q[32];
+  for (int j = 0; j < 32; ++j)
+    q[j] = (uint8_t)clampi((int)truncf(__fadd_rn(__fmul_rn(__fsub_rn(x[j], mn), id), 0.5f)), 0, levels);
+  uint8_t* qs = blk + (levels == 31 ? 8 : 4);
+  for (int j = 0; j < 16; ++j) qs[j] = (uint8_t)((q[j] & 0x0F) | ((q[j + 16] & 0x0F) << 4));
+  if (levels == 31) {
+    uint32_t qh = 0;
+    for (int j = 0; j < 32; ++j) qh |= (uint32_t)(q[j] >> 4) << j;
+    for (int b = 0; b < 4; ++b) blk[4 + b] = (uint8_t)(qh >> (8 * b));
+  }
+}
+
+// Q5_0: block [d][qh][qs].
+__device__ void q5_0_block(const float* x, uint8_t* blk) {
+  float amax = -1.0f, mx = 0.0f;
+  for (int j = 0; j < 32; ++j) {
+    const float a = fabsf(x[j]);
+    if (a > amax) {
+      amax = a;
+      mx = x[j];
+    }
+  }
+  const float d = __fdiv_rn(mx, -16.0f);
+  const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+  st16(blk, f2h_bits(d));
+  uint8_t q[32];
+  for (int j = 0; j < 32; ++j) q[j] = (uint8_t)clampi((int)truncf(__fadd_rn(__fmul_rn(x[j], id), 16.5f)), 0, 31);
+  uint32_t qh = 0;
+  for (int j = 0; j < 32; ++j) qh |= (uint32_t)(q[j] >> 4) << j;
+  for (int b = 0; b < 4; ++b) blk[2 + b] = (uint8_t)(qh >> (8 * b));
+  for (int j = 0; j < 16; ++j) blk[6 + j] = (uint8_t)((q[j] & 0x0F) | ((q[j + 16] & 0x0F) << 4));
 }
 
 __device__ void kq45_block(const float* x, uint8_t* blk, int levels, bool five) {
@@ -155,6 +204,9 @@ __global__ void quant_weights_kernel(const float* __restrict__ w, uint8_t* __res
     uint8_t* blk = out + i * BB;  // each thread owns one whole block of the output
     if (DT == Q4_0) q4_0_block(x, blk);
     else if (DT == Q8_0) q8_0_block(x, blk);
+    else if (DT == Q4_1) qmin_block(x, blk, 15);
+    else if (DT == Q5_1) qmin_block(x, blk, 31);
+    else if (DT == Q5_0) q5_0_block(x, blk);
     else if (DT == Q4_K) kq45_block(x, blk, 15, false);
     else if (DT == Q5_K) kq45_block(x, blk, 31, true);
     else q6_k_block(x, blk);
@@ -172,6 +224,9 @@ cudaError_t launch_quant_weights(int dt, const float* w, void* out, int64_t N, i
   switch (dt) {
     case Q4_0: quant_weights_kernel<Q4_0><<<(int)grid, block, 0, s>>>(w, o, N, K); break;
     case Q8_0: quant_weights_kernel<Q8_0><<<(int)grid, block, 0, s>>>(w, o, N, K); break;
+    case Q4_1: quant_weights_kernel<Q4_1><<<(int)grid, block, 0, s>>>(w, o, N, K); break;
+    case Q5_0: quant_weights_kernel<Q5_0><<<(int)grid, block, 0, s>>>(w, o, N, K); break;
+    case Q5_1: quant_weights_kernel<Q5_1><<<(int)grid, block, 0, s>>>(w, o, N, K); break;
     case Q4_K: quant_weights_kernel<Q4_K><<<(int)grid, block, 0, s>>>(w, o, N, K); break;
     case Q5_K: quant_weights_kernel<Q5_K><<<(int)grid, block, 0, s>>>(w, o, N, K); break;
     case Q6_K: quant_weights_kernel<Q6_K><<<(int)grid, block, 0, s>>>(w, o, N, K); break;

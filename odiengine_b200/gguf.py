@@ -28,8 +28,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from . import (ODI_DTYPE_Q4_0, ODI_DTYPE_Q4_K, ODI_DTYPE_Q5_K, ODI_DTYPE_Q6_K, ODI_DTYPE_Q8_0, DeviceWeight,
-               gguf_bytes, repack)
+from . import (ODI_DTYPE_Q4_0, ODI_DTYPE_Q4_1, ODI_DTYPE_Q4_K, ODI_DTYPE_Q5_0, ODI_DTYPE_Q5_1, ODI_DTYPE_Q5_K,
+               ODI_DTYPE_Q6_K, ODI_DTYPE_Q8_0, DeviceWeight, gguf_bytes, repack)
 
 GGUF_MAGIC = b"GGUF"
 GGUF_VERSION = 3
@@ -43,7 +43,8 @@ _SCALAR = {T_U8: "<B", T_I8: "<b", T_U16: "<H", T_I16: "<h", T_U32: "<I", T_I32:
 # ggml tensor types (src/format/gguf_types.hpp:33-63) and the odi_dtype_t each maps to
 GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q8_0 = 0, 1, 2, 3, 6, 7, 8
 GGML_Q4_K, GGML_Q5_K, GGML_Q6_K = 12, 13, 14
-ODI_OF_GGML = {GGML_Q4_0: ODI_DTYPE_Q4_0, GGML_Q8_0: ODI_DTYPE_Q8_0, GGML_Q4_K: ODI_DTYPE_Q4_K,
+ODI_OF_GGML = {GGML_Q4_0: ODI_DTYPE_Q4_0, GGML_Q4_1: ODI_DTYPE_Q4_1, GGML_Q5_0: ODI_DTYPE_Q5_0,
+               GGML_Q5_1: ODI_DTYPE_Q5_1, GGML_Q8_0: ODI_DTYPE_Q8_0, GGML_Q4_K: ODI_DTYPE_Q4_K,
                GGML_Q5_K: ODI_DTYPE_Q5_K, GGML_Q6_K: ODI_DTYPE_Q6_K}
 GGML_OF_ODI = {v: k for k, v in ODI_OF_GGML.items()}
 

@@ -137,8 +137,10 @@ void CUDABackend::release_weights() {
 // dimensions of `a` are not iterated, exactly as there.
 void CUDABackend::matmul(Tensor& out, const Tensor& a, const Tensor& b) {
   if (!dtype_is_quantized(b.dtype()) || odi_cuda_supports_dtype(b.dtype()) != 1) {
-    // fp32 x fp32, and the legacy Q4_1 / Q5_0 / Q5_1 block types, keep the
-    // CPU backend's implementation.
+    // fp32 x fp32 (and any block type the library does not compute) keep the
+    // CPU backend's implementation.  Q4_1 / Q5_0 / Q5_1 run on the GPU and
+    // give the product the block format defines; the CPU backend's fallback
+    // for them reads the dequantized weight transposed (cpu_backend.cpp:211-216).
     CPUBackend::matmul(out, a, b);
     return;
   }

@@ -5,7 +5,8 @@ Thin ctypes bindings over two checker libraries:
 * ``liboracle.so`` -- this project's C restatement (odi_oracle.c) of the
   reference path: the fp32 block loops of ``CPUBackend::matmul_q4_0`` /
   ``matmul_q8_0`` (src/compute/cpu/cpu_backend.cpp:786-854), the same loop
-  order for Q4_K/Q5_K/Q6_K, the Q4_0/Q8_0 quantisers of gguf 0.19.0, the Q8_0
+  order for Q4_1/Q5_0/Q5_1 (cpu_backend.cpp:704-767 decode) and
+  Q4_K/Q5_K/Q6_K, the Q4_0/Q8_0/Q4_1/Q5_0/Q5_1 quantisers of gguf 0.19.0, the Q8_0
   activation quantiser, the Q8-activation integer dot and error bounds, and
   the tiled device layout.
 * ``_ref/libodi_ref.so`` -- the reference's own, unmodified CPU backend
@@ -23,10 +24,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
-Q8_0, Q4_0, Q4_K, Q5_K, Q6_K = 6, 7, 11, 12, 13
+Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, Q4_K, Q5_K, Q6_K = 6, 7, 8, 9, 10, 11, 12, 13
 DTYPES = {"Q8_0": Q8_0, "Q4_0": Q4_0, "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K}
-BLOCK_ELEMS = {Q8_0: 32, Q4_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
-BLOCK_BYTES = {Q8_0: 34, Q4_0: 18, Q4_K: 144, Q5_K: 176, Q6_K: 210}
+BLOCK_ELEMS = {Q8_0: 32, Q4_0: 32, Q4_1: 32, Q5_0: 32, Q5_1: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+BLOCK_BYTES = {Q8_0: 34, Q4_0: 18, Q4_1: 20, Q5_0: 22, Q5_1: 24, Q4_K: 144, Q5_K: 176, Q6_K: 210}
 
 _lib = None
 _ref = None
@@ -90,6 +91,7 @@ def ref_lib():
         L.ref_matmul_time.restype = ctypes.c_double
         L.ref_matmul_time.argtypes = L.ref_matmul.argtypes + [ctypes.c_int]
         L.ref_last_error.restype = ctypes.c_char_p
+        L.ref_dequantize.argtypes = [ctypes.c_int, _vp, _vp, ctypes.c_longlong]
         _ref = L
     return _ref
 
@@ -145,6 +147,17 @@ def matmul_reference_impl(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int,
     out = np.zeros((M, N), dtype=np.float32)
     rc = L.ref_matmul(dtype, _p(out), _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, nthreads)
     if rc:
+        raise RuntimeError(L.ref_last_error().decode())
+    return out
+
+
+def dequantize_reference_impl(dtype: int, blocks: np.ndarray, n: int) -> np.ndarray:
+    """The reference's own CPUBackend::dequantize (oracle/_ref) of n values."""
+    L = ref_lib()
+    if L is None:
+        raise FileNotFoundError("oracle/_ref/libodi_ref.so not built")
+    out = np.zeros(n, dtype=np.float32)
+    if L.ref_dequantize(dtype, _p(out), _p(np.ascontiguousarray(blocks)), n):
         raise RuntimeError(L.ref_last_error().decode())
     return out
 

@@ -123,8 +123,8 @@ int orc_block_bytes(int dtype) {
 }
 
 static int supported(int dtype) {
-  return dtype == ORC_Q8_0 || dtype == ORC_Q4_0 || dtype == ORC_Q4_K || dtype == ORC_Q5_K ||
-         dtype == ORC_Q6_K;
+  return dtype == ORC_Q8_0 || dtype == ORC_Q4_0 || dtype == ORC_Q4_1 || dtype == ORC_Q5_0 ||
+         dtype == ORC_Q5_1 || dtype == ORC_Q4_K || dtype == ORC_Q5_K || dtype == ORC_Q6_K;
 }
 
 int64_t orc_row_bytes(int dtype, int64_t K) {
@@ -153,6 +153,43 @@ static void dec_q8_0(const uint8_t* blk, float* out, cvt_fn cvt) {
   float d = cvt(rd16(blk));
   const int8_t* qs = (const int8_t*)(blk + 2);
   for (int j = 0; j < 32; ++j) out[j] = (float)qs[j] * d;
+}
+
+/* The fifth bit of element l of a Q5_0 / Q5_1 block: bit l of the
+ * little-endian qh word. */
+static int qh_bit(const uint8_t* qh, int l) { return (qh[l >> 3] >> (l & 7)) & 1; }
+
+/* Q4_1: value = q * d + m  (cpu_backend.cpp:704-721; block d, m, qs[16]) */
+static void dec_q4_1(const uint8_t* blk, float* out, cvt_fn cvt) {
+  float d = cvt(rd16(blk)), m = cvt(rd16(blk + 2));
+  const uint8_t* qs = blk + 4;
+  for (int j = 0; j < 16; ++j) {
+    out[j] = (float)(qs[j] & 0x0F) * d + m;
+    out[j + 16] = (float)(qs[j] >> 4) * d + m;
+  }
+}
+
+/* Q5_0: value = (q - 16) * d, q = nibble | qh bit << 4  (cpu_backend.cpp:723-745;
+ * block d, qh[4], qs[16]) */
+static void dec_q5_0(const uint8_t* blk, float* out, cvt_fn cvt) {
+  float d = cvt(rd16(blk));
+  const uint8_t* qh = blk + 2;
+  const uint8_t* qs = blk + 6;
+  for (int j = 0; j < 16; ++j) {
+    out[j] = (float)(((qs[j] & 0x0F) | (qh_bit(qh, j) << 4)) - 16) * d;
+    out[j + 16] = (float)(((qs[j] >> 4) | (qh_bit(qh, j + 16) << 4)) - 16) * d;
+  }
+}
+
+/* Q5_1: value = q * d + m  (cpu_backend.cpp:747-767; block d, m, qh[4], qs[16]) */
+static void dec_q5_1(const uint8_t* blk, float* out, cvt_fn cvt) {
+  float d = cvt(rd16(blk)), m = cvt(rd16(blk + 2));
+  const uint8_t* qh = blk + 4;
+  const uint8_t* qs = blk + 8;
+  for (int j = 0; j < 16; ++j) {
+    out[j] = (float)((qs[j] & 0x0F) | (qh_bit(qh, j) << 4)) * d + m;
+    out[j + 16] = (float)((qs[j] >> 4) | (qh_bit(qh, j + 16) << 4)) * d + m;
+  }
 }
 
 /* K-quant 6-bit scale/min unpacking (GGML format, 12 bytes for 8 pairs). */
@@ -229,6 +266,9 @@ static void dec_block(int dtype, const uint8_t* blk, float* out, cvt_fn cvt) {
   switch (dtype) {
     case ORC_Q4_0: dec_q4_0(blk, out, cvt); break;
     case ORC_Q8_0: dec_q8_0(blk, out, cvt); break;
+    case ORC_Q4_1: dec_q4_1(blk, out, cvt); break;
+    case ORC_Q5_0: dec_q5_0(blk, out, cvt); break;
+    case ORC_Q5_1: dec_q5_1(blk, out, cvt); break;
     case ORC_Q4_K: dec_q4_k(blk, out, cvt); break;
     case ORC_Q5_K: dec_q5_k(blk, out, cvt); break;
     case ORC_Q6_K: dec_q6_k(blk, out, cvt); break;
@@ -300,6 +340,53 @@ static void quant_q4_0_block(const float* x, uint8_t* blk) {
 }
 
 static int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+/* Q4_1 (levels 15) / Q5_1 (levels 31), gguf 0.19.0 Q4_1 / Q5_1.quantize_blocks:
+ * d = (max - min) / levels, id = d ? 1/d : 0,
+ * q = min(levels, trunc((x - min) * id + 0.5)); d and min stored as fp16;
+ * element j in the low nibble of qs[j], element j+16 in the high nibble,
+ * the fifth bits (Q5_1) packed little-endian into qh, element j at bit j. */
+static void quant_qmin_block(const float* x, uint8_t* blk, int levels) {
+  float mx = x[0], mn = x[0];
+  for (int j = 1; j < 32; ++j) {
+    if (x[j] > mx) mx = x[j];
+    if (x[j] < mn) mn = x[j];
+  }
+  float d = (mx - mn) / (float)levels;
+  float id = (d == 0.0f) ? 0.0f : 1.0f / d;
+  wr16(blk, orc_fp32_to_fp16(d));
+  wr16(blk + 2, orc_fp32_to_fp16(mn));
+  uint8_t q[32];
+  for (int j = 0; j < 32; ++j) q[j] = (uint8_t)clampi((int)truncf((x[j] - mn) * id + 0.5f), 0, levels);
+  uint8_t* qs = blk + (levels == 31 ? 8 : 4);
+  for (int j = 0; j < 16; ++j) qs[j] = (uint8_t)((q[j] & 0x0F) | ((q[j + 16] & 0x0F) << 4));
+  if (levels == 31) {
+    memset(blk + 4, 0, 4);
+    for (int j = 0; j < 32; ++j) blk[4 + (j >> 3)] |= (uint8_t)((q[j] >> 4) << (j & 7));
+  }
+}
+
+/* Q5_0, gguf 0.19.0 Q5_0.quantize_blocks: max = the signed value of largest
+ * magnitude (first on ties), d = max / -16, id = d ? 1/d : 0,
+ * q = min(31, trunc(x*id + 16.5)); nibbles and fifth bits as Q5_1. */
+static void quant_q5_0_block(const float* x, uint8_t* blk) {
+  float amax = -1.0f, mx = 0.0f;
+  for (int j = 0; j < 32; ++j) {
+    float a = fabsf(x[j]);
+    if (a > amax) {
+      amax = a;
+      mx = x[j];
+    }
+  }
+  float d = mx / -16.0f;
+  float id = (d == 0.0f) ? 0.0f : 1.0f / d;
+  wr16(blk, orc_fp32_to_fp16(d));
+  uint8_t q[32];
+  for (int j = 0; j < 32; ++j) q[j] = (uint8_t)clampi((int)truncf(x[j] * id + 16.5f), 0, 31);
+  memset(blk + 2, 0, 4);
+  for (int j = 0; j < 32; ++j) blk[2 + (j >> 3)] |= (uint8_t)((q[j] >> 4) << (j & 7));
+  for (int j = 0; j < 16; ++j) blk[6 + j] = (uint8_t)((q[j] & 0x0F) | ((q[j + 16] & 0x0F) << 4));
+}
 
 /* Q4_K / Q5_K quantiser (this project's own; the format is GGML's).
  * Per 32-value sub-block: min mn (clamped to <= 0) and range; scale =
@@ -413,6 +500,9 @@ int orc_quantize(int dtype, const float* w, int64_t N, int64_t K, void* out) {
       switch (dtype) {
         case ORC_Q4_0: quant_q4_0_block(tmp, blk); break;
         case ORC_Q8_0: quant_q8_0_block(tmp, blk); break;
+        case ORC_Q4_1: quant_qmin_block(tmp, blk, 15); break;
+        case ORC_Q5_0: quant_q5_0_block(tmp, blk); break;
+        case ORC_Q5_1: quant_qmin_block(tmp, blk, 31); break;
         case ORC_Q4_K: quant_kq45_block(tmp, blk, 15, 0); break;
         case ORC_Q5_K: quant_kq45_block(tmp, blk, 31, 1); break;
         case ORC_Q6_K: quant_q6_k_block(tmp, blk); break;
@@ -454,10 +544,12 @@ static void* mm_worker(void* arg) {
           const int8_t* qs = (const int8_t*)(blk + 2);
           for (int64_t k = k0; k < k1; ++k) sum += am[k] * (float)qs[k - k0] * d;
         } else {
-          /* Q4_0 uses the reference's own converter; the K-quants have no
-           * reference code, so their semantics are gguf's IEEE decode. */
-          dec_block(j->dtype, blk, temp,
-                    j->dtype == ORC_Q4_0 ? orc_fp16_to_fp32_ref : orc_fp16_to_fp32);
+          /* The 32-value block types use the reference's own converter; the
+           * K-quants have no reference code, so their semantics are gguf's
+           * IEEE decode.  (The reference itself runs Q4_1 / Q5_0 / Q5_1
+           * through dequantize + matmul_f32 with a layout bug,
+           * cpu_backend.cpp:211-216; this is the product the format defines.) */
+          dec_block(j->dtype, blk, temp, be == 32 ? orc_fp16_to_fp32_ref : orc_fp16_to_fp32);
           for (int64_t k = k0; k < k1; ++k) sum += am[k] * temp[k - k0];
         }
       }
@@ -571,6 +663,26 @@ static void block_codes(int dtype, const uint8_t* blk, wcodes* c) {
       c->A[0] = orc_fp16_to_fp32(rd16(blk));
       for (int j = 0; j < 32; ++j) c->q[j] = (int8_t)blk[2 + j];
       c->gsize = 32; c->ngroups = 1; c->has_min = 0;
+      break;
+    }
+    case ORC_Q4_1:
+    case ORC_Q5_0:
+    case ORC_Q5_1: {
+      /* Q4_1 / Q5_1: d*q + m = d*q - (-m); Q5_0: (q-16)*d = d*q - 16d */
+      float d = orc_fp16_to_fp32(rd16(blk));
+      const uint8_t* qh = blk + (dtype == ORC_Q5_1 ? 4 : 2);
+      const uint8_t* qs = blk + (dtype == ORC_Q4_1 ? 4 : dtype == ORC_Q5_0 ? 6 : 8);
+      for (int j = 0; j < 16; ++j) {
+        c->q[j] = qs[j] & 0x0F;
+        c->q[j + 16] = qs[j] >> 4;
+        if (dtype != ORC_Q4_1) {
+          c->q[j] |= qh_bit(qh, j) << 4;
+          c->q[j + 16] |= qh_bit(qh, j + 16) << 4;
+        }
+      }
+      c->A[0] = d;
+      c->B[0] = dtype == ORC_Q5_0 ? 16.0f * d : -orc_fp16_to_fp32(rd16(blk + 2));
+      c->gsize = 32; c->ngroups = 1; c->has_min = 1;
       break;
     }
     case ORC_Q4_K:
@@ -749,6 +861,9 @@ int orc_fp32_bound(int dtype, const float* a, const void* b, int64_t M, int64_t 
 /* Units are stored g-major: offset = (g * KBu + kb) * unit_bytes.            */
 /*   Q4_0 slice (144 B): d[8] fp16, then qs[8][16]                            */
 /*   Q8_0 slice (272 B): d[8] fp16, then qs[8][32]                            */
+/*   Q4_1 slice (176 B): d[8], m[8] fp16, qs[8][16], 16 B pad                 */
+/*   Q5_0 slice (176 B): d[8] fp16, qh[8][4], qs[8][16]                       */
+/*   Q5_1 slice (208 B): d[8], m[8] fp16, qh[8][4], qs[8][16], 16 B pad       */
 /*   Q4_K slice (144 B): the GGUF block verbatim                              */
 /*   Q5_K slice (176 B): the GGUF block verbatim                              */
 /*   Q6_K slice (208 B): scales[16], ql[128], qh[64]; tail: d[64] fp16        */
@@ -759,6 +874,9 @@ static int slice_bytes(int dtype) {
   switch (dtype) {
     case ORC_Q4_0: return 144;
     case ORC_Q8_0: return 272;
+    case ORC_Q4_1: return 176;
+    case ORC_Q5_0: return 176;
+    case ORC_Q5_1: return 208;
     case ORC_Q4_K: return 144;
     case ORC_Q5_K: return 176;
     case ORC_Q6_K: return 208;
@@ -783,18 +901,24 @@ int64_t orc_tiled_bytes(int dtype, int64_t N, int64_t K) {
 static void move_slice(int dtype, uint8_t* row_gguf, int64_t nb_row, int64_t kb, uint8_t* slice,
                        uint8_t* tail_d, int dir) {
   int bb = orc_block_bytes(dtype);
-  if (dtype == ORC_Q4_0 || dtype == ORC_Q8_0) {
-    int qb = bb - 2;
+  if (orc_block_elems(dtype) == 32) {
+    /* fields [d][m][qh][qs] of each block, field-major over the 8 blocks:
+     * {block offset, size, slice offset} */
+    int has_m = dtype == ORC_Q4_1 || dtype == ORC_Q5_1, has_h = dtype == ORC_Q5_0 || dtype == ORC_Q5_1;
+    int f[4][3], nf = 0;
+    int boff = 2, soff = 16;
+    f[nf][0] = 0, f[nf][1] = 2, f[nf][2] = 0, ++nf;
+    if (has_m) f[nf][0] = boff, f[nf][1] = 2, f[nf][2] = soff, ++nf, boff += 2, soff += 16;
+    if (has_h) f[nf][0] = boff, f[nf][1] = 4, f[nf][2] = soff, ++nf, boff += 4, soff += 32;
+    f[nf][0] = boff, f[nf][1] = bb - boff, f[nf][2] = soff, ++nf;
     for (int j = 0; j < 8; ++j) {
       int64_t b = kb * 8 + j;
       if (b >= nb_row) break;
       uint8_t* blk = row_gguf + b * bb;
-      if (dir == 0) {
-        memcpy(slice + 2 * j, blk, 2);
-        memcpy(slice + 16 + qb * j, blk + 2, (size_t)qb);
-      } else {
-        memcpy(blk, slice + 2 * j, 2);
-        memcpy(blk + 2, slice + 16 + qb * j, (size_t)qb);
+      for (int i = 0; i < nf; ++i) {
+        uint8_t* sp = slice + f[i][2] + f[i][1] * j;
+        if (dir == 0) memcpy(sp, blk + f[i][0], (size_t)f[i][1]);
+        else memcpy(blk + f[i][0], sp, (size_t)f[i][1]);
       }
     }
     return;

@@ -42,6 +42,21 @@ int ref_matmul(int dtype, float* out, const float* a, const void* b, long long M
   }
 }
 
+// The reference's CPUBackend::dequantize (cpu_backend.cpp:625-648) of n
+// values: x a packed block buffer, out fp32 [n].  0 / 1 as ref_matmul.
+int ref_dequantize(int dtype, float* out, const void* x, long long n) {
+  try {
+    odi::CPUBackend backend(1);
+    odi::Tensor tx(const_cast<void*>(x), {n}, static_cast<odi_dtype_t>(dtype));
+    odi::Tensor to(out, {n}, ODI_DTYPE_F32);
+    backend.dequantize(to, tx);
+    return 0;
+  } catch (const std::exception& e) {
+    std::snprintf(g_err, sizeof g_err, "%s", e.what());
+    return 1;
+  }
+}
+
 // Timing helper: runs the reference matmul `reps` times on one backend object
 // and returns the total seconds (steady clock), or -1 if it threw.
 double ref_matmul_time(int dtype, float* out, const float* a, const void* b, long long M,

@@ -18,6 +18,14 @@ What each array pins:
                          (oracle/_ref) on x and the gguf-quantised W
   ragged_*               K = 80 (not a multiple of 32): reference matmul over
                          3 blocks per row, only the first 80 values used
+  q4_1/q5_0/q5_1_bytes   gguf 0.19.0 quants.quantize(W, Q4_1 / Q5_0 / Q5_1)
+  <t>_dequant            gguf 0.19.0 quants.dequantize of those bytes
+  ref_<t>_dequant        the UNMODIFIED reference CPUBackend::dequantize
+                         (cpu_backend.cpp:704-767) of the same bytes
+  ref_<t>_y              the UNMODIFIED reference CPUBackend::matmul on them:
+                         its dequantize + matmul_f32 fallback reads the
+                         [N][K] dequantized buffer as [K][N]
+                         (cpu_backend.cpp:211-216), kept as evidence of that
 """
 import os
 import sys
@@ -63,6 +71,12 @@ def main():
         out[f"{names[dt]}_dequant"] = quants.dequantize(b, gt[dt])
         out[f"ref_{names[dt]}_y"] = O.matmul_reference_impl(dt, x, b, N)
     out["act_q8_0_bytes"] = quants.quantize(x, T.Q8_0)
+    for dt, gtype, nm in ((O.Q4_1, T.Q4_1, "q4_1"), (O.Q5_0, T.Q5_0, "q5_0"), (O.Q5_1, T.Q5_1, "q5_1")):
+        b = quants.quantize(w, gtype)
+        out[f"{nm}_bytes"] = b
+        out[f"{nm}_dequant"] = quants.dequantize(b, gtype)
+        out[f"ref_{nm}_dequant"] = O.dequantize_reference_impl(dt, b, N * K).reshape(N, K)
+        out[f"ref_{nm}_y"] = O.matmul_reference_impl(dt, x, b, N)
     rng = np.random.default_rng(7)
     for dt in (O.Q4_K, O.Q5_K, O.Q6_K):
         b = O.quantize(dt, w)

@@ -208,7 +208,7 @@ def cuda_backends(cuda_lib):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K, O.Q4_1, O.Q5_0, O.Q5_1])
 @pytest.mark.parametrize("N,K,M", [(96, 512, 1), (300, 1024, 5), (4096, 4096, 1), (512, 2048, 32)])
 def test_cuda_backend_matmul(cuda_backends, dt, N, K, M):
     q8, f32 = cuda_backends
@@ -281,6 +281,30 @@ def test_cuda_backend_dequantize(cuda_backends, dt):
     b = weight(dt, N, K, seed=7)
     got = q8.dequantize(b, dt, (K, N))
     assert np.array_equal(got.reshape(N, K), O.dequantize(dt, b, N, K))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dt", [O.Q4_1, O.Q5_0, O.Q5_1])
+def test_legacy_types_cuda_correct_where_cpu_backend_reads_transposed(cuda_backends, dt):
+    """Q4_1 / Q5_0 / Q5_1: CUDABackend computes the product the block format
+    defines; the reference CPUBackend's dequantize + matmul_f32 fallback
+    reads the [N][K] dequantized weight as [K][N] (cpu_backend.cpp:211-216)
+    and returns that product instead.  Same calls, same tensors."""
+    _, f32 = cuda_backends
+    N, K, M = 64, 512, 2
+    b = weight(dt, N, K, seed=3)
+    x = O.seeded_acts(M, K, seed=4)
+    y = f32.matmul(np.full((M, N), np.nan, np.float32), x, b, dt, (K, N))
+    _check_f32(dt, x, b, N, y)
+    cpu = Backend(BACKEND_CPU)
+    try:
+        yc = cpu.matmul(np.full((M, N), np.nan, np.float32), x, b, dt, (K, N))
+    finally:
+        cpu.close()
+    deq = O.dequantize(dt, b, N, K).astype(np.float64)
+    transposed_read = x.astype(np.float64) @ deq.reshape(-1).reshape(K, N)
+    assert np.abs(yc - transposed_read).max() <= 1e-4 * np.abs(transposed_read).max()
+    assert np.abs(yc - y).max() > 0.1 * np.abs(y).max()
 
 
 @pytest.mark.gpu

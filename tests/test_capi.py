@@ -35,7 +35,7 @@ def test_python_signatures_cover_header():
     assert set(declared_symbols()) <= set(ob.SIGNATURES)
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K, O.Q4_1, O.Q5_0, O.Q5_1])
 @pytest.mark.parametrize("N,K", [(1, 256), (65, 512), (4096, 14336), (32000, 4096)])
 def test_layout_sizes_match_oracle(dt, N, K):
     assert ob.tiled_bytes(dt, N, K) == O.tiled_bytes(dt, N, K)
@@ -44,9 +44,9 @@ def test_layout_sizes_match_oracle(dt, N, K):
 
 def test_supports_dtype():
     L = ob.lib()
-    for dt in (6, 7, 11, 12, 13):
+    for dt in (6, 7, 8, 9, 10, 11, 12, 13):
         assert L.odi_cuda_supports_dtype(dt) == 1
-    for dt in (0, 1, 8, 9, 10, 14):
+    for dt in (0, 1, 2, 5, 14):
         assert L.odi_cuda_supports_dtype(dt) == 0
 
 
@@ -56,5 +56,5 @@ def test_bad_arguments_report_odi_error_codes():
     rc = L.odi_cuda_matmul(11, None, None, None, 1, 64, 300, 0, None, 0, 0, None)
     assert rc == ob.ODI_ERROR_INVALID_ARGUMENT  # K-quant K % 256 != 0
     assert b"256" in L.odi_cuda_last_error()
-    rc = L.odi_cuda_matmul(8, None, None, None, 1, 64, 256, 0, None, 0, 0, None)
-    assert rc == 202  # ODI_ERROR_MODEL_UNSUPPORTED_DTYPE for Q4_1
+    rc = L.odi_cuda_matmul(14, None, None, None, 1, 64, 256, 0, None, 0, 0, None)
+    assert rc == 202  # ODI_ERROR_MODEL_UNSUPPORTED_DTYPE for Q8_K

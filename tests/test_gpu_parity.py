@@ -20,7 +20,8 @@ import oracle as O
 
 pytestmark = pytest.mark.gpu
 
-ALL = [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K]
+LEGACY = [O.Q4_1, O.Q5_0, O.Q5_1]
+ALL = [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K] + LEGACY
 U24 = 2.0 ** -24
 
 
@@ -68,7 +69,7 @@ def test_repack_bit_exact(cuda_lib, dt, N, K):
     assert np.array_equal(back, b.reshape(-1))
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0] + LEGACY)
 @pytest.mark.parametrize("K", [32, 80, 300])
 def test_repack_ragged_bit_exact(cuda_lib, dt, K):
     b, _ = make(dt, 70, K)
@@ -91,6 +92,13 @@ def test_dequantize_golden(cuda_lib, golden):
         t = upload(cuda_lib, dt, rb, rb.shape[0], 256)
         got = cuda_lib.dequantize_dev(dt, t, rb.shape[0], 256).cpu().numpy()
         assert np.array_equal(got.view(np.uint32), golden[f"{name}_rand_dequant"].view(np.uint32))
+    # Q4_1 / Q5_0 / Q5_1: gguf's decode and the reference's own dequantize, bit for bit
+    N, K = golden["w"].shape
+    for dt, name in ((O.Q4_1, "q4_1"), (O.Q5_0, "q5_0"), (O.Q5_1, "q5_1")):
+        b = golden[f"{name}_bytes"]
+        got = cuda_lib.dequantize_dev(dt, upload(cuda_lib, dt, b, N, K), N, K).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), golden[f"{name}_dequant"].view(np.uint32))
+        assert np.array_equal(got.view(np.uint32), golden[f"ref_{name}_dequant"].view(np.uint32))
 
 
 @pytest.mark.parametrize("dt", ALL)
@@ -104,7 +112,8 @@ def test_quantize_weight_bit_exact(cuda_lib, dt, N, K):
 
 def test_quantize_weight_golden(cuda_lib, golden):
     w = golden["w"]
-    for dt, name in ((O.Q4_0, "q4_0"), (O.Q8_0, "q8_0"), (O.Q4_K, "q4k"), (O.Q5_K, "q5k"), (O.Q6_K, "q6k")):
+    for dt, name in ((O.Q4_0, "q4_0"), (O.Q8_0, "q8_0"), (O.Q4_K, "q4k"), (O.Q5_K, "q5k"), (O.Q6_K, "q6k"),
+                     (O.Q4_1, "q4_1"), (O.Q5_0, "q5_0"), (O.Q5_1, "q5_1")):
         got = cuda_lib.quantize_weight(dt, to_dev(w)).cpu().numpy()
         assert np.array_equal(got, golden[f"{name}_bytes"].reshape(-1))
 
@@ -189,7 +198,7 @@ def test_matmul_f32_small(cuda_lib, dt, N, K, M):
     check_f32(dt, x, b, N, y)
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0] + LEGACY)
 @pytest.mark.parametrize("K", [32, 80, 300, 4000])
 @pytest.mark.parametrize("mode", [0, 1])
 def test_matmul_ragged_k(cuda_lib, dt, K, mode):
@@ -233,7 +242,7 @@ def test_matmul_multi_pass_tokens(cuda_lib, dt, M):
 # Llama-2-7B decode shapes (out x in) and the 4096 x 14336 headline shape.
 FULL = [(O.Q4_K, 4096, 14336), (O.Q4_K, 4096, 4096), (O.Q4_K, 11008, 4096), (O.Q8_0, 4096, 4096),
         (O.Q8_0, 4096, 11008), (O.Q6_K, 32000, 4096), (O.Q6_K, 4096, 11008), (O.Q4_0, 4096, 4096),
-        (O.Q5_K, 4096, 4096),
+        (O.Q5_K, 4096, 4096), (O.Q4_1, 4096, 4096), (O.Q5_0, 4096, 4096), (O.Q5_1, 4096, 11008),
         # Llama-3-70B shapes (clusters of 2 with 16-span chunks, multi-wave grids)
         (O.Q4_K, 128256, 8192), (O.Q4_K, 28672, 8192), (O.Q4_K, 8192, 28672)]
 

@@ -5,7 +5,9 @@ import pytest
 
 import oracle as O
 
-NAMES = {O.Q4_0: "q4_0", O.Q8_0: "q8_0", O.Q4_K: "q4k", O.Q5_K: "q5k", O.Q6_K: "q6k"}
+NAMES = {O.Q4_0: "q4_0", O.Q8_0: "q8_0", O.Q4_1: "q4_1", O.Q5_0: "q5_0", O.Q5_1: "q5_1", O.Q4_K: "q4k",
+         O.Q5_K: "q5k", O.Q6_K: "q6k"}
+LEGACY = [O.Q4_1, O.Q5_0, O.Q5_1]
 
 
 def f32eq(a, b):
@@ -42,15 +44,15 @@ def test_fp32_to_fp16_rne(oracle_mod):
     assert np.array_equal(got, v.astype(np.float16).view(np.uint16))
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0] + LEGACY)
 def test_quantize_matches_gguf_golden(golden, dt):
     got = O.quantize(dt, golden["w"])
     assert np.array_equal(got, golden[f"{NAMES[dt]}_bytes"])
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0] + LEGACY)
 def test_fixture_scales_not_subnormal(golden, dt):
-    """Q4_0/Q8_0 scales must be normal fp16 so the reference converter is exact."""
+    """The 32-value block scales must be normal fp16 so the reference converter is exact."""
     b = golden[f"{NAMES[dt]}_bytes"]
     bb = O.BLOCK_BYTES[dt]
     d = b.reshape(-1, bb)[:, :2].copy().view(np.uint16).ravel()
@@ -78,7 +80,7 @@ def test_activation_planes_consistent_with_blocks(golden):
     assert np.array_equal(sums[..., 1], q[..., 16:].sum(-1))
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K] + LEGACY)
 def test_dequantize_matches_gguf_golden(golden, dt):
     b = golden[f"{NAMES[dt]}_bytes"]
     N, K = golden["w"].shape
@@ -127,6 +129,37 @@ def test_matmul_restatement_vs_live_reference(dt):
     assert f32eq(O.matmul_ref(dt, x, b, 48), O.matmul_reference_impl(dt, x, b, 48))
 
 
+@pytest.mark.parametrize("dt", LEGACY)
+def test_legacy_dequantize_matches_reference_golden(golden, dt):
+    """The restated Q4_1 / Q5_0 / Q5_1 decode (cpu_backend.cpp:704-767) equals
+    the reference's own CPUBackend::dequantize of the same blocks."""
+    b = golden[f"{NAMES[dt]}_bytes"]
+    N, K = golden["w"].shape
+    assert f32eq(O.dequantize(dt, b, N, K), golden[f"ref_{NAMES[dt]}_dequant"])
+
+
+@pytest.mark.parametrize("dt", LEGACY)
+def test_reference_legacy_matmul_reads_the_weight_transposed(golden, dt):
+    """The reference's matmul for Q4_1 / Q5_0 / Q5_1 dequantizes b into a
+    buffer declared [K, N] but filled in GGUF order [N][K], then multiplies
+    by it as [K][N] (cpu_backend.cpp:211-216 with 229-265).  The golden
+    output is that product (to fp32 rounding), not the one the format
+    defines; this build computes the latter (the restatement here and the
+    GPU path)."""
+    b = golden[f"{NAMES[dt]}_bytes"]
+    x = golden["x"].astype(np.float64)
+    N, K = golden["w"].shape
+    deq = O.dequantize(dt, b, N, K).astype(np.float64)
+    ref = golden[f"ref_{NAMES[dt]}_y"].astype(np.float64)
+    read_as_kn = deq.reshape(-1).reshape(K, N)
+    bound = 2.0 * (K + 16) * 2.0 ** -24 * (np.abs(x) @ np.abs(read_as_kn)) + 1e-30
+    assert (np.abs(ref - x @ read_as_kn) <= bound).all()
+    correct = x @ deq.T
+    assert np.abs(ref - correct).max() > 1e3 * bound.max()
+    y = O.matmul_ref(dt, golden["x"], b, N)
+    assert (np.abs(y - correct) <= O.fp32_bound(dt, golden["x"], b, N)).all()
+
+
 def test_reference_throws_on_kquants():
     if O.ref_lib() is None:
         pytest.skip("oracle/_ref not built")
@@ -135,7 +168,7 @@ def test_reference_throws_on_kquants():
         O.matmul_reference_impl(O.Q4_K, O.seeded_acts(1, 256), O.quantize(O.Q4_K, w), 8)
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K] + LEGACY)
 @pytest.mark.parametrize("N,K", [(1, 256), (65, 512), (130, 768), (64, 4096)])
 def test_repack_roundtrip(dt, N, K):
     w = O.seeded_weights(N, K, seed=N + K)
@@ -145,7 +178,7 @@ def test_repack_roundtrip(dt, N, K):
     assert np.array_equal(O.unpack(dt, t, N, K), b)
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0] + LEGACY)
 @pytest.mark.parametrize("K", [32, 80, 288, 300])
 def test_repack_roundtrip_ragged(dt, K):
     Kb = (K + 31) // 32 * 32
@@ -154,7 +187,7 @@ def test_repack_roundtrip_ragged(dt, K):
     assert np.array_equal(O.unpack(dt, t, 70, K), b)
 
 
-@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K])
+@pytest.mark.parametrize("dt", [O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K] + LEGACY)
 def test_q8act_bound_holds(dt):
     """The Q8-activation product stays within its analytic bound of the exact
     real product of fp32 x and the decoded weights."""
