@@ -157,8 +157,11 @@ int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t 
 /* --- the quantized matrix product ------------------------------------------ */
 
 /* Device scratch needed by odi_cuda_matmul: 256 bytes holding the device
- * error word for the streaming GEMV (activations are staged on chip, never
- * in global memory); the tensor-core path adds its fp16 activation tiles
+ * error word for the streaming GEMV with one token (its activations are
+ * staged on chip); with 2 or more tokens in ACT_Q8 mode the tokens are
+ * quantized once into Q8 records after those 256 bytes
+ * (ceil(K/256) * M * 384 bytes), so each pass of up to 8 tokens streams the
+ * weight once; the tensor-core path adds its fp16 activation tiles
  * (1024 + ceil(M/256)*256 * ceil(K/256)*256 * 2 bytes). */
 size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode);
 
@@ -172,7 +175,8 @@ int odi_cuda_tc_supported(int dtype);
  *   d_workspace: at least odi_cuda_matmul_workspace_bytes, zero before its
  *     first use (a call leaves it zero unless a kernel wait gave up; see
  *     odi_cuda_workspace_status).
- * One kernel launch per 8 tokens.  Asynchronous on `stream`. */
+ * One kernel launch per 8 tokens (plus one quantizing the tokens when there
+ * are 2 or more in ACT_Q8 mode).  Asynchronous on `stream`. */
 int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M,
                     int64_t N, int64_t K, int act_mode, void* d_workspace,
                     size_t workspace_bytes, int flags, void* stream);
@@ -199,7 +203,10 @@ typedef struct odi_cuda_matmul_opts {
 } odi_cuda_matmul_opts;
 
 /* odi_cuda_matmul with the operations above (ACT_Q8 / ACT_F32, and AUTO
- * below ODI_CUDA_TC_MIN_TOKENS); opts == NULL is odi_cuda_matmul. */
+ * below ODI_CUDA_TC_MIN_TOKENS); opts == NULL is odi_cuda_matmul.  With an
+ * RMSNorm or SwiGLU prologue the activations are staged on chip (256 bytes
+ * of workspace suffice); otherwise the workspace rules of odi_cuda_matmul
+ * apply (a smaller workspace is accepted and takes the on-chip path). */
 int odi_cuda_matmul_fused(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M,
                           int64_t N, int64_t K, int act_mode, void* d_workspace, size_t workspace_bytes,
                           int flags, const odi_cuda_matmul_opts* opts, void* stream);

@@ -61,6 +61,51 @@ __global__ void act_quant_q8_kernel(const float* __restrict__ x, int64_t M, int6
   }
 }
 
+// act_q8_records: fp32 x [M][ldx] -> the streaming GEMV's Q8 activation
+// records, span-major: record (kb, m) at (kb * M + m) * Q8_REC_BYTES holds the
+// 256 codes of span kb then 8 x {dx, sdx, sdx_lo, sdx_hi} (fp32: the fp16
+// scale widened, and the block / half-block code sums times dx), zero past
+// K.  One warp per 32-value block, lane = value; the arithmetic is the GEMV's
+// own staging quantiser's, so the records are bit-identical to the ones it
+// builds in shared memory.
+__global__ void act_q8_records_kernel(const float* __restrict__ x, int64_t ldx, int64_t M, int64_t K, int64_t KB,
+                                      uint8_t* __restrict__ recs) {
+  pdl_wait();  // x may be written by the previous kernel on the stream
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t total = KB * M * 8;
+  for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += nwarps) {
+    const int64_t kb = w / (M * 8);
+    const int64_t rem = w - kb * M * 8;
+    const int64_t m = rem >> 3;
+    const int j = (int)(rem & 7);
+    const int64_t k = kb * 256 + 32 * j + lane;
+    const float v = k < K ? x[m * ldx + k] : 0.0f;
+    float am = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const float d = __fdiv_rn(am, 127.0f);
+    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+    const int q = (int)roundf(__fmul_rn(v, id));
+    int s = q;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);  // within 16-lane halves
+    const int s_lo = __shfl_sync(0xffffffffu, s, 0), s_hi = __shfl_sync(0xffffffffu, s, 16);
+    uint8_t* rec = recs + (kb * M + m) * Q8_REC_BYTES;
+    rec[32 * j + lane] = (uint8_t)(int8_t)q;
+    if (lane == 0) {
+      const float dx = __half2float(__float2half_rn(d));
+      float4 r;
+      r.x = dx;
+      r.y = __fmul_rn((float)(s_lo + s_hi), dx);
+      r.z = __fmul_rn((float)s_lo, dx);
+      r.w = __fmul_rn((float)s_hi, dx);
+      *reinterpret_cast<float4*>(rec + 256 + 16 * j) = r;
+    }
+  }
+}
+
 __global__ void act_pack_f32_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t Kp,
                                     float* __restrict__ tiles) {
   pdl_wait();
@@ -104,6 +149,16 @@ cudaError_t launch_act_quant(const float* x, int64_t M, int64_t K, uint8_t* tile
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = small_cfg(grid_for(warps * 32, 256), pdl, stream, attr);
   return cudaLaunchKernelEx(&cfg, act_quant_q8_kernel, x, M, K, Kp, tiles, blocks);
+}
+
+cudaError_t launch_act_q8_records(const float* x, int64_t ldx, int64_t M, int64_t K, uint8_t* recs, bool pdl,
+                                  cudaStream_t stream) {
+  const int64_t KB = (K + 255) / 256;
+  const int64_t warps = KB * M * 8;
+  if (warps == 0) return cudaSuccess;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = small_cfg(grid_for(warps * 32, 256), pdl, stream, attr);
+  return cudaLaunchKernelEx(&cfg, act_q8_records_kernel, x, ldx, M, K, KB, recs);
 }
 
 cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* tiles, bool pdl,

@@ -76,12 +76,25 @@ int check_shape(int dt, int64_t N, int64_t K) {
   return ODI_CUDA_OK;
 }
 
+// Multi-token ACT_Q8 products without an activation prologue quantize the
+// tokens once, into Q8 records after the workspace header
+// (act_q8_records_kernel), so a pass of up to 8 tokens stages 384 bytes per
+// (span, token) instead of the fp32 row and streams the weight once.
+size_t q8_records_bytes(int64_t M, int64_t K) { return (size_t)((K + 255) / 256) * (size_t)M * Q8_REC_BYTES; }
+bool wants_records(bool f32, int64_t M, const GemvFuse* fu) {
+  return !f32 && M >= 2 && !(fu && (fu->norm_w || fu->swiglu));
+}
+
 // The streaming GEMV over M tokens: one launch per pass of plan.mt tokens.
 // With `sc`, each pass scatters its rows into every rank's gathered buffer.
 int run_gemv(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N, int64_t K,
-             bool f32, int* err, bool pdl, cudaStream_t s, const GemvScatter* sc, const GemvFuse* fu = nullptr) {
+             bool f32, int* err, size_t ws_bytes, bool pdl, cudaStream_t s, const GemvScatter* sc,
+             const GemvFuse* fu = nullptr) {
   const int64_t ldx = (fu && fu->swiglu) ? 2 * K : K;
-  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current());
+  const bool pre = wants_records(f32, M, fu) && ws_bytes >= WS_HEADER + q8_records_bytes(M, K);
+  uint8_t* recs = reinterpret_cast<uint8_t*>(err) + WS_HEADER;
+  if (pre) CK(launch_act_q8_records(d_x, ldx, M, K, recs, pdl, s), "act_q8_records launch");
+  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current(), pre);
   if (plan.C == 0)
     return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
   for (int64_t m0 = 0; m0 < M; m0 += plan.mt) {
@@ -95,6 +108,8 @@ int run_gemv(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int
     a.ldx = ldx;
     a.fu = fu ? *fu : GemvFuse{};
     a.M = (int)((M - m0) < plan.mt ? (M - m0) : plan.mt);
+    a.recs = plan.pre ? recs + m0 * Q8_REC_BYTES : nullptr;
+    a.rec_ld = M;
     a.sc = GemvScatter{};
     if (sc) {
       a.sc = *sc;
@@ -267,9 +282,12 @@ int odi_cuda_tc_supported(int dtype) { return tc_supported(dtype) ? 1 : 0; }
 
 size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode) {
   if (!dtype_ok(dtype) || M < 1 || N < 1 || K < 1) return 0;
-  if (resolve_act_mode(dtype, M, act_mode) == ODI_CUDA_ACT_F16)
+  const int mode = resolve_act_mode(dtype, M, act_mode);
+  if (mode == ODI_CUDA_ACT_F16)
     return (size_t)(TC_X16_OFFSET + tc_x16_bytes(M, K));  // error word + fp16 activation tiles
-  return WS_HEADER;  // the device error word; activations are staged on chip
+  if (wants_records(mode == ODI_CUDA_ACT_F32, M, nullptr))
+    return WS_HEADER + q8_records_bytes(M, K);  // error word + the tokens' Q8 records
+  return WS_HEADER;  // the device error word; one token's activations are staged on chip
 }
 
 int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N,
@@ -307,7 +325,7 @@ int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d
   }
   const bool f32 = mode == ODI_CUDA_ACT_F32;
   const bool pdl = (flags & ODI_CUDA_FLAG_PDL) != 0;
-  return run_gemv(dtype, d_w_tiled, d_x, d_y, M, N, K, f32, (int*)d_workspace, pdl, s, nullptr);
+  return run_gemv(dtype, d_w_tiled, d_x, d_y, M, N, K, f32, (int*)d_workspace, workspace_bytes, pdl, s, nullptr);
 }
 
 int odi_cuda_matmul_fused(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N,
@@ -337,7 +355,7 @@ int odi_cuda_matmul_fused(int dtype, const void* d_w_tiled, const float* d_x, fl
   fu.ssq_in = opts->norm_ssq;
   fu.ssq_n = opts->norm_ssq_count;
   fu.ssq_out = opts->out_ssq;
-  return run_gemv(dtype, d_w_tiled, d_x, d_y, M, N, K, mode == ODI_CUDA_ACT_F32, (int*)d_workspace,
+  return run_gemv(dtype, d_w_tiled, d_x, d_y, M, N, K, mode == ODI_CUDA_ACT_F32, (int*)d_workspace, workspace_bytes,
                   (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, nullptr, &fu);
 }
 
@@ -491,7 +509,9 @@ int64_t odi_cuda_scatter_signals(int dtype, int64_t M, int64_t N, int64_t K, int
   if (!dtype_ok(dtype) || M < 1 || N < 1 || K < 1) return -1;
   const int mode = resolve_act_mode(dtype, M, act_mode);
   if (mode != ODI_CUDA_ACT_Q8 && mode != ODI_CUDA_ACT_F32) return -1;
-  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), mode == ODI_CUDA_ACT_F32, num_sms_current());
+  const bool f32 = mode == ODI_CUDA_ACT_F32;
+  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current(),
+                                       wants_records(f32, M, nullptr));
   if (plan.C == 0) return -1;
   return (M + plan.mt - 1) / plan.mt;  // one arrival per launch (pass)
 }
@@ -515,7 +535,11 @@ int odi_cuda_matmul_scatter(int dtype, const void* d_w_tiled, const float* d_x, 
   if (!d_w_tiled || !d_x || !d_workspace) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
   if (((uintptr_t)d_w_tiled | (uintptr_t)d_workspace) & 15)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight and workspace must be 16-byte aligned");
-  if (workspace_bytes < WS_HEADER) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small");
+  // the pass count must be the one odi_cuda_scatter_signals reported: the
+  // multi-token records need their workspace
+  const size_t need = odi_cuda_matmul_workspace_bytes(dtype, M, N, K, mode);
+  if (workspace_bytes < need)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
   GemvScatter g{};
   for (int p = 0; p < sc->nranks; ++p) {
     g.out[p] = sc->out[p];
@@ -526,7 +550,7 @@ int odi_cuda_matmul_scatter(int dtype, const void* d_w_tiled, const float* d_x, 
   g.row0 = sc->row0;
   g.ld = sc->ld;
   return run_gemv(dtype, d_w_tiled, d_x, nullptr, M, N, K, mode == ODI_CUDA_ACT_F32, (int*)d_workspace,
-                  (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, &g);
+                  workspace_bytes, (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, &g);
 }
 
 int odi_cuda_wait_peers(const unsigned long long* d_counters, unsigned long long* d_consumed,

@@ -72,6 +72,9 @@ inline bool dtype_ok(int dt) { return is_block32(dt) || dt == Q4_K || dt == Q5_K
 // holds the 256 fp32 values, zero past K.
 // ----------------------------------------------------------------------------
 constexpr int ACT_Q8_BYTES = 320;
+// The streaming GEMV's Q8 record of one (span, token), as it sits in shared
+// memory: 256 int8 codes, then 8 x {dx, sdx, sdx_lo, sdx_hi} fp32.
+constexpr int Q8_REC_BYTES = 384;
 constexpr int ACT_F32_BYTES = 1024;
 
 struct ActRec {

@@ -7,6 +7,8 @@ namespace odi_cuda {
 
 cudaError_t launch_act_quant(const float* x, int64_t M, int64_t K, uint8_t* tiles, uint8_t* blocks,
                              bool pdl, cudaStream_t stream);
+cudaError_t launch_act_q8_records(const float* x, int64_t ldx, int64_t M, int64_t K, uint8_t* recs, bool pdl,
+                                  cudaStream_t stream);
 cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* tiles, bool pdl,
                                 cudaStream_t stream);
 cudaError_t launch_repack(int dt, const void* gguf, void* tiled, int64_t N, int64_t K, cudaStream_t s);
@@ -27,6 +29,7 @@ struct GemvPlan {
   int xq_bytes;      // staged activations: chunk * mt records, 128-aligned
   int smem_bytes;    // dynamic shared memory per CTA
   int mt;            // tokens per pass (template instantiation)
+  int pre;           // activations arrive as Q8 records (Q8_REC_BYTES), quantized beforehand
 };
 
 // Output scatter of a row shard into every rank's gathered buffer (the
@@ -67,10 +70,16 @@ struct GemvArgs {
   int M;              // tokens in this pass (<= mt)
   GemvScatter sc;     // row offset of this pass's tokens is folded into sc.out
   GemvFuse fu;
+  // Pre-quantized activations (plan.pre): Q8 records of this pass's first
+  // token, record (kb, m) at recs + (kb * rec_ld + m) * Q8_REC_BYTES
+  const uint8_t* recs;
+  int64_t rec_ld;
 };
 
 // Plan for dtype / tokens / fp32-activation mode on a device with num_sms SMs.
-GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms);
+// pre: the activations are quantized beforehand into Q8 records (ACT_Q8
+// only), so a record takes Q8_REC_BYTES of shared memory, not the fp32 staging.
+GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms, bool pre = false);
 cudaError_t launch_gemv(int dt, bool f32act, const GemvPlan& plan, const GemvArgs& a, bool pdl,
                         cudaStream_t s);
 

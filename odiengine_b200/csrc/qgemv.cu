@@ -11,12 +11,13 @@ static int tokens_per_pass(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 
 // distributed-shared-memory reduction per tile.  Estimated time in units of
 // one span, per CTA slot: waves * (chunk + 1) (+ half a CTA of tail when the
 // grid needs more than one wave) (+ the reduction and cluster cost).
-GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms) {
+GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms, bool pre) {
   GemvPlan p{};
   p.G = (int)((N + UNIT_ROWS - 1) / UNIT_ROWS);
   p.KB = (int)((K + UNIT_COLS - 1) / UNIT_COLS);
   const int slots = CTAS_PER_SM * (num_sms > 0 ? num_sms : 148);
-  (void)f32act;
+  p.pre = (pre && !f32act) ? 1 : 0;
+  const int rec = p.pre ? Q8_REC_BYTES : XR_STRIDE;
   p.mt = tokens_per_pass(M);
   for (;;) {
     double best = 1e30;
@@ -25,7 +26,7 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
       if (C > p.KB) break;
       const int chunk = (p.KB + C - 1) / C;
       const int ceff = (p.KB + chunk - 1) / chunk;
-      if ((int64_t)chunk * p.mt * XR_STRIDE > XR_BUDGET) continue;
+      if ((int64_t)chunk * p.mt * rec > XR_BUDGET) continue;
       const double ctas = (double)p.G * ceff;
       const double waves = ctas / slots;
       double t = (waves > 1.0 ? waves : 1.0) * (chunk + 1);
@@ -51,7 +52,7 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
     }
     p.mt /= 2;
   }
-  p.xq_bytes = (p.chunk * p.mt * XR_STRIDE + 127) / 128 * 128;
+  p.xq_bytes = (p.chunk * p.mt * rec + 127) / 128 * 128;
   p.stage_bytes = (unit_bytes(dt) + 127) / 128 * 128;
   const int xr_off = p.mt == 1 ? SmemMap<1>::xr(p.C)
                      : p.mt == 2 ? SmemMap<2>::xr(p.C)
@@ -73,9 +74,9 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
   return p;
 }
 
-template <int DT, int MT, bool F32>
+template <int DT, int MT, bool F32, bool PRE>
 static cudaError_t launch_t(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
-  auto kern = qgemv_kernel<DT, MT, F32>;
+  auto kern = qgemv_kernel<DT, MT, F32, PRE>;
   // The shared-memory opt-in is per function and per device.
   static bool attr_set[64] = {};
   int dev = 0;
@@ -113,11 +114,19 @@ static cudaError_t launch_t(const GemvPlan& pl, const GemvArgs& a, bool pdl, cud
 
 template <int DT, bool F32>
 static cudaError_t launch_mt(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
+  if (!F32 && pl.pre) {  // pre-quantized records: multi-token passes only
+    switch (pl.mt) {
+      case 1: return launch_t<DT, 1, F32, false>(pl, a, pdl, s);
+      case 2: return launch_t<DT, 2, F32, !F32>(pl, a, pdl, s);
+      case 4: return launch_t<DT, 4, F32, !F32>(pl, a, pdl, s);
+      default: return launch_t<DT, 8, F32, !F32>(pl, a, pdl, s);
+    }
+  }
   switch (pl.mt) {
-    case 1: return launch_t<DT, 1, F32>(pl, a, pdl, s);
-    case 2: return launch_t<DT, 2, F32>(pl, a, pdl, s);
-    case 4: return launch_t<DT, 4, F32>(pl, a, pdl, s);
-    default: return launch_t<DT, 8, F32>(pl, a, pdl, s);
+    case 1: return launch_t<DT, 1, F32, false>(pl, a, pdl, s);
+    case 2: return launch_t<DT, 2, F32, false>(pl, a, pdl, s);
+    case 4: return launch_t<DT, 4, F32, false>(pl, a, pdl, s);
+    default: return launch_t<DT, 8, F32, false>(pl, a, pdl, s);
   }
 }
 

@@ -212,9 +212,8 @@ __device__ __forceinline__ void prologue8(const GemvArgs& a, int kb0, int r, int
 // Staging: x (or the gate half of a SwiGLU input) of every span of the chunk
 // by cp.async in one group, so it costs one memory round trip whatever the
 // chunk length.  The RMSNorm sum of squares is reduced while the copies fly.
-// Then one warp per staged (span, token) applies the prologue -- its second
-// input read one record ahead, so its latency overlaps the previous record
-// -- and quantises.
+// Then each warp applies the prologue to two staged (span, token) records at
+// a time -- their second inputs loaded together -- and quantises them.
 template <bool F32, int MT>
 __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr,
                                            float* __restrict__ fuse_smem) {
@@ -234,82 +233,132 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
   if (a.fu.norm_w) row_rms<MT>(a, fuse_smem, fuse_smem + MT);  // overlaps the copies
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   consumer_sync();
-  // lane = (block b = lane/4, 8 values)
+  // lane = (block b = lane/4, 8 values).  A warp takes two records per
+  // iteration (records r and r + NCW), so their dependent chains (reduce,
+  // divide, round, shuffle) interleave.
   const int b = lane >> 2, part = lane & 3;
   const int off = 32 * b + 8 * part;
   const int nrec = nsp * a.M;
   const bool pro = a.fu.swiglu || a.fu.norm_w;
-  float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0;
-  if (pro && warp < nrec) prologue8(a, kb0, warp, off, n0, n1);
-  for (int r = warp; r < nrec; r += NCW) {
-    const int j = r / a.M, m = r - j * a.M;
-    uint8_t* rec = xr + (j * MT + m) * XR_STRIDE;
-    float4 v0 = lds128f(rec + 4 * off);
-    float4 v1 = lds128f(rec + 4 * (off + 4));
+  for (int r0 = warp; r0 < nrec; r0 += 2 * NCW) {
+    const bool two = r0 + NCW < nrec;
+    uint8_t* rec[2];
+    float vv[2][8];
+    int mi[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int ri = (i == 1 && two) ? r0 + NCW : r0;
+      const int j = ri / a.M;
+      mi[i] = ri - j * a.M;
+      rec[i] = xr + (j * MT + mi[i]) * XR_STRIDE;
+      const float4 v0 = lds128f(rec[i] + 4 * off), v1 = lds128f(rec[i] + 4 * (off + 4));
+      vv[i][0] = v0.x; vv[i][1] = v0.y; vv[i][2] = v0.z; vv[i][3] = v0.w;
+      vv[i][4] = v1.x; vv[i][5] = v1.y; vv[i][6] = v1.z; vv[i][7] = v1.w;
+    }
     if (pro) {
-      const float4 e0 = n0, e1 = n1;
-      if (r + NCW < nrec) prologue8(a, kb0, r + NCW, off, n0, n1);
-      float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      const float ee[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
-      if (a.fu.swiglu) {
+      float4 e0[2], e1[2];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) vv[e] = silu_f(vv[e]) * ee[e];  // past K: silu(0) * 0
-      } else {
-        const float rr = fuse_smem[m];
+      for (int i = 0; i < 2; ++i) prologue8(a, kb0, (i == 1 && two) ? r0 + NCW : r0, off, e0[i], e1[i]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) vv[e] = vv[e] * rr * ee[e];
+      for (int i = 0; i < 2; ++i) {
+        const float ee[8] = {e0[i].x, e0[i].y, e0[i].z, e0[i].w, e1[i].x, e1[i].y, e1[i].z, e1[i].w};
+        if (a.fu.swiglu) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) vv[i][e] = silu_f(vv[i][e]) * ee[e];  // past K: silu(0) * 0
+        } else {
+          const float rr = fuse_smem[mi[i]];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) vv[i][e] = vv[i][e] * rr * ee[e];
+        }
       }
-      v0 = make_float4(vv[0], vv[1], vv[2], vv[3]);
-      v1 = make_float4(vv[4], vv[5], vv[6], vv[7]);
       if (F32) {  // the fp32 dot reads the staged values
-        *reinterpret_cast<float4*>(rec + 4 * off) = v0;
-        *reinterpret_cast<float4*>(rec + 4 * (off + 4)) = v1;
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (i == 1 && !two) break;
+          *reinterpret_cast<float4*>(rec[i] + 4 * off) = make_float4(vv[i][0], vv[i][1], vv[i][2], vv[i][3]);
+          *reinterpret_cast<float4*>(rec[i] + 4 * (off + 4)) = make_float4(vv[i][4], vv[i][5], vv[i][6], vv[i][7]);
+        }
       }
     }
     if (F32) {
-      float s = ((v0.x + v0.y) + (v0.z + v0.w)) + ((v1.x + v1.y) + (v1.z + v1.w));
-      s += __shfl_xor_sync(0xffffffffu, s, 1);  // 16-value sums (parts 0-1, 2-3)
-      if ((part & 1) == 0) reinterpret_cast<float*>(rec + XR_VALS)[2 * b + (part >> 1)] = s;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        float s = ((vv[i][0] + vv[i][1]) + (vv[i][2] + vv[i][3])) + ((vv[i][4] + vv[i][5]) + (vv[i][6] + vv[i][7]));
+        s += __shfl_xor_sync(0xffffffffu, s, 1);  // 16-value sums (parts 0-1, 2-3)
+        if ((part & 1) == 0 && (i == 0 || two)) reinterpret_cast<float*>(rec[i] + XR_VALS)[2 * b + (part >> 1)] = s;
+      }
       continue;
     }
-    float am = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
-                     fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-    const float d = __fdiv_rn(am, 127.0f);
-    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    uint32_t packed[2] = {0u, 0u};
-    int s = 0;
+    float dq[2], dx[2];
+    int sh[2], sf[2], shi[2];
+    uint32_t packed[2][2];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int qq = (int)roundf(__fmul_rn(vv[e], id));
-      s += qq;
-      packed[e >> 2] |= (uint32_t)(qq & 0xFF) << (8 * (e & 3));
+    for (int i = 0; i < 2; ++i) {
+      float am = fmaxf(fmaxf(fmaxf(fabsf(vv[i][0]), fabsf(vv[i][1])), fmaxf(fabsf(vv[i][2]), fabsf(vv[i][3]))),
+                       fmaxf(fmaxf(fabsf(vv[i][4]), fabsf(vv[i][5])), fmaxf(fabsf(vv[i][6]), fabsf(vv[i][7]))));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      dq[i] = __fdiv_rn(am, 127.0f);
     }
-    const int s_half = s + __shfl_xor_sync(0xffffffffu, s, 1);        // 16 codes: parts 0-1 or 2-3
-    const int s_full = s_half + __shfl_xor_sync(0xffffffffu, s_half, 2);
-    const int s_hi = __shfl_sync(0xffffffffu, s_half, (lane & ~3) | 2);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float id = dq[i] == 0.0f ? 0.0f : __fdiv_rn(1.0f, dq[i]);
+      packed[i][0] = packed[i][1] = 0u;
+      int sacc = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int qq = (int)roundf(__fmul_rn(vv[i][e], id));
+        sacc += qq;
+        packed[i][e >> 2] |= (uint32_t)(qq & 0xFF) << (8 * (e & 3));
+      }
+      sh[i] = sacc + __shfl_xor_sync(0xffffffffu, sacc, 1);  // 16 codes: parts 0-1 or 2-3
+      sf[i] = sh[i] + __shfl_xor_sync(0xffffffffu, sh[i], 2);
+      shi[i] = __shfl_sync(0xffffffffu, sh[i], (lane & ~3) | 2);
+      dx[i] = __half2float(__float2half_rn(dq[i]));
+    }
     __syncwarp();  // every lane has read its fp32 values before codes land on them
-    *reinterpret_cast<uint2*>(rec + 32 * b + 8 * part) = make_uint2(packed[0], packed[1]);
-    if (part == 0) {
-      const float dx = __half2float(__float2half_rn(d));
-      XRec rq;
-      rq.dx = dx;
-      rq.sdx = __fmul_rn((float)s_full, dx);
-      rq.sdx_lo = __fmul_rn((float)s_half, dx);
-      rq.sdx_hi = __fmul_rn((float)s_hi, dx);
-      *reinterpret_cast<XRec*>(rec + 256 + 16 * b) = rq;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      if (i == 1 && !two) break;
+      *reinterpret_cast<uint2*>(rec[i] + 32 * b + 8 * part) = make_uint2(packed[i][0], packed[i][1]);
+      if (part == 0) {
+        XRec rq;
+        rq.dx = dx[i];
+        rq.sdx = __fmul_rn((float)sf[i], dx[i]);
+        rq.sdx_lo = __fmul_rn((float)sh[i], dx[i]);
+        rq.sdx_hi = __fmul_rn((float)shi[i], dx[i]);
+        *reinterpret_cast<XRec*>(rec[i] + 256 + 16 * b) = rq;
+      }
     }
     __syncwarp();
   }
   consumer_sync();
 }
 
+// Pre-quantized staging: the chunk's Q8 records, made by
+// act_q8_records_kernel, copied as they are (16-byte cp.async by all 128
+// consumer threads, one memory round trip); record (j, m) of the chunk to
+// xr + (j * MT + m) * Q8_REC_BYTES.
+template <int MT>
+__device__ __forceinline__ void stage_records(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr) {
+  constexpr int V = Q8_REC_BYTES / 16;  // 16-byte pieces per record
+  const int per_span = a.M * V;
+  for (int c = threadIdx.x; c < nsp * per_span; c += NCW * 32) {
+    const int j = c / per_span, rem = c - j * per_span;
+    const int m = rem / V, v = rem - m * V;
+    cp_async16(xr + (j * MT + m) * Q8_REC_BYTES + 16 * v,
+               a.recs + ((int64_t)(kb0 + j) * a.rec_ld + m) * Q8_REC_BYTES + 16 * v, 16);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  consumer_sync();
+}
+
 // ---------------------------------------------------------------------------
 // ACT_Q8 units: one lane, one row, the whole 256-column span, MT tokens.
 // ---------------------------------------------------------------------------
-template <int MT>
+template <int MT, int RS>
 __device__ __forceinline__ void unit_q8_q4k(const uint8_t* __restrict__ sl, const uint8_t* __restrict__ xs, int M,
                                             float (&acc)[MT], bool five) {
   const uint4 hd = lds128(sl);
@@ -359,7 +408,7 @@ __device__ __forceinline__ void unit_q8_q4k(const uint8_t* __restrict__ sl, cons
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       if (m < M) {
-        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint8_t* xr = xs + m * RS;
         const uint4 x0 = lds128(xr + 64 * p), x1 = lds128(xr + 64 * p + 16);
         const uint4 x2 = lds128(xr + 64 * p + 32), x3 = lds128(xr + 64 * p + 48);
         const float4 ra = lds128f(xr + 256 + 32 * p), rb = lds128f(xr + 256 + 32 * p + 16);
@@ -376,7 +425,7 @@ __device__ __forceinline__ void unit_q8_q4k(const uint8_t* __restrict__ sl, cons
   }
 }
 
-template <int MT>
+template <int MT, int RS>
 __device__ __forceinline__ void unit_q8_q6k(const uint8_t* __restrict__ sl, float d, const uint8_t* __restrict__ xs,
                                             int M, float (&acc)[MT]) {
   const uint4 scv = lds128(sl);  // 16 int8 scales
@@ -412,7 +461,7 @@ __device__ __forceinline__ void unit_q8_q6k(const uint8_t* __restrict__ sl, floa
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         if (m < M) {
-          const uint8_t* xr = xs + m * XR_STRIDE;
+          const uint8_t* xr = xs + m * RS;
           const int xo = 128 * h + 32 * cl;
           const uint4 x0 = lds128(xr + xo), x1 = lds128(xr + xo + 16);
           const uint4 x2 = lds128(xr + xo + 64), x3 = lds128(xr + xo + 80);
@@ -434,7 +483,7 @@ __device__ __forceinline__ void unit_q8_q6k(const uint8_t* __restrict__ sl, floa
   }
 }
 
-template <int MT>
+template <int MT, int RS>
 __device__ __forceinline__ void unit_q8_q8_0(const uint8_t* __restrict__ sl, const uint8_t* __restrict__ xs, int M,
                                              float (&acc)[MT]) {
   const uint4 dv = lds128(sl);
@@ -446,7 +495,7 @@ __device__ __forceinline__ void unit_q8_q8_0(const uint8_t* __restrict__ sl, con
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       if (m < M) {
-        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint8_t* xr = xs + m * RS;
         const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
         const float dx = *reinterpret_cast<const float*>(xr + 256 + 16 * j);
         const int dd = dot16<false>(q1, x1, dot16<false>(q0, x0, 0));
@@ -456,7 +505,7 @@ __device__ __forceinline__ void unit_q8_q8_0(const uint8_t* __restrict__ sl, con
   }
 }
 
-template <int MT>
+template <int MT, int RS>
 __device__ __forceinline__ void unit_q8_q4_0(const uint8_t* __restrict__ sl, const uint8_t* __restrict__ xs, int M,
                                              float (&acc)[MT]) {
   const uint4 dv = lds128(sl);
@@ -469,7 +518,7 @@ __device__ __forceinline__ void unit_q8_q4_0(const uint8_t* __restrict__ sl, con
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       if (m < M) {
-        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint8_t* xr = xs + m * RS;
         const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
         const float2 r = *reinterpret_cast<const float2*>(xr + 256 + 16 * j);  // dx, sdx
         // (q - 8) . x = lo . x0 + (hi . x1) / 16 - 8 * sum(x); the division is exact
@@ -495,7 +544,7 @@ __device__ __forceinline__ uint4 fifth_bits16(uint32_t qh, int base) {
 // code.  The integer dot of the codes with the int8 activations is exact;
 // the min (or the -16 offset) folds into the block's sum of activation
 // codes: sum((d q + m) x) = d dx sum(q xq) + m sdx.
-template <int DT, int MT>
+template <int DT, int MT, int RS>
 __device__ __forceinline__ void unit_q8_legacy(const uint8_t* __restrict__ sl, const uint8_t* __restrict__ xs,
                                                int M, float (&acc)[MT]) {
   constexpr bool FIVE = has_qh(DT), MIN = has_min(DT);
@@ -533,7 +582,7 @@ __device__ __forceinline__ void unit_q8_legacy(const uint8_t* __restrict__ sl, c
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       if (m < M) {
-        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint8_t* xr = xs + m * RS;
         const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
         const float2 r = *reinterpret_cast<const float2*>(xr + 256 + 16 * j);  // dx, sdx
         const int dd = FIVE ? dot16<false>(lo, x0, dot16<false>(hi, x1, 0))
@@ -644,7 +693,7 @@ __device__ __forceinline__ void unit_f32(const uint8_t* __restrict__ sl, float t
   }
 }
 
-template <int DT, int MT, bool F32>
+template <int DT, int MT, bool F32, int RS>
 __device__ __forceinline__ void unit(const uint8_t* __restrict__ st, int row, const uint8_t* __restrict__ xs, int M,
                                      float (&acc)[MT]) {
   const uint8_t* sl = st + row * slice_bytes(DT);
@@ -652,17 +701,17 @@ __device__ __forceinline__ void unit(const uint8_t* __restrict__ st, int row, co
   if (F32) {
     unit_f32<DT, MT>(sl, tail_d, xs, M, acc);
   } else if (DT == Q4_K) {
-    unit_q8_q4k<MT>(sl, xs, M, acc, false);
+    unit_q8_q4k<MT, RS>(sl, xs, M, acc, false);
   } else if (DT == Q5_K) {
-    unit_q8_q4k<MT>(sl, xs, M, acc, true);
+    unit_q8_q4k<MT, RS>(sl, xs, M, acc, true);
   } else if (DT == Q6_K) {
-    unit_q8_q6k<MT>(sl, tail_d, xs, M, acc);
+    unit_q8_q6k<MT, RS>(sl, tail_d, xs, M, acc);
   } else if (DT == Q8_0) {
-    unit_q8_q8_0<MT>(sl, xs, M, acc);
+    unit_q8_q8_0<MT, RS>(sl, xs, M, acc);
   } else if (DT == Q4_1 || DT == Q5_0 || DT == Q5_1) {
-    unit_q8_legacy<DT, MT>(sl, xs, M, acc);
+    unit_q8_legacy<DT, MT, RS>(sl, xs, M, acc);
   } else {
-    unit_q8_q4_0<MT>(sl, xs, M, acc);
+    unit_q8_q4_0<MT, RS>(sl, xs, M, acc);
   }
 }
 
@@ -683,6 +732,11 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* local, int rank) {
 }
 __device__ __forceinline__ void st_dsmem_f32(uint32_t remote, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_dsmem_v4(uint32_t remote, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
@@ -718,7 +772,8 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 //   red   [2][64][MT] fp32  the two unit-parity sums of each row
 //   part  [C][MT*64] fp32   tile partials; rank 0 receives those of the other
 //                           ranks here over distributed shared memory
-//   xr    chunk x MT records of XR_STRIDE bytes: staged activations
+//   xr    chunk x MT records of XR_STRIDE (Q8_REC_BYTES when pre-quantized)
+//         bytes: staged activations
 //   ring  stages x stage_bytes weight units
 template <int MT>
 struct SmemMap {
@@ -775,8 +830,9 @@ __device__ __forceinline__ void signal_peers(const GemvArgs& a) {
 // ---------------------------------------------------------------------------
 // The kernel: grid = G * C CTAs, clusters of C along x.
 // ---------------------------------------------------------------------------
-template <int DT, int MT, bool F32>
+template <int DT, int MT, bool F32, bool PRE>
 __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const GemvArgs a, const GemvPlan pl) {
+  constexpr int RS = PRE ? Q8_REC_BYTES : XR_STRIDE;  // bytes per staged (span, token) record
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
@@ -802,7 +858,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     GCHK((int)hw_n == pl.C, 3, hw_n, pl.C);
     GCHK(S >= 2 && S <= MAX_STAGES && (S & 1) == 0 && (ring - smem) + S * SB <= pl.smem_bytes, 4, S,
          (ring - smem) + S * SB);
-    GCHK((xr - smem) + nsp * MT * XR_STRIDE <= (ring - smem), 5, nsp, pl.xq_bytes);
+    GCHK((xr - smem) + nsp * MT * RS <= (ring - smem), 5, nsp, pl.xq_bytes);
   }
 #endif
 
@@ -811,8 +867,9 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 2);  // the two warps of a unit-parity pair
     }
-    // rank 0 receives one arrival per consumer thread of every other rank
-    if (pl.C > 1) mbar_init(redbar, (pl.C - 1) * NCW * 32);
+    // rank 0 receives one arrival per pushing thread of every other rank
+    // (16 float4 per token of the 64-row partial)
+    if (pl.C > 1) mbar_init(redbar, (pl.C - 1) * 16 * a.M);
     fence_mbar_init();
   }
   __syncthreads();
@@ -860,7 +917,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
 
   // ---------------- consumers
   pdl_wait();  // x is written by earlier kernels on the stream; y may be read by them
-  stage_acts<F32, MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
+  if (PRE)
+    stage_records<MT>(a, kb0, nsp, xr);
+  else
+    stage_acts<F32, MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
 
   const int row = 32 * (warp & 1) + lane;
   const int up = warp >> 1;  // this warp takes units j = up, up + 2, ...
@@ -873,7 +933,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   for (int j = up; j < nsp; j += 2) {
     if (!mbar_wait(&full[s], par, a.err, ERR_FULL_WAIT)) break;
     if (!GCHK(s >= 0 && s < S && j < nsp, 7, s, j)) break;
-    unit<DT, MT, F32>(ring + s * SB, row, xr + j * MT * XR_STRIDE, a.M, acc);
+    unit<DT, MT, F32, RS>(ring + s * SB, row, xr + j * MT * RS, a.M, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     s += 2;
@@ -885,24 +945,36 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
 
   // Tile reduction: unit parities (fixed order) -> CTA partial -> ranks (fixed
   // order).  Ranks other than 0 push their partial into rank 0's shared
-  // memory and signal its reduction mbarrier; rank 0 waits, adds, writes y.
+  // memory as float4 stores, each pushing thread then arriving (release) on
+  // rank 0's reduction mbarrier; rank 0 waits, adds, writes y.
 #pragma unroll
   for (int m = 0; m < MT; ++m)
     if (m < a.M) red[(up * UNIT_ROWS + row) * MT + m] = acc[m];
   consumer_sync();
   const int tid = threadIdx.x;
   if (pl.C > 1) cluster_wait();
-  for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
-    const int m = t >> 6, r = t & 63;
-    const float v = red[(0 * UNIT_ROWS + r) * MT + m] + red[(1 * UNIT_ROWS + r) * MT + m];
-    if (pl.C == 1) {
-      const int64_t n = (int64_t)g * UNIT_ROWS + r;
-      const float nv = n < a.N ? store_out(a, m, n, v) : 0.f;
-      if (a.fu.ssq_out) red[(0 * UNIT_ROWS + r) * MT + m] = nv * nv;  // the slot this thread just read
-    } else if (rank == 0) {
-      part[t] = v;
-    } else {
-      st_dsmem_f32(dsmem_addr(part + rank * UNIT_ROWS * MT + t, 0), v);
+  if (pl.C > 1 && rank != 0) {
+    for (int u = tid; u < 16 * a.M; u += NCW * 32) {
+      const int t0 = 4 * u, m = t0 >> 6, r0 = t0 & 63;
+      float4 v;
+      v.x = red[(0 * UNIT_ROWS + r0) * MT + m] + red[(1 * UNIT_ROWS + r0) * MT + m];
+      v.y = red[(0 * UNIT_ROWS + r0 + 1) * MT + m] + red[(1 * UNIT_ROWS + r0 + 1) * MT + m];
+      v.z = red[(0 * UNIT_ROWS + r0 + 2) * MT + m] + red[(1 * UNIT_ROWS + r0 + 2) * MT + m];
+      v.w = red[(0 * UNIT_ROWS + r0 + 3) * MT + m] + red[(1 * UNIT_ROWS + r0 + 3) * MT + m];
+      st_dsmem_v4(dsmem_addr(part + rank * UNIT_ROWS * MT + t0, 0), v);
+      mbar_arrive_remote(dsmem_addr(redbar, 0));  // releases this thread's push
+    }
+  } else {
+    for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
+      const int m = t >> 6, r = t & 63;
+      const float v = red[(0 * UNIT_ROWS + r) * MT + m] + red[(1 * UNIT_ROWS + r) * MT + m];
+      if (pl.C == 1) {
+        const int64_t n = (int64_t)g * UNIT_ROWS + r;
+        const float nv = n < a.N ? store_out(a, m, n, v) : 0.f;
+        if (a.fu.ssq_out) red[(0 * UNIT_ROWS + r) * MT + m] = nv * nv;  // the slot this thread just read
+      } else {
+        part[t] = v;
+      }
     }
   }
   if (pl.C == 1 && a.fu.ssq_out) {
@@ -910,9 +982,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     write_ssq(a, red, MT, 1, g, pl.G);
   }
   if (pl.C > 1) {
-    if (rank != 0) {
-      mbar_arrive_remote(dsmem_addr(redbar, 0));  // releases this thread's pushes
-    } else {
+    if (rank == 0) {
       mbar_wait_cluster(redbar, 0, a.err, ERR_REDUCE_WAIT);
       consumer_sync();  // rank 0's own partial, written by other threads
       for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
