@@ -211,6 +211,28 @@ int odi_cuda_matmul_fused(int dtype, const void* d_w_tiled, const float* d_x, fl
                           int64_t N, int64_t K, int act_mode, void* d_workspace, size_t workspace_bytes,
                           int flags, const odi_cuda_matmul_opts* opts, void* stream);
 
+/* Pre-quantized activations.  A Q8 record holds one (256-column span,
+ * token): 256 int8 codes (Q8_0 per 32 values, the gguf quantiser), then 8 x
+ * {scale, scale * sum of codes, ... of the first 16, ... of the last 16}
+ * fp32; records are span-major, (span kb, token m) at (kb * M + m) * 384.
+ * odi_cuda_q8_records_bytes gives the size for M rows of K values. */
+size_t odi_cuda_q8_records_bytes(int64_t M, int64_t K);
+
+/* fp32 rows x [M][K] -> Q8 records, after the optional prologue of opts
+ * (norm_weight / norm_ssq: RMSNorm; swiglu: x rows are [gate K | up K]).
+ * The records equal the ones odi_cuda_matmul_fused builds on chip from the
+ * same inputs, so odi_cuda_quantize_records + odi_cuda_matmul_q8rec gives
+ * odi_cuda_matmul_fused's result bit for bit.  opts may be NULL. */
+int odi_cuda_quantize_records(const float* d_x, int64_t M, int64_t K, const odi_cuda_matmul_opts* opts, void* d_recs,
+                              int flags, void* stream);
+
+/* The streaming GEMV (ACT_Q8) on pre-quantized Q8 records; opts' epilogue
+ * fields (accumulate, out_ssq) apply, its prologue fields must be unset.
+ * Workspace: 256 bytes. */
+int odi_cuda_matmul_q8rec(int dtype, const void* d_w_tiled, const void* d_recs, float* d_y, int64_t M, int64_t N,
+                          int64_t K, void* d_workspace, size_t workspace_bytes, int flags,
+                          const odi_cuda_matmul_opts* opts, void* stream);
+
 /* Reads and clears the device-side error word of a workspace (kernel waits
  * that gave up set it).  Synchronises `stream`.  *status = 0 when clean. */
 int odi_cuda_workspace_status(void* d_workspace, int* status, void* stream);
@@ -290,11 +312,15 @@ int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void
  * projections (q is rotated in registers and left unchanged in memory);
  * the rotated k and v are written as fp16 into the caches at the state's
  * pos (nothing is written when pos >= ctx).  Same results as the two calls;
- * same scratch and alignment rules as odi_cuda_attention_decode. */
+ * same scratch and alignment rules as odi_cuda_attention_decode.  If
+ * d_out_records is non-NULL (16-byte aligned,
+ * odi_cuda_q8_records_bytes(1, heads * head_dim) bytes), the output row is
+ * also written as the Q8 records odi_cuda_quantize_records would make of
+ * it, ready for odi_cuda_matmul_q8rec. */
 int odi_cuda_rope_attention(const float* d_q, const float* d_k, const float* d_v, void* d_kcache, void* d_vcache,
-                            float* d_out, const odi_cuda_decode_state* d_state, int heads, int kv_heads,
-                            int head_dim, int ctx, float theta, float scale, void* d_scratch, size_t scratch_bytes,
-                            void* stream);
+                            float* d_out, void* d_out_records, const odi_cuda_decode_state* d_state, int heads,
+                            int kv_heads, int head_dim, int ctx, float theta, float scale, void* d_scratch,
+                            size_t scratch_bytes, void* stream);
 
 /* out[F] = silu(gate) * up with gate_up = [gate F | up F] (context.cpp:272-275). */
 int odi_cuda_silu_mul(const float* d_gate_up, float* d_out, int64_t F, void* stream);

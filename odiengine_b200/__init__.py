@@ -86,8 +86,11 @@ SIGNATURES = {
     "odi_cuda_attention_scratch_bytes": (_sz, [_int, _int, _int]),
     "odi_cuda_attention_decode": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, ctypes.c_float, _vp, _sz,
                                          _vp]),
-    "odi_cuda_rope_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, ctypes.c_float,
-                                       ctypes.c_float, _vp, _sz, _vp]),
+    "odi_cuda_rope_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int,
+                                       ctypes.c_float, ctypes.c_float, _vp, _sz, _vp]),
+    "odi_cuda_q8_records_bytes": (_sz, [_i64, _i64]),
+    "odi_cuda_quantize_records": (_int, [_vp, _i64, _i64, _vp, _vp, _int, _vp]),
+    "odi_cuda_matmul_q8rec": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _int, _vp, _vp]),
     "odi_cuda_silu_mul": (_int, [_vp, _vp, _i64, _vp]),
     "odi_cuda_add": (_int, [_vp, _vp, _i64, _vp]),
     "odi_cuda_argmax": (_int, [_vp, _i64, _vp, _vp, _int, _vp]),

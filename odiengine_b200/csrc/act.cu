@@ -106,6 +106,85 @@ __global__ void act_q8_records_kernel(const float* __restrict__ x, int64_t ldx, 
   }
 }
 
+// act_q8_records with the decode step's activation prologues (GemvFuse):
+// RMSNorm (x * rms * norm_w, rms from the token's sums-of-squares slots or
+// from the row) or SwiGLU (silu(gate) * up of a [gate K | up K] row), then
+// the same quantisation.  The arithmetic and its order are the streaming
+// GEMV's own fused prologue (row_rms and stage_acts), so the records equal
+// the ones that GEMV builds in shared memory.
+__device__ __forceinline__ float act_silu(float g) { return g / (1.0f + expf(-g)); }
+
+// 1 / sqrt(sum(x^2) / K + eps) for token m, summed as the GEMV's row_rms
+// does with its 128 consumer threads: thread t (of 128) adds slots (or
+// squares) t, t + 128, ...; each 32-thread group reduces by xor shuffles;
+// the four group sums combine as (g0 + g1) + (g2 + g3).  One warp plays the
+// 128 threads as four virtual groups.
+__device__ float act_rms(const GemvFuse& fu, const float* __restrict__ x, int64_t m, int64_t ldx, int64_t K,
+                         int lane) {
+  float g[4];
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    float s = 0.f;
+    const int t = 32 * v + lane;
+    if (fu.ssq_in) {
+      const float* sq = fu.ssq_in + m * fu.ssq_n;
+      for (int i = t; i < fu.ssq_n; i += 128) s += sq[i];
+    } else {
+      const float* xm = x + m * ldx;
+      for (int64_t k = t; k < K; k += 128) s = fmaf(xm[k], xm[k], s);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    g[v] = s;
+  }
+  const float tot = (g[0] + g[1]) + (g[2] + g[3]);
+  return 1.0f / sqrtf(tot / (float)K + fu.eps);
+}
+
+__global__ void act_records_fused_kernel(const float* __restrict__ x, int64_t ldx, int64_t M, int64_t K,
+                                         int64_t KB, const GemvFuse fu, uint8_t* __restrict__ recs) {
+  pdl_wait();  // x (and the sums of squares) are written by the kernels before
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t total = KB * M * 8;
+  for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += nwarps) {
+    const int64_t kb = w / (M * 8);
+    const int64_t rem = w - kb * M * 8;
+    const int64_t m = rem >> 3;
+    const int j = (int)(rem & 7);
+    const int64_t k = kb * 256 + 32 * j + lane;
+    float v = k < K ? x[m * ldx + k] : 0.0f;
+    if (fu.swiglu) {
+      v = k < K ? act_silu(v) * x[m * ldx + K + k] : 0.0f;
+    } else if (fu.norm_w) {
+      const float r = act_rms(fu, x, m, ldx, K, lane);
+      if (k < K) v = v * r * fu.norm_w[k];
+    }
+    float am = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const float d = __fdiv_rn(am, 127.0f);
+    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+    const int q = (int)roundf(__fmul_rn(v, id));
+    int s = q;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const int s_lo = __shfl_sync(0xffffffffu, s, 0), s_hi = __shfl_sync(0xffffffffu, s, 16);
+    uint8_t* rec = recs + (kb * M + m) * Q8_REC_BYTES;
+    rec[32 * j + lane] = (uint8_t)(int8_t)q;
+    if (lane == 0) {
+      const float dx = __half2float(__float2half_rn(d));
+      float4 r;
+      r.x = dx;
+      r.y = __fmul_rn((float)(s_lo + s_hi), dx);
+      r.z = __fmul_rn((float)s_lo, dx);
+      r.w = __fmul_rn((float)s_hi, dx);
+      *reinterpret_cast<float4*>(rec + 256 + 16 * j) = r;
+    }
+  }
+}
+
 __global__ void act_pack_f32_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t Kp,
                                     float* __restrict__ tiles) {
   pdl_wait();
@@ -159,6 +238,16 @@ cudaError_t launch_act_q8_records(const float* x, int64_t ldx, int64_t M, int64_
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = small_cfg(grid_for(warps * 32, 256), pdl, stream, attr);
   return cudaLaunchKernelEx(&cfg, act_q8_records_kernel, x, ldx, M, K, KB, recs);
+}
+
+cudaError_t launch_act_records_fused(const float* x, int64_t ldx, int64_t M, int64_t K, const GemvFuse& fu,
+                                    uint8_t* recs, bool pdl, cudaStream_t stream) {
+  const int64_t KB = (K + 255) / 256;
+  const int64_t warps = KB * M * 8;
+  if (warps == 0) return cudaSuccess;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = small_cfg(grid_for(warps * 32, 256), pdl, stream, attr);
+  return cudaLaunchKernelEx(&cfg, act_records_fused_kernel, x, ldx, M, K, KB, fu, recs);
 }
 
 cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* tiles, bool pdl,

@@ -87,13 +87,16 @@ bool wants_records(bool f32, int64_t M, const GemvFuse* fu) {
 
 // The streaming GEMV over M tokens: one launch per pass of plan.mt tokens.
 // With `sc`, each pass scatters its rows into every rank's gathered buffer.
+// ext_recs: the activations already quantized into Q8 records (x unused).
 int run_gemv(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N, int64_t K,
              bool f32, int* err, size_t ws_bytes, bool pdl, cudaStream_t s, const GemvScatter* sc,
-             const GemvFuse* fu = nullptr) {
+             const GemvFuse* fu = nullptr, const uint8_t* ext_recs = nullptr) {
   const int64_t ldx = (fu && fu->swiglu) ? 2 * K : K;
-  const bool pre = wants_records(f32, M, fu) && ws_bytes >= WS_HEADER + q8_records_bytes(M, K);
-  uint8_t* recs = reinterpret_cast<uint8_t*>(err) + WS_HEADER;
-  if (pre) CK(launch_act_q8_records(d_x, ldx, M, K, recs, pdl, s), "act_q8_records launch");
+  const bool pre = ext_recs || (wants_records(f32, M, fu) && ws_bytes >= WS_HEADER + q8_records_bytes(M, K));
+  const uint8_t* recs = ext_recs ? ext_recs : reinterpret_cast<uint8_t*>(err) + WS_HEADER;
+  if (pre && !ext_recs)
+    CK(launch_act_q8_records(d_x, ldx, M, K, reinterpret_cast<uint8_t*>(err) + WS_HEADER, pdl, s),
+       "act_q8_records launch");
   const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current(), pre);
   if (plan.C == 0)
     return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
@@ -359,6 +362,69 @@ int odi_cuda_matmul_fused(int dtype, const void* d_w_tiled, const float* d_x, fl
                   (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, nullptr, &fu);
 }
 
+size_t odi_cuda_q8_records_bytes(int64_t M, int64_t K) {
+  if (M < 1 || K < 1) return 0;
+  return q8_records_bytes(M, K);
+}
+
+// opts -> GemvFuse (norm / swiglu prologue, accumulate / out_ssq epilogue);
+// 0 or an error status.
+static int fuse_from_opts(const odi_cuda_matmul_opts* opts, GemvFuse* fu) {
+  *fu = GemvFuse{};
+  if (!opts) return ODI_CUDA_OK;
+  if (opts->norm_weight && opts->swiglu)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "norm_weight and swiglu are exclusive");
+  if (opts->norm_ssq && opts->norm_ssq_count < 1)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "norm_ssq_count must be positive");
+  fu->norm_w = opts->norm_weight;
+  fu->eps = opts->norm_eps;
+  fu->swiglu = opts->swiglu ? 1 : 0;
+  fu->accumulate = opts->accumulate ? 1 : 0;
+  fu->ssq_in = opts->norm_ssq;
+  fu->ssq_n = opts->norm_ssq_count;
+  fu->ssq_out = opts->out_ssq;
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_quantize_records(const float* d_x, int64_t M, int64_t K, const odi_cuda_matmul_opts* opts, void* d_recs,
+                              int flags, void* stream) {
+  if (!d_x || !d_recs) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "quantize_records: null buffer");
+  if (M < 1 || K < 1 || M > (1 << 20)) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "quantize_records: bad M or K");
+  if ((uintptr_t)d_recs & 15) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "records must be 16-byte aligned");
+  GemvFuse fu;
+  int rc = fuse_from_opts(opts, &fu);
+  if (rc) return rc;
+  if (fu.accumulate || fu.ssq_out)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "quantize_records: accumulate / out_ssq belong to the product");
+  const int64_t ldx = fu.swiglu ? 2 * K : K;
+  const bool pdl = (flags & ODI_CUDA_FLAG_PDL) != 0;
+  if (fu.norm_w || fu.swiglu)
+    CK(launch_act_records_fused(d_x, ldx, M, K, fu, (uint8_t*)d_recs, pdl, (cudaStream_t)stream),
+       "quantize_records launch");
+  else
+    CK(launch_act_q8_records(d_x, ldx, M, K, (uint8_t*)d_recs, pdl, (cudaStream_t)stream), "quantize_records launch");
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_matmul_q8rec(int dtype, const void* d_w_tiled, const void* d_recs, float* d_y, int64_t M, int64_t N,
+                          int64_t K, void* d_workspace, size_t workspace_bytes, int flags,
+                          const odi_cuda_matmul_opts* opts, void* stream) {
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (M < 1 || M > (1 << 20)) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M=%lld", (long long)M);
+  if (!d_w_tiled || !d_recs || !d_y || !d_workspace) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null buffer");
+  if (((uintptr_t)d_w_tiled | (uintptr_t)d_workspace | (uintptr_t)d_recs) & 15)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight, records and workspace must be 16-byte aligned");
+  if (workspace_bytes < WS_HEADER) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small");
+  GemvFuse fu;
+  rc = fuse_from_opts(opts, &fu);
+  if (rc) return rc;
+  if (fu.norm_w || fu.swiglu)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "matmul_q8rec: the prologue belongs to odi_cuda_quantize_records");
+  return run_gemv(dtype, d_w_tiled, nullptr, d_y, M, N, K, false, (int*)d_workspace, workspace_bytes,
+                  (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, nullptr, &fu, (const uint8_t*)d_recs);
+}
+
 int odi_cuda_workspace_status(void* d_workspace, int* status, void* stream) {
   if (!d_workspace || !status) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
   int v = 0;
@@ -464,14 +530,16 @@ int odi_cuda_attention_decode(const float* d_q, const void* d_kcache, const void
 }
 
 int odi_cuda_rope_attention(const float* d_q, const float* d_k, const float* d_v, void* d_kcache, void* d_vcache,
-                            float* d_out, const odi_cuda_decode_state* d_state, int heads, int kv_heads,
-                            int head_dim, int ctx, float theta, float scale, void* d_scratch, size_t scratch_bytes,
-                            void* stream) {
+                            float* d_out, void* d_out_records, const odi_cuda_decode_state* d_state, int heads,
+                            int kv_heads, int head_dim, int ctx, float theta, float scale, void* d_scratch,
+                            size_t scratch_bytes, void* stream) {
   if (!d_k || !d_v) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "rope_attention: null k or v");
+  if ((uintptr_t)d_out_records & 15) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "records must be 16-byte aligned");
   AttRope rp;
   rp.k = d_k;
   rp.v = d_v;
   rp.theta = theta;
+  rp.out_recs = (uint8_t*)d_out_records;
   return attention_common(d_q, d_kcache, d_vcache, d_out, d_state, heads, kv_heads, head_dim, ctx, scale, d_scratch,
                           scratch_bytes, rp, stream);
 }

@@ -111,6 +111,7 @@ __global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, con
 }
 
 // Flash decoding in one launch, streamed by the bulk-copy engine.
+// (With orec, the outputs are also written as Q8 records for the next GEMV.)
 // CTA (kvh, split) serves the G = heads / kv_heads query heads of kv head
 // kvh over the 64-position chunks c = split, split + nsplit, ... of
 // kv_len = pos + 1.  Thread 0 streams each chunk's K and V tiles (64 x HD
@@ -148,7 +149,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
                                                            int* __restrict__ err, const DecodeState* st, int ctx,
                                                            int nsplit, float scale, const float* __restrict__ kraw,
                                                            const float* __restrict__ vraw, float theta, int rope,
-                                                           __half* __restrict__ kcw, __half* __restrict__ vcw) {
+                                                           __half* __restrict__ kcw, __half* __restrict__ vcw,
+                                                           uint8_t* __restrict__ orec) {
   constexpr int DPL = HD / 32;           // dims per lane
   constexpr int TILE = ATT_CHUNK * HD;   // halves per K (or V) tile
   constexpr int PW = ATT_CHUNK / 4;      // positions per warp per chunk (16)
@@ -390,7 +392,34 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
         M = mn;
       }
     }
-    o[(int64_t)h * HD + d] = L > 0.f ? a / L : 0.f;
+    const float val = L > 0.f ? a / L : 0.f;
+    o[(int64_t)h * HD + d] = val;
+    if (orec) {
+      // The output row as the next GEMV's Q8 record (one token): each warp
+      // holds 32 consecutive values = one Q8 block; the quantisation of
+      // act_q8_records_kernel, bit for bit.
+      const int lane = threadIdx.x & 31;
+      const int64_t col = (int64_t)h * HD + d;
+      const int64_t kb = col >> 8;
+      const int j = (int)((col & 255) >> 5);
+      float am = fabsf(val);
+#pragma unroll
+      for (int w = 16; w; w >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, w));
+      const float dq = __fdiv_rn(am, 127.0f);
+      const float id = dq == 0.0f ? 0.0f : __fdiv_rn(1.0f, dq);
+      const int q = (int)roundf(__fmul_rn(val, id));
+      int sq = q;
+#pragma unroll
+      for (int w = 8; w; w >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, w);
+      const int s_lo = __shfl_sync(0xffffffffu, sq, 0), s_hi = __shfl_sync(0xffffffffu, sq, 16);
+      uint8_t* rec = orec + kb * Q8_REC_BYTES;
+      rec[32 * j + lane] = (uint8_t)(int8_t)q;
+      if (lane == 0) {
+        const float dx = __half2float(__float2half_rn(dq));
+        *reinterpret_cast<float4*>(rec + 256 + 16 * j) =
+            make_float4(dx, __fmul_rn((float)(s_lo + s_hi), dx), __fmul_rn((float)s_lo, dx), __fmul_rn((float)s_hi, dx));
+      }
+    }
   }
   if (threadIdx.x == 0) cnt[kvh] = 0;
 }
@@ -557,7 +586,7 @@ static cudaError_t launch_att_t(const float* q, const __half* kc, const __half* 
   float* part = reinterpret_cast<float*>(base + att_part_offset(heads));
   return launch_pdl_smem(kern, dim3(kv_heads, nsplit), dim3(ATT_THREADS), smem, s, q, kc, vc, o, part, cnt, err, st,
                          ctx, nsplit, scale, rp.k, rp.v, rp.theta, rp.k ? 1 : 0, const_cast<__half*>(kc),
-                         const_cast<__half*>(vc));
+                         const_cast<__half*>(vc), rp.out_recs);
 }
 
 template <int HD>

@@ -9,6 +9,9 @@ cudaError_t launch_act_quant(const float* x, int64_t M, int64_t K, uint8_t* tile
                              bool pdl, cudaStream_t stream);
 cudaError_t launch_act_q8_records(const float* x, int64_t ldx, int64_t M, int64_t K, uint8_t* recs, bool pdl,
                                   cudaStream_t stream);
+struct GemvFuse;
+cudaError_t launch_act_records_fused(const float* x, int64_t ldx, int64_t M, int64_t K, const GemvFuse& fu,
+                                    uint8_t* recs, bool pdl, cudaStream_t stream);
 cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* tiles, bool pdl,
                                 cudaStream_t stream);
 cudaError_t launch_repack(int dt, const void* gguf, void* tiled, int64_t N, int64_t K, cudaStream_t s);
@@ -122,6 +125,7 @@ struct AttRope {
   const float* k = nullptr;
   const float* v = nullptr;
   float theta = 0.f;
+  uint8_t* out_recs = nullptr;  // also write the outputs as one token's Q8 records
 };
 cudaError_t launch_attention(const float* q, const __half* kc, const __half* vc, float* o, void* scratch,
                              const DecodeState* st, int heads, int kv_heads, int hd, int ctx, float scale,

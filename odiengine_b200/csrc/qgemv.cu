@@ -114,9 +114,9 @@ static cudaError_t launch_t(const GemvPlan& pl, const GemvArgs& a, bool pdl, cud
 
 template <int DT, bool F32>
 static cudaError_t launch_mt(const GemvPlan& pl, const GemvArgs& a, bool pdl, cudaStream_t s) {
-  if (!F32 && pl.pre) {  // pre-quantized records: multi-token passes only
+  if (!F32 && pl.pre) {  // pre-quantized Q8 records
     switch (pl.mt) {
-      case 1: return launch_t<DT, 1, F32, false>(pl, a, pdl, s);
+      case 1: return launch_t<DT, 1, F32, !F32>(pl, a, pdl, s);
       case 2: return launch_t<DT, 2, F32, !F32>(pl, a, pdl, s);
       case 4: return launch_t<DT, 4, F32, !F32>(pl, a, pdl, s);
       default: return launch_t<DT, 8, F32, !F32>(pl, a, pdl, s);

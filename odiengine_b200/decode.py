@@ -133,13 +133,17 @@ class DecodeModel:
     a CUDA graph that ``generate`` replays."""
 
     def __init__(self, cfg: LlamaConfig, weights: ModelWeights, device=None, max_record: int = 4096,
-                 fused: bool = True):
+                 fused: bool = True, records: bool = True):
         import torch
 
         self.cfg, self.w = cfg, weights
         # fused: RMSNorm, SwiGLU and the residual adds run inside the GEMVs
         # (odi_cuda_matmul_fused); otherwise as separate kernels
         self.fused = fused
+        # records (with fused): every GEMV input is quantized once into Q8
+        # records -- by a small kernel that also applies RMSNorm / SwiGLU, or
+        # by the attention itself -- instead of by every CTA of the GEMV
+        self.records = fused and records and cfg.act_mode == ACT_Q8
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         dev, f32 = self.device, torch.float32
         E, F, H, hd = cfg.hidden, cfg.ffn, cfg.heads, cfg.head_dim
@@ -155,6 +159,10 @@ class DecodeModel:
         # residual GEMV) for the next fused RMSNorm
         self.ssq_slots = (E + 63) // 64
         self.ssq = torch.zeros(self.ssq_slots, dtype=f32, device=dev)
+        rb = lib().odi_cuda_q8_records_bytes
+        self.rec_e = torch.zeros(rb(1, E), dtype=torch.uint8, device=dev)        # x (normalised)
+        self.rec_a = torch.zeros(rb(1, H * hd), dtype=torch.uint8, device=dev)   # attention output
+        self.rec_f = torch.zeros(rb(1, F), dtype=torch.uint8, device=dev)        # SwiGLU output
         self.kc = torch.zeros((cfg.layers, cfg.kv_heads, cfg.ctx, hd), dtype=torch.float16, device=dev)
         self.vc = torch.zeros_like(self.kc)
         sb = lib().odi_cuda_attention_scratch_bytes(H, hd, cfg.ctx)
@@ -218,11 +226,60 @@ class DecodeModel:
         check(lib().odi_cuda_matmul_fused(dw.dtype, dw.data_ptr, _ptr(x), _ptr(y), 1, dw.N, dw.K, self.cfg.act_mode,
                                           _ptr(ws), ws.numel(), FLAG_PDL, ctypes.byref(o), s))
 
+    def _opts(self, norm=None, swiglu=False, accumulate=False):
+        from . import MatmulOpts
+
+        ssq = _ptr(self.ssq)
+        return MatmulOpts(_ptr(norm) if norm is not None else None, self.cfg.eps, 1 if swiglu else 0,
+                          1 if accumulate else 0, ssq if norm is not None else None, self.ssq_slots,
+                          ssq if accumulate else None)
+
+    def _records(self, x, K, rec, s, norm=None, swiglu=False):
+        o = self._opts(norm=norm, swiglu=swiglu)
+        check(lib().odi_cuda_quantize_records(_ptr(x), 1, K, ctypes.byref(o), _ptr(rec), FLAG_PDL, s))
+
+    def _gemv_rec(self, dw: DeviceWeight, rec, y, s, accumulate=False):
+        o = self._opts(accumulate=accumulate)
+        ws = dw._ws
+        check(lib().odi_cuda_matmul_q8rec(dw.dtype, dw.data_ptr, _ptr(rec), _ptr(y), 1, dw.N, dw.K, _ptr(ws),
+                                          ws.numel(), FLAG_PDL, ctypes.byref(o), s))
+
     def step(self) -> None:
-        if self.fused:
+        if self.records:
+            self._step_records()
+        elif self.fused:
             self._step_fused()
         else:
             self._step_unfused()
+
+    def _step_records(self) -> None:
+        """8 launches per layer, every GEMV on pre-quantized records: records
+        of RMSNorm(x), QKV GEMV, attention (rope and the KV append fused in,
+        writing the O GEMV's records), O GEMV (+= x), records of RMSNorm(x),
+        gate|up GEMV, records of SwiGLU(gate|up), down GEMV (+= x)."""
+        cfg, L, s = self.cfg, lib(), self.stream.cuda_stream
+        E, F, H, KV, hd = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim
+        st = _ptr(self.state)
+        q = _ptr(self.qkv)
+        k = q + H * hd * 4
+        v = k + KV * hd * 4
+        scale = 1.0 / math.sqrt(hd)
+        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, E, st, _ptr(self.x), _ptr(self.ssq), s))
+        for li, lw in enumerate(self.w.layers):
+            kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
+            self._records(self.x, E, self.rec_e, s, norm=lw.attn_norm)
+            self._gemv_rec(lw.wqkv, self.rec_e, self.qkv, s)
+            check(L.odi_cuda_rope_attention(q, k, v, kc, vc, _ptr(self.attn), _ptr(self.rec_a), st, H, KV, hd,
+                                            cfg.ctx, cfg.theta, scale, _ptr(self.att_scratch),
+                                            self.att_scratch.numel() * 4, s))
+            self._gemv_rec(lw.wo, self.rec_a, self.x, s, accumulate=True)
+            self._records(self.x, E, self.rec_e, s, norm=lw.ffn_norm)
+            self._gemv_rec(lw.wgu, self.rec_e, self.gu, s)
+            self._records(self.gu, F, self.rec_f, s, swiglu=True)
+            self._gemv_rec(lw.wdown, self.rec_f, self.x, s, accumulate=True)
+        self._records(self.x, E, self.rec_e, s, norm=self.w.out_norm)
+        self._gemv_rec(self.w.output, self.rec_e, self.logits, s)
+        check(L.odi_cuda_argmax(_ptr(self.logits), cfg.vocab, st, _ptr(self.record), self.max_record, s))
 
     def _step_fused(self) -> None:
         """5 launches per layer: QKV GEMV (RMSNorm fused), attention (rope and
@@ -239,8 +296,9 @@ class DecodeModel:
         for li, lw in enumerate(self.w.layers):
             kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
             self._gemv_fused(lw.wqkv, self.x, self.qkv, s, norm=lw.attn_norm)
-            check(L.odi_cuda_rope_attention(q, k, v, kc, vc, _ptr(self.attn), st, H, KV, hd, cfg.ctx, cfg.theta,
-                                            scale, _ptr(self.att_scratch), self.att_scratch.numel() * 4, s))
+            check(L.odi_cuda_rope_attention(q, k, v, kc, vc, _ptr(self.attn), None, st, H, KV, hd, cfg.ctx,
+                                            cfg.theta, scale, _ptr(self.att_scratch), self.att_scratch.numel() * 4,
+                                            s))
             self._gemv_fused(lw.wo, self.attn, self.x, s, accumulate=True)
             self._gemv_fused(lw.wgu, self.x, self.gu, s, norm=lw.ffn_norm)
             self._gemv_fused(lw.wdown, self.gu, self.x, s, swiglu=True, accumulate=True)
@@ -275,6 +333,8 @@ class DecodeModel:
         check(L.odi_cuda_argmax(_ptr(self.logits), cfg.vocab, st, _ptr(self.record), self.max_record, s))
 
     def launches_per_step(self) -> int:
+        if self.records:
+            return 1 + 8 * self.cfg.layers + 3  # embed, per layer, records + output GEMV + argmax
         if self.fused:
             return 1 + 5 * self.cfg.layers + 2  # embed, per layer, output GEMV + argmax
         return 1 + 10 * self.cfg.layers + 3  # embed, per layer, final norm + output GEMV + argmax

@@ -175,9 +175,13 @@ def test_rope_attention_equals_two_calls(cuda_lib, hd, H, KV, pos, ctx):
         scratch = torch.zeros(sb // 4 + 1, device="cuda")
         out = torch.zeros((H, hd), device="cuda")
         if fused:
+            rec = torch.zeros(L.odi_cuda_q8_records_bytes(1, H * hd), dtype=torch.uint8, device="cuda")
             cuda_lib.check(L.odi_cuda_rope_attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kc.data_ptr(),
-                                                     vc.data_ptr(), out.data_ptr(), st.data_ptr(), H, KV, hd, ctx,
-                                                     theta, scale, scratch.data_ptr(), sb, None))
+                                                     vc.data_ptr(), out.data_ptr(), rec.data_ptr(), st.data_ptr(),
+                                                     H, KV, hd, ctx, theta, scale, scratch.data_ptr(), sb, None))
+            # the records it wrote are the quantisation of its output row
+            rec2 = torch.zeros_like(rec)
+            cuda_lib.check(L.odi_cuda_quantize_records(out.data_ptr(), 1, H * hd, None, rec2.data_ptr(), 0, None))
         else:
             cuda_lib.check(L.odi_cuda_rope_kv(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), kc.data_ptr(),
                                               vc.data_ptr(), st.data_ptr(), H, KV, hd, ctx, theta, None))
@@ -186,6 +190,8 @@ def test_rope_attention_equals_two_calls(cuda_lib, hd, H, KV, pos, ctx):
                                                        None))
         torch.cuda.synchronize()
         assert int(scratch.view(torch.int32)[0]) == 0
+        if fused:
+            assert torch.equal(rec, rec2)
         outs.append((out.cpu().numpy(), kc.cpu().numpy(), vc.cpu().numpy(), qd.cpu().numpy()))
     (o1, k1, v1, q1), (o2, k2, v2, q2) = outs
     assert np.array_equal(o1, o2)
@@ -275,7 +281,8 @@ def test_tiny_model_matches_oracle(cuda_lib, act_mode, tol, fused):
 
     cfg = _tiny(act_mode)
     mw = seeded_model(cfg, seed=7)
-    dm = DecodeModel(cfg, mw, fused=fused)
+    # (the Q8 records path is taken with Q8 activations; with fp32 ones the fused GEMVs stage on chip)
+    dm = DecodeModel(cfg, mw, fused=fused, records=act_mode == 0)
     ref = LlamaRef(cfg, _oracle_weights(cuda_lib, cfg, mw))
     prompt = [5, 17, 999, 3, 250]
     dm.prefill(prompt[:-1])
@@ -293,6 +300,26 @@ def test_tiny_model_matches_oracle(cuda_lib, act_mode, tol, fused):
         if top2[1] - top2[0] > 2 * tol * scale:
             assert got == int(np.argmax(lr))
         token, pos = got, pos + 1
+
+
+def test_records_mode_equals_fused_mode(cuda_lib):
+    """The decode step on pre-quantized records (8 launches per layer) and
+    with on-chip staging (5 per layer) quantize the same values the same
+    way: identical logits and tokens."""
+    from odiengine_b200.decode import DecodeModel, seeded_model
+
+    cfg = _tiny(0)
+    mw = seeded_model(cfg, seed=5)
+    a = DecodeModel(cfg, mw, records=True)
+    b = DecodeModel(cfg, mw, records=False)
+    assert a.records and not b.records
+    for m in (a, b):
+        m.reset(7, 0)
+    for _ in range(10):
+        ta, tb = a.generate(1), b.generate(1)
+        assert ta == tb
+        assert np.array_equal(a.logits.cpu().numpy(), b.logits.cpu().numpy())
+    assert a.status() == 0 and b.status() == 0
 
 
 def test_graph_replay_equals_eager(cuda_lib):
@@ -366,6 +393,64 @@ def test_matmul_fused_ops(cuda_lib, dt, mode):
     y0 = rng.standard_normal((M, N)).astype(np.float32)
     y = run(x, _t(y0), ob.MatmulOpts(None, 0.0, 0, 1))
     assert (np.abs(y - (y0 + x.astype(np.float64) @ W.T)) <= tol(x.astype(np.float64)) + 1e-6 * np.abs(y0)).all()
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K, O.Q8_0])
+@pytest.mark.parametrize("M", [1, 3])
+def test_records_path_equals_fused(cuda_lib, dt, M):
+    """odi_cuda_quantize_records (RMSNorm from slots or from the row, SwiGLU,
+    none) followed by odi_cuda_matmul_q8rec (with the accumulate / out_ssq
+    epilogue) gives odi_cuda_matmul_fused's results bit for bit: the records
+    are the ones that GEMV quantizes on chip."""
+    import ctypes
+
+    import torch
+
+    ob = cuda_lib
+    L = ob.lib()
+    N, K = 320, 2048
+    rng = np.random.default_rng(dt + 10 * M)
+    b = O.quantize(dt, O.seeded_weights(N, K, seed=dt + 1))
+    dw = ob.DeviceWeight(ob.QuantWeight(dt, (K, N), b))
+    ws = ob.new_workspace(256, torch.device("cuda"))
+    rec = torch.zeros(L.odi_cuda_q8_records_bytes(M, K), dtype=torch.uint8, device="cuda")
+    x = _t(rng.standard_normal((M, 2 * K)).astype(np.float32) * 2)
+    nw = _t((1 + 0.02 * rng.standard_normal(K)).astype(np.float32))
+    slots = (K + 63) // 64
+    ssq = _t((x[:, :K].cpu().numpy().reshape(M, slots, 64) ** 2).sum(-1).astype(np.float32))
+    y0 = rng.standard_normal((M, N)).astype(np.float32)
+    cases = [("norm_slots", ob.MatmulOpts(nw.data_ptr(), 1e-5, 0, 0, ssq.data_ptr(), slots, None)),
+             ("norm_row", ob.MatmulOpts(nw.data_ptr(), 1e-5, 0, 0, None, 0, None)),
+             ("swiglu", ob.MatmulOpts(None, 0.0, 1, 0, None, 0, None)),
+             ("plain", ob.MatmulOpts(None, 0.0, 0, 0, None, 0, None))]
+    for name, pro in cases:
+        xs = x if name == "swiglu" else _t(x[:, :K].cpu().numpy())
+        for acc in (0, 1):
+            outs = []
+            for path in ("fused", "records"):
+                y = _t(y0)
+                oss = torch.zeros((M, (N + 63) // 64), device="cuda")
+                epi = ob.MatmulOpts(pro.norm_weight, pro.norm_eps, pro.swiglu, acc, pro.norm_ssq,
+                                    pro.norm_ssq_count, oss.data_ptr() if acc else None)
+                if path == "fused":
+                    ob.check(L.odi_cuda_matmul_fused(dt, dw.data_ptr, xs.data_ptr(), y.data_ptr(), M, N, K, 0,
+                                                     ws.data_ptr(), ws.numel(), 0, ctypes.byref(epi), None))
+                else:
+                    ob.check(L.odi_cuda_quantize_records(xs.data_ptr(), M, K, ctypes.byref(pro), rec.data_ptr(), 0,
+                                                         None))
+                    o2 = ob.MatmulOpts(None, 0.0, 0, acc, None, 0, oss.data_ptr() if acc else None)
+                    ob.check(L.odi_cuda_matmul_q8rec(dt, dw.data_ptr, rec.data_ptr(), y.data_ptr(), M, N, K,
+                                                     ws.data_ptr(), ws.numel(), 0, ctypes.byref(o2), None))
+                torch.cuda.synchronize()
+                assert ob.workspace_status(ws) == 0
+                outs.append((y.cpu().numpy(), oss.cpu().numpy()))
+            assert np.array_equal(outs[0][0], outs[1][0]), (name, acc)
+            assert np.array_equal(outs[0][1], outs[1][1]), (name, acc)
+    # the prologue belongs to the records, not to the product
+    bad = ob.MatmulOpts(nw.data_ptr(), 1e-5, 0, 0, None, 0, None)
+    rc = L.odi_cuda_matmul_q8rec(dt, dw.data_ptr, rec.data_ptr(), y.data_ptr(), M, N, K, ws.data_ptr(), ws.numel(),
+                                 0, ctypes.byref(bad), None)
+    assert rc == 2  # ODI_CUDA_ERR_INVALID_ARGUMENT
 
 
 @pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
