@@ -220,9 +220,11 @@ size_t odi_cuda_q8_records_bytes(int64_t M, int64_t K);
 
 /* fp32 rows x [M][K] -> Q8 records, after the optional prologue of opts
  * (norm_weight / norm_ssq: RMSNorm; swiglu: x rows are [gate K | up K]).
- * The records equal the ones odi_cuda_matmul_fused builds on chip from the
- * same inputs, so odi_cuda_quantize_records + odi_cuda_matmul_q8rec gives
- * odi_cuda_matmul_fused's result bit for bit.  opts may be NULL. */
+ * The records equal, bit for bit, the ones odi_cuda_matmul_fused builds on
+ * chip from the same inputs; odi_cuda_matmul_q8rec on them then equals
+ * odi_cuda_matmul_fused up to the order of the fp32 cross-CTA reduction,
+ * which the two paths may split differently on products of several waves.
+ * opts may be NULL. */
 int odi_cuda_quantize_records(const float* d_x, int64_t M, int64_t K, const odi_cuda_matmul_opts* opts, void* d_recs,
                               int flags, void* stream);
 

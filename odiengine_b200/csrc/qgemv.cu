@@ -35,6 +35,10 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
       // 0.5 + 0.25 * log2(C) spans (fitted to measured C = 1..8 timings of
       // the 7B and 70B decode shapes)
       if (ceff > 1) t += 0.5 + 0.25 * (ceff >= 8 ? 3 : ceff >= 4 ? 2 : 1);
+      // With pre-quantized records a CTA's weight streaming is the larger
+      // part of its life and each further wave of CTAs adds about two
+      // spans of start-up and reduction (fitted the same way)
+      if (p.pre) t += 2.0 * (waves > 1.0 ? waves : 1.0);
       if (t < best) {
         best = t;
         bestC = ceff;

@@ -305,7 +305,7 @@ def test_tiny_model_matches_oracle(cuda_lib, act_mode, tol, fused):
 def test_records_mode_equals_fused_mode(cuda_lib):
     """The decode step on pre-quantized records (8 launches per layer) and
     with on-chip staging (5 per layer) quantize the same values the same
-    way: identical logits and tokens."""
+    way: identical logits and tokens (single-wave GEMVs at this size)."""
     from odiengine_b200.decode import DecodeModel, seeded_model
 
     cfg = _tiny(0)
@@ -401,7 +401,8 @@ def test_records_path_equals_fused(cuda_lib, dt, M):
     """odi_cuda_quantize_records (RMSNorm from slots or from the row, SwiGLU,
     none) followed by odi_cuda_matmul_q8rec (with the accumulate / out_ssq
     epilogue) gives odi_cuda_matmul_fused's results bit for bit: the records
-    are the ones that GEMV quantizes on chip."""
+    are the ones that GEMV quantizes on chip, and at this size (one wave)
+    both paths split the reduction the same way."""
     import ctypes
 
     import torch
