@@ -18,6 +18,10 @@ Reported (one JSON line on rank 0):
               measured HBM copy bandwidth in MEASURED_PEAKS.json
   cpu_baseline the oracle's restatement of the reference loop on the host
               cores (the reference itself throws on Q4_K), bounded sample
+  configs     (1 GPU) the reference's other configurations: the 7B decode
+              GEMV sweep (Q8_0 / Q4_K / Q6_K, M = 1 and 8), the tensor-core
+              prefill GEMM (Q4_K, M = 512 and 2048, TFLOP/s) and the 70B
+              Q4_K GEMV shapes (M = 1 and 32)
   decode_7b   (1 GPU) the second half of the metric: tokens/s of greedy
               decode of a Llama-2-7B-shaped Q4_K/Q6_K model with 2048 prompt
               tokens in the fp16 KV cache, 256 timed steps (CUDA events
@@ -459,9 +463,13 @@ def run_ours(args, rank, world, local_rank):
                         "sample": "unmodified CPUBackend::matmul, Q4_0 4096x4096 M=1 (config 1)"}
 
     decode = None
-    if world == 1 and not args.no_decode:
+    configs = None
+    if world == 1 and (not args.no_decode or not args.no_configs):
         del g_step, g_gemv
-        decode = run_decode(args, local_rank)
+        if not args.no_decode:
+            decode = run_decode(args, local_rank)
+        if not args.no_configs:
+            configs = run_config_legs(args)
 
     if rank == 0:
         line = {
@@ -480,9 +488,10 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "gpu_launches": args.steps * SWEEPS * R * (2 if fused else 1),
             "decode_7b": decode,
+            "configs": configs,
         }
         print(json.dumps(line), flush=True)
-    if decode is None:
+    if world > 1 or (args.no_decode and args.no_configs):
         del g_step, g_gemv
     if fused:
         torch.cuda.synchronize()
@@ -495,6 +504,107 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier(device_ids=[local_rank])
         sym.close()
     return 0
+
+
+def time_products(dt, N, K, M, act_mode, reps=20, seed=0, dev=None):
+    """Device time per product y = x . W^T (us) of odi_cuda_matmul chained
+    with programmatic dependent launch in a CUDA graph, over a ring of
+    distinct weight copies larger than 4 x L2 (every product streams its
+    weight from HBM), each copy with its own activations.  Returns
+    (us per product, algorithmic bytes per product, ring copies)."""
+    import torch
+
+    import odiengine_b200 as ob
+
+    L = ob.lib()
+    dev = dev or torch.device("cuda", torch.cuda.current_device())
+    wb = ob.tiled_bytes(dt, N, K)
+    R = max(2, -(-4 * L2_BYTES // wb))
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    with torch.cuda.stream(stream):
+        wf = torch.empty((N, K), dtype=torch.float32, device=dev).normal_(0.0, 0.02, generator=gen)
+        base = ob.repack(dt, ob.quantize_weight(dt, wf, stream=stream), N, K, stream=stream)
+        del wf
+        ring = [base] + [base.clone() for _ in range(R - 1)]
+        xs = [torch.empty((M, K), dtype=torch.float32, device=dev).normal_(0.0, 1.0, generator=gen) for _ in range(R)]
+        ys = [torch.zeros((M, N), dtype=torch.float32, device=dev) for _ in range(R)]
+    stream.synchronize()
+    ws = ob.new_workspace(ob.workspace_bytes(dt, M, N, K, act_mode), dev)
+
+    def body():
+        for r in range(R):
+            ob.check(L.odi_cuda_matmul(dt, ring[r].data_ptr(), xs[r].data_ptr(), ys[r].data_ptr(), M, N, K,
+                                       act_mode, ws.data_ptr(), ws.numel(), ob.FLAG_PDL, sp))
+
+    with torch.cuda.stream(stream):
+        body()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        body()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    stream.synchronize()
+    if ob.workspace_status(ws):
+        raise RuntimeError("a bounded device wait gave up")
+    us = e0.elapsed_time(e1) * 1e3 / (reps * R)
+    del g, ring, base, xs, ys
+    torch.cuda.empty_cache()
+    return us, ob.gguf_bytes(dt, N, K) + M * K * 4 + M * N * 4, R
+
+
+def run_config_legs(args):
+    """The reference configurations beside the headline, on one GPU:
+    config 2 (7B decode GEMV shapes, Q8_0 / Q4_K / Q6_K, M = 1 and 8),
+    config 3 (prefill GEMM on the tensor cores, Q4_K, M = 512 and 2048),
+    config 5 (70B Q4_K GEMV shapes, M = 1 and 32)."""
+    import odiengine_b200 as ob
+
+    peak_hbm, kind = measured_peak()
+    peak_tc = measured_tc_peak()
+    out = {"gemv_sweep": [], "prefill_gemm": [], "gemv_70b": [],
+           "method": "CUDA events over CUDA-graph replays of PDL-chained odi_cuda_matmul (ODI_CUDA_ACT_AUTO) over a "
+                     "ring of weight copies > 4 x L2; GB/s = (packed weight + fp32 x + fp32 y bytes) / time"}
+    names = {ob.ODI_DTYPE_Q8_0: "Q8_0", ob.ODI_DTYPE_Q4_K: "Q4_K", ob.ODI_DTYPE_Q6_K: "Q6_K"}
+    for dt in (ob.ODI_DTYPE_Q8_0, ob.ODI_DTYPE_Q4_K, ob.ODI_DTYPE_Q6_K):
+        for N, K in ((4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)):
+            for M in (1, 8):
+                us, b, R = time_products(dt, N, K, M, ob.ACT_AUTO, reps=10)
+                gbs = b / us / 1e3
+                out["gemv_sweep"].append({"dtype": names[dt], "N": N, "K": K, "M": M, "us": round(us, 3),
+                                          "GBs": round(gbs, 1), "hbm_frac": round(gbs / peak_hbm, 4)})
+    for N, K in ((14336, 4096), (4096, 14336)):
+        for M in (512, 2048):
+            us, _, R = time_products(ob.ODI_DTYPE_Q4_K, N, K, M, ob.ACT_AUTO, reps=5)
+            tf = 2.0 * M * N * K / us / 1e6
+            out["prefill_gemm"].append({"dtype": "Q4_K", "N": N, "K": K, "M": M, "us": round(us, 2),
+                                        "TFLOPs": round(tf, 1), "tensor_frac": round(tf / peak_tc, 4),
+                                        "path": "tcgen05 (fp16-decoded weights, fp32 accumulate in TMEM)"})
+    for N, K in ((28672, 8192), (8192, 28672), (128256, 8192)):
+        for M in (1, 32):
+            us, b, R = time_products(ob.ODI_DTYPE_Q4_K, N, K, M, ob.ACT_AUTO, reps=5)
+            gbs = b / us / 1e3
+            out["gemv_70b"].append({"dtype": "Q4_K", "N": N, "K": K, "M": M, "us": round(us, 2),
+                                    "GBs": round(gbs, 1), "hbm_frac": round(gbs / peak_hbm, 4)})
+    out["peaks"] = {"hbm_gbs": peak_hbm, "bf16_tflops": peak_tc, "kind": kind}
+    return out
+
+
+def measured_tc_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
 
 
 DEC_PROMPT, DEC_GEN = 2048, 256
@@ -513,7 +623,7 @@ def run_decode(args, local_rank):
     from odiengine_b200.decode import DecodeModel, LlamaConfig, seeded_model
 
     dev = torch.device("cuda", local_rank)
-    P, G = DEC_PROMPT, DEC_GEN
+    P, G = args.decode_prompt, args.decode_gen
     cfg = LlamaConfig(ctx=P + G + 8)
     t0 = time.perf_counter()
     mw = seeded_model(cfg, seed=0, device=dev)
@@ -646,6 +756,11 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="leave out the 7B-shape decode tokens/s")
+    ap.add_argument("--decode-only", action="store_true", help="run only the 7B-shape decode leg (1 GPU)")
+    ap.add_argument("--decode-prompt", type=int, default=DEC_PROMPT, help="prompt tokens in the KV cache")
+    ap.add_argument("--decode-gen", type=int, default=DEC_GEN, help="timed greedy steps")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="leave out the other reference configurations (GEMV sweep, prefill GEMM, 70B shapes)")
     ap.add_argument("--profile", action="store_true", help="small case for ncu: 3 products, no timing")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="N > 1: gather the row shards from the GEMV epilogue (fused) or with ncclAllGather")
@@ -655,6 +770,17 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.decode_only:
+        if world > 1:
+            raise SystemExit("--decode-only runs on one GPU")
+        import torch
+
+        import odiengine_b200 as ob
+
+        torch.cuda.set_device(local_rank)
+        ob.init(local_rank)
+        print(json.dumps({"decode_7b": run_decode(args, local_rank)}), flush=True)
+        return 0
     if world > 1:
         import datetime
 

@@ -118,24 +118,39 @@ __device__ __forceinline__ float act_silu(float g) { return g / (1.0f + expf(-g)
 // does with its 128 consumer threads: thread t (of 128) adds slots (or
 // squares) t, t + 128, ...; each 32-thread group reduces by xor shuffles;
 // the four group sums combine as (g0 + g1) + (g2 + g3).  One warp plays the
-// 128 threads as four virtual groups.
+// 128 threads as four virtual groups.  With up to 128 slots (hidden sizes up
+// to 8192) every slot is loaded at once, so the sum costs one round trip.
 __device__ float act_rms(const GemvFuse& fu, const float* __restrict__ x, int64_t m, int64_t ldx, int64_t K,
                          int lane) {
   float g[4];
+  if (fu.ssq_in && fu.ssq_n <= 128) {
+    const float* sq = fu.ssq_in + m * fu.ssq_n;
+    float v4[4];
 #pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    float s = 0.f;
-    const int t = 32 * v + lane;
-    if (fu.ssq_in) {
-      const float* sq = fu.ssq_in + m * fu.ssq_n;
-      for (int i = t; i < fu.ssq_n; i += 128) s += sq[i];
-    } else {
-      const float* xm = x + m * ldx;
-      for (int64_t k = t; k < K; k += 128) s = fmaf(xm[k], xm[k], s);
+    for (int v = 0; v < 4; ++v) v4[v] = 32 * v + lane < fu.ssq_n ? sq[32 * v + lane] : 0.f;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      float s = 0.f + v4[v];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      g[v] = s;
     }
+  } else {
 #pragma unroll
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    g[v] = s;
+    for (int v = 0; v < 4; ++v) {
+      float s = 0.f;
+      const int t = 32 * v + lane;
+      if (fu.ssq_in) {
+        const float* sq = fu.ssq_in + m * fu.ssq_n;
+        for (int i = t; i < fu.ssq_n; i += 128) s += sq[i];
+      } else {
+        const float* xm = x + m * ldx;
+        for (int64_t k = t; k < K; k += 128) s = fmaf(xm[k], xm[k], s);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      g[v] = s;
+    }
   }
   const float tot = (g[0] + g[1]) + (g[2] + g[3]);
   return 1.0f / sqrtf(tot / (float)K + fu.eps);
@@ -154,12 +169,14 @@ __global__ void act_records_fused_kernel(const float* __restrict__ x, int64_t ld
     const int64_t m = rem >> 3;
     const int j = (int)(rem & 7);
     const int64_t k = kb * 256 + 32 * j + lane;
+    // every input of this value is requested before any is used
     float v = k < K ? x[m * ldx + k] : 0.0f;
+    const float e = k >= K ? 0.0f : fu.swiglu ? x[m * ldx + K + k] : fu.norm_w ? fu.norm_w[k] : 0.0f;
     if (fu.swiglu) {
-      v = k < K ? act_silu(v) * x[m * ldx + K + k] : 0.0f;
+      v = k < K ? act_silu(v) * e : 0.0f;
     } else if (fu.norm_w) {
       const float r = act_rms(fu, x, m, ldx, K, lane);
-      if (k < K) v = v * r * fu.norm_w[k];
+      if (k < K) v = v * r * e;
     }
     float am = fabsf(v);
 #pragma unroll

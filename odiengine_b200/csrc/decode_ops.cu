@@ -117,10 +117,10 @@ __global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, con
 // kv_len = pos + 1.  Thread 0 streams each chunk's K and V tiles (64 x HD
 // fp16 each, contiguous in the [kv_head][ctx][HD] cache) into a two-stage
 // shared-memory ring with cp.async.bulk (no multicast), completing on an
-// mbarrier; the four warps take 16 positions each.  Scores: lane l holds
-// dims [l*HD/32, +HD/32) of q; the 16 partial dots are summed across lanes
-// by a halving butterfly (16 shuffles), after which lanes 2t and 2t+1 hold
-// position t's score.  Online softmax per warp and head (running max m,
+// mbarrier; its warps take ATT_PW positions each.  Scores: lane l holds
+// dims [l*HD/32, +HD/32) of q; the partial dots are summed across lanes by
+// a halving butterfly, after which lanes 32/ATT_PW * t .. hold position t's
+// score.  Online softmax per warp and head (running max m,
 // sum l, output acc), then the CTA folds its warps and writes (m, l,
 // acc[HD]) per head for its split.  The last CTA of kv head kvh to finish
 // (arrival counter) folds the splits in split order, writes the heads'
@@ -134,11 +134,13 @@ __global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, con
 // the CTA stops consuming (the decision is made uniform by a CTA-wide vote),
 // drains its copies in flight and still arrives, so counters stay balanced.
 constexpr int ATT_STAGES = 2;
-constexpr int ATT_THREADS = 128;
+constexpr int ATT_PW = 8;                       // positions per warp per chunk
+constexpr int ATT_WARPS = ATT_CHUNK / ATT_PW;   // warps per CTA
+constexpr int ATT_THREADS = 32 * ATT_WARPS;
 
 template <int HD, int G>
 constexpr int att_smem_bytes() {
-  return ATT_STAGES * 2 * ATT_CHUNK * HD * 2 + 4 * G * (HD + 2) * 4 + ATT_STAGES * 8;
+  return ATT_STAGES * 2 * ATT_CHUNK * HD * 2 + ATT_WARPS * G * (HD + 2) * 4 + ATT_STAGES * 8;
 }
 
 template <int HD, int G>
@@ -153,11 +155,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
                                                            uint8_t* __restrict__ orec) {
   constexpr int DPL = HD / 32;           // dims per lane
   constexpr int TILE = ATT_CHUNK * HD;   // halves per K (or V) tile
-  constexpr int PW = ATT_CHUNK / 4;      // positions per warp per chunk (16)
+  constexpr int PW = ATT_PW;             // positions per warp per chunk
+  constexpr int LPP = 32 / PW;           // lanes per position after the butterfly
+  constexpr int NW = ATT_WARPS;
   extern __shared__ __align__(128) uint8_t att_smem[];
   __half* tiles = reinterpret_cast<__half*>(att_smem);  // [stage][K | V][TILE]
-  float* fold = reinterpret_cast<float*>(att_smem + ATT_STAGES * 2 * TILE * 2);  // [4][G][HD + 2]
-  uint64_t* full = reinterpret_cast<uint64_t*>(fold + 4 * G * (HD + 2));
+  float* fold = reinterpret_cast<float*>(att_smem + ATT_STAGES * 2 * TILE * 2);  // [NW][G][HD + 2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(fold + NW * G * (HD + 2));
   __shared__ int is_last;
   pdl_launch_dependents();
   pdl_wait();  // q and the cache are written by the kernels before
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
     v0h = __float2half_rn(vraw[(int64_t)kvh * HD + t]);
     v1h = __float2half_rn(vraw[(int64_t)kvh * HD + t + HALF]);
   }
-  const int pidx = (lane >> 1) & 15;  // the position whose score this lane ends with
+  const int pidx = (lane / LPP) & (PW - 1);  // the position whose score this lane ends with
   int i = 0;
   for (; i < nmine; ++i) {
     const int s = i % ATT_STAGES;
@@ -277,7 +281,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
           }
           sc[t] = d;
         }
-        // halving butterfly: 16 positions x 32 lanes -> position pidx on lanes 2*pidx, 2*pidx + 1
+        // halving butterfly: PW positions x 32 lanes -> position pidx on lanes LPP*pidx .. +LPP-1
 #pragma unroll
         for (int w = 16, n = PW / 2; n >= 1; w >>= 1, n >>= 1) {
           const bool up = lane & w;
@@ -288,7 +292,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
             sc[t] = keep + __shfl_xor_sync(0xffffffffu, send, w);
           }
         }
-        const float sfull = sc[0] + __shfl_xor_sync(0xffffffffu, sc[0], 1);
+        float sfull = sc[0];
+#pragma unroll
+        for (int w = LPP / 2; w; w >>= 1) sfull += __shfl_xor_sync(0xffffffffu, sfull, w);
         const bool valid = pidx < nvalid;
         const float sv = valid ? sfull : -INFINITY;
         float mx = sv;
@@ -297,14 +303,14 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
         const float mn = fmaxf(m[g], mx);  // finite: nvalid > 0
         const float corr = expf(m[g] - mn);
         const float pv = valid ? expf(sv - mn) : 0.f;
-        float ps = (lane & 1) ? 0.f : pv;
+        float ps = (lane & (LPP - 1)) ? 0.f : pv;
 #pragma unroll
         for (int w = 16; w; w >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, w);
         l[g] = l[g] * corr + ps;
 #pragma unroll
         for (int e = 0; e < DPL; ++e) acc[g][e] *= corr;
         for (int t = 0; t < nvalid; ++t) {  // rows past the chunk's end hold stale data: not read
-          const float pt = __shfl_sync(0xffffffffu, pv, 2 * t);
+          const float pt = __shfl_sync(0xffffffffu, pv, LPP * t);
 #pragma unroll
           for (int e = 0; e < DPL / 2; ++e) {
             const float2 vv = __half22float2(reinterpret_cast<const __half2*>(Vs + t * HD)[e]);
@@ -323,7 +329,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
     for (int j = i; j < issued; ++j)
       mbar_wait(&full[j % ATT_STAGES], (uint32_t)(j / ATT_STAGES) & 1u, err, ERR_DRAIN_WAIT);
   }
-  // fold the four warps, per head
+  // fold the warps, per head
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     float* f = fold + (warp * G + g) * (HD + 2);
@@ -339,10 +345,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
     const int g = idx / HD, d = idx - g * HD;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, fold[(w * G + g) * (HD + 2)]);
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, fold[(w * G + g) * (HD + 2)]);
     float a = 0.f, L = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const float* f = fold + (w * G + g) * (HD + 2);
       if (f[0] != -INFINITY) {
         const float sc = expf(f[0] - M);
