@@ -228,12 +228,33 @@ size_t odi_cuda_q8_records_bytes(int64_t M, int64_t K);
 int odi_cuda_quantize_records(const float* d_x, int64_t M, int64_t K, const odi_cuda_matmul_opts* opts, void* d_recs,
                               int flags, void* stream);
 
-/* The streaming GEMV (ACT_Q8) on pre-quantized Q8 records; opts' epilogue
- * fields (accumulate, out_ssq) apply, its prologue fields must be unset.
- * Workspace: 256 bytes. */
+/* Options of odi_cuda_matmul_q8rec (all zero / NULL: the plain product). */
+typedef struct odi_cuda_q8rec_opts {
+  int accumulate;              /* y += product */
+  float* out_ssq;              /* as odi_cuda_matmul_opts.out_ssq */
+  /* The input records hold u = x * w of an RMSNorm (x its input, w its
+   * weights): each token's records are scaled by 1 / sqrt(sum(x^2) / K + eps)
+   * first, the sum from norm_ssq_count slots per token (out_ssq of x's
+   * writer).  The quantisation of u differs from that of the normalised row
+   * only by the fp16 rounding of each block scale. */
+  const float* norm_ssq;
+  int norm_ssq_count;
+  float norm_eps;
+  /* Records of the stored y for the next product ([N/256][M], 16-byte
+   * aligned; N a multiple of 256): of y * out_norm_weight (the next
+   * RMSNorm's weights) or of y itself; or, with out_swiglu, the weight's
+   * rows being 32 gate rows then the 32 matching up rows in every 64-row
+   * tile (N a multiple of 512), of silu(gate) * up ([N/512][M] records). */
+  void* out_records;
+  const float* out_norm_weight;
+  int out_swiglu;
+} odi_cuda_q8rec_opts;
+
+/* The streaming GEMV (ACT_Q8) on pre-quantized Q8 records, with the options
+ * above (opts may be NULL).  Workspace: 256 bytes. */
 int odi_cuda_matmul_q8rec(int dtype, const void* d_w_tiled, const void* d_recs, float* d_y, int64_t M, int64_t N,
                           int64_t K, void* d_workspace, size_t workspace_bytes, int flags,
-                          const odi_cuda_matmul_opts* opts, void* stream);
+                          const odi_cuda_q8rec_opts* opts, void* stream);
 
 /* Reads and clears the device-side error word of a workspace (kernel waits
  * that gave up set it).  Synchronises `stream`.  *status = 0 when clean. */
@@ -273,9 +294,11 @@ typedef struct odi_cuda_decode_state {
 /* x[E] = table[token] (Backend::embedding, cpu_backend.cpp:610-619; table
  * fp32 [vocab][E], an out-of-range token reads row 0).  d_ssq (or NULL):
  * the sum of squares of every 64 values, ceil(E / 64) floats, for a fused
- * RMSNorm (odi_cuda_matmul_opts.norm_ssq). */
+ * RMSNorm (odi_cuda_matmul_opts.norm_ssq).  d_records (or NULL; E a
+ * multiple of 256): x * d_norm_w (x itself when d_norm_w is NULL) as one
+ * token's Q8 records, for odi_cuda_matmul_q8rec with norm_ssq. */
 int odi_cuda_embed(const float* d_table, int64_t vocab, int64_t E, const odi_cuda_decode_state* d_state, float* d_x,
-                   float* d_ssq, void* stream);
+                   float* d_ssq, const float* d_norm_w, void* d_records, void* stream);
 
 /* y = x / sqrt(mean(x^2) + eps) * w per row of n (Backend::rms_norm,
  * cpu_backend.cpp:388-414).  y may alias x. */

@@ -80,7 +80,7 @@ SIGNATURES = {
     "odi_cuda_matmul_host_noalloc": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "odi_cuda_dequantize_host": (_int, [_vp, _vp, _vp]),
     "odi_cuda_tc_supported": (_int, [_int]),
-    "odi_cuda_embed": (_int, [_vp, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "odi_cuda_embed": (_int, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp]),
     "odi_cuda_rms_norm": (_int, [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
     "odi_cuda_rope_kv": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, ctypes.c_float, _vp]),
     "odi_cuda_attention_scratch_bytes": (_sz, [_int, _int, _int]),
@@ -117,6 +117,14 @@ class MatmulOpts(ctypes.Structure):
     _fields_ = [("norm_weight", ctypes.c_void_p), ("norm_eps", ctypes.c_float), ("swiglu", ctypes.c_int),
                 ("accumulate", ctypes.c_int), ("norm_ssq", ctypes.c_void_p), ("norm_ssq_count", ctypes.c_int),
                 ("out_ssq", ctypes.c_void_p)]
+
+
+class Q8RecOpts(ctypes.Structure):
+    """odi_cuda_q8rec_opts (include/odi_cuda.h)."""
+
+    _fields_ = [("accumulate", ctypes.c_int), ("out_ssq", ctypes.c_void_p), ("norm_ssq", ctypes.c_void_p),
+                ("norm_ssq_count", ctypes.c_int), ("norm_eps", ctypes.c_float), ("out_records", ctypes.c_void_p),
+                ("out_norm_weight", ctypes.c_void_p), ("out_swiglu", ctypes.c_int)]
 
 
 class Scatter(ctypes.Structure):

@@ -82,27 +82,7 @@ __global__ void act_q8_records_kernel(const float* __restrict__ x, int64_t ldx, 
     const int j = (int)(rem & 7);
     const int64_t k = kb * 256 + 32 * j + lane;
     const float v = k < K ? x[m * ldx + k] : 0.0f;
-    float am = fabsf(v);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const float d = __fdiv_rn(am, 127.0f);
-    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-    const int q = (int)roundf(__fmul_rn(v, id));
-    int s = q;
-#pragma unroll
-    for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);  // within 16-lane halves
-    const int s_lo = __shfl_sync(0xffffffffu, s, 0), s_hi = __shfl_sync(0xffffffffu, s, 16);
-    uint8_t* rec = recs + (kb * M + m) * Q8_REC_BYTES;
-    rec[32 * j + lane] = (uint8_t)(int8_t)q;
-    if (lane == 0) {
-      const float dx = __half2float(__float2half_rn(d));
-      float4 r;
-      r.x = dx;
-      r.y = __fmul_rn((float)(s_lo + s_hi), dx);
-      r.z = __fmul_rn((float)s_lo, dx);
-      r.w = __fmul_rn((float)s_hi, dx);
-      *reinterpret_cast<float4*>(rec + 256 + 16 * j) = r;
-    }
+    q8_block_to_record(v, lane, recs + (kb * M + m) * Q8_REC_BYTES, j);
   }
 }
 
@@ -178,27 +158,7 @@ __global__ void act_records_fused_kernel(const float* __restrict__ x, int64_t ld
       const float r = act_rms(fu, x, m, ldx, K, lane);
       if (k < K) v = v * r * e;
     }
-    float am = fabsf(v);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const float d = __fdiv_rn(am, 127.0f);
-    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-    const int q = (int)roundf(__fmul_rn(v, id));
-    int s = q;
-#pragma unroll
-    for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const int s_lo = __shfl_sync(0xffffffffu, s, 0), s_hi = __shfl_sync(0xffffffffu, s, 16);
-    uint8_t* rec = recs + (kb * M + m) * Q8_REC_BYTES;
-    rec[32 * j + lane] = (uint8_t)(int8_t)q;
-    if (lane == 0) {
-      const float dx = __half2float(__float2half_rn(d));
-      float4 r;
-      r.x = dx;
-      r.y = __fmul_rn((float)(s_lo + s_hi), dx);
-      r.z = __fmul_rn((float)s_lo, dx);
-      r.w = __fmul_rn((float)s_hi, dx);
-      *reinterpret_cast<float4*>(rec + 256 + 16 * j) = r;
-    }
+    q8_block_to_record(v, lane, recs + (kb * M + m) * Q8_REC_BYTES, j);
   }
 }
 

@@ -113,6 +113,7 @@ int run_gemv(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int
     a.M = (int)((M - m0) < plan.mt ? (M - m0) : plan.mt);
     a.recs = plan.pre ? recs + m0 * Q8_REC_BYTES : nullptr;
     a.rec_ld = M;
+    if (a.fu.rec_out) a.fu.rec_out += m0 * Q8_REC_BYTES;
     a.sc = GemvScatter{};
     if (sc) {
       a.sc = *sc;
@@ -408,7 +409,7 @@ int odi_cuda_quantize_records(const float* d_x, int64_t M, int64_t K, const odi_
 
 int odi_cuda_matmul_q8rec(int dtype, const void* d_w_tiled, const void* d_recs, float* d_y, int64_t M, int64_t N,
                           int64_t K, void* d_workspace, size_t workspace_bytes, int flags,
-                          const odi_cuda_matmul_opts* opts, void* stream) {
+                          const odi_cuda_q8rec_opts* opts, void* stream) {
   int rc = check_shape(dtype, N, K);
   if (rc) return rc;
   if (M < 1 || M > (1 << 20)) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M=%lld", (long long)M);
@@ -416,11 +417,30 @@ int odi_cuda_matmul_q8rec(int dtype, const void* d_w_tiled, const void* d_recs, 
   if (((uintptr_t)d_w_tiled | (uintptr_t)d_workspace | (uintptr_t)d_recs) & 15)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "weight, records and workspace must be 16-byte aligned");
   if (workspace_bytes < WS_HEADER) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small");
-  GemvFuse fu;
-  rc = fuse_from_opts(opts, &fu);
-  if (rc) return rc;
-  if (fu.norm_w || fu.swiglu)
-    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "matmul_q8rec: the prologue belongs to odi_cuda_quantize_records");
+  GemvFuse fu{};
+  if (opts) {
+    fu.accumulate = opts->accumulate ? 1 : 0;
+    fu.ssq_out = opts->out_ssq;
+    if (opts->norm_ssq) {
+      if (opts->norm_ssq_count < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "norm_ssq_count must be positive");
+      fu.rec_scale = 1;
+      fu.ssq_in = opts->norm_ssq;
+      fu.ssq_n = opts->norm_ssq_count;
+      fu.eps = opts->norm_eps;
+    }
+    if (opts->out_records) {
+      if ((uintptr_t)opts->out_records & 15)
+        return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "out_records must be 16-byte aligned");
+      if (opts->out_swiglu ? (N % 512 != 0) : (N % 256 != 0))
+        return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "out_records need N %% 256 == 0 (%% 512 with out_swiglu)");
+      if (opts->out_swiglu && opts->out_norm_weight)
+        return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "out_swiglu and out_norm_weight are exclusive");
+      fu.rec_out = (uint8_t*)opts->out_records;
+      fu.rec_out_ld = M;
+      fu.rec_norm_w = opts->out_norm_weight;
+      fu.rec_swiglu = opts->out_swiglu ? 1 : 0;
+    }
+  }
   return run_gemv(dtype, d_w_tiled, nullptr, d_y, M, N, K, false, (int*)d_workspace, workspace_bytes,
                   (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, nullptr, &fu, (const uint8_t*)d_recs);
 }
@@ -455,9 +475,12 @@ static_assert(sizeof(odi_cuda_decode_state) == sizeof(DecodeState), "decode stat
 extern "C" {
 
 int odi_cuda_embed(const float* d_table, int64_t vocab, int64_t E, const odi_cuda_decode_state* d_state, float* d_x,
-                   float* d_ssq, void* stream) {
+                   float* d_ssq, const float* d_norm_w, void* d_records, void* stream) {
   if (!d_table || !d_state || !d_x || vocab < 1 || E < 1) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "embed: bad argument");
-  CK(launch_embed(d_table, vocab, E, reinterpret_cast<const DecodeState*>(d_state), d_x, d_ssq, (cudaStream_t)stream),
+  if (d_records && (E % 256 || (uintptr_t)d_records & 15))
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "embed: records need E %% 256 == 0 and 16-byte alignment");
+  CK(launch_embed(d_table, vocab, E, reinterpret_cast<const DecodeState*>(d_state), d_x, d_ssq, d_norm_w,
+                  (uint8_t*)d_records, (cudaStream_t)stream),
      "embed launch");
   return ODI_CUDA_OK;
 }

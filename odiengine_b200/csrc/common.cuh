@@ -168,6 +168,30 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// One Q8_0 block of 32 values, one per lane, into a Q8 record: the codes at
+// rec + 32 * j + lane, {dx, sdx, sdx_lo, sdx_hi} at rec + 256 + 16 * j.  The
+// gguf Q8_0 quantiser in IEEE fp32 (d = amax / 127, id = d ? 1 / d : 0,
+// q = round-half-away(v * id), d kept as fp16), then dx = that fp16 widened
+// and the block's code sums times dx.  All 32 lanes of the warp take part.
+__device__ __forceinline__ void q8_block_to_record(float v, int lane, uint8_t* rec, int j) {
+  float am = fabsf(v);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+  const float d = __fdiv_rn(am, 127.0f);
+  const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+  const int q = (int)roundf(__fmul_rn(v, id));
+  int s = q;
+#pragma unroll
+  for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);  // within 16-lane halves
+  const int s_lo = __shfl_sync(0xffffffffu, s, 0), s_hi = __shfl_sync(0xffffffffu, s, 16);
+  rec[32 * j + lane] = (uint8_t)(int8_t)q;
+  if (lane == 0) {
+    const float dx = __half2float(__float2half_rn(d));
+    *reinterpret_cast<float4*>(rec + 256 + 16 * j) =
+        make_float4(dx, __fmul_rn((float)(s_lo + s_hi), dx), __fmul_rn((float)s_lo, dx), __fmul_rn((float)s_hi, dx));
+  }
+}
+
 // Programmatic dependent launch controls (no-ops when not launched with PDL).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {

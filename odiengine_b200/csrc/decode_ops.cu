@@ -32,9 +32,11 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // One CTA of 64 threads per 64 values; with ssq, each CTA also leaves the
-// sum of squares of its values (the slot a fused RMSNorm reads).
+// sum of squares of its values (the slot a fused RMSNorm reads); with recs,
+// the row times norm_w (or the row) as Q8 records for the first product.
 __global__ void embed_kernel(const float* __restrict__ table, const DecodeState* st, float* __restrict__ x,
-                             float* __restrict__ ssq, int64_t E, int64_t vocab) {
+                             float* __restrict__ ssq, int64_t E, int64_t vocab, const float* __restrict__ norm_w,
+                             uint8_t* __restrict__ recs) {
   __shared__ float red[2];
   pdl_launch_dependents();
   pdl_wait();
@@ -48,6 +50,10 @@ __global__ void embed_kernel(const float* __restrict__ table, const DecodeState*
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
     if (threadIdx.x == 0) ssq[blockIdx.x] = red[0] + red[1];
+  }
+  if (recs) {  // E is a multiple of 256: whole warps, whole records
+    const float u = (norm_w && i < E) ? v * norm_w[i] : v;
+    q8_block_to_record(u, threadIdx.x & 31, recs + (i >> 8) * Q8_REC_BYTES, (int)((i & 255) >> 5));
   }
 }
 
@@ -404,27 +410,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
       // The output row as the next GEMV's Q8 record (one token): each warp
       // holds 32 consecutive values = one Q8 block; the quantisation of
       // act_q8_records_kernel, bit for bit.
-      const int lane = threadIdx.x & 31;
       const int64_t col = (int64_t)h * HD + d;
-      const int64_t kb = col >> 8;
-      const int j = (int)((col & 255) >> 5);
-      float am = fabsf(val);
-#pragma unroll
-      for (int w = 16; w; w >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, w));
-      const float dq = __fdiv_rn(am, 127.0f);
-      const float id = dq == 0.0f ? 0.0f : __fdiv_rn(1.0f, dq);
-      const int q = (int)roundf(__fmul_rn(val, id));
-      int sq = q;
-#pragma unroll
-      for (int w = 8; w; w >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, w);
-      const int s_lo = __shfl_sync(0xffffffffu, sq, 0), s_hi = __shfl_sync(0xffffffffu, sq, 16);
-      uint8_t* rec = orec + kb * Q8_REC_BYTES;
-      rec[32 * j + lane] = (uint8_t)(int8_t)q;
-      if (lane == 0) {
-        const float dx = __half2float(__float2half_rn(dq));
-        *reinterpret_cast<float4*>(rec + 256 + 16 * j) =
-            make_float4(dx, __fmul_rn((float)(s_lo + s_hi), dx), __fmul_rn((float)s_lo, dx), __fmul_rn((float)s_hi, dx));
-      }
+      q8_block_to_record(val, threadIdx.x & 31, orec + (col >> 8) * Q8_REC_BYTES, (int)((col & 255) >> 5));
     }
   }
   if (threadIdx.x == 0) cnt[kvh] = 0;
@@ -537,8 +524,9 @@ static int grid_for(int64_t n, int threads) {
 }
 
 cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x, float* ssq,
-                         cudaStream_t s) {
-  return launch_pdl(embed_kernel, dim3((unsigned)((E + 63) / 64)), dim3(64), s, table, st, x, ssq, E, vocab);
+                         const float* norm_w, uint8_t* recs, cudaStream_t s) {
+  return launch_pdl(embed_kernel, dim3((unsigned)((E + 63) / 64)), dim3(64), s, table, st, x, ssq, E, vocab, norm_w,
+                    recs);
 }
 
 cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,

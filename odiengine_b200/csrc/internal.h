@@ -61,6 +61,18 @@ struct GemvFuse {
   const float* ssq_in;  // norm: sums of squares of x in ssq_n slots per token (else summed from x)
   int ssq_n;
   float* ssq_out;       // sums of squares of the stored y, one slot per 64-row tile: [M][G]
+  // Pre-quantized input (plan.pre) that holds u = x * norm weights: scale its
+  // records by each token's 1 / sqrt(mean(x^2) + eps), from ssq_in / ssq_n.
+  int rec_scale;
+  // Records of the stored y for the next product, [ceil(N/256)][rec_out_ld]
+  // (this pass's first token at rec_out): of y * rec_norm_w (the next
+  // RMSNorm's weights; y itself when null), or -- rec_swiglu, the rows of
+  // each 64-row tile being 32 gate rows then the 32 matching up rows -- of
+  // silu(gate) * up, N / 2 values.
+  uint8_t* rec_out;
+  int64_t rec_out_ld;
+  const float* rec_norm_w;
+  int rec_swiglu;
 };
 
 struct GemvArgs {
@@ -114,7 +126,7 @@ inline size_t att_part_offset(int heads) { return (ATT_CNT_OFFSET + (size_t)head
 size_t attention_scratch(int heads, int hd, int ctx);
 int attention_splits(int kv_heads, int ctx, int num_sms);
 cudaError_t launch_embed(const float* table, int64_t vocab, int64_t E, const DecodeState* st, float* x, float* ssq,
-                         cudaStream_t s);
+                         const float* norm_w, uint8_t* recs, cudaStream_t s);
 cudaError_t launch_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,
                             cudaStream_t s);
 cudaError_t launch_rope_kv(float* q, float* k, const float* v, __half* kc, __half* vc, const DecodeState* st,

@@ -341,7 +341,8 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
 // consumer threads, one memory round trip); record (j, m) of the chunk to
 // xr + (j * MT + m) * Q8_REC_BYTES.
 template <int MT>
-__device__ __forceinline__ void stage_records(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr) {
+__device__ __forceinline__ void stage_records(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr,
+                                              float* __restrict__ fuse_smem) {
   constexpr int V = Q8_REC_BYTES / 16;  // 16-byte pieces per record
   const int per_span = a.M * V;
   for (int c = threadIdx.x; c < nsp * per_span; c += NCW * 32) {
@@ -351,8 +352,19 @@ __device__ __forceinline__ void stage_records(const GemvArgs& a, int kb0, int ns
                a.recs + ((int64_t)(kb0 + j) * a.rec_ld + m) * Q8_REC_BYTES + 16 * v, 16);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
+  if (a.fu.rec_scale) row_rms<MT>(a, fuse_smem, fuse_smem + MT);  // overlaps the copies
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   consumer_sync();
+  if (a.fu.rec_scale) {
+    // records of u = x * w: the token's 1 / rms scales every block factor
+    for (int i = threadIdx.x; i < nsp * a.M * 32; i += NCW * 32) {
+      const int rj = i >> 5, f = i & 31;
+      const int j = rj / a.M, m = rj - j * a.M;
+      float* xf = reinterpret_cast<float*>(xr + (j * MT + m) * Q8_REC_BYTES + 256);
+      xf[f] = xf[f] * fuse_smem[m];
+    }
+    consumer_sync();
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -809,6 +821,31 @@ __device__ __forceinline__ void write_ssq(const GemvArgs& a, const float* buf, i
   }
 }
 
+// The tile's stored y (fin[r * MT + m]) as records for the next product:
+// one warp per 32-row block, lane = row (fu.rec_out).
+__device__ __forceinline__ void write_records(const GemvArgs& a, const float* fin, int MTs, int g) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (!a.fu.rec_swiglu) {
+    for (int b = warp; b < 2 * a.M; b += NCW) {
+      const int m = b >> 1, r = 32 * (b & 1) + lane;
+      const int64_t n = (int64_t)g * UNIT_ROWS + r;
+      float u = n < a.N ? fin[r * MTs + m] : 0.f;
+      if (a.fu.rec_norm_w && n < a.N) u = u * a.fu.rec_norm_w[n];
+      q8_block_to_record(u, lane, a.fu.rec_out + ((n >> 8) * a.fu.rec_out_ld + m) * Q8_REC_BYTES,
+                         (int)((n & 255) >> 5));
+    }
+  } else {
+    // rows 0-31 of the tile are gate rows, 32-63 the matching up rows: one
+    // block of the SwiGLU output, columns 32g .. 32g + 31
+    for (int m = warp; m < a.M; m += NCW) {
+      const float v = silu_f(fin[lane * MTs + m]) * fin[(32 + lane) * MTs + m];
+      const int64_t n = (int64_t)g * 32 + lane;
+      q8_block_to_record(v, lane, a.fu.rec_out + ((n >> 8) * a.fu.rec_out_ld + m) * Q8_REC_BYTES,
+                         (int)((n & 255) >> 5));
+    }
+  }
+}
+
 // After this CTA's output stores (consumer_sync between), one thread per
 // writing CTA: the CTA's stores are ordered before its arrival on the
 // launch's local completion count (GPU scope); the last of the
@@ -918,7 +955,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   // ---------------- consumers
   pdl_wait();  // x is written by earlier kernels on the stream; y may be read by them
   if (PRE)
-    stage_records<MT>(a, kb0, nsp, xr);
+    stage_records<MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
   else
     stage_acts<F32, MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
 
@@ -971,7 +1008,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
       if (pl.C == 1) {
         const int64_t n = (int64_t)g * UNIT_ROWS + r;
         const float nv = n < a.N ? store_out(a, m, n, v) : 0.f;
-        if (a.fu.ssq_out) red[(0 * UNIT_ROWS + r) * MT + m] = nv * nv;  // the slot this thread just read
+        if (a.fu.ssq_out) red[(0 * UNIT_ROWS + r) * MT + m] = nv * nv;  // the slots this thread just read
+        if (a.fu.rec_out) red[(1 * UNIT_ROWS + r) * MT + m] = nv;
       } else {
         part[t] = v;
       }
@@ -980,6 +1018,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   if (pl.C == 1 && a.fu.ssq_out) {
     consumer_sync();
     write_ssq(a, red, MT, 1, g, pl.G);
+  }
+  if (pl.C == 1 && a.fu.rec_out) {
+    consumer_sync();
+    write_records(a, red + UNIT_ROWS * MT, MT, g);
   }
   if (pl.C > 1) {
     if (rank == 0) {
@@ -992,10 +1034,15 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
         const int64_t n = (int64_t)g * UNIT_ROWS + r;
         const float nv = n < a.N ? store_out(a, m, n, v) : 0.f;
         if (a.fu.ssq_out) part[t] = nv * nv;  // the slot this thread just read
+        if (a.fu.rec_out) red[(UNIT_ROWS + r) * MT + m] = nv;  // red is free by now
       }
       if (a.fu.ssq_out) {
         consumer_sync();
         write_ssq(a, part, 1, UNIT_ROWS, g, pl.G);
+      }
+      if (a.fu.rec_out) {
+        consumer_sync();
+        write_records(a, red + UNIT_ROWS * MT, MT, g);
       }
       if (a.sc.n) {
         consumer_sync();

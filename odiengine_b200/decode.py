@@ -85,23 +85,54 @@ class ModelWeights:
     layers: list = field(default_factory=list)
     out_norm: object = None
     output: Optional[DeviceWeight] = None
+    # gate|up rows interleaved by 32 in every 64-row tile (interleave_gate_up):
+    # the gate|up GEMV can then hand the down GEMV its SwiGLU records
+    gu_interleaved: bool = False
 
 
-def _seeded_quant(dtype: int, N: int, K: int, gen, device, std: float = 0.02) -> DeviceWeight:
+def gate_up_order(F: int):
+    """Row order of an interleaved gate|up weight: row p of the stored weight
+    is row gate_up_order(F)[p] of the [gate F | up F] weight.  Every 64-row
+    tile holds 32 gate rows and the 32 matching up rows (F % 32 == 0)."""
+    import numpy as np
+
+    if F % 32:
+        raise ValueError("interleaving gate|up needs F % 32 == 0")
+    p = np.arange(2 * F)
+    t, i = p // 64, p % 64
+    return np.where(i < 32, 32 * t + i, F + 32 * t + (i - 32))
+
+
+def interleave_gate_up(blocks, F: int, row_bytes: int):
+    """GGUF block rows of a [gate F | up F] weight (device uint8 tensor) in
+    the interleaved order."""
     import torch
+
+    idx = torch.as_tensor(gate_up_order(F), device=blocks.device)
+    return blocks.view(2 * F, row_bytes).index_select(0, idx).reshape(-1)
+
+
+def _seeded_quant(dtype: int, N: int, K: int, gen, device, std: float = 0.02, interleave: bool = False) -> DeviceWeight:
+    import torch
+
+    from . import gguf_bytes
 
     w = torch.empty((N, K), dtype=torch.float32, device=device).normal_(0.0, std, generator=gen)
     blocks = quantize_weight(dtype, w)
     del w
+    if interleave:
+        blocks = interleave_gate_up(blocks, N // 2, gguf_bytes(dtype, 1, K))
     tiled = repack(dtype, blocks, N, K)
     del blocks
     return DeviceWeight.from_tiled(dtype, N, K, tiled)
 
 
-def seeded_model(cfg: LlamaConfig, seed: int = 0, device=None) -> ModelWeights:
+def seeded_model(cfg: LlamaConfig, seed: int = 0, device=None, interleave_gate_up: bool = True) -> ModelWeights:
     """A random-init model of the given shape: weights N(0, 0.02) quantised on
     the device (attention and gate/up cfg.attn_dtype, down and output
-    cfg.down_dtype), norm weights 1 + N(0, 0.02), embeddings N(0, 1)."""
+    cfg.down_dtype), norm weights 1 + N(0, 0.02), embeddings N(0, 1).  The
+    same seed gives the same model whether or not the gate|up rows are
+    interleaved (only their order in HBM differs)."""
     import torch
 
     device = device or torch.device("cuda", torch.cuda.current_device())
@@ -120,10 +151,11 @@ def seeded_model(cfg: LlamaConfig, seed: int = 0, device=None) -> ModelWeights:
             wqkv=_seeded_quant(cfg.attn_dtype, cfg.qkv_rows, E, gen, device),
             wo=_seeded_quant(cfg.attn_dtype, E, cfg.heads * cfg.head_dim, gen, device),
             ffn_norm=norm(),
-            wgu=_seeded_quant(cfg.attn_dtype, 2 * F, E, gen, device),
+            wgu=_seeded_quant(cfg.attn_dtype, 2 * F, E, gen, device, interleave=interleave_gate_up),
             wdown=_seeded_quant(cfg.down_dtype, E, F, gen, device)))
     mw.out_norm = norm()
     mw.output = _seeded_quant(cfg.down_dtype, cfg.vocab, E, gen, device)
+    mw.gu_interleaved = interleave_gate_up
     return mw
 
 
@@ -132,18 +164,41 @@ class DecodeModel:
     forward pass (embed .. argmax) on ``stream``; ``capture()`` records it as
     a CUDA graph that ``generate`` replays."""
 
+    MODES = ("epilogue", "records", "fused", "separate")
+
     def __init__(self, cfg: LlamaConfig, weights: ModelWeights, device=None, max_record: int = 4096,
-                 fused: bool = True, records: bool = True):
+                 mode: str = "auto", fused: bool = True, records: bool = True):
+        """mode:
+          epilogue  every GEMV runs on Q8 records written by the kernel before
+                    it (the embedding, the attention, the residual and gate|up
+                    GEMVs' epilogues): 5 launches per layer.  Needs Q8
+                    activations and interleaved gate|up weights.
+          records   every GEMV runs on Q8 records made by a small kernel that
+                    applies RMSNorm / SwiGLU (the attention writes its own):
+                    8 launches per layer.
+          fused     RMSNorm, SwiGLU and the residual adds fused into the GEMVs,
+                    activations staged and quantized by every GEMV CTA.
+          separate  every operation its own kernel.
+          auto      epilogue when the weights allow it, else records (Q8
+                    activations) or fused (fp32 activations).
+        (fused=False / records=False select separate / fused.)"""
         import torch
 
         self.cfg, self.w = cfg, weights
-        # fused: RMSNorm, SwiGLU and the residual adds run inside the GEMVs
-        # (odi_cuda_matmul_fused); otherwise as separate kernels
-        self.fused = fused
-        # records (with fused): every GEMV input is quantized once into Q8
-        # records -- by a small kernel that also applies RMSNorm / SwiGLU, or
-        # by the attention itself -- instead of by every CTA of the GEMV
-        self.records = fused and records and cfg.act_mode == ACT_Q8
+        q8 = cfg.act_mode == ACT_Q8
+        if mode == "auto":
+            mode = ("separate" if not fused else "fused" if not (records and q8)
+                    else "epilogue" if weights.gu_interleaved else "records")
+        if mode not in self.MODES:
+            raise ValueError(f"unknown decode mode {mode!r}")
+        if (mode == "epilogue") != weights.gu_interleaved:
+            raise ValueError(f"mode {mode!r} needs gate|up weights {'interleaved' if mode == 'epilogue' else 'in [gate | up] order'}"
+                             " (seeded_model / load_llama interleave_gate_up)")
+        if mode in ("epilogue", "records") and not q8:
+            raise ValueError(f"mode {mode!r} runs on Q8 activations (cfg.act_mode = ACT_Q8)")
+        self.mode = mode
+        self.fused = mode != "separate"
+        self.records = mode == "records"
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         dev, f32 = self.device, torch.float32
         E, F, H, hd = cfg.hidden, cfg.ffn, cfg.heads, cfg.head_dim
@@ -239,18 +294,53 @@ class DecodeModel:
         check(lib().odi_cuda_quantize_records(_ptr(x), 1, K, ctypes.byref(o), _ptr(rec), FLAG_PDL, s))
 
     def _gemv_rec(self, dw: DeviceWeight, rec, y, s, accumulate=False):
-        o = self._opts(accumulate=accumulate)
+        self._q8rec(dw, rec, y, s, accumulate=accumulate)
+
+    def step(self) -> None:
+        {"epilogue": self._step_epilogue, "records": self._step_records, "fused": self._step_fused,
+         "separate": self._step_unfused}[self.mode]()
+
+    def _q8rec(self, dw: DeviceWeight, rec, y, s, accumulate=False, norm=False, out_rec=None, out_norm=None,
+               out_swiglu=False):
+        from . import Q8RecOpts
+
+        ssq = _ptr(self.ssq)
+        o = Q8RecOpts(1 if accumulate else 0, ssq if accumulate else None, ssq if norm else None, self.ssq_slots,
+                      self.cfg.eps, _ptr(out_rec) if out_rec is not None else None,
+                      _ptr(out_norm) if out_norm is not None else None, 1 if out_swiglu else 0)
         ws = dw._ws
         check(lib().odi_cuda_matmul_q8rec(dw.dtype, dw.data_ptr, _ptr(rec), _ptr(y), 1, dw.N, dw.K, _ptr(ws),
                                           ws.numel(), FLAG_PDL, ctypes.byref(o), s))
 
-    def step(self) -> None:
-        if self.records:
-            self._step_records()
-        elif self.fused:
-            self._step_fused()
-        else:
-            self._step_unfused()
+    def _step_epilogue(self) -> None:
+        """5 launches per layer, each GEMV on the Q8 records its producer wrote:
+        QKV GEMV (records of x * attn_norm, scaled by 1/rms from the slots),
+        attention (rope and the KV append fused in; writes the O GEMV's
+        records), O GEMV (+= x, slots, records of x * ffn_norm), gate|up GEMV
+        (scaled records; writes SwiGLU records), down GEMV (+= x, slots,
+        records of x * the next norm's weights)."""
+        cfg, L, s = self.cfg, lib(), self.stream.cuda_stream
+        E, H, KV, hd = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim
+        st = _ptr(self.state)
+        q = _ptr(self.qkv)
+        k = q + H * hd * 4
+        v = k + KV * hd * 4
+        scale = 1.0 / math.sqrt(hd)
+        layers = self.w.layers
+        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, E, st, _ptr(self.x), _ptr(self.ssq),
+                               _ptr(layers[0].attn_norm), _ptr(self.rec_e), s))
+        for li, lw in enumerate(layers):
+            nxt = layers[li + 1].attn_norm if li + 1 < len(layers) else self.w.out_norm
+            kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
+            self._q8rec(lw.wqkv, self.rec_e, self.qkv, s, norm=True)
+            check(L.odi_cuda_rope_attention(q, k, v, kc, vc, _ptr(self.attn), _ptr(self.rec_a), st, H, KV, hd,
+                                            cfg.ctx, cfg.theta, scale, _ptr(self.att_scratch),
+                                            self.att_scratch.numel() * 4, s))
+            self._q8rec(lw.wo, self.rec_a, self.x, s, accumulate=True, out_rec=self.rec_e, out_norm=lw.ffn_norm)
+            self._q8rec(lw.wgu, self.rec_e, self.gu, s, norm=True, out_rec=self.rec_f, out_swiglu=True)
+            self._q8rec(lw.wdown, self.rec_f, self.x, s, accumulate=True, out_rec=self.rec_e, out_norm=nxt)
+        self._q8rec(self.w.output, self.rec_e, self.logits, s, norm=True)
+        check(L.odi_cuda_argmax(_ptr(self.logits), cfg.vocab, st, _ptr(self.record), self.max_record, s))
 
     def _step_records(self) -> None:
         """8 launches per layer, every GEMV on pre-quantized records: records
@@ -264,7 +354,8 @@ class DecodeModel:
         k = q + H * hd * 4
         v = k + KV * hd * 4
         scale = 1.0 / math.sqrt(hd)
-        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, E, st, _ptr(self.x), _ptr(self.ssq), s))
+        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, E, st, _ptr(self.x), _ptr(self.ssq), None, None,
+                               s))
         for li, lw in enumerate(self.w.layers):
             kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
             self._records(self.x, E, self.rec_e, s, norm=lw.attn_norm)
@@ -292,7 +383,8 @@ class DecodeModel:
         k = q + H * hd * 4
         v = k + KV * hd * 4
         scale = 1.0 / math.sqrt(hd)
-        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, cfg.hidden, st, _ptr(self.x), _ptr(self.ssq), s))
+        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, cfg.hidden, st, _ptr(self.x), _ptr(self.ssq),
+                               None, None, s))
         for li, lw in enumerate(self.w.layers):
             kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
             self._gemv_fused(lw.wqkv, self.x, self.qkv, s, norm=lw.attn_norm)
@@ -313,7 +405,7 @@ class DecodeModel:
         k = q + H * hd * 4
         v = k + KV * hd * 4
         scale = 1.0 / math.sqrt(hd)
-        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, E, st, _ptr(self.x), None, s))
+        check(L.odi_cuda_embed(_ptr(self.w.token_embd), cfg.vocab, E, st, _ptr(self.x), None, None, None, s))
         for li, lw in enumerate(self.w.layers):
             kc, vc = _ptr(self.kc[li]), _ptr(self.vc[li])
             check(L.odi_cuda_rms_norm(_ptr(self.x), _ptr(lw.attn_norm), _ptr(self.h), 1, E, cfg.eps, s))
@@ -333,6 +425,8 @@ class DecodeModel:
         check(L.odi_cuda_argmax(_ptr(self.logits), cfg.vocab, st, _ptr(self.record), self.max_record, s))
 
     def launches_per_step(self) -> int:
+        if self.mode == "epilogue":
+            return 1 + 5 * self.cfg.layers + 2  # embed, per layer, output GEMV + argmax
         if self.records:
             return 1 + 8 * self.cfg.layers + 3  # embed, per layer, records + output GEMV + argmax
         if self.fused:

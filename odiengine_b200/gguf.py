@@ -298,14 +298,16 @@ def llama_config(f: GGUFFile, ctx: int = None):
                        attn_dtype=ODI_OF_GGML[q.ggml_type], down_dtype=ODI_OF_GGML[d.ggml_type])
 
 
-def load_llama(path: str, device=None, ctx: int = None):
+def load_llama(path: str, device=None, ctx: int = None, interleave_gate_up: bool = True):
     """The loader hook: open a GGUF Llama model and upload its weights to HBM
     once.  Returns (LlamaConfig, ModelWeights) for DecodeModel.  Each
     quantized weight goes up as its GGUF blocks and is repacked on the device
-    into the tiled layout; Q|K|V and gate|up are stacked by block rows."""
+    into the tiled layout; Q|K|V and gate|up are stacked by block rows (gate
+    and up interleaved by 32 rows per 64-row tile with interleave_gate_up,
+    the layout of DecodeModel's epilogue mode)."""
     import torch
 
-    from .decode import LayerWeights, ModelWeights
+    from .decode import LayerWeights, ModelWeights, interleave_gate_up as interleave
 
     device = device or torch.device("cuda", torch.cuda.current_device())
     with GGUFFile(path) as f:
@@ -321,10 +323,12 @@ def load_llama(path: str, device=None, ctx: int = None):
                                  f"{GGML_OF_ODI[dtype]} dims {(K, N)}")
             return torch.from_numpy(f.tensor(name).copy()).to(device, non_blocking=False)
 
-        def weight(names, dtype, Ns, K):
+        def weight(names, dtype, Ns, K, gate_up=False):
             parts = [blocks(n, dtype, N, K) for n, N in zip(names, Ns)]
             gg = parts[0] if len(parts) == 1 else torch.cat(parts)
             N = sum(Ns)
+            if gate_up:
+                gg = interleave(gg, N // 2, gguf_bytes(dtype, 1, K))
             return DeviceWeight.from_tiled(dtype, N, K, repack(dtype, gg, N, K))
 
         def f32(name, n):
@@ -343,9 +347,11 @@ def load_llama(path: str, device=None, ctx: int = None):
                             [H * hd, KV * hd, KV * hd], E),
                 wo=weight([p + "attn_output.weight"], cfg.attn_dtype, [E], H * hd),
                 ffn_norm=f32(p + "ffn_norm.weight", E),
-                wgu=weight([p + "ffn_gate.weight", p + "ffn_up.weight"], cfg.attn_dtype, [F, F], E),
+                wgu=weight([p + "ffn_gate.weight", p + "ffn_up.weight"], cfg.attn_dtype, [F, F], E,
+                           gate_up=interleave_gate_up),
                 wdown=weight([p + "ffn_down.weight"], cfg.down_dtype, [E], F)))
         mw.out_norm = f32("output_norm.weight", E)
         mw.output = weight(["output.weight"], cfg.down_dtype, [cfg.vocab], E)
+        mw.gu_interleaved = interleave_gate_up
         torch.cuda.synchronize(device)
     return cfg, mw

@@ -169,7 +169,7 @@ def _oracle_from_host(cfg, host):
 @pytest.mark.gpu
 def test_load_llama_uploads_blocks_and_decodes(cuda_lib, tiny_file):
     from odiengine_b200 import gguf
-    from odiengine_b200.decode import DecodeModel
+    from odiengine_b200.decode import DecodeModel, gate_up_order
     from oracle.llama import LlamaRef
 
     cfg, host, path = tiny_file
@@ -183,6 +183,8 @@ def test_load_llama_uploads_blocks_and_decodes(cuda_lib, tiny_file):
         assert np.array_equal(got, want)
         got = cuda_lib.unpack(lw.wgu.dtype, lw.wgu.tiled, lw.wgu.N, lw.wgu.K).cpu().numpy().ravel()
         want = np.concatenate([_flat(host[p + n]) for n in ("ffn_gate.weight", "ffn_up.weight")])
+        assert mw.gu_interleaved  # gate and up rows interleaved by 32 in every 64-row tile
+        want = want.reshape(2 * cfg.ffn, -1)[gate_up_order(cfg.ffn)].ravel()
         assert np.array_equal(got, want)
         got = cuda_lib.unpack(lw.wdown.dtype, lw.wdown.tiled, lw.wdown.N, lw.wdown.K).cpu().numpy().ravel()
         assert np.array_equal(got, _flat(host[p + "ffn_down.weight"]))

@@ -47,7 +47,8 @@ def test_embed_and_add(cuda_lib):
     st = _state(37, 0)
     td = _t(table)
     ssq = torch.zeros(2, device="cuda")
-    cuda_lib.check(L.odi_cuda_embed(td.data_ptr(), 50, 96, st.data_ptr(), x.data_ptr(), ssq.data_ptr(), None))
+    cuda_lib.check(L.odi_cuda_embed(td.data_ptr(), 50, 96, st.data_ptr(), x.data_ptr(), ssq.data_ptr(), None, None,
+                                    None))
     torch.cuda.synchronize()
     assert np.array_equal(x.cpu().numpy(), table[37])
     assert np.allclose(ssq.cpu().numpy(), [np.sum(table[37][:64] ** 2), np.sum(table[37][64:] ** 2)], rtol=1e-5)
@@ -258,9 +259,19 @@ def _tiny(act_mode):
 
 
 def _oracle_weights(ob, cfg, mw):
+    from odiengine_b200.decode import gate_up_order
+
     def deq(dw):
         blocks = ob.unpack(dw.dtype, dw.tiled, dw.N, dw.K).cpu().numpy()
         return O.dequantize(dw.dtype, blocks, dw.N, dw.K).astype(np.float64)
+
+    def deq_gu(dw):  # back to [gate | up] row order
+        w = deq(dw)
+        if not mw.gu_interleaved:
+            return w
+        out = np.empty_like(w)
+        out[gate_up_order(cfg.ffn)] = w
+        return out
 
     W = {"token_embd": mw.token_embd.cpu().numpy().astype(np.float64),
          "out_norm": mw.out_norm.cpu().numpy(), "output": deq(mw.output)}
@@ -269,20 +280,20 @@ def _oracle_weights(ob, cfg, mw):
         W[f"ffn_norm.{l}"] = lw.ffn_norm.cpu().numpy()
         W[f"wqkv.{l}"] = deq(lw.wqkv)
         W[f"wo.{l}"] = deq(lw.wo)
-        W[f"wgu.{l}"] = deq(lw.wgu)
+        W[f"wgu.{l}"] = deq_gu(lw.wgu)
         W[f"wdown.{l}"] = deq(lw.wdown)
     return W
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused", "separate"])
-@pytest.mark.parametrize("act_mode,tol", [(1, 2e-3), (0, 6e-2)], ids=["f32", "q8"])
-def test_tiny_model_matches_oracle(cuda_lib, act_mode, tol, fused):
+@pytest.mark.parametrize("mode,act_mode,tol", [("epilogue", 0, 6e-2), ("records", 0, 6e-2), ("fused", 0, 6e-2),
+                                              ("fused", 1, 2e-3), ("separate", 0, 6e-2), ("separate", 1, 2e-3)])
+def test_tiny_model_matches_oracle(cuda_lib, mode, act_mode, tol):
     from odiengine_b200.decode import DecodeModel, seeded_model
 
     cfg = _tiny(act_mode)
-    mw = seeded_model(cfg, seed=7)
-    # (the Q8 records path is taken with Q8 activations; with fp32 ones the fused GEMVs stage on chip)
-    dm = DecodeModel(cfg, mw, fused=fused, records=act_mode == 0)
+    mw = seeded_model(cfg, seed=7, interleave_gate_up=mode == "epilogue")
+    dm = DecodeModel(cfg, mw, mode=mode)
+    assert dm.mode == mode
     ref = LlamaRef(cfg, _oracle_weights(cuda_lib, cfg, mw))
     prompt = [5, 17, 999, 3, 250]
     dm.prefill(prompt[:-1])
@@ -309,9 +320,9 @@ def test_records_mode_equals_fused_mode(cuda_lib):
     from odiengine_b200.decode import DecodeModel, seeded_model
 
     cfg = _tiny(0)
-    mw = seeded_model(cfg, seed=5)
-    a = DecodeModel(cfg, mw, records=True)
-    b = DecodeModel(cfg, mw, records=False)
+    mw = seeded_model(cfg, seed=5, interleave_gate_up=False)
+    a = DecodeModel(cfg, mw, mode="records")
+    b = DecodeModel(cfg, mw, mode="fused")
     assert a.records and not b.records
     for m in (a, b):
         m.reset(7, 0)
@@ -439,7 +450,7 @@ def test_records_path_equals_fused(cuda_lib, dt, M):
                 else:
                     ob.check(L.odi_cuda_quantize_records(xs.data_ptr(), M, K, ctypes.byref(pro), rec.data_ptr(), 0,
                                                          None))
-                    o2 = ob.MatmulOpts(None, 0.0, 0, acc, None, 0, oss.data_ptr() if acc else None)
+                    o2 = ob.Q8RecOpts(acc, oss.data_ptr() if acc else None, None, 0, 0.0, None, None, 0)
                     ob.check(L.odi_cuda_matmul_q8rec(dt, dw.data_ptr, rec.data_ptr(), y.data_ptr(), M, N, K,
                                                      ws.data_ptr(), ws.numel(), 0, ctypes.byref(o2), None))
                 torch.cuda.synchronize()
@@ -447,11 +458,89 @@ def test_records_path_equals_fused(cuda_lib, dt, M):
                 outs.append((y.cpu().numpy(), oss.cpu().numpy()))
             assert np.array_equal(outs[0][0], outs[1][0]), (name, acc)
             assert np.array_equal(outs[0][1], outs[1][1]), (name, acc)
-    # the prologue belongs to the records, not to the product
-    bad = ob.MatmulOpts(nw.data_ptr(), 1e-5, 0, 0, None, 0, None)
+    # records of the output need whole 256-column spans (N = 320 is not)
+    bad = ob.Q8RecOpts(0, None, None, 0, 0.0, rec.data_ptr(), None, 0)
     rc = L.odi_cuda_matmul_q8rec(dt, dw.data_ptr, rec.data_ptr(), y.data_ptr(), M, N, K, ws.data_ptr(), ws.numel(),
                                  0, ctypes.byref(bad), None)
     assert rc == 2  # ODI_CUDA_ERR_INVALID_ARGUMENT
+    assert b"256" in L.odi_cuda_last_error()
+
+
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
+@pytest.mark.parametrize("M", [1, 2])
+def test_q8rec_epilogue_records(cuda_lib, dt, M):
+    """odi_cuda_matmul_q8rec's epilogue records equal odi_cuda_quantize_records
+    of the same values bit for bit (of y, of y * w_next, and -- gate|up rows
+    interleaved by 32 per 64-row tile -- of silu(gate) * up); records of
+    u = x * w scaled by 1/rms (norm_ssq) give the RMSNorm product within the
+    Q8 bound of odi_cuda_matmul_fused's test."""
+    import ctypes
+
+    import torch
+
+    from odiengine_b200.decode import gate_up_order
+
+    ob = cuda_lib
+    L = ob.lib()
+    N, K = 1024, 1024
+    rng = np.random.default_rng(dt * 10 + M)
+    b = O.quantize(dt, O.seeded_weights(N, K, seed=dt + 3))
+    ws = ob.new_workspace(256, torch.device("cuda"))
+    rb = L.odi_cuda_q8_records_bytes
+
+    def dev_weight(blocks):
+        return ob.DeviceWeight(ob.QuantWeight(dt, (K, N), np.ascontiguousarray(blocks)))
+
+    def records(x, Kx, opts=None):
+        r = torch.zeros(rb(M, Kx), dtype=torch.uint8, device="cuda")
+        ob.check(L.odi_cuda_quantize_records(x.data_ptr(), M, Kx, ctypes.byref(opts) if opts else None, r.data_ptr(),
+                                             0, None))
+        return r
+
+    def q8rec(dw, rec, opts):
+        y = torch.zeros((M, N), device="cuda")
+        ob.check(L.odi_cuda_matmul_q8rec(dt, dw.data_ptr, rec.data_ptr(), y.data_ptr(), M, N, K, ws.data_ptr(),
+                                         ws.numel(), 0, ctypes.byref(opts), None))
+        torch.cuda.synchronize()
+        assert ob.workspace_status(ws) == 0
+        return y
+
+    x = _t(rng.standard_normal((M, K)).astype(np.float32))
+    rin = records(x, K)
+    dw = dev_weight(b)
+    # plain and times-weights records of y
+    wn = _t((1 + 0.02 * rng.standard_normal(N)).astype(np.float32))
+    for nw in (None, wn):
+        rout = torch.zeros(rb(M, N), dtype=torch.uint8, device="cuda")
+        y = q8rec(dw, rin, ob.Q8RecOpts(0, None, None, 0, 0.0, rout.data_ptr(), nw.data_ptr() if nw is not None else None,
+                                        0))
+        assert torch.equal(rout, records(y * nw if nw is not None else y, N))
+    # SwiGLU records from the interleaved gate|up weight
+    F = N // 2
+    order = gate_up_order(F)
+    dwi = dev_weight(b.reshape(N, -1)[order])
+    rout = torch.zeros(rb(M, F), dtype=torch.uint8, device="cuda")
+    y = q8rec(dwi, rin, ob.Q8RecOpts(0, None, None, 0, 0.0, rout.data_ptr(), None, 1))
+    logical = torch.empty_like(y)
+    logical[:, torch.as_tensor(order, device="cuda")] = y  # back to [gate | up]
+    assert torch.equal(rout, records(logical.contiguous(), F, ob.MatmulOpts(None, 0.0, 1, 0, None, 0, None)))
+    # records of u = x * w scaled by 1 / rms from slots, against the fused RMSNorm product
+    nwk = _t((1 + 0.02 * rng.standard_normal(K)).astype(np.float32))
+    slots = K // 64
+    ssq = _t((x.cpu().numpy().reshape(M, slots, 64).astype(np.float64) ** 2).sum(-1).astype(np.float32))
+    y = q8rec(dw, records(x * nwk, K), ob.Q8RecOpts(0, None, ssq.data_ptr(), slots, 1e-5, None, None, 0))
+    yf = torch.zeros((M, N), device="cuda")
+    o = ob.MatmulOpts(nwk.data_ptr(), 1e-5, 0, 0, ssq.data_ptr(), slots, None)
+    ob.check(L.odi_cuda_matmul_fused(dt, dw.data_ptr, x.data_ptr(), yf.data_ptr(), M, N, K, 0, ws.data_ptr(),
+                                     ws.numel(), 0, ctypes.byref(o), None))
+    torch.cuda.synchronize()
+    W = O.dequantize(dt, b, N, K).astype(np.float64)
+    xn = x.cpu().numpy()
+    h = np.stack([rms_norm(xn[i], nwk.cpu().numpy(), 1e-5) for i in range(M)])
+    _, bact = O.matmul_q8act(dt, h.astype(np.float32), b, N)
+    tol = 1e-4 * (np.abs(h) @ np.abs(W).T) + 2 * bact
+    assert (np.abs(y.cpu().numpy() - h @ W.T) <= tol).all()
+    assert (np.abs(yf.cpu().numpy() - h @ W.T) <= tol).all()
 
 
 @pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K])
