@@ -27,9 +27,9 @@ __global__ void act_quant_q8_kernel(const float* __restrict__ x, int64_t M, int6
     float a = fabsf(v);
 #pragma unroll
     for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    const float d = __fdiv_rn(a, 127.0f);
-    const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-    const int q = (int)roundf(__fmul_rn(v, id));
+    const float d = q8_scale(a);
+    const float id = q8_inv(d);
+    const int q = q8_round(__fmul_rn(v, id));
     const __half dh = __float2half_rn(d);
     int s = q;
 #pragma unroll

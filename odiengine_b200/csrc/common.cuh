@@ -168,6 +168,27 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// The Q8_0 quantiser's three roundings without a division routine.
+//  * q8_scale: amax / 127 correctly rounded, as q0 = amax * RN(1/127) and
+//    one residual correction q0 + fma(-q0, 127, amax) * RN(1/127) (the
+//    correction step of Markstein's division theorem).  Equal to IEEE
+//    amax / 127.0f for every non-negative finite fp32 amax, subnormals
+//    included (checked exhaustively against the host's division).
+//  * q8_inv: 1 / d correctly rounded (__frcp_rn), 0 for d == 0.
+//  * q8_round: round half away from zero, as trunc(t + copysign(0.5 - 2^-25,
+//    t)): the addend is the float below one half, so t + addend reaches the
+//    next integer exactly when frac(|t|) >= 1/2.  Equal to roundf(t) for
+//    every fp32 |t| < 2^23 (checked exhaustively); codes are within 128.
+__device__ __forceinline__ float q8_scale(float amax) {
+  const float r = 0x1.020408p-7f;  // RN(1/127)
+  const float q0 = __fmul_rn(amax, r);
+  return __fmaf_rn(__fmaf_rn(-q0, 127.0f, amax), r, q0);
+}
+__device__ __forceinline__ float q8_inv(float d) { return d == 0.0f ? 0.0f : __frcp_rn(d); }
+__device__ __forceinline__ int q8_round(float t) {
+  return __float2int_rz(__fadd_rn(t, copysignf(0x1.fffffep-2f, t)));
+}
+
 // One Q8_0 block of 32 values, one per lane, into a Q8 record: the codes at
 // rec + 32 * j + lane, {dx, sdx, sdx_lo, sdx_hi} at rec + 256 + 16 * j.  The
 // gguf Q8_0 quantiser in IEEE fp32 (d = amax / 127, id = d ? 1 / d : 0,
@@ -177,9 +198,9 @@ __device__ __forceinline__ void q8_block_to_record(float v, int lane, uint8_t* r
   float am = fabsf(v);
 #pragma unroll
   for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-  const float d = __fdiv_rn(am, 127.0f);
-  const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-  const int q = (int)roundf(__fmul_rn(v, id));
+  const float d = q8_scale(am);
+  const float id = q8_inv(d);
+  const int q = q8_round(__fmul_rn(v, id));
   int s = q;
 #pragma unroll
   for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);  // within 16-lane halves

@@ -119,6 +119,10 @@ __device__ __forceinline__ int dot16(uint4 w, uint4 x, int acc) {
   acc = dp4a_ss(w.z, x.z, acc);
   return dp4a_ss(w.w, x.w, acc);
 }
+// The low bytes of four ints (codes in [-128, 127]) packed, a in byte 0.
+__device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
 __device__ __forceinline__ uint4 and4(uint4 v, uint32_t m) { return make_uint4(v.x & m, v.y & m, v.z & m, v.w & m); }
 __device__ __forceinline__ uint4 shr4(uint4 v, int s) { return make_uint4(v.x >> s, v.y >> s, v.z >> s, v.w >> s); }
 __device__ __forceinline__ uint4 or4(uint4 a, uint4 b) { return make_uint4(a.x | b.x, a.y | b.y, a.z | b.z, a.w | b.w); }
@@ -299,19 +303,17 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
                        fmaxf(fmaxf(fabsf(vv[i][4]), fabsf(vv[i][5])), fmaxf(fabsf(vv[i][6]), fabsf(vv[i][7]))));
       am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
       am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-      dq[i] = __fdiv_rn(am, 127.0f);
+      dq[i] = q8_scale(am);
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const float id = dq[i] == 0.0f ? 0.0f : __fdiv_rn(1.0f, dq[i]);
-      packed[i][0] = packed[i][1] = 0u;
-      int sacc = 0;
+      const float id = q8_inv(dq[i]);
+      int qq[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int qq = (int)roundf(__fmul_rn(vv[i][e], id));
-        sacc += qq;
-        packed[i][e >> 2] |= (uint32_t)(qq & 0xFF) << (8 * (e & 3));
-      }
+      for (int e = 0; e < 8; ++e) qq[e] = q8_round(__fmul_rn(vv[i][e], id));
+      packed[i][0] = pack4_s8(qq[0], qq[1], qq[2], qq[3]);
+      packed[i][1] = pack4_s8(qq[4], qq[5], qq[6], qq[7]);
+      const int sacc = __dp4a((int)packed[i][1], 0x01010101, __dp4a((int)packed[i][0], 0x01010101, 0));
       sh[i] = sacc + __shfl_xor_sync(0xffffffffu, sacc, 1);  // 16 codes: parts 0-1 or 2-3
       sf[i] = sh[i] + __shfl_xor_sync(0xffffffffu, sh[i], 2);
       shi[i] = __shfl_sync(0xffffffffu, sh[i], (lane & ~3) | 2);
