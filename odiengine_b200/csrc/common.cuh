@@ -173,12 +173,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 //    one residual correction q0 + fma(-q0, 127, amax) * RN(1/127) (the
 //    correction step of Markstein's division theorem).  Equal to IEEE
 //    amax / 127.0f for every non-negative finite fp32 amax, subnormals
-//    included (checked exhaustively against the host's division).
+//    included (tests/q8_math_check.c walks them all against the host's
+//    division).
 //  * q8_inv: 1 / d correctly rounded (__frcp_rn), 0 for d == 0.
 //  * q8_round: round half away from zero, as trunc(t + copysign(0.5 - 2^-25,
 //    t)): the addend is the float below one half, so t + addend reaches the
 //    next integer exactly when frac(|t|) >= 1/2.  Equal to roundf(t) for
-//    every fp32 |t| < 2^23 (checked exhaustively); codes are within 128.
+//    every fp32 |t| < 2^23 (same check); codes are within 128.
 __device__ __forceinline__ float q8_scale(float amax) {
   const float r = 0x1.020408p-7f;  // RN(1/127)
   const float q0 = __fmul_rn(amax, r);
