@@ -190,6 +190,12 @@ __device__ __forceinline__ int q8_round(float t) {
   return __float2int_rz(__fadd_rn(t, copysignf(0x1.fffffep-2f, t)));
 }
 
+// Bulk prefetch of global bytes into L2 (no shared-memory destination, no
+// completion to wait on).  src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // One Q8_0 block of 32 values, one per lane, into a Q8 record: the codes at
 // rec + 32 * j + lane, {dx, sdx, sdx_lo, sdx_hi} at rec + 256 + 16 * j.  The
 // gguf Q8_0 quantiser in IEEE fp32 (d = amax / 127, id = d ? 1 / d : 0,

@@ -941,6 +941,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
         if (!GCHK(s < S && (int64_t)g * pl.KB + kb0 + i < (int64_t)pl.G * pl.KB, 6, s, i)) break;
         mbar_arrive_expect_tx(&full[s], UB);
         bulk_g2s(ring + s * SB, wsrc + (int64_t)i * UB, UB, &full[s]);
+        if (i + S < nsp) bulk_prefetch_l2(wsrc + (int64_t)(i + S) * UB, UB);  // the L2 lookahead
         if (++s == S) s = 0;
       }
       // Drain: every copy issued must land before the CTA may exit.
@@ -960,6 +961,12 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     stage_records<MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
   else
     stage_acts<F32, MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
+  // L2 lookahead: the ring holds units 0..S-1; ask L2 for units S..2S-1 now
+  // that the activations are staged (asked for earlier, these bytes queue
+  // ahead of the activation loads and delay them), so HBM streams them while
+  // the first units are consumed.  The producer keeps the lookahead S units
+  // ahead of each refill.
+  if (threadIdx.x == 0 && nsp > S) bulk_prefetch_l2(wsrc + (int64_t)S * UB, (uint32_t)(min(nsp, 2 * S) - S) * UB);
 
   const int row = 32 * (warp & 1) + lane;
   const int up = warp >> 1;  // this warp takes units j = up, up + 2, ...
