@@ -707,6 +707,228 @@ __device__ __forceinline__ void unit_f32(const uint8_t* __restrict__ sl, float t
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core units for a pass of 8 tokens (MT = 8, ACT_Q8).  At 8 tokens the
+// dp4a units issue about 8x the M = 1 work per weight byte and the GEMV is
+// instruction-bound; here the integer dot products of a warp's 32 rows run as
+// mma.sync (m16n8k32 s8, m16n8k16 for Q6_K's 16-value scales), the tokens
+// being the n = 8 columns, and the CUDA cores only unpack the codes and apply
+// the per-(row, block, token) scales, which the format makes unavoidable (so
+// tcgen05's larger tiles would not shorten this path).  Thread (g = lane / 4,
+// t = lane % 4) holds rows g and g + 8 of each 16-row tile and tokens 2t and
+// 2t + 1: acc[4 * mt + 2 * h + e] is unit row 32 * half + 16 * mt + 8 * h + g,
+// token 2t + e.  The integer sums are exact and each block's scaling and
+// accumulation follow the dp4a units' operations in the same order, so the
+// results equal the dp4a path's.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %10, %10, %10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%7, %7, %7, %7};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint32_t lo_nib(uint32_t w) { return w & 0x0F0F0F0Fu; }
+__device__ __forceinline__ uint32_t hi_nib(uint32_t w) { return (w >> 4) & 0x0F0F0F0Fu; }
+// d * (byte b of w), b known after unrolling: scale_byte with a run-time index
+__device__ __forceinline__ float scale_byte_rt(float d, float nd23, uint32_t w, int b) {
+  return fmaf(d, __int_as_float(__byte_perm(w, 0x4Bu, 0x4550u | b)), nd23);
+}
+// acc += D * (A_row * dx_token) [- C_row * sdx_token], the four elements of a
+// tile, in the dp4a units' order of operations
+template <bool MIN>
+__device__ __forceinline__ void tc_apply(float* acc, const int (&d)[4], float A0, float A1, float C0, float C1,
+                                         float dx0, float dx1, float s0, float s1) {
+  acc[0] = fmaf(i2f(d[0]), A0 * dx0, acc[0]);
+  acc[1] = fmaf(i2f(d[1]), A0 * dx1, acc[1]);
+  acc[2] = fmaf(i2f(d[2]), A1 * dx0, acc[2]);
+  acc[3] = fmaf(i2f(d[3]), A1 * dx1, acc[3]);
+  if (MIN) {
+    acc[0] = fmaf(-C0, s0, acc[0]);
+    acc[1] = fmaf(-C0, s1, acc[1]);
+    acc[2] = fmaf(-C1, s0, acc[2]);
+    acc[3] = fmaf(-C1, s1, acc[3]);
+  }
+}
+
+// Q4_K / Q5_K header of one row (the unpacking of unit_q8_q4k): d, dmin and
+// the 6-bit scales and mins as bytes.
+struct KHead {
+  float d, dmin, nd, nm;  // nd, nm: -2^23 d, -2^23 dmin for scale_byte
+  uint32_t scL, mnL, scH, mnH;
+};
+__device__ __forceinline__ KHead khead(const uint8_t* sl) {
+  const uint4 hd = lds128(sl);
+  KHead h;
+  h.d = h2f_lo(hd.x);
+  h.dmin = h2f_hi(hd.x);
+  h.nd = -8388608.0f * h.d;
+  h.nm = -8388608.0f * h.dmin;
+  h.scL = hd.y & 0x3F3F3F3Fu;
+  h.mnL = hd.z & 0x3F3F3F3Fu;
+  h.scH = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+  h.mnH = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+  return h;
+}
+
+template <int DT, int RS>
+__device__ __forceinline__ void unit_tc(const uint8_t* __restrict__ st, int half, const uint8_t* __restrict__ xs,
+                                        float (&acc)[8]) {
+  constexpr int SB = slice_bytes(DT);
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint8_t* xg = xs + g * RS;                                // token g's codes (B fragments)
+  const uint8_t* xr0 = xs + (2 * t) * RS + 256, *xr1 = xr0 + RS;  // tokens 2t, 2t+1: XRec per block
+  const uint8_t* sl[2][2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    sl[mt][0] = st + (32 * half + 16 * mt + g) * SB;
+    sl[mt][1] = sl[mt][0] + 8 * SB;
+  }
+  if constexpr (DT == Q4_K || DT == Q5_K) {
+    constexpr bool FIVE = DT == Q5_K;
+    constexpr int QS = FIVE ? 48 : 16;
+    KHead hd[2][2];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) hd[mt][h] = khead(sl[mt][h]);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      // codes of blocks 2p (low nibbles) and 2p + 1 (high): bytes 4t.. and 16 + 4t..
+      uint32_t w[2][2][2], q5[2][2][2];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            w[mt][h][u] = lds32(sl[mt][h] + QS + 32 * p + 16 * u + 4 * t);
+            if (FIVE) q5[mt][h][u] = lds32(sl[mt][h] + 16 + 16 * u + 4 * t);
+          }
+#pragma unroll
+      for (int hi = 0; hi < 2; ++hi) {
+        const int j = 2 * p + hi;
+        const uint32_t b0 = lds32(xg + 32 * j + 4 * t), b1 = lds32(xg + 32 * j + 16 + 4 * t);
+        const float4 r0 = lds128f(xr0 + 16 * j), r1 = lds128f(xr1 + 16 * j);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint32_t a[2][2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              a[h][u] = hi ? hi_nib(w[mt][h][u]) : lo_nib(w[mt][h][u]);
+              if (FIVE) a[h][u] |= ((q5[mt][h][u] >> j) & 0x01010101u) << 4;
+            }
+          int d[4];
+          mma_k32(d, a[0][0], a[1][0], a[0][1], a[1][1], b0, b1);
+          float A[2], C[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const KHead& k = hd[mt][h];
+            const uint32_t scw = j < 4 ? k.scL : k.scH, mnw = j < 4 ? k.mnL : k.mnH;
+            A[h] = scale_byte_rt(k.d, k.nd, scw, j & 3);
+            C[h] = scale_byte_rt(k.dmin, k.nm, mnw, j & 3);
+          }
+          tc_apply<true>(acc + 4 * mt, d, A[0], A[1], C[0], C[1], r0.x, r1.x, r0.y, r1.y);
+        }
+      }
+    }
+  } else if constexpr (DT == Q8_0 || DT == Q4_0) {
+    // value = d_j * q (Q8_0) or d_j * (q - 8) (Q4_0: the -8 folds into sdx)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t b0 = lds32(xg + 32 * j + 4 * t), b1 = lds32(xg + 32 * j + 16 + 4 * t);
+      const float4 r0 = lds128f(xr0 + 16 * j), r1 = lds128f(xr1 + 16 * j);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t a[2][2];
+        float A[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          A[h] = h2f((uint16_t)ldsu16(sl[mt][h] + 2 * j));
+          if (DT == Q8_0) {
+            a[h][0] = lds32(sl[mt][h] + 16 + 32 * j + 4 * t);
+            a[h][1] = lds32(sl[mt][h] + 16 + 32 * j + 16 + 4 * t);
+          } else {  // byte l: value l (low nibble), value l + 16 (high)
+            const uint32_t q = lds32(sl[mt][h] + 16 + 16 * j + 4 * t);
+            a[h][0] = lo_nib(q);
+            a[h][1] = hi_nib(q);
+          }
+        }
+        int d[4];
+        mma_k32(d, a[0][0], a[1][0], a[0][1], a[1][1], b0, b1);
+        tc_apply<DT == Q4_0>(acc + 4 * mt, d, A[0], A[1], 8.0f * A[0], 8.0f * A[1], r0.x, r1.x, r0.y, r1.y);
+      }
+    }
+  } else {  // Q6_K: value = (d * sc) * (q - 32), q 6-bit, one int8 scale per 16 values
+    float dd[2][2];
+    uint4 scw[2][2];  // the row's 16 int8 scales, each byte + 128 (x ^ 0x80)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        dd[mt][h] = h2f((uint16_t)ldsu16(st + UNIT_ROWS * 208 + 2 * (32 * half + 16 * mt + 8 * h + g)));
+        const uint4 v = lds128(sl[mt][h]);
+        scw[mt][h] = make_uint4(v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u);
+      }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c = (cc >> 1) | ((cc & 1) << 1);  // 0, 2, 1, 3: the dp4a unit's order
+        // column group c of half hh: 32 values, block j = 4 hh + c of the span;
+        // low nibbles of ql[64 hh + 32 (c & 1) + l] for c < 2, high for c >= 2,
+        // bits 2c..2c+1 of qh[32 hh + l] on top
+        const int j = 4 * hh + c;
+        const uint32_t b0 = lds32(xg + 32 * j + 4 * t), b1 = lds32(xg + 32 * j + 16 + 4 * t);
+        const float4 r0 = lds128f(xr0 + 16 * j), r1 = lds128f(xr1 + 16 * j);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint32_t a[2][2];
+          float A[2][2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint8_t* s6 = sl[mt][h];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const uint32_t ql = lds32(s6 + 16 + 64 * hh + 32 * (c & 1) + 16 * u + 4 * t);
+              const uint32_t qh = lds32(s6 + 144 + 32 * hh + 16 * u + 4 * t);
+              a[h][u] = (c < 2 ? lo_nib(ql) : hi_nib(ql)) | (((qh >> (2 * c)) & 0x03030303u) << 4);
+              const int si = 2 * j + u;  // scale of values 16u..16u+15 of the block
+              const uint32_t sw = si < 4 ? scw[mt][h].x : si < 8 ? scw[mt][h].y : si < 12 ? scw[mt][h].z : scw[mt][h].w;
+              A[h][u] = dd[mt][h] * (__int_as_float(__byte_perm(sw, 0x4Bu, 0x4550u | (si & 3))) - 8388736.0f);
+            }
+          }
+          int d0[4], d1[4];
+          mma_k16(d0, a[0][0], a[1][0], b0);  // values 0..15 of the block
+          mma_k16(d1, a[0][1], a[1][1], b1);  // values 16..31
+          // per element: values 0..15 with their scale and -32 * sum, then 16..31
+          float* ac = acc + 4 * mt;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int h = e >> 1;
+            const float dx = (e & 1) ? r1.x : r0.x;
+            const float slo = (e & 1) ? r1.z : r0.z, shi = (e & 1) ? r1.w : r0.w;
+            float v = fmaf(i2f(d0[e]), A[h][0] * dx, ac[e]);
+            v = fmaf(-32.0f * A[h][0], slo, v);
+            v = fmaf(i2f(d1[e]), A[h][1] * dx, v);
+            ac[e] = fmaf(-32.0f * A[h][1], shi, v);
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int DT, int MT, bool F32, int RS>
 __device__ __forceinline__ void unit(const uint8_t* __restrict__ st, int row, const uint8_t* __restrict__ xs, int M,
                                      float (&acc)[MT]) {
@@ -970,6 +1192,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
 
   const int row = 32 * (warp & 1) + lane;
   const int up = warp >> 1;  // this warp takes units j = up, up + 2, ...
+  // 8-token passes of the five main types run their dot products on mma.sync
+  constexpr bool TC = !F32 && MT == 8 && (DT == Q4_K || DT == Q5_K || DT == Q6_K || DT == Q8_0 || DT == Q4_0);
   float acc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
@@ -979,7 +1203,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   for (int j = up; j < nsp; j += 2) {
     if (!mbar_wait(&full[s], par, a.err, ERR_FULL_WAIT)) break;
     if (!GCHK(s >= 0 && s < S && j < nsp, 7, s, j)) break;
-    unit<DT, MT, F32, RS>(ring + s * SB, row, xr + j * MT * RS, a.M, acc);
+    if constexpr (TC)
+      unit_tc<DT, RS>(ring + s * SB, warp & 1, xr + j * MT * RS, acc);
+    else
+      unit<DT, MT, F32, RS>(ring + s * SB, row, xr + j * MT * RS, a.M, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     s += 2;
@@ -993,9 +1220,17 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   // order).  Ranks other than 0 push their partial into rank 0's shared
   // memory as float4 stores, each pushing thread then arriving (release) on
   // rank 0's reduction mbarrier; rank 0 waits, adds, writes y.
+  if constexpr (TC) {
 #pragma unroll
-  for (int m = 0; m < MT; ++m)
-    if (m < a.M) red[(up * UNIT_ROWS + row) * MT + m] = acc[m];
+    for (int i = 0; i < 8; ++i) {  // row 32 (warp & 1) + 16 (i >> 2) + 8 ((i >> 1) & 1) + g, token 2t + (i & 1)
+      const int r = 32 * (warp & 1) + 16 * (i >> 2) + 8 * ((i >> 1) & 1) + (lane >> 2), m = 2 * (lane & 3) + (i & 1);
+      if (m < a.M) red[(up * UNIT_ROWS + r) * MT + m] = acc[i];
+    }
+  } else {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      if (m < a.M) red[(up * UNIT_ROWS + row) * MT + m] = acc[m];
+  }
   consumer_sync();
   const int tid = threadIdx.x;
   if (pl.C > 1) cluster_wait();
