@@ -17,9 +17,9 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
   p.KB = (int)((K + UNIT_COLS - 1) / UNIT_COLS);
   const int slots = CTAS_PER_SM * (num_sms > 0 ? num_sms : 148);
   p.pre = (pre && !f32act) ? 1 : 0;
-  const int rec = p.pre ? Q8_REC_BYTES : XR_STRIDE;
   p.mt = tokens_per_pass(M);
   for (;;) {
+    const int rec = stage_stride(p.pre, p.mt);
     double best = 1e30;
     int bestC = 0, bestChunk = 0;
     for (int C = 1; C <= 8; C *= 2) {
@@ -56,7 +56,7 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
     }
     p.mt /= 2;
   }
-  p.xq_bytes = (p.chunk * p.mt * rec + 127) / 128 * 128;
+  p.xq_bytes = (p.chunk * p.mt * stage_stride(p.pre, p.mt) + 127) / 128 * 128;
   p.stage_bytes = (unit_bytes(dt) + 127) / 128 * 128;
   const int xr_off = p.mt == 1 ? SmemMap<1>::xr(p.C)
                      : p.mt == 2 ? SmemMap<2>::xr(p.C)

@@ -46,6 +46,14 @@ constexpr int XR_BUDGET = 24 * 1024;      // staged activations per CTA
 // 32-value block).
 constexpr int XR_VALS = 1024;
 constexpr int XR_STRIDE = XR_VALS + 64;
+// Shared-memory stride of a staged (span, token) record: XR_STRIDE, or
+// Q8_REC_BYTES for pre-quantized records.  8-token passes add 16 bytes so the
+// records of the 8 tokens start in different banks: the tensor-core units
+// read a word of every token's codes in one instruction (10% on the 8-token
+// GEMVs; fewer tokens read each record by broadcast and keep the dense stride).
+__host__ __device__ constexpr int stage_stride(bool pre, int mt) {
+  return (pre ? Q8_REC_BYTES : XR_STRIDE) + (mt == 8 ? 16 : 0);
+}
 
 // Q8 activation record of one 32-value block, pre-scaled for the kernels:
 // dx = the fp16 scale widened to fp32; sdx = (sum of codes) * dx, and the
@@ -231,7 +239,7 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
     const int64_t left = a.K - k;
     const int nvalid = left <= 0 ? 0 : (left >= 4 ? 4 : (int)left);
     for (int m = tid >> 6; m < a.M; m += 2)
-      copy4(xr + (j * MT + m) * XR_STRIDE + 16 * q, a.x + (int64_t)m * a.ldx + (nvalid ? k : 0), nvalid, vec);
+      copy4(xr + (j * MT + m) * stage_stride(false, MT) + 16 * q, a.x + (int64_t)m * a.ldx + (nvalid ? k : 0), nvalid, vec);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   if (a.fu.norm_w) row_rms<MT>(a, fuse_smem, fuse_smem + MT);  // overlaps the copies
@@ -254,7 +262,7 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
       const int ri = (i == 1 && two) ? r0 + NCW : r0;
       const int j = ri / a.M;
       mi[i] = ri - j * a.M;
-      rec[i] = xr + (j * MT + mi[i]) * XR_STRIDE;
+      rec[i] = xr + (j * MT + mi[i]) * stage_stride(false, MT);
       const float4 v0 = lds128f(rec[i] + 4 * off), v1 = lds128f(rec[i] + 4 * (off + 4));
       vv[i][0] = v0.x; vv[i][1] = v0.y; vv[i][2] = v0.z; vv[i][3] = v0.w;
       vv[i][4] = v1.x; vv[i][5] = v1.y; vv[i][6] = v1.z; vv[i][7] = v1.w;
@@ -350,7 +358,7 @@ __device__ __forceinline__ void stage_records(const GemvArgs& a, int kb0, int ns
   for (int c = threadIdx.x; c < nsp * per_span; c += NCW * 32) {
     const int j = c / per_span, rem = c - j * per_span;
     const int m = rem / V, v = rem - m * V;
-    cp_async16(xr + (j * MT + m) * Q8_REC_BYTES + 16 * v,
+    cp_async16(xr + (j * MT + m) * stage_stride(true, MT) + 16 * v,
                a.recs + ((int64_t)(kb0 + j) * a.rec_ld + m) * Q8_REC_BYTES + 16 * v, 16);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
@@ -362,7 +370,7 @@ __device__ __forceinline__ void stage_records(const GemvArgs& a, int kb0, int ns
     for (int i = threadIdx.x; i < nsp * a.M * 32; i += NCW * 32) {
       const int rj = i >> 5, f = i & 31;
       const int j = rj / a.M, m = rj - j * a.M;
-      float* xf = reinterpret_cast<float*>(xr + (j * MT + m) * Q8_REC_BYTES + 256);
+      float* xf = reinterpret_cast<float*>(xr + (j * MT + m) * stage_stride(true, MT) + 256);
       xf[f] = xf[f] * fuse_smem[m];
     }
     consumer_sync();
@@ -698,7 +706,7 @@ __device__ __forceinline__ void unit_f32(const uint8_t* __restrict__ sl, float t
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       if (m < M) {
-        const uint8_t* xr = xs + m * XR_STRIDE;
+        const uint8_t* xr = xs + m * stage_stride(false, MT);
         float v = fmaf(G.A, dot16_f32<DT>(G.cw, xr + 64 * g), acc[m]);
         if (DT != Q8_0) v = fmaf(-G.B, reinterpret_cast<const float*>(xr + XR_VALS)[g], v);
         acc[m] = v;
@@ -1008,7 +1016,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 //   red   [2][64][MT] fp32  the two unit-parity sums of each row
 //   part  [C][MT*64] fp32   tile partials; rank 0 receives those of the other
 //                           ranks here over distributed shared memory
-//   xr    chunk x MT records of XR_STRIDE (Q8_REC_BYTES when pre-quantized)
+//   xr    chunk x MT records of stage_stride(PRE, MT) bytes
 //         bytes: staged activations
 //   ring  stages x stage_bytes weight units
 template <int MT>
@@ -1093,7 +1101,7 @@ __device__ __forceinline__ void signal_peers(const GemvArgs& a) {
 // ---------------------------------------------------------------------------
 template <int DT, int MT, bool F32, bool PRE>
 __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const GemvArgs a, const GemvPlan pl) {
-  constexpr int RS = PRE ? Q8_REC_BYTES : XR_STRIDE;  // bytes per staged (span, token) record
+  constexpr int RS = stage_stride(PRE, MT);  // bytes per staged (span, token) record
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
