@@ -580,8 +580,11 @@ def run_config_legs(args):
             for M in (1, 8):
                 us, b, R = time_products(dt, N, K, M, ob.ACT_AUTO, reps=10)
                 gbs = b / us / 1e3
+                path = ("Q8 records, one 8-token pass, int8 mma.sync dots" if M == 8
+                        else "Q8_0 activations quantised on chip, int8 dp4a dots")
                 out["gemv_sweep"].append({"dtype": names[dt], "N": N, "K": K, "M": M, "us": round(us, 3),
-                                          "GBs": round(gbs, 1), "hbm_frac": round(gbs / peak_hbm, 4)})
+                                          "GBs": round(gbs, 1), "hbm_frac": round(gbs / peak_hbm, 4),
+                                          "path": path})
     for N, K in ((14336, 4096), (4096, 14336)):
         for M in (512, 2048):
             us, _, R = time_products(ob.ODI_DTYPE_Q4_K, N, K, M, ob.ACT_AUTO, reps=5)
