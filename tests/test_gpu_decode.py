@@ -355,18 +355,21 @@ def test_graph_replay_equals_eager(cuda_lib):
 
 @pytest.mark.parametrize("dt", [O.Q4_K, O.Q6_K, O.Q8_0])
 @pytest.mark.parametrize("mode", [0, 1], ids=["q8", "f32"])
-def test_matmul_fused_ops(cuda_lib, dt, mode):
+@pytest.mark.parametrize("M", [2, 6, 8])
+def test_matmul_fused_ops(cuda_lib, dt, mode, M):
     """odi_cuda_matmul_fused: RMSNorm prologue, SwiGLU prologue, accumulate
     epilogue, against float64 compositions of the separate operations.
     Tolerance: fp32 GEMV 1e-4 * (|W| @ |a|); Q8 GEMV adds the activation
-    quantisation bound of the oracle (0.5625 d_x sum|w| per block)."""
+    quantisation bound of the oracle (0.5625 d_x sum|w| per block).  With a
+    prologue the tokens are staged on chip, so M = 6 and 8 run the 8-token
+    pass (the tensor-core units in Q8 mode) on shared-memory staged records."""
     import ctypes
 
     import torch
 
     ob = cuda_lib
-    N, K, M = 320, 2048, 2
-    rng = np.random.default_rng(dt + mode)
+    N, K = 320, 2048
+    rng = np.random.default_rng(dt + mode + 100 * M)
     b = O.quantize(dt, O.seeded_weights(N, K, seed=dt))
     W = O.dequantize(dt, b, N, K).astype(np.float64)
     dw = ob.DeviceWeight(ob.QuantWeight(dt, (K, N), b))
