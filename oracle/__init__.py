@@ -65,7 +65,9 @@ def lib():
         L.orc_quantize_q8_0_act.argtypes = [_vp, _i64, _i64, _vp]
         L.orc_quantize_act_planes.argtypes = [_vp, _i64, _i64, _vp, _vp]
         L.orc_matmul_q8act.argtypes = [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]
+        L.orc_matmul_q8act_mt.argtypes = [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, ctypes.c_int]
         L.orc_fp32_bound.argtypes = [ctypes.c_int, _vp, _vp, _i64, _i64, _i64, _vp]
+        L.orc_fp32_bound_mt.argtypes = [ctypes.c_int, _vp, _vp, _i64, _i64, _i64, _vp, ctypes.c_int]
         L.orc_term_magnitude.argtypes = [ctypes.c_int, _vp, _i64, _i64, _vp]
         L.orc_block_factors.argtypes = [ctypes.c_int, _vp, _i64, _i64, _vp, _vp, _vp]
         L.orc_tiled_bytes.restype = _i64
@@ -125,12 +127,14 @@ def dequantize(dtype: int, blocks: np.ndarray, N: int, K: int, ref_fp16: bool = 
     return out
 
 
-def matmul_ref(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int, nthreads: int = 1) -> np.ndarray:
-    """Restated reference product: out[M,N] = x[M,K] . dequant(W)^T."""
+def matmul_ref(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int, nthreads: int = 0) -> np.ndarray:
+    """Restated reference product: out[M,N] = x[M,K] . dequant(W)^T (rows
+    split over nthreads host threads, 0: all; results do not depend on it)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     M, K = x.shape
     out = np.zeros((M, N), dtype=np.float32)
-    rc = lib().orc_matmul_ref(dtype, _p(out), _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, nthreads)
+    rc = lib().orc_matmul_ref(dtype, _p(out), _p(x), _p(np.ascontiguousarray(blocks)), M, K, N,
+                              nthreads or host_threads())
     if rc:
         raise ValueError(f"orc_matmul_ref failed ({rc})")
     return out
@@ -182,25 +186,40 @@ def quantize_act_planes(x: np.ndarray):
     return xq, xs
 
 
-def matmul_q8act(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int, with_mag: bool = False):
+def host_threads() -> int:
+    """Host threads the checkers use by default (all cores this process may run on)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def matmul_q8act(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int, with_mag: bool = False,
+                 nthreads: int = 0):
     """Q8-activation product and its bound against the exact real product.
-    With with_mag, also the sum of |block terms| (for fp32 reordering bounds)."""
+    With with_mag, also the sum of |block terms| (for fp32 reordering bounds).
+    Rows are split over nthreads host threads (0: all); results do not
+    depend on the thread count."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     M, K = x.shape
     out = np.zeros((M, N), dtype=np.float32)
     bound = np.zeros((M, N), dtype=np.float32)
     mag = np.zeros((M, N), dtype=np.float32)
-    rc = lib().orc_matmul_q8act(dtype, _p(out), _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, _p(bound), _p(mag))
+    rc = lib().orc_matmul_q8act_mt(dtype, _p(out), _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, _p(bound),
+                                   _p(mag), nthreads or host_threads())
     if rc:
         raise ValueError(f"orc_matmul_q8act failed ({rc})")
     return (out, bound, mag) if with_mag else (out, bound)
 
 
-def fp32_bound(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int) -> np.ndarray:
+def fp32_bound(dtype: int, x: np.ndarray, blocks: np.ndarray, N: int, nthreads: int = 0) -> np.ndarray:
+    """Per-output bound on |y_fp32 - y_exact| for any fp32 summation order
+    (rows split over nthreads host threads, 0: all)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     M, K = x.shape
     bound = np.zeros((M, N), dtype=np.float32)
-    rc = lib().orc_fp32_bound(dtype, _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, _p(bound))
+    rc = lib().orc_fp32_bound_mt(dtype, _p(x), _p(np.ascontiguousarray(blocks)), M, K, N, _p(bound),
+                                 nthreads or host_threads())
     if rc:
         raise ValueError(f"orc_fp32_bound failed ({rc})")
     return bound

@@ -761,11 +761,115 @@ int orc_block_factors(int dtype, const void* blocks, int64_t N, int64_t K, float
   return 0;
 }
 
-int orc_matmul_q8act(int dtype, float* out, const float* a, const void* b, int64_t M, int64_t K,
-                     int64_t N, float* bound, float* mag_out) {
+/* Rows [n0, n1) of the Q8-activation product: each weight block is decoded
+ * once per row and applied to every token.  For each (m, n) the terms are
+ * added in block order (kb, then group g), as the kernels order them. */
+typedef struct {
+  int dtype;
+  const void* b;
+  const int8_t* xq;
+  const act_rec* xs;
+  int64_t M, K, N, n0, n1;
+  float *out, *bound, *mag_out;
+  const float* a;
+  int rc;
+} q8_job;
+
+static void* q8act_rows(void* arg) {
+  q8_job* j = (q8_job*)arg;
+  const int dtype = j->dtype;
+  const int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
+  const int64_t M = j->M, K = j->K, N = j->N, nb = (K + be - 1) / be, Kp = (K + 255) / 256 * 256;
+  const double u = 1.0 / 16777216.0;
+  float* y = (float*)calloc((size_t)M + 1, sizeof(float));
+  double* mag = (double*)calloc((size_t)M + 1, sizeof(double));
+  double* act_err = (double*)calloc((size_t)M + 1, sizeof(double));
+  if (!y || !mag || !act_err) {
+    free(y); free(mag); free(act_err);
+    j->rc = -3;
+    return NULL;
+  }
+  wcodes c;
+  for (int64_t n = j->n0; n < j->n1; ++n) {
+    for (int64_t m = 0; m < M; ++m) { y[m] = 0.0f; mag[m] = 0.0; act_err[m] = 0.0; }
+    int64_t terms = 0;
+    for (int64_t kb = 0; kb < nb; ++kb) {
+      block_codes(dtype, (const uint8_t*)j->b + (n * nb + kb) * bb, &c);
+      for (int g = 0; g < c.ngroups; ++g) {
+        const int64_t k0 = kb * be + (int64_t)g * c.gsize;
+        const int64_t xb = k0 / 32;
+        double dsum = 0.0; /* sum of |w| over the group, for the activation error */
+        if (j->bound) {
+          for (int l = 0; l < c.gsize && k0 + l < K; ++l) {
+            double w = (double)c.A[g] * c.q[g * c.gsize + l] - (c.has_min ? (double)c.B[g] : 0.0);
+            dsum += fabs(w);
+          }
+        }
+        for (int64_t m = 0; m < M; ++m) {
+          const act_rec* r = &j->xs[m * (Kp / 32) + xb];
+          const int8_t* xm = j->xq + m * Kp + k0;
+          int isum = 0, xsum = 0;
+          for (int h0 = 0; h0 < c.gsize; h0 += 16) {
+            /* The kernels convert each 16-value partial dot separately, so
+             * the reordering magnitude is summed over 16-value halves. */
+            int ih = 0, xh = 0;
+            for (int l = h0; l < h0 + 16; ++l) {
+              int xv = xm[l];
+              ih += c.q[g * c.gsize + l] * xv;
+              xh += xv;
+            }
+            isum += ih;
+            xsum += xh;
+            mag[m] += fabs((double)ih * c.A[g] * r->d) + (c.has_min ? fabs((double)xh * c.B[g] * r->d) : 0.0);
+          }
+          float t1 = (float)isum * (c.A[g] * r->d);
+          float t2 = c.has_min ? (float)xsum * (c.B[g] * r->d) : 0.0f;
+          y[m] += t1;
+          y[m] -= t2;
+          /* activation error: |x - q*d_x| <= 0.5*d32 + 127*|d32 - d16|
+           * where d32 is the unrounded scale; bounded by 0.5625*d16. */
+          if (j->bound) act_err[m] += 0.5625 * (double)r->d * dsum;
+        }
+        terms += 2;
+      }
+    }
+    for (int64_t m = 0; m < M; ++m) {
+      j->out[m * N + n] = y[m];
+      if (j->mag_out) j->mag_out[m * N + n] = (float)mag[m];
+      if (j->bound) j->bound[m * N + n] = (float)(act_err[m] + 2.0 * (double)(terms + 8) * u * mag[m] + 1e-30);
+    }
+  }
+  free(y); free(mag); free(act_err);
+  j->rc = 0;
+  return NULL;
+}
+
+/* Run `fn` over nthreads row ranges of [0, N) (jobs: an array of job
+ * structs of `size` bytes whose n0/n1 fields are filled in by `set`). */
+static int run_rows(void* (*fn)(void*), void* jobs, size_t size, int nthreads, int64_t N,
+                    void (*set)(void*, int64_t, int64_t), int (*rc_of)(void*)) {
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > 256) nthreads = 256;
+  if (nthreads > N) nthreads = (int)(N > 0 ? N : 1);
+  pthread_t th[256];
+  for (int t = 0; t < nthreads; ++t) set((char*)jobs + t * size, N * t / nthreads, N * (t + 1) / nthreads);
+  if (nthreads == 1) {
+    fn(jobs);
+  } else {
+    for (int t = 0; t < nthreads; ++t) pthread_create(&th[t], NULL, fn, (char*)jobs + t * size);
+    for (int t = 0; t < nthreads; ++t) pthread_join(th[t], NULL);
+  }
+  for (int t = 0; t < nthreads; ++t)
+    if (rc_of((char*)jobs + t * size)) return rc_of((char*)jobs + t * size);
+  return 0;
+}
+
+static void q8_set(void* p, int64_t n0, int64_t n1) { ((q8_job*)p)->n0 = n0; ((q8_job*)p)->n1 = n1; }
+static int q8_rc(void* p) { return ((q8_job*)p)->rc; }
+
+int orc_matmul_q8act_mt(int dtype, float* out, const float* a, const void* b, int64_t M, int64_t K,
+                        int64_t N, float* bound, float* mag_out, int nthreads) {
   if (!supported(dtype) || M < 0 || N < 0 || K < 0) return -1;
-  int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
-  int64_t nb = (K + be - 1) / be;
   int64_t Kp = (K + 255) / 256 * 256;
   int8_t* xq = (int8_t*)calloc((size_t)(M * Kp + 1), 1);
   act_rec* xs = (act_rec*)calloc((size_t)(M * (Kp / 32) + 1), sizeof(act_rec));
@@ -775,82 +879,79 @@ int orc_matmul_q8act(int dtype, float* out, const float* a, const void* b, int64
     return -3;
   }
   orc_quantize_act_planes(a, M, K, xq, xs);
-  wcodes c;
-  const double u = 1.0 / 16777216.0;
-  for (int64_t n = 0; n < N; ++n) {
-    for (int64_t m = 0; m < M; ++m) {
-      float y = 0.0f;
-      double mag = 0.0, act_err = 0.0;
-      int64_t terms = 0;
-      for (int64_t kb = 0; kb < nb; ++kb) {
-        block_codes(dtype, (const uint8_t*)b + (n * nb + kb) * bb, &c);
-        for (int g = 0; g < c.ngroups; ++g) {
-          int64_t k0 = kb * be + (int64_t)g * c.gsize;
-          int64_t xb = k0 / 32;
-          const act_rec* r = &xs[m * (Kp / 32) + xb];
-          int isum = 0, xsum = 0;
-          for (int h0 = 0; h0 < c.gsize; h0 += 16) {
-            /* The kernels convert each 16-value partial dot separately, so
-             * the reordering magnitude is summed over 16-value halves. */
-            int ih = 0, xh = 0;
-            for (int l = h0; l < h0 + 16; ++l) {
-              int xv = xq[m * Kp + k0 + l];
-              ih += c.q[g * c.gsize + l] * xv;
-              xh += xv;
-            }
-            isum += ih;
-            xsum += xh;
-            mag += fabs((double)ih * c.A[g] * r->d) + (c.has_min ? fabs((double)xh * c.B[g] * r->d) : 0.0);
-          }
-          float t1 = (float)isum * (c.A[g] * r->d);
-          float t2 = c.has_min ? (float)xsum * (c.B[g] * r->d) : 0.0f;
-          y += t1;
-          y -= t2;
-          terms += 2;
-          if (bound) {
-            /* activation error: |x - q*d_x| <= 0.5*d32 + 127*|d32 - d16|
-             * where d32 is the unrounded scale; bounded by 0.5625*d16. */
-            double dsum = 0.0;
-            for (int l = 0; l < c.gsize && k0 + l < K; ++l) {
-              double w = (double)c.A[g] * c.q[g * c.gsize + l] - (c.has_min ? (double)c.B[g] : 0.0);
-              dsum += fabs(w);
-            }
-            act_err += 0.5625 * (double)r->d * dsum;
-          }
-        }
-      }
-      out[m * N + n] = y;
-      if (mag_out) mag_out[m * N + n] = (float)mag;
-      if (bound) bound[m * N + n] = (float)(act_err + 2.0 * (double)(terms + 8) * u * mag + 1e-30);
-    }
-  }
+  q8_job jobs[256];
+  for (int t = 0; t < 256; ++t)
+    jobs[t] = (q8_job){dtype, b, xq, xs, M, K, N, 0, 0, out, bound, mag_out, a, 0};
+  int rc = run_rows(q8act_rows, jobs, sizeof(q8_job), nthreads, N, q8_set, q8_rc);
   free(xq);
   free(xs);
-  return 0;
+  return rc;
+}
+
+int orc_matmul_q8act(int dtype, float* out, const float* a, const void* b, int64_t M, int64_t K,
+                     int64_t N, float* bound, float* mag_out) {
+  return orc_matmul_q8act_mt(dtype, out, a, b, M, K, N, bound, mag_out, 1);
+}
+
+typedef struct {
+  int dtype;
+  const float* a;
+  const void* b;
+  int64_t M, K, N, n0, n1;
+  float* bound;
+  int rc;
+} b32_job;
+
+/* Rows [n0, n1) of the fp32 reordering bound; each block decoded once per row. */
+static void* fp32_bound_rows(void* arg) {
+  b32_job* j = (b32_job*)arg;
+  const int be = orc_block_elems(j->dtype), bb = orc_block_bytes(j->dtype);
+  const int64_t M = j->M, K = j->K, N = j->N, nb = (K + be - 1) / be;
+  const double u = 1.0 / 16777216.0;
+  double* mag = (double*)calloc((size_t)M + 1, sizeof(double));
+  if (!mag) {
+    j->rc = -3;
+    return NULL;
+  }
+  wcodes c;
+  double w[256];
+  for (int64_t n = j->n0; n < j->n1; ++n) {
+    for (int64_t m = 0; m < M; ++m) mag[m] = 0.0;
+    for (int64_t kb = 0; kb < nb; ++kb) {
+      block_codes(j->dtype, (const uint8_t*)j->b + (n * nb + kb) * bb, &c);
+      int ne = 0;
+      for (int e = 0; e < be && kb * be + e < K; ++e, ++ne) {
+        int g = e / c.gsize;
+        w[e] = fabs((double)c.A[g] * c.q[e]) + (c.has_min ? fabs((double)c.B[g]) : 0.0);
+      }
+      for (int64_t m = 0; m < M; ++m) {
+        const float* am = j->a + m * K + kb * be;
+        double s = mag[m];
+        for (int e = 0; e < ne; ++e) s += fabs((double)am[e]) * w[e];
+        mag[m] = s;
+      }
+    }
+    for (int64_t m = 0; m < M; ++m) j->bound[m * N + n] = (float)(2.0 * (double)(K + 16) * u * mag[m] + 1e-30);
+  }
+  free(mag);
+  j->rc = 0;
+  return NULL;
+}
+
+static void b32_set(void* p, int64_t n0, int64_t n1) { ((b32_job*)p)->n0 = n0; ((b32_job*)p)->n1 = n1; }
+static int b32_rc(void* p) { return ((b32_job*)p)->rc; }
+
+int orc_fp32_bound_mt(int dtype, const float* a, const void* b, int64_t M, int64_t K, int64_t N, float* bound,
+                      int nthreads) {
+  if (!supported(dtype) || M < 0 || N < 0 || K < 0) return -1;
+  b32_job jobs[256];
+  for (int t = 0; t < 256; ++t) jobs[t] = (b32_job){dtype, a, b, M, K, N, 0, 0, bound, 0};
+  return run_rows(fp32_bound_rows, jobs, sizeof(b32_job), nthreads, N, b32_set, b32_rc);
 }
 
 int orc_fp32_bound(int dtype, const float* a, const void* b, int64_t M, int64_t K, int64_t N,
                    float* bound) {
-  if (!supported(dtype)) return -1;
-  int be = orc_block_elems(dtype), bb = orc_block_bytes(dtype);
-  int64_t nb = (K + be - 1) / be;
-  const double u = 1.0 / 16777216.0;
-  wcodes c;
-  for (int64_t n = 0; n < N; ++n) {
-    for (int64_t m = 0; m < M; ++m) {
-      double mag = 0.0;
-      for (int64_t kb = 0; kb < nb; ++kb) {
-        block_codes(dtype, (const uint8_t*)b + (n * nb + kb) * bb, &c);
-        for (int e = 0; e < be && kb * be + e < K; ++e) {
-          int g = e / c.gsize;
-          double w = fabs((double)c.A[g] * c.q[e]) + (c.has_min ? fabs((double)c.B[g]) : 0.0);
-          mag += fabs((double)a[m * K + kb * be + e]) * w;
-        }
-      }
-      bound[m * N + n] = (float)(2.0 * (double)(K + 16) * u * mag + 1e-30);
-    }
-  }
-  return 0;
+  return orc_fp32_bound_mt(dtype, a, b, M, K, N, bound, 1);
 }
 
 /* ------------------------------------------------------------------------- */

@@ -98,10 +98,15 @@ int orc_block_factors(int dtype, const void* blocks, int64_t N, int64_t K, float
 
 int orc_matmul_q8act(int dtype, float* out, const float* a, const void* b,
                      int64_t M, int64_t K, int64_t N, float* bound, float* mag);
+/* The same on nthreads host threads (rows split evenly; identical results). */
+int orc_matmul_q8act_mt(int dtype, float* out, const float* a, const void* b, int64_t M, int64_t K,
+                        int64_t N, float* bound, float* mag, int nthreads);
 
 /* Rigorous bound on |y_fp32 - y_exact| for any fp32 summation order of the
  * reference product: 2*(K+8)*2^-24 * sum_k |a_k| * |w_k|  (plus tiny). */
 int orc_fp32_bound(int dtype, const float* a, const void* b, int64_t M, int64_t K, int64_t N, float* bound);
+int orc_fp32_bound_mt(int dtype, const float* a, const void* b, int64_t M, int64_t K, int64_t N, float* bound,
+                      int nthreads);
 
 /* Tiled device layout. */
 int64_t orc_tiled_bytes(int dtype, int64_t N, int64_t K);

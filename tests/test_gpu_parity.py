@@ -180,7 +180,7 @@ SMALL = [(1, 256), (33, 512), (64, 256), (100, 1280), (257, 2048)]
 
 @pytest.mark.parametrize("dt", ALL)
 @pytest.mark.parametrize("N,K", SMALL)
-@pytest.mark.parametrize("M", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 7, 8])
 def test_matmul_q8_small(cuda_lib, dt, N, K, M):
     b, x = make(dt, N, K, seed=N + K + M, M=M)
     t = upload(cuda_lib, dt, b, N, K)
@@ -229,8 +229,8 @@ def test_matmul_golden_reference_outputs(cuda_lib, golden):
         assert (np.abs(y - golden[f"ragged_ref_{name}_y"]) <= 2 * bound).all()
 
 
-@pytest.mark.parametrize("dt", [O.Q4_K, O.Q8_0, O.Q6_K])
-@pytest.mark.parametrize("M", [9, 16, 32])
+@pytest.mark.parametrize("dt", [O.Q4_K, O.Q8_0, O.Q6_K, O.Q5_K, O.Q4_0])
+@pytest.mark.parametrize("M", [9, 13, 16, 32])
 def test_matmul_multi_pass_tokens(cuda_lib, dt, M):
     N, K = 192, 1024
     b, x = make(dt, N, K, seed=M, M=M)
