@@ -144,22 +144,42 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # reference arm / CPU baseline
 # ---------------------------------------------------------------------------
-def cpu_port_gemv_time(nthreads: int, budget_s: float, N=N_ROWS, K=K_COLS):
-    """Oracle restatement of the reference loop (matmul_q4_0's structure over
-    Q4_K blocks) on nthreads host threads; returns (seconds per GEMV, reps)."""
+CPU_REPS = 8  # GEMVs of the workload per CPU sample (one reference-arm step)
+
+
+def host_threads():
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_port_gemv_time(nthreads: int, reps: int = CPU_REPS, N=N_ROWS, K=K_COLS):
+    """The oracle's restatement of the reference loop (matmul_q4_0's
+    per-block dequantise-and-accumulate structure over Q4_K blocks) on
+    nthreads host threads: mean seconds per GEMV over `reps` GEMVs of the
+    workload, after one untimed GEMV.  Both arms use this one sample, so
+    their CPU figures agree.  The reference runs an M=1 product on ONE thread
+    (parallel_for is serial below 4 x threads rows, cpu_backend.cpp:149), so
+    the port on every host thread is a generous baseline."""
     import oracle as O
 
-    w = O.seeded_weights(N, K, seed=0)
-    b = O.quantize(O.Q4_K, w)
-    x = O.seeded_acts(M_TOK, K, seed=1)
+    if "b" not in _PORT:
+        w = O.seeded_weights(N, K, seed=0)
+        _PORT["b"] = O.quantize(O.Q4_K, w)
+        _PORT["x"] = O.seeded_acts(M_TOK, K, seed=1)
+    b, x = _PORT["b"], _PORT["x"]
     O.matmul_ref(O.Q4_K, x, b, N, nthreads)  # warm
-    reps, t0 = 0, time.perf_counter()
-    while True:
+    t0 = time.perf_counter()
+    for _ in range(reps):
         O.matmul_ref(O.Q4_K, x, b, N, nthreads)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= budget_s or reps >= 200:
-            return el / reps, reps
+    return (time.perf_counter() - t0) / reps
+
+
+def cpu_sample_text(nthreads, reps=CPU_REPS):
+    return (f"{reps} Q4_K {N_ROWS}x{K_COLS} M=1 GEMVs on {nthreads} host threads: the oracle's restatement of the "
+            "reference block loop (CPUBackend::matmul throws for K-quants); the reference itself runs M=1 on one "
+            "thread (cpu_backend.cpp:149), so this is a generous baseline")
 
 
 def reference_q4_0_config1(budget_s: float):
@@ -185,53 +205,44 @@ def reference_q4_0_config1(budget_s: float):
 
 
 def run_reference(args, rank):
+    """The reference arm: the reference's CPU loop for this path on the host
+    cores (the oracle restatement: CPUBackend::matmul throws on Q4_K), same
+    metric and config as our arm; each step = one CPU sample of CPU_REPS
+    GEMVs of the workload."""
     if rank != 0:
         return 0
-    nthreads = os.cpu_count() or 1
+    nthreads = host_threads()
     step_bytes = algo_bytes(N_ROWS, K_COLS, M_TOK)
     times = []
     for i in range(args.warmup + args.steps):
-        t = _one_port_gemv(nthreads)
+        t = cpu_port_gemv_time(nthreads)
         if i >= args.warmup:
             times.append(t)
-    tmed = sum(times) / len(times)
-    value = step_bytes / tmed / 1e9
+    tmean = sum(times) / len(times)
+    value = step_bytes / tmean / 1e9
+    R = max(4, -(-4 * L2_BYTES // q4k_bytes(N_ROWS, K_COLS)))
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(tmed * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(tmean * CPU_REPS * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": dict(workload_config(max(4, -(-4 * L2_BYTES // q4k_bytes(N_ROWS, K_COLS))), args.gpus),
-                       act_mode="f32 (the reference's arithmetic)",
-                       reference_step="one GEMV of the workload on the host cores"),
+        "config": workload_config(R, args.gpus),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": nthreads, "kind": "port",
-                         "sample": "one Q4_K 4096x14336 M=1 GEMV per step (oracle restatement of the "
-                                   "reference block loop; CPUBackend::matmul throws for K-quants)"},
+                         "sample": cpu_sample_text(nthreads)},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     if not args.no_decode:
         t_cpu, sample = cpu_decode_sample(nthreads)
-        line["decode_7b"] = {"metric": "7B-shape Q4_K decode tokens/s (1 sequence, greedy)",
-                             "value": round(1.0 / t_cpu, 4), "unit": "tokens/s",
-                             "cpu_baseline": {"value": round(1.0 / t_cpu, 4), "unit": "tokens/s",
-                                              "cores": nthreads, "kind": "port", "sample": sample}}
+        print(json.dumps({"aux": "decode_7b", "impl": "reference",
+                          "metric": "7B-shape Q4_K decode tokens/s (1 sequence, greedy)",
+                          "value": round(1.0 / t_cpu, 4), "unit": "tokens/s",
+                          "cpu_baseline": {"value": round(1.0 / t_cpu, 4), "unit": "tokens/s", "cores": nthreads,
+                                           "kind": "port", "sample": sample}}), flush=True)
     print(json.dumps(line), flush=True)
     return 0
 
 
 _PORT = {}
-
-
-def _one_port_gemv(nthreads):
-    import oracle as O
-
-    if not _PORT:
-        w = O.seeded_weights(N_ROWS, K_COLS, seed=0)
-        _PORT["b"] = O.quantize(O.Q4_K, w)
-        _PORT["x"] = O.seeded_acts(M_TOK, K_COLS, seed=1)
-    t0 = time.perf_counter()
-    O.matmul_ref(O.Q4_K, _PORT["x"], _PORT["b"], N_ROWS, nthreads)
-    return time.perf_counter() - t0
 
 
 METRIC = "Q4_K decode GEMV HBM GB/s (4096x14336, M=1)"
@@ -441,25 +452,25 @@ def run_ours(args, rank, world, local_rank):
                "h2d_bytes_per_step": SWEEPS * R * M * K * 4, "d2h_bytes_per_step": SWEEPS * R * M * N * 4,
                "steps": e2e_steps,
                "ms_per_step": round(el * 1e3, 4),
-               "call": "odi_cuda_matmul_host per weight (pinned host x/y, synchronous per call)"}
+               "call": "odi_cuda_matmul_host per weight, synchronous per call; pinned host x/y: x fetched by a kernel "
+                       "the GEMV overlaps, y stored by the GEMV into host memory"}
         ref_y = ys[-1].cpu().numpy()
         _np.testing.assert_allclose(hy[-1].numpy(), ref_y, rtol=0, atol=0)
         for h in hw:
             L.odi_cuda_weight_free(h)
 
-    # --- CPU baseline (rank 0, N = 1 only)
+    # --- CPU baseline (rank 0, N = 1 only): the reference arm's own sample
     cpu = None
     ref_cfg1 = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        nth = os.cpu_count() or 1
-        per, reps_c = cpu_port_gemv_time(nth, args.cpu_budget)
+        nth = host_threads()
+        per = cpu_port_gemv_time(nth)
         cpu = {"value": round(algo_bytes(N, K, M) / per / 1e9, 4), "unit": "GB/s", "cores": nth, "kind": "port",
-               "sample": f"{reps_c} Q4_K {N}x{K} M=1 GEMVs on {nth} threads (oracle restatement of the "
-                         "reference loop; the reference throws on K-quants)"}
+               "sample": cpu_sample_text(nth)}
         r1 = reference_q4_0_config1(min(5.0, args.cpu_budget))
         if r1:
-            ref_cfg1 = {"value": round(r1[0], 4), "unit": "GB/s", "ms_per_call": round(r1[1] * 1e3, 3),
-                        "threads_used": r1[2], "kind": "reference",
+            ref_cfg1 = {"aux": "reference_cpu_config1", "value": round(r1[0], 4), "unit": "GB/s",
+                        "ms_per_call": round(r1[1] * 1e3, 3), "threads_used": r1[2], "kind": "reference",
                         "sample": "unmodified CPUBackend::matmul, Q4_0 4096x4096 M=1 (config 1)"}
 
     decode = None
@@ -472,6 +483,12 @@ def run_ours(args, rank, world, local_rank):
             configs = run_config_legs(args)
 
     if rank == 0:
+        # Full detail first, one JSON object per line; the headline comes last
+        # and ends with compact summaries of the same numbers, so the end of
+        # stdout carries them.
+        for aux in (ref_cfg1, decode and dict(aux="decode_7b", **decode), configs and dict(aux="configs", **configs)):
+            if aux:
+                print(json.dumps(aux), flush=True)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
@@ -480,16 +497,21 @@ def run_ours(args, rank, world, local_rank):
             "config": workload_config(R, world, args.gather),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(),
+                         "traffic_source": TRAFFIC_SOURCE,
                          "kernel": "qgemv_kernel<Q4_K,1,false>", "us_per_launch": round(us_gemv, 3),
                          "algorithmic_bytes_per_launch": algo_bytes(N, K, M), "peak_kind": peak_kind},
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "reference_cpu_config1": ref_cfg1,
             "clocks": clk.summary(),
             "gpu_launches": args.steps * SWEEPS * R * (2 if fused else 1),
-            "decode_7b": decode,
-            "configs": configs,
         }
+        if decode:
+            line["decode_7b"] = {"value": decode["value"], "unit": "tokens/s",
+                                 "frac": decode["roofline"]["frac"],
+                                 "e2e": decode["e2e"]["value"],
+                                 "cpu": decode["cpu_baseline"]["value"] if decode.get("cpu_baseline") else None}
+        if configs:
+            line["configs_frac"] = config_summary(configs)
         print(json.dumps(line), flush=True)
     if world > 1 or (args.no_decode and args.no_configs):
         del g_step, g_gemv
@@ -737,6 +759,23 @@ def cpu_decode_sample(nthreads: int, reps: int = 3):
                f"{nthreads} threads; oracle restatement of the reference loop; matrix products only")
 
 
+TRAFFIC_SOURCE = ("profiles/qgemv_q4k_4096x14336_m1.md: ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                  "launch of this kernel at this shape (bench.py --profile); ncu cannot run inside the timed bench")
+
+
+def config_summary(configs):
+    """The configuration legs in one short dict: HBM fraction per GEMV shape
+    and token count, tensor fraction per prefill shape."""
+    out = {}
+    for r in configs.get("gemv_sweep", []):
+        out[f"{r['dtype']} {r['N']}x{r['K']} M{r['M']}"] = r["hbm_frac"]
+    for r in configs.get("prefill_gemm", []):
+        out[f"prefill {r['N']}x{r['K']} M{r['M']} TF"] = r["tensor_frac"]
+    for r in configs.get("gemv_70b", []):
+        out[f"70b {r['N']}x{r['K']} M{r['M']}"] = r["hbm_frac"]
+    return out
+
+
 def traffic_per_launch():
     """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
     import re
@@ -748,6 +787,44 @@ def traffic_per_launch():
         return int(m.group(1)) if m else None
     except OSError:
         return None
+
+
+# Small cases for ncu captures of the other configurations' kernels (one GPU):
+# name -> (dtype, N, K, M, act_mode name, what it captures)
+PROFILE_CASES = {
+    "tc_prefill_m2048": ("Q4_K", 4096, 14336, 2048, "ACT_AUTO", "qgemm_tc_kernel, the tcgen05 prefill GEMM"),
+    "gemv8_q6k_4096": ("Q6_K", 4096, 4096, 8, "ACT_AUTO", "qgemv_kernel<Q6_K,8,...>, the 8-token mma.sync GEMV"),
+    "gemv8_q4k_14336": ("Q4_K", 4096, 14336, 8, "ACT_AUTO", "qgemv_kernel<Q4_K,8,...>, the 8-token mma.sync GEMV"),
+}
+
+
+def run_profile_case(name, local_rank):
+    """Three eager products of one configuration on the device (seeded
+    weights quantised on the device, fp32 activations), nothing timed."""
+    import torch
+
+    import odiengine_b200 as ob
+
+    dtn, N, K, M, mode, _ = PROFILE_CASES[name]
+    torch.cuda.set_device(local_rank)
+    ob.init(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dt = ob.DTYPES[dtn]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    wf = torch.empty((N, K), dtype=torch.float32, device=dev).normal_(0.0, 0.02, generator=gen)
+    w = ob.repack(dt, ob.quantize_weight(dt, wf), N, K)
+    del wf
+    x = torch.empty((M, K), dtype=torch.float32, device=dev).normal_(0.0, 1.0, generator=gen)
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    am = getattr(ob, mode)
+    ws = ob.new_workspace(ob.workspace_bytes(dt, M, N, K, am), dev)
+    for _ in range(3):
+        ob.matmul_dev(dt, w, x, y, N, K, am, ws)
+    torch.cuda.synchronize()
+    assert ob.workspace_status(ws) == 0
+    print(json.dumps({"profile_case": name, "ok": True}))
+    return 0
 
 
 def main():
@@ -765,6 +842,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="leave out the other reference configurations (GEMV sweep, prefill GEMM, 70B shapes)")
     ap.add_argument("--profile", action="store_true", help="small case for ncu: 3 products, no timing")
+    ap.add_argument("--profile-case", default=None, choices=list(PROFILE_CASES),
+                    help="small case for ncu of another configuration's kernel: 3 products, no timing")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="N > 1: gather the row shards from the GEMV epilogue (fused) or with ncclAllGather")
     args = ap.parse_args()
@@ -773,6 +852,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.profile_case:
+        return run_profile_case(args.profile_case, local_rank)
     if args.decode_only:
         if world > 1:
             raise SystemExit("--decode-only runs on one GPU")

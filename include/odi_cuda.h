@@ -267,15 +267,21 @@ int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t 
 
 /* Host-buffer form of Backend::matmul as the reference Context calls it
  * (context.cpp:152, 188-190): h_x [M, K] and h_y [M, N] are host memory;
- * the call copies x in, runs the product on the weight's device copy,
- * copies y out and waits.  Uses a library-owned per-device workspace. */
+ * the call brings x in, runs the product on the weight's device copy,
+ * brings y out and waits.  Uses a library-owned per-device workspace.
+ * Page-locked buffers (cudaHostAlloc / cudaHostRegister) are reached from
+ * the device directly -- x fetched by a kernel the product overlaps, y
+ * stored by the product itself -- which saves the two copies' latency;
+ * pageable buffers go through cudaMemcpyAsync.
+ * Returns ODI_CUDA_ERR_OPERATION_FAILED (h_y not to be used) when a kernel's
+ * bounded wait gave up, as cpu_backend.cpp:177-227 throws on failure. */
 int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
                          int act_mode, void* stream);
 
 /* Host-buffer form of Backend::dequantize (backend.hpp:111;
  * cpu_backend.cpp:625-648) for an uploaded weight: h_out receives N*K fp32
- * values in block order ([N][K]).  Synchronous; uses a temporary device
- * buffer of N*K*4 bytes. */
+ * values in block order ([N][K]).  Synchronous; the values pass through the
+ * library's per-device output buffer (grown once to N*K*4 bytes, kept). */
 int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* stream);
 
 /* --- decode step: the non-matmul operations of Context::forward ------------- */
@@ -400,10 +406,29 @@ int odi_cuda_matmul_scatter(int dtype, const void* d_w_tiled, const float* d_x, 
  * until every source rank p's counter reached d_consumed[p] +
  * increments[p] (increments = odi_cuda_scatter_signals of rank p's shard),
  * then advances d_consumed.  d_counters / d_consumed are this rank's own
- * arrays (nranks uint64, zero at start).  Bounded: a rank that never
- * arrives sets the workspace error word (see odi_cuda_workspace_status). */
+ * arrays (nranks uint64, zero at start).  Bounded: a rank that has not
+ * arrived after one second sets ODI_CUDA_WS_ERR_PEER_WAIT in the workspace
+ * error word (see odi_cuda_workspace_status) and the kernel returns; the
+ * gathered output is then invalid.  The counterpart of the all-gather that
+ * follows a row-sharded Backend::matmul (backend.hpp:38); the reference has
+ * no multi-GPU path. */
 int odi_cuda_wait_peers(const unsigned long long* d_counters, unsigned long long* d_consumed,
                         const unsigned long long* increments, int nranks, void* d_workspace, void* stream);
+
+/* odi_cuda_wait_peers with the give-up time chosen by the caller
+ * (1 us .. 60 s), for failure detection that must answer faster than the
+ * default second. */
+int odi_cuda_wait_peers_timeout(const unsigned long long* d_counters, unsigned long long* d_consumed,
+                                const unsigned long long* increments, int nranks, uint64_t timeout_us,
+                                void* d_workspace, void* stream);
+
+/* Bits of the workspace error word (odi_cuda_workspace_status): a bounded
+ * device wait that gave up. */
+#define ODI_CUDA_WS_ERR_FULL_WAIT 1
+#define ODI_CUDA_WS_ERR_EMPTY_WAIT 2
+#define ODI_CUDA_WS_ERR_DRAIN_WAIT 4
+#define ODI_CUDA_WS_ERR_REDUCE_WAIT 8
+#define ODI_CUDA_WS_ERR_PEER_WAIT 32
 
 /* Zeroed device buffer for sharing with other processes: *d_ptr and the
  * ODI_CUDA_IPC_HANDLE_BYTES-byte handle to pass to the other ranks. */
@@ -412,6 +437,43 @@ int odi_cuda_sym_free(void* d_ptr);
 /* Map another rank's buffer (handle from its odi_cuda_sym_alloc). */
 int odi_cuda_ipc_open(const void* ipc_handle, void** d_ptr);
 int odi_cuda_ipc_close(void* d_ptr);
+
+/* --- row-sharded product over an NCCL communicator ---------------------------
+ * A weight too large (or too slow) for one GPU is split by output rows across
+ * the GPUs of one node, one process each; every rank computes its rows and the
+ * slices are all-gathered with NCCL over NVLink.  This is the C-ABI form of
+ * the row sharding a Backend::matmul (backend.hpp:38) needs once the model
+ * spans GPUs; the reference has no multi-GPU path.  NCCL (libnccl.so.2) is
+ * opened at run time: these calls fail with ODI_CUDA_ERR_BACKEND_UNAVAILABLE
+ * where it is absent, and nothing else depends on it. */
+#define ODI_CUDA_NCCL_ID_BYTES 128
+typedef struct odi_cuda_comm odi_cuda_comm;
+
+/* A new communicator id: one rank makes it and hands the bytes to the others
+ * over any host channel. */
+int odi_cuda_nccl_unique_id(void* id /* ODI_CUDA_NCCL_ID_BYTES */);
+/* Joins the communicator as `rank` of `nranks` on the current device (every
+ * rank calls it; it returns when all have joined). */
+int odi_cuda_nccl_init(const void* id, int nranks, int rank, odi_cuda_comm** comm);
+int odi_cuda_nccl_free(odi_cuda_comm* comm);
+int odi_cuda_comm_ranks(const odi_cuda_comm* comm, int* nranks, int* rank);
+
+/* Device workspace of odi_cuda_matmul_sharded: the product's workspace for
+ * the shard, then the gather buffer of nranks * M * S fp32. */
+size_t odi_cuda_sharded_workspace_bytes(const odi_cuda_comm* comm, int dtype, int64_t M, int64_t S, int64_t K,
+                                        int act_mode);
+
+/* d_y [M, N] = d_x [M, K] . W^T on every rank, W [N rows] split by rows:
+ * rank r holds rows [r*S, min(N, (r+1)*S)) as its own tiled weight of S rows
+ * (rows past N zero; S = ceil(N / nranks) is the usual split).  The rank
+ * computes its S rows, the slices are all-gathered in place (ncclAllGather
+ * on `stream`), and -- unless M = 1 and N = nranks * S, where the gathered
+ * slices are y itself -- one small kernel lays them out as [M, N].  All
+ * ranks call it with the same M, N, S, K and act_mode, in the same order
+ * as their other collectives. */
+int odi_cuda_matmul_sharded(odi_cuda_comm* comm, int dtype, const void* d_w_shard, const float* d_x, float* d_y,
+                            int64_t M, int64_t N, int64_t S, int64_t K, int act_mode, void* d_workspace,
+                            size_t workspace_bytes, int flags, void* stream);
 
 /* Size of the static device array behind odi_cuda_matmul_host_noalloc. */
 #define ODI_CUDA_NOALLOC_SCRATCH_BYTES (8u << 20)
@@ -434,8 +496,16 @@ int odi_cuda_ipc_close(void* d_ptr);
  *
  * Limit: round_up(W, 256) + round_up(M*K*4, 256) + M*N*4 <=
  * ODI_CUDA_NOALLOC_SCRATCH_BYTES, W = odi_cuda_matmul_workspace_bytes (256
- * on the streaming GEMV, so M=1 fits any N up to about two million); a
- * larger call returns ODI_CUDA_ERR_INVALID_ARGUMENT and runs nothing.
+ * for one token or fp32 activations, so M=1 fits any N up to about two
+ * million; 256 + ceil(K/256)*M*384 for a multi-token Q8 product; the fp16
+ * activation tiles on the tensor-core path); a larger call returns
+ * ODI_CUDA_ERR_INVALID_ARGUMENT and runs nothing.
+ *
+ * The call itself allocates nothing, but the first call of each kernel
+ * variant (dtype x activation mode x tokens per pass) may make the CUDA
+ * driver load that kernel's code under lazy module loading, which can
+ * reserve device memory: make one call of each variant in use (or run with
+ * CUDA_MODULE_LOADING=EAGER) before the phase that must not allocate.
  *
  * The first call on a device, with that device current, looks up the
  * array's device address; make that first call before any stream capture on

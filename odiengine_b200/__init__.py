@@ -97,6 +97,13 @@ SIGNATURES = {
     "odi_cuda_scatter_signals": (_i64, [_int, _i64, _i64, _i64, _int]),
     "odi_cuda_matmul_scatter": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp, _vp]),
     "odi_cuda_wait_peers": (_int, [_vp, _vp, _vp, _int, _vp, _vp]),
+    "odi_cuda_wait_peers_timeout": (_int, [_vp, _vp, _vp, _int, ctypes.c_uint64, _vp, _vp]),
+    "odi_cuda_nccl_unique_id": (_int, [_vp]),
+    "odi_cuda_nccl_init": (_int, [_vp, _int, _int, ctypes.POINTER(_vp)]),
+    "odi_cuda_nccl_free": (_int, [_vp]),
+    "odi_cuda_comm_ranks": (_int, [_vp, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+    "odi_cuda_sharded_workspace_bytes": (_sz, [_vp, _int, _i64, _i64, _i64, _int]),
+    "odi_cuda_matmul_sharded": (_int, [_vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp]),
     "odi_cuda_sym_alloc": (_int, [_sz, ctypes.POINTER(_vp), _vp]),
     "odi_cuda_sym_free": (_int, [_vp]),
     "odi_cuda_ipc_open": (_int, [_vp, ctypes.POINTER(_vp)]),

@@ -4,6 +4,7 @@
 // records a thread-local message; CUDA failures are mapped to
 // ODI_ERROR_GPU_OUT_OF_MEMORY (allocation) or ODI_ERROR_OPERATION_FAILED.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -32,6 +33,39 @@ int cuda_fail(cudaError_t e, const char* what) {
   const int code = (e == cudaErrorMemoryAllocation) ? ODI_CUDA_ERR_GPU_OUT_OF_MEMORY
                                                     : ODI_CUDA_ERR_OPERATION_FAILED;
   return fail(code, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+// Host-side fault injection for the failure-detection tests: ODI_CUDA_INJECT,
+// a comma-separated list read once per process.
+//   init  -- odi_cuda_init reports no usable device (BACKEND_UNAVAILABLE);
+//   alloc -- every device allocation the library makes fails as out of
+//            memory (weight upload, host-call buffers, symmetric buffers);
+//   wait  -- the host-buffer products find their error word set, as after a
+//            kernel wait that gave up (the word is written on the device by
+//            a memset, so the read-back path is the real one);
+//   nccl  -- odi_cuda_nccl_init fails as a communicator that cannot form
+//            (BACKEND_INIT_FAILED).
+// Nothing is made to fail on the GPU itself.
+enum { INJ_INIT = 1, INJ_ALLOC = 2, INJ_WAIT = 4, INJ_NCCL = 8 };
+int injected() {
+  static const int v = [] {
+    const char* e = getenv("ODI_CUDA_INJECT");
+    if (!e) return 0;
+    const std::string s = std::string(",") + e + ",";
+    return (s.find(",init,") != std::string::npos ? INJ_INIT : 0) |
+           (s.find(",alloc,") != std::string::npos ? INJ_ALLOC : 0) |
+           (s.find(",wait,") != std::string::npos ? INJ_WAIT : 0) |
+           (s.find(",nccl,") != std::string::npos ? INJ_NCCL : 0);
+  }();
+  return v;
+}
+
+cudaError_t dev_malloc(void** p, size_t n) {
+  if (injected() & INJ_ALLOC) {
+    *p = nullptr;
+    return cudaErrorMemoryAllocation;
+  }
+  return cudaMalloc(p, n);
 }
 
 #define CK(call, what)                         \
@@ -145,7 +179,13 @@ int odi_cuda_device_count(void) {
   return n;
 }
 
+static_assert(ODI_CUDA_WS_ERR_FULL_WAIT == ERR_FULL_WAIT && ODI_CUDA_WS_ERR_EMPTY_WAIT == ERR_EMPTY_WAIT &&
+                  ODI_CUDA_WS_ERR_DRAIN_WAIT == ERR_DRAIN_WAIT && ODI_CUDA_WS_ERR_REDUCE_WAIT == ERR_REDUCE_WAIT &&
+                  ODI_CUDA_WS_ERR_PEER_WAIT == ERR_PEER_WAIT,
+              "error word bits");
+
 int odi_cuda_init(int device) {
+  if (injected() & INJ_INIT) return fail(ODI_CUDA_ERR_BACKEND_UNAVAILABLE, "no usable CUDA device (ODI_CUDA_INJECT=init)");
   int n = 0;
   cudaError_t e = cudaGetDeviceCount(&n);
   if (e != cudaSuccess || n == 0)
@@ -223,9 +263,9 @@ int odi_cuda_weight_upload(const void* host_blocks, int dtype, int64_t N, int64_
   const int64_t gb = odi_cuda_gguf_bytes(dtype, N, K), tb = odi_cuda_tiled_bytes(dtype, N, K);
   void* staging = nullptr;
   void* tiled = nullptr;
-  cudaError_t e = cudaMalloc(&staging, (size_t)gb);
+  cudaError_t e = dev_malloc(&staging, (size_t)gb);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (upload staging)");
-  e = cudaMalloc(&tiled, (size_t)tb);
+  e = dev_malloc(&tiled, (size_t)tb);
   if (e == cudaSuccess) e = cudaMemcpy(staging, host_blocks, (size_t)gb, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = launch_repack(dtype, staging, tiled, N, K, nullptr);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -644,23 +684,33 @@ int odi_cuda_matmul_scatter(int dtype, const void* d_w_tiled, const float* d_x, 
                   workspace_bytes, (flags & ODI_CUDA_FLAG_PDL) != 0, (cudaStream_t)stream, &g);
 }
 
-int odi_cuda_wait_peers(const unsigned long long* d_counters, unsigned long long* d_consumed,
-                        const unsigned long long* increments, int nranks, void* d_workspace, void* stream) {
+int odi_cuda_wait_peers_timeout(const unsigned long long* d_counters, unsigned long long* d_consumed,
+                                const unsigned long long* increments, int nranks, uint64_t timeout_us,
+                                void* d_workspace, void* stream) {
   if (!d_counters || !d_consumed || !increments || !d_workspace)
     return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
   if (nranks < 1 || nranks > MAX_PEERS) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid nranks %d", nranks);
+  if (timeout_us < 1 || timeout_us > 60000000ull)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "timeout %llu us outside 1 us .. 60 s", (unsigned long long)timeout_us);
   PeerWait w{};
   for (int p = 0; p < nranks; ++p) w.inc[p] = increments[p];
   w.n = nranks;
+  w.timeout_ns = timeout_us * 1000ull;
   CK(launch_wait_peers(d_counters, d_consumed, w, (int*)d_workspace, (cudaStream_t)stream), "wait_peers launch");
   return ODI_CUDA_OK;
+}
+
+int odi_cuda_wait_peers(const unsigned long long* d_counters, unsigned long long* d_consumed,
+                        const unsigned long long* increments, int nranks, void* d_workspace, void* stream) {
+  return odi_cuda_wait_peers_timeout(d_counters, d_consumed, increments, nranks, PEER_WAIT_DEFAULT_NS / 1000,
+                                     d_workspace, stream);
 }
 
 int odi_cuda_sym_alloc(size_t bytes, void** d_ptr, void* ipc_handle) {
   if (!d_ptr || !ipc_handle || bytes == 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
   *d_ptr = nullptr;
   void* p = nullptr;
-  CK(cudaMalloc(&p, bytes), "cudaMalloc (symmetric buffer)");
+  CK(dev_malloc(&p, bytes), "cudaMalloc (symmetric buffer)");
   cudaError_t e = cudaMemset(p, 0, bytes);
   cudaIpcMemHandle_t h;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
@@ -696,6 +746,102 @@ int odi_cuda_ipc_close(void* d_ptr) {
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// Row-sharded product over an NCCL communicator (shard.cu).
+// ---------------------------------------------------------------------------
+struct odi_cuda_comm {
+  void* nccl;
+  int nranks, rank, device;
+};
+
+extern "C" {
+
+int odi_cuda_nccl_unique_id(void* id) {
+  if (!id) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null id");
+  static_assert(ODI_CUDA_NCCL_ID_BYTES >= 128, "NCCL unique id size");
+  const char* why = "";
+  if (nccl_unique_id(id, &why))
+    return fail(nccl_available() ? ODI_CUDA_ERR_BACKEND_INIT_FAILED : ODI_CUDA_ERR_BACKEND_UNAVAILABLE,
+                "ncclGetUniqueId: %s", why);
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_nccl_init(const void* id, int nranks, int rank, odi_cuda_comm** comm) {
+  if (!id || !comm) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  *comm = nullptr;
+  if (nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "rank %d outside %d ranks", rank, nranks);
+  if (injected() & INJ_NCCL)
+    return fail(ODI_CUDA_ERR_BACKEND_INIT_FAILED, "NCCL communicator init failed (ODI_CUDA_INJECT=nccl)");
+  int dev = 0;
+  CK(cudaGetDevice(&dev), "cudaGetDevice");
+  void* c = nullptr;
+  const char* why = "";
+  if (nccl_comm_init(id, nranks, rank, &c, &why))
+    return fail(nccl_available() ? ODI_CUDA_ERR_BACKEND_INIT_FAILED : ODI_CUDA_ERR_BACKEND_UNAVAILABLE,
+                "ncclCommInitRank: %s", why);
+  odi_cuda_comm* h = new (std::nothrow) odi_cuda_comm{c, nranks, rank, dev};
+  if (!h) {
+    nccl_comm_destroy(c, &why);
+    return fail(ODI_CUDA_ERR_OUT_OF_MEMORY, "host allocation failed");
+  }
+  *comm = h;
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_nccl_free(odi_cuda_comm* comm) {
+  if (!comm) return ODI_CUDA_OK;
+  const char* why = "";
+  const int r = nccl_comm_destroy(comm->nccl, &why);
+  delete comm;
+  if (r) return fail(ODI_CUDA_ERR_OPERATION_FAILED, "ncclCommDestroy: %s", why);
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_comm_ranks(const odi_cuda_comm* comm, int* nranks, int* rank) {
+  if (!comm) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null communicator");
+  if (nranks) *nranks = comm->nranks;
+  if (rank) *rank = comm->rank;
+  return ODI_CUDA_OK;
+}
+
+size_t odi_cuda_sharded_workspace_bytes(const odi_cuda_comm* comm, int dtype, int64_t M, int64_t S, int64_t K,
+                                        int act_mode) {
+  if (!comm || M < 1 || S < 1 || K < 1) return 0;
+  const size_t pw = odi_cuda_matmul_workspace_bytes(dtype, M, S, K, act_mode);
+  if (!pw) return 0;
+  return (pw + 255) / 256 * 256 + (size_t)comm->nranks * (size_t)M * (size_t)S * sizeof(float);
+}
+
+int odi_cuda_matmul_sharded(odi_cuda_comm* comm, int dtype, const void* d_w_shard, const float* d_x, float* d_y,
+                            int64_t M, int64_t N, int64_t S, int64_t K, int act_mode, void* d_workspace,
+                            size_t workspace_bytes, int flags, void* stream) {
+  if (!comm) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null communicator");
+  if (M < 1 || N < 1 || S < 1 || (int64_t)comm->nranks * S < N || (int64_t)(comm->nranks - 1) * S >= N)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "shard of S=%lld rows does not split N=%lld over %d ranks",
+                (long long)S, (long long)N, comm->nranks);
+  if (!d_y) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null output");
+  const size_t need = odi_cuda_sharded_workspace_bytes(comm, dtype, M, S, K, act_mode);
+  if (!need) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid sharded product");
+  if (workspace_bytes < need)
+    return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
+  const size_t pw = (odi_cuda_matmul_workspace_bytes(dtype, M, S, K, act_mode) + 255) / 256 * 256;
+  cudaStream_t s = (cudaStream_t)stream;
+  // M = 1 with every shard full: the rank-major slices are y itself
+  const bool direct = M == 1 && N == (int64_t)comm->nranks * S;
+  float* slots = direct ? d_y : reinterpret_cast<float*>(static_cast<uint8_t*>(d_workspace) + pw);
+  float* mine = slots + (int64_t)comm->rank * M * S;
+  int rc = odi_cuda_matmul(dtype, d_w_shard, d_x, mine, M, S, K, act_mode, d_workspace, pw, flags, stream);
+  if (rc) return rc;
+  const char* why = "";
+  if (nccl_all_gather_f32(mine, slots, (size_t)(M * S), comm->nccl, s, &why))
+    return fail(ODI_CUDA_ERR_OPERATION_FAILED, "ncclAllGather: %s", why);
+  if (!direct) CK(launch_unshard(slots, d_y, M, N, S, comm->nranks, s), "unshard launch");
+  return ODI_CUDA_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
 // Host-buffer matmul with a library-owned per-device arena.
 // ---------------------------------------------------------------------------
 namespace {
@@ -715,7 +861,7 @@ cudaError_t grow(void** p, size_t* have, size_t need, bool zero) {
   if (*p) cudaFree(*p);
   *p = nullptr;
   *have = 0;
-  cudaError_t e = cudaMalloc(p, need);
+  cudaError_t e = dev_malloc(p, need);
   if (e != cudaSuccess) return e;
   if (zero) {
     e = cudaMemset(*p, 0, need);
@@ -723,6 +869,35 @@ cudaError_t grow(void** p, size_t* have, size_t need, bool zero) {
   }
   *have = need;
   return cudaSuccess;
+}
+
+// The device address of page-locked host memory (registered or allocated
+// through CUDA), or nullptr for pageable memory.
+template <typename T>
+T* device_view(T* host) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, host) != cudaSuccess) {
+    cudaGetLastError();  // pageable memory on older drivers reports an error; clear it
+    return nullptr;
+  }
+  if (at.type != cudaMemoryTypeHost || !at.devicePointer) return nullptr;
+  return static_cast<T*>(at.devicePointer);
+}
+
+// End of a synchronous host-buffer call: wait for the stream, then read the
+// workspace's error word.  A kernel wait that gave up fails the call (its
+// output is not to be trusted); the word is cleared for the next call.
+int finish_host_call(Arena& A, cudaStream_t s) {
+  int err = 0;
+  if (injected() & INJ_WAIT) CK(cudaMemsetAsync(A.ws, 0x01, 1, s), "injected wait failure");
+  CK(cudaMemcpyAsync(&err, A.ws, sizeof(int), cudaMemcpyDeviceToHost, s), "read error word");
+  CK(cudaStreamSynchronize(s), "sync");
+  if (err) {
+    CK(cudaMemsetAsync(A.ws, 0, sizeof(int), s), "clear error word");
+    CK(cudaStreamSynchronize(s), "sync");
+    return fail(ODI_CUDA_ERR_OPERATION_FAILED, "a kernel wait gave up (error word 0x%x); the output is invalid", err);
+  }
+  return ODI_CUDA_OK;
 }
 }  // namespace
 
@@ -741,12 +916,25 @@ extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, 
   CK(grow((void**)&A.x, &A.x_bytes, (size_t)(M * w->K) * sizeof(float), false), "x alloc");
   CK(grow((void**)&A.y, &A.y_bytes, (size_t)(M * w->N) * sizeof(float), false), "y alloc");
   cudaStream_t s = (cudaStream_t)stream;
-  CK(cudaMemcpyAsync(A.x, h_x, (size_t)(M * w->K) * sizeof(float), cudaMemcpyHostToDevice, s), "H2D x");
-  int rc = odi_cuda_matmul(w->dtype, w->data, A.x, A.y, M, w->N, w->K, act_mode, A.ws, A.ws_bytes, 0, stream);
+  // Page-locked host buffers are reached from the device directly: x is
+  // fetched by a small kernel that the product follows with programmatic
+  // dependent launch (the product streams its weights meanwhile), and the
+  // product stores y straight into host memory.  Pageable buffers take the
+  // copy engines.
+  const float* dx = device_view(h_x);
+  float* dy = device_view(h_y);
+  const int mode = resolve_act_mode(w->dtype, M, act_mode);
+  if (mode == ODI_CUDA_ACT_F16) dy = nullptr;  // the tensor-core epilogue writes device memory only
+  const bool pdl = dx != nullptr;
+  if (dx)
+    CK(launch_fetch_host(dx, A.x, M * w->K, s), "fetch x");
+  else
+    CK(cudaMemcpyAsync(A.x, h_x, (size_t)(M * w->K) * sizeof(float), cudaMemcpyHostToDevice, s), "H2D x");
+  int rc = odi_cuda_matmul(w->dtype, w->data, A.x, dy ? dy : A.y, M, w->N, w->K, act_mode, A.ws, A.ws_bytes,
+                           pdl ? ODI_CUDA_FLAG_PDL : 0, stream);
   if (rc) return rc;
-  CK(cudaMemcpyAsync(h_y, A.y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
-  CK(cudaStreamSynchronize(s), "sync");
-  return ODI_CUDA_OK;
+  if (!dy) CK(cudaMemcpyAsync(h_y, A.y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
+  return finish_host_call(A, s);
 }
 
 extern "C" int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* stream) {
@@ -755,14 +943,15 @@ extern "C" int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, 
   CK(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev != w->device) return fail(ODI_CUDA_ERR_INVALID_STATE, "weight lives on device %d, current is %d", w->device, dev);
   const size_t bytes = (size_t)(w->N * w->K) * sizeof(float);
-  float* d_out = nullptr;
-  CK(cudaMalloc(&d_out, bytes), "cudaMalloc (dequantize output)");
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  Arena& A = g_arena[dev & 63];
+  // the values land in the arena's output buffer (grown once to the largest
+  // weight dequantized), not in a buffer allocated per call
+  CK(grow((void**)&A.y, &A.y_bytes, bytes, false), "dequantize output alloc");
   cudaStream_t s = (cudaStream_t)stream;
-  cudaError_t e = launch_dequant(w->dtype, w->data, d_out, w->N, w->K, s);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(h_out, d_out, bytes, cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  cudaFree(d_out);
-  if (e != cudaSuccess) return cuda_fail(e, "dequantize_host");
+  CK(launch_dequant(w->dtype, w->data, A.y, w->N, w->K, s), "dequantize launch");
+  CK(cudaMemcpyAsync(h_out, A.y, bytes, cudaMemcpyDeviceToHost, s), "D2H dequantized");
+  CK(cudaStreamSynchronize(s), "sync");
   return ODI_CUDA_OK;
 }
 
@@ -845,6 +1034,7 @@ extern "C" int odi_cuda_matmul_host_noalloc(const odi_cuda_weight* w, const floa
   if (rc) return rc;
   CK(cudaMemcpyAsync(h_y, d_y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
   int err = 0;
+  if (injected() & INJ_WAIT) CK(cudaMemsetAsync(scr, 0x01, 1, s), "injected wait failure");
   CK(cudaMemcpyAsync(&err, scr, sizeof(int), cudaMemcpyDeviceToHost, s), "read error word");
   CK(cudaStreamSynchronize(s), "sync");
   if (err) return fail(ODI_CUDA_ERR_OPERATION_FAILED, "a kernel wait gave up (error word 0x%x)", err);

@@ -14,6 +14,9 @@ cudaError_t launch_act_records_fused(const float* x, int64_t ldx, int64_t M, int
                                     uint8_t* recs, bool pdl, cudaStream_t stream);
 cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* tiles, bool pdl,
                                 cudaStream_t stream);
+// n fp32 values from page-locked host memory (its device address) to device
+// memory; releases programmatic dependents at once.
+cudaError_t launch_fetch_host(const float* src, float* dst, int64_t n, cudaStream_t s);
 cudaError_t launch_repack(int dt, const void* gguf, void* tiled, int64_t N, int64_t K, cudaStream_t s);
 cudaError_t launch_unpack(int dt, const void* tiled, void* gguf, int64_t N, int64_t K, cudaStream_t s);
 cudaError_t launch_dequant(int dt, const void* tiled, float* out, int64_t N, int64_t K, cudaStream_t s);
@@ -103,10 +106,21 @@ cudaError_t launch_gemv(int dt, bool f32act, const GemvPlan& plan, const GemvArg
 constexpr int ERR_PEER_WAIT = 32;
 struct PeerWait {
   unsigned long long inc[MAX_PEERS];
+  unsigned long long timeout_ns;  // give up after this long (device global timer)
   int n;
 };
+constexpr unsigned long long PEER_WAIT_DEFAULT_NS = 1000000000ull;  // one second
 cudaError_t launch_wait_peers(const unsigned long long* cnt, unsigned long long* consumed, const PeerWait& w,
                               int* err, cudaStream_t s);
+
+// NCCL, opened at run time (shard.cu).  Each returns 0, or -1 with *why set.
+bool nccl_available();
+int nccl_unique_id(void* out, const char** why);
+int nccl_comm_init(const void* id, int nranks, int rank, void** comm, const char** why);
+int nccl_comm_destroy(void* comm, const char** why);
+int nccl_all_gather_f32(const float* send, float* recv, size_t count, void* comm, cudaStream_t s, const char** why);
+// y [M][N] from a rank-major gather buffer [g][M][S]
+cudaError_t launch_unshard(const float* src, float* y, int64_t M, int64_t N, int64_t S, int g, cudaStream_t s);
 
 // Decode-step kernels (decode_ops.cu).  The token and position live on the
 // device; argmax advances them, so one captured graph serves every step.

@@ -8,8 +8,11 @@
 // rank (acquire, system scope), then advances consumed[src]: the state lives
 // on the device, so a CUDA graph replaying the pair stays in step.
 //
-// The wait is bounded (WAIT_BUDGET_CYCLES): a rank that never arrives sets
-// ERR_PEER_WAIT in the error word and the kernel returns.
+// The wait is bounded (PeerWait::timeout_ns of the device's global timer, one
+// second by default): a rank that never arrives sets ERR_PEER_WAIT in the
+// error word and the kernel returns.  The consumed counts advance all the
+// same, so the host, which must treat the gathered product as invalid, can
+// keep the pair in step once the late rank's arrival lands.
 #include "internal.h"
 
 namespace odi_cuda {
@@ -18,6 +21,12 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 __global__ void wait_peers_kernel(const unsigned long long* __restrict__ cnt, unsigned long long* __restrict__ consumed,
@@ -29,9 +38,9 @@ __global__ void wait_peers_kernel(const unsigned long long* __restrict__ cnt, un
   if (r < w.n) {
     const unsigned long long target = consumed[r] + w.inc[r];
     if (ld_acquire_sys(cnt + r) < target) {
-      const long long t0 = clock64();
+      const unsigned long long t0 = global_ns();
       while (ld_acquire_sys(cnt + r) < target) {
-        if (clock64() - t0 > WAIT_BUDGET_CYCLES) {
+        if (global_ns() - t0 > w.timeout_ns) {
           if (err) atomicOr(err, ERR_PEER_WAIT);
           break;
         }

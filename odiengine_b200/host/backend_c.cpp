@@ -51,6 +51,24 @@ void* odi_be_create(int kind, int num_threads, int device, int act_mode) {
   return nullptr;
 }
 
+// The backend the integrated factory (create_backend, cpu_backend.cpp:992-1019
+// with the CUDA case patched to create_cuda_backend) returns for `kind`;
+// NULL with the C API's last error set when it returns none.
+void* odi_be_create_via_factory(int kind, int num_threads) {
+  odi_clear_error();
+  try {
+    if (kind == ODI_BACKEND_CUDA) return odi::create_cuda_backend(num_threads).release();
+    if (kind == ODI_BACKEND_CPU) return odi::create_backend(ODI_BACKEND_CPU, num_threads).release();
+    odi_set_error(ODI_ERROR_BACKEND_NOT_SUPPORTED, "unknown backend kind");
+  } catch (const std::exception& e) {
+    odi_set_error(ODI_ERROR_OPERATION_FAILED, e.what());
+  }
+  return nullptr;
+}
+int odi_be_factory_error(void) { return (int)odi_get_last_error(); }
+const char* odi_be_factory_message(void) { return odi_get_last_error_message(); }
+int odi_be_cuda_available(void) { return odi::cuda_backend_available() ? 1 : 0; }
+
 void odi_be_destroy(void* be) { delete static_cast<odi::Backend*>(be); }
 
 int odi_be_matmul(void* be, void* out, int out_ndim, const int64_t* out_shape, const void* a, int a_dtype,

@@ -86,19 +86,51 @@ size_t CUDABackend::cached_weights() const {
 }
 
 bool CUDABackend::supports_dtype(odi_dtype_t dtype) const {
-  // fp32 runs through the inherited CPU code; the quantized types listed in
-  // odi_cuda_supports_dtype run on the GPU.
-  return dtype == ODI_DTYPE_F32 || odi_cuda_supports_dtype(dtype) == 1 || CPUBackend::supports_dtype(dtype);
+  // Unquantized types run through the inherited CPU element-wise code; of the
+  // quantized types only those the GPU computes (odi_cuda_supports_dtype).
+  // Q8_K and any other block type the library lacks are refused, never run
+  // on the CPU.
+  if (dtype_is_quantized(dtype)) return odi_cuda_supports_dtype(dtype) == 1;
+  return CPUBackend::supports_dtype(dtype);
 }
+
+namespace {
+[[noreturn]] void unsupported(const char* op, odi_dtype_t dt) {
+  throw std::runtime_error(std::string(op) + ": quantization type " + std::to_string((int)dt) +
+                           " is not supported by the CUDA backend");
+}
+
+// FNV-1a over the first and last 64 bytes of a weight's blocks: a cached
+// device copy whose host bytes no longer match (another tensor now lives at
+// the same address) is uploaded again.
+uint64_t fingerprint(const void* data, size_t bytes) {
+  const unsigned char* p = static_cast<const unsigned char*>(data);
+  uint64_t h = 1469598103934665603ull;
+  auto mix = [&](const unsigned char* q, size_t n) {
+    for (size_t i = 0; i < n; ++i) h = (h ^ q[i]) * 1099511628211ull;
+  };
+  const size_t n = bytes < 64 ? bytes : 64;
+  mix(p, n);
+  mix(p + bytes - n, n);
+  return h ^ bytes;
+}
+}  // namespace
 
 odi_cuda_weight* CUDABackend::weight_for(const Tensor& b, int64_t N, int64_t K) {
   const Key key{b.data(), (int)b.dtype(), N, K};
+  const int64_t gb = odi_cuda_gguf_bytes((int)b.dtype(), N, K);
+  const uint64_t fp = gb > 0 ? fingerprint(b.data(), (size_t)gb) : 0;
   std::lock_guard<std::mutex> lk(mu_);
   auto it = weights_.find(key);
-  if (it != weights_.end()) return it->second;
+  if (it != weights_.end()) {
+    if (it->second.fp == fp) return it->second.w;
+    ck(odi_cuda_weight_free(it->second.w), "stale weight free");
+    weight_bytes_ -= (size_t)odi_cuda_tiled_bytes((int)b.dtype(), N, K);
+    weights_.erase(it);
+  }
   odi_cuda_weight* w = nullptr;
   ck(odi_cuda_weight_upload(b.data(), (int)b.dtype(), N, K, &w), "weight upload");
-  weights_.emplace(key, w);
+  weights_.emplace(key, Cached{w, fp});
   weight_bytes_ += (size_t)odi_cuda_tiled_bytes((int)b.dtype(), N, K);
   return w;
 }
@@ -123,7 +155,7 @@ void CUDABackend::release_weights() {
   std::lock_guard<std::mutex> lk(mu_);
   int first_rc = ODI_CUDA_OK;
   for (auto& kv : weights_) {
-    int rc = odi_cuda_weight_free(kv.second);
+    int rc = odi_cuda_weight_free(kv.second.w);
     if (rc != ODI_CUDA_OK && first_rc == ODI_CUDA_OK) first_rc = rc;
   }
   weights_.clear();
@@ -136,14 +168,16 @@ void CUDABackend::release_weights() {
 // must equal b.shape(-2) (b.shape(0) for a vector b).  Leading batch
 // dimensions of `a` are not iterated, exactly as there.
 void CUDABackend::matmul(Tensor& out, const Tensor& a, const Tensor& b) {
-  if (!dtype_is_quantized(b.dtype()) || odi_cuda_supports_dtype(b.dtype()) != 1) {
-    // fp32 x fp32 (and any block type the library does not compute) keep the
-    // CPU backend's implementation.  Q4_1 / Q5_0 / Q5_1 run on the GPU and
-    // give the product the block format defines; the CPU backend's fallback
-    // for them reads the dequantized weight transposed (cpu_backend.cpp:211-216).
+  if (!dtype_is_quantized(b.dtype())) {
+    // fp32 x fp32 is not the quantized product: the CPU backend's own code.
     CPUBackend::matmul(out, a, b);
     return;
   }
+  // Every supported block type runs on the GPU, Q4_1 / Q5_0 / Q5_1 included
+  // (the product the block format defines; the CPU backend's fallback for
+  // them reads the dequantized weight transposed, cpu_backend.cpp:211-216).
+  // A block type the library lacks is refused, not run on the CPU.
+  if (odi_cuda_supports_dtype(b.dtype()) != 1) unsupported("matmul", b.dtype());
   if (a.ndim() < 1 || b.ndim() < 1) throw std::runtime_error("matmul: invalid tensor dimensions");
   int64_t M = a.ndim() >= 2 ? a.shape(-2) : 1;
   const int64_t K = a.shape(-1);
@@ -169,10 +203,7 @@ void CUDABackend::quantized_matmul(Tensor& out, const Tensor& a, const Tensor& b
 // A weight tensor has shape [K, N] (K the contiguous dimension); a 1-D
 // tensor is one row.
 void CUDABackend::dequantize(Tensor& out, const Tensor& x) {
-  if (odi_cuda_supports_dtype(x.dtype()) != 1) {
-    CPUBackend::dequantize(out, x);
-    return;
-  }
+  if (odi_cuda_supports_dtype(x.dtype()) != 1) unsupported("dequantize", x.dtype());
   if (!out.data() || !x.data()) throw std::runtime_error("dequantize: null tensor data");
   const int64_t K = x.ndim() >= 2 ? x.shape(0) : x.numel();
   if (K <= 0 || x.numel() % K) throw std::runtime_error("dequantize: invalid shape");

@@ -15,6 +15,9 @@
 //     copied in and the result copied out on every call, so `out` is ready
 //     when matmul returns, as Context expects (context.cpp:76-78).
 //   dequantize of a supported quantized tensor (backend.hpp:111): on the GPU.
+//   A quantized type the library does not compute (e.g. Q8_K) is refused by
+//   matmul and dequantize with std::runtime_error and reported unsupported
+//   by supports_dtype: the quantized path has no CPU fallback.
 //   Everything else (element-wise ops, norms, attention, fp32 x fp32
 //   matmul) is the CPU backend's, inherited unchanged.
 //
@@ -25,6 +28,7 @@
 
 #include <cstdint>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <tuple>
@@ -82,8 +86,10 @@ class CUDABackend : public CPUBackend {
   // The file must outlive the backend's use of its weights.
   size_t upload_model(const GGUFFile& file);
 
-  // Drops every cached device copy of a weight (e.g. after unloading a model
-  // whose mmap address may be reused).
+  // Drops every cached device copy of a weight.  Call it when a model is
+  // unloaded: a later tensor at a reused mmap address is recognised by a
+  // fingerprint of its first and last 64 bytes and uploaded again, but only
+  // an explicit release frees the HBM of weights no longer used.
   void release_weights();
 
   // Number of weights currently held in HBM, and their bytes.
@@ -93,14 +99,24 @@ class CUDABackend : public CPUBackend {
 
  private:
   using Key = std::tuple<const void*, int, int64_t, int64_t>;
+  struct Cached {
+    odi_cuda_weight* w;
+    uint64_t fp;  // fingerprint of the host bytes it was uploaded from
+  };
   odi_cuda_weight* weight_for(const Tensor& b, int64_t N, int64_t K);
   void bind_device() const;
 
   int device_ = 0;
   ActMode act_ = ActMode::AUTO;
   mutable std::mutex mu_;
-  std::map<Key, odi_cuda_weight*> weights_;
+  std::map<Key, Cached> weights_;
   size_t weight_bytes_ = 0;
 };
+
+// The factory cases for ODI_BACKEND_CUDA (cuda_factory.cpp): the CUDA
+// backend, or nullptr with ODI_ERROR_BACKEND_UNAVAILABLE recorded through
+// odi_set_error when no usable device exists; never a CPU backend.
+std::unique_ptr<Backend> create_cuda_backend(int num_threads);
+bool cuda_backend_available();
 
 }  // namespace odi

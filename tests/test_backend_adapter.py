@@ -41,7 +41,13 @@ FACADE = {
     "odi_be_gguf_tensor": (_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(_int), ctypes.POINTER(_int),
                                   _shape]),
     "odi_be_upload_model": (_int, [_vp, _vp, ctypes.POINTER(_i64)]),
+    "odi_be_create_via_factory": (_vp, [_int, _int]),
+    "odi_be_factory_error": (_int, []),
+    "odi_be_factory_message": (ctypes.c_char_p, []),
+    "odi_be_cuda_available": (_int, []),
 }
+ODI_ERROR_BACKEND_UNAVAILABLE = 300
+Q8_K = 15  # odi_dtype_t (include/odi/odi_types.h): a block type the CUDA library does not compute
 
 
 class BackendError(RuntimeError):
@@ -168,6 +174,26 @@ def test_cpu_backend_errors_through_facade():
                       O.Q4_K, (256, 32))
     finally:
         be.close()
+
+
+def test_factory_cuda_without_gpu_is_unavailable_not_cpu():
+    """The integrated factory's CUDA case (create_cuda_backend): with no
+    usable GPU it returns no backend and records ODI_ERROR_BACKEND_UNAVAILABLE
+    -- it never hands out a CPUBackend for a CUDA request, as the reference's
+    TODO case does (cpu_backend.cpp:1010-1013)."""
+    need_adapter()
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    L = Backend.lib()
+    assert not L.odi_be_create_via_factory(BACKEND_CUDA, 1)
+    assert L.odi_be_factory_error() == ODI_ERROR_BACKEND_UNAVAILABLE
+    assert b"CUDA" in L.odi_be_factory_message()
+    assert L.odi_be_cuda_available() == 0
+    h = L.odi_be_create_via_factory(BACKEND_CPU, 1)  # the CPU case is the reference's own
+    assert h
+    L.odi_be_destroy(h)
 
 
 def test_cuda_backend_unavailable_without_gpu():
@@ -325,3 +351,65 @@ def test_cuda_backend_uploads_once_and_reports():
         be.sync()
     finally:
         be.close()
+
+
+@pytest.mark.gpu
+def test_factory_cuda_with_gpu_is_the_cuda_backend(cuda_lib):
+    need_adapter()
+    L = Backend.lib()
+    assert L.odi_be_cuda_available() == 1
+    h = L.odi_be_create_via_factory(BACKEND_CUDA, 1)
+    assert h, L.odi_be_factory_message()
+    be = Backend.__new__(Backend)
+    be.h = h
+    try:
+        t, name, _, _, _ = be.info()
+        assert (t, name) == (BACKEND_CUDA, "CUDA")
+    finally:
+        be.close()
+
+
+@pytest.mark.gpu
+def test_cuda_backend_refuses_unsupported_quantized_types(cuda_backends):
+    """No CPU fallback in the quantized path: a block type the library does
+    not compute is reported unsupported and refused by matmul and
+    dequantize, where the reference CPUBackend would claim it
+    (cpu_backend.cpp:123-143) and then throw or fall back."""
+    q8, _ = cuda_backends
+    L = Backend.lib()
+    assert L.odi_be_supports_dtype(q8.h, O.Q4_K) == 1
+    assert L.odi_be_supports_dtype(q8.h, F32) == 1
+    assert L.odi_be_supports_dtype(q8.h, Q8_K) == 0
+    K, N = 256, 64
+    fake = np.zeros(N * 292, np.uint8)  # Q8_K is 292 bytes per 256 values
+    with pytest.raises(BackendError, match="not supported by the CUDA backend"):
+        q8.matmul(np.zeros((1, N), np.float32), np.zeros((1, K), np.float32), fake, Q8_K, (K, N))
+    with pytest.raises(BackendError, match="not supported by the CUDA backend"):
+        q8.dequantize(fake, Q8_K, (K, N))
+
+
+_INJECT_SCRIPT = r"""
+import ctypes, sys
+sys.path.insert(0, {root!r})
+sys.path.insert(0, {tests!r})
+import test_backend_adapter as T
+L = T.Backend.lib()
+h = L.odi_be_create_via_factory(T.BACKEND_CUDA, 1)
+print("handle", bool(h), "code", L.odi_be_factory_error(), L.odi_be_factory_message().decode())
+"""
+
+
+@pytest.mark.gpu
+def test_factory_cuda_init_failure_maps_to_unavailable(cuda_lib):
+    """A device that fails to initialise (host-side injection,
+    ODI_CUDA_INJECT=init, in a child process) gives no backend and
+    ODI_ERROR_BACKEND_UNAVAILABLE, on a machine that has a GPU."""
+    import subprocess
+    import sys
+
+    need_adapter()
+    env = dict(os.environ, ODI_CUDA_INJECT="init")
+    code = _INJECT_SCRIPT.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert "handle False code 300" in r.stdout, r.stdout

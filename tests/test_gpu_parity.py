@@ -309,3 +309,39 @@ def test_backend_errors(cuda_lib):
         be.matmul(np.zeros((1, 64), np.float32), np.zeros((1, 256), np.float32), w)
     with pytest.raises(RuntimeError, match="require F32 activations"):
         be.matmul(np.zeros((1, 64), np.float32), np.zeros((1, 512), np.float16), w)
+
+
+@pytest.mark.parametrize("dt,N,K,M", [(O.Q4_K, 4096, 14336, 1), (O.Q8_0, 300, 1024, 3), (O.Q6_K, 4096, 4096, 9)])
+@pytest.mark.parametrize("offset", [0, 1], ids=["aligned", "offset4"])
+def test_matmul_host_pinned_buffers(cuda_lib, dt, N, K, M, offset):
+    """odi_cuda_matmul_host on page-locked host buffers (x fetched by the
+    device, y stored by the product into host memory) gives the results of
+    the device-buffer product bit for bit; pageable buffers (the copy-engine
+    path) too.  offset4 starts both buffers 4 bytes into a pinned block, so
+    the fetch takes its unaligned path."""
+    import ctypes
+
+    import torch
+
+    ob = cuda_lib
+    L = ob.lib()
+    b, x = make(dt, N, K, seed=N + M, M=M)
+    h = ctypes.c_void_p()
+    bb = np.ascontiguousarray(b)
+    ob.check(L.odi_cuda_weight_upload(bb.ctypes.data_as(ctypes.c_void_p), dt, N, K, ctypes.byref(h)))
+    try:
+        t = upload(ob, dt, b, N, K)
+        want, _ = run_matmul(ob, dt, t, x, N, K, ob.ACT_AUTO)
+        hx = torch.empty(M * K + 4, dtype=torch.float32).pin_memory()
+        hy = torch.full((M * N + 4,), float("nan"), dtype=torch.float32).pin_memory()
+        hx[offset:offset + M * K] = torch.from_numpy(x.reshape(-1))
+        ob.check(L.odi_cuda_matmul_host(h, hx.data_ptr() + 4 * offset, hy.data_ptr() + 4 * offset, M, ob.ACT_AUTO,
+                                        None))
+        got = hy[offset:offset + M * N].numpy().reshape(M, N)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        yp = np.full((M, N), np.nan, np.float32)  # pageable
+        ob.check(L.odi_cuda_matmul_host(h, x.ctypes.data_as(ctypes.c_void_p), yp.ctypes.data_as(ctypes.c_void_p), M,
+                                        ob.ACT_AUTO, None))
+        assert np.array_equal(yp.view(np.uint32), want.view(np.uint32))
+    finally:
+        L.odi_cuda_weight_free(h)

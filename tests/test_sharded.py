@@ -20,6 +20,8 @@ import pytest
 import oracle as O
 from odiengine_b200.sharded import shard_rows
 
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+
 
 def _free_port():
     s = socket.socket()
@@ -174,3 +176,161 @@ def test_sharded_two_gpus_match_one():
             _, _, mag = O.matmul_q8act(dt, xs, b, N, with_mag=True)
             bound = 2.0 * (K / 8 + 64) * 2.0 ** -24 * mag.astype(np.float64)
         assert (np.abs(y.astype(np.float64) - ref) <= 2 * bound + 1e-30).all()
+
+
+# --------------------------------------------------------------------------
+# The C-ABI sharded product (odi_cuda_nccl_* / odi_cuda_matmul_sharded): what a
+# C++ Backend calls to shard without Python
+# --------------------------------------------------------------------------
+def _capi_shard_weight(ob, dt, blocks, N, K, world, rank):
+    """This rank's S-row tiled weight on the device: its GGUF block-rows, the
+    last rank's padded with zero rows."""
+    import torch
+
+    from odiengine_b200.sharded import shard_blocks, shard_rows
+
+    _, _, S = shard_rows(N, world, rank)
+    mine = shard_blocks(blocks, dt, N, K, world, rank)
+    pad = np.zeros(S * ob.gguf_bytes(dt, 1, K), np.uint8)
+    pad[: mine.size] = mine
+    return ob.repack(dt, torch.from_numpy(pad).cuda(), S, K), S
+
+
+def _capi_product(ob, comm, dt, w, x, N, S, K, mode):
+    import torch
+
+    L = ob.lib()
+    M = x.shape[0]
+    y = torch.full((M, N), float("nan"), device="cuda")
+    ws = ob.new_workspace(L.odi_cuda_sharded_workspace_bytes(comm, dt, M, S, K, mode))
+    ob.check(L.odi_cuda_matmul_sharded(comm, dt, w.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, S, K, mode,
+                                       ws.data_ptr(), ws.numel(), 0, None))
+    torch.cuda.synchronize()
+    assert ob.workspace_status(ws) == 0
+    return y.cpu().numpy()
+
+
+CAPI_CASES = [(O.Q4_K, 1024, 2048, 1, 0), (O.Q6_K, 512, 1024, 3, 0), (O.Q4_K, 1000, 2048, 32, 3)]
+
+
+@pytest.mark.gpu
+def test_capi_sharded_one_rank_equals_plain_product(cuda_lib):
+    """A one-rank communicator: the sharded product is the plain product bit
+    for bit (the all-gather is in place; M > 1 goes through the unshard
+    kernel)."""
+    import ctypes
+
+    import torch
+
+    ob = cuda_lib
+    L = ob.lib()
+    uid = ctypes.create_string_buffer(128)
+    ob.check(L.odi_cuda_nccl_unique_id(uid))
+    comm = ctypes.c_void_p()
+    ob.check(L.odi_cuda_nccl_init(uid, 1, 0, ctypes.byref(comm)))
+    try:
+        n, r = ctypes.c_int(), ctypes.c_int()
+        ob.check(L.odi_cuda_comm_ranks(comm, ctypes.byref(n), ctypes.byref(r)))
+        assert (n.value, r.value) == (1, 0)
+        for dt, N, K, M, mode in CAPI_CASES:
+            b = O.quantize(dt, O.seeded_weights(N, K, seed=1))
+            w, S = _capi_shard_weight(ob, dt, b, N, K, 1, 0)
+            x = torch.from_numpy(O.seeded_acts(M, K, seed=2)).cuda()
+            y = _capi_product(ob, comm, dt, w, x, N, S, K, mode)
+            ref = torch.empty((M, N), device="cuda")
+            ob.matmul_dev(dt, w, x, ref, N, K, mode)
+            torch.cuda.synchronize()
+            assert np.array_equal(y.view(np.uint32), ref.cpu().numpy().view(np.uint32)), (dt, N, K, M)
+        # a split that does not cover N is refused
+        with pytest.raises(ob.OdiCudaError, match="does not split"):
+            ob.check(L.odi_cuda_matmul_sharded(comm, O.Q4_K, 16, 16, 16, 1, 1024, 512, 2048, 0, 16, 1 << 20, 0,
+                                               None))
+    finally:
+        ob.check(L.odi_cuda_nccl_free(comm))
+
+
+def _capi_worker(rank, world, uid_bytes, out_q):
+    import ctypes
+
+    import torch
+
+    torch.cuda.set_device(rank)
+    import odiengine_b200 as ob
+
+    ob.init(rank)
+    L = ob.lib()
+    uid = ctypes.create_string_buffer(bytes(uid_bytes), 128)
+    comm = ctypes.c_void_p()
+    ob.check(L.odi_cuda_nccl_init(uid, world, rank, ctypes.byref(comm)))
+    try:
+        res = []
+        for dt, N, K, M, mode in CAPI_CASES:
+            b = O.quantize(dt, O.seeded_weights(N, K, seed=1))
+            w, S = _capi_shard_weight(ob, dt, b, N, K, world, rank)
+            x = torch.from_numpy(O.seeded_acts(M, K, seed=2)).cuda()
+            res.append(_capi_product(ob, comm, dt, w, x, N, S, K, mode))
+        if rank == 0:
+            out_q.put(res)
+    finally:
+        ob.check(L.odi_cuda_nccl_free(comm))
+
+
+@pytest.mark.gpu
+def test_capi_sharded_two_gpus():
+    """Two processes, one GPU each, a communicator made from one rank's id:
+    every rank's gathered product lies within the oracle's bound (the shard's
+    work split differs from the whole weight's, so only the fp32 summation
+    order differs)."""
+    import ctypes
+
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import odiengine_b200 as ob
+
+    uid = ctypes.create_string_buffer(128)
+    ob.check(ob.lib().odi_cuda_nccl_unique_id(uid))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_capi_worker, args=(r, 2, uid.raw, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for (dt, N, K, M, mode), y in zip(CAPI_CASES, got):
+        b = O.quantize(dt, O.seeded_weights(N, K, seed=1))
+        xs = O.seeded_acts(M, K, seed=2)
+        if mode == 3 and M >= 9:
+            y16, bound = O.matmul_f16(dt, xs, b, N)
+            assert (np.abs(y.astype(np.float64) - y16) <= bound + 1e-30).all()
+        else:
+            yq, _, mag = O.matmul_q8act(dt, xs, b, N, with_mag=True)
+            bound = 2.0 * (K / 8 + 64) * 2.0 ** -24 * mag.astype(np.float64)
+            assert (np.abs(y.astype(np.float64) - yq) <= bound + 1e-30).all()
+
+
+@pytest.mark.gpu
+def test_capi_nccl_init_failure_injected():
+    """A communicator that cannot form (host-side injection,
+    ODI_CUDA_INJECT=nccl, in a child process) is reported as
+    ODI_CUDA_ERR_BACKEND_INIT_FAILED (odi_error_t 301), with nothing left
+    half-made."""
+    import subprocess
+    import sys
+
+    code = (
+        "import ctypes, sys; sys.path.insert(0, %r)\n"
+        "import odiengine_b200 as ob\n"
+        "L = ob.lib(); ob.init(0)\n"
+        "uid = ctypes.create_string_buffer(128); ob.check(L.odi_cuda_nccl_unique_id(uid))\n"
+        "c = ctypes.c_void_p(); rc = L.odi_cuda_nccl_init(uid, 1, 0, ctypes.byref(c))\n"
+        "print(rc, c.value, L.odi_cuda_last_error().decode())\n" % ROOT)
+    env = dict(os.environ, ODI_CUDA_INJECT="nccl")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    rc, ptr, msg = r.stdout.strip().split(" ", 2)
+    assert rc == "301" and ptr == "None" and "ODI_CUDA_INJECT=nccl" in msg

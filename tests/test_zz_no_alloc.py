@@ -68,10 +68,15 @@ def test_noalloc_matches_matmul_host_twice(cuda_lib, dt, N, K, M, mode):
         ref1 = _call(L.odi_cuda_matmul_host, ob, h, x1, N, mode)
         ref2 = _call(L.odi_cuda_matmul_host, ob, h, x2, N, mode)
         _call(L.odi_cuda_matmul_host_noalloc, ob, h, x2, N, mode)  # first call on the device: set-up
-        free0 = _free_bytes(L)
+        # Free device memory is device-wide, so another process (or this one's
+        # caching allocator) can move it; the library itself must take none:
+        # the reading after the two calls may not fall below the lowest of
+        # several readings taken before them.
+        free0 = min(_free_bytes(L) for _ in range(3))
         y1 = _call(L.odi_cuda_matmul_host_noalloc, ob, h, x1, N, mode)
         y2 = _call(L.odi_cuda_matmul_host_noalloc, ob, h, x2, N, mode)
-        assert _free_bytes(L) == free0, "the no-allocation entry point changed free device memory"
+        assert max(_free_bytes(L) for _ in range(3)) >= free0, \
+            "the no-allocation entry point took device memory"
         np.testing.assert_array_equal(y1, ref1)
         np.testing.assert_array_equal(y2, ref2)
         assert not np.array_equal(y1, y2)
