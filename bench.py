@@ -452,8 +452,8 @@ def run_ours(args, rank, world, local_rank):
                "h2d_bytes_per_step": SWEEPS * R * M * K * 4, "d2h_bytes_per_step": SWEEPS * R * M * N * 4,
                "steps": e2e_steps,
                "ms_per_step": round(el * 1e3, 4),
-               "call": "odi_cuda_matmul_host per weight, synchronous per call; pinned host x/y: x fetched by a kernel "
-                       "the GEMV overlaps, y stored by the GEMV into host memory"}
+               "call": "odi_cuda_matmul_host per weight, synchronous per call; pinned host x/y: x copied in, y "
+                       "stored by the GEMV into host memory, the error word read from mapped memory"}
         ref_y = ys[-1].cpu().numpy()
         _np.testing.assert_allclose(hy[-1].numpy(), ref_y, rtol=0, atol=0)
         for h in hw:
@@ -476,17 +476,23 @@ def run_ours(args, rank, world, local_rank):
     decode = None
     configs = None
     if world == 1 and (not args.no_decode or not args.no_configs):
-        del g_step, g_gemv
+        g_step = g_gemv = None  # release the graphs before the other legs allocate
         if not args.no_decode:
             decode = run_decode(args, local_rank)
         if not args.no_configs:
             configs = run_config_legs(args)
 
+    sharded = None
+    if world > 1 and not args.no_configs:
+        g_step = g_gemv = None  # graphs with collectives go before the next ones are made
+        sharded = run_sharded_70b(args, rank, world, local_rank)
+
     if rank == 0:
         # Full detail first, one JSON object per line; the headline comes last
         # and ends with compact summaries of the same numbers, so the end of
         # stdout carries them.
-        for aux in (ref_cfg1, decode and dict(aux="decode_7b", **decode), configs and dict(aux="configs", **configs)):
+        for aux in (ref_cfg1, decode and dict(aux="decode_7b", **decode), configs and dict(aux="configs", **configs),
+                    sharded and dict(aux="sharded_70b", **sharded)):
             if aux:
                 print(json.dumps(aux), flush=True)
         line = {
@@ -512,9 +518,11 @@ def run_ours(args, rank, world, local_rank):
                                  "cpu": decode["cpu_baseline"]["value"] if decode.get("cpu_baseline") else None}
         if configs:
             line["configs_frac"] = config_summary(configs)
+        if sharded:
+            line["sharded_70b_frac"] = {f"{r['N']}x{r['K']} M{r['M']}": [r["frac_gemv"], r["frac_nccl"], r.get("frac_fused")]
+                                        for r in sharded["rows"]}
         print(json.dumps(line), flush=True)
-    if world > 1 or (args.no_decode and args.no_configs):
-        del g_step, g_gemv
+    g_step = g_gemv = None
     if fused:
         torch.cuda.synchronize()
         st = ob.workspace_status(ws)
@@ -526,6 +534,154 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier(device_ids=[local_rank])
         sym.close()
     return 0
+
+
+SHARD_SHAPES = ((28672, 8192), (8192, 28672), (128256, 8192))  # the 70B shapes of the row-sharding config
+
+
+def run_sharded_70b(args, rank, world, local_rank, reps=10):
+    """The row-sharding configuration (strong scaling): each 70B-shaped Q4_K
+    weight split by output rows over the `world` ranks (S = N / world rows
+    each), at M = 1 and 32 tokens (ODI_CUDA_ACT_AUTO).  Per shape and token
+    count, device time per product (CUDA events around graph replays over a
+    ring of shard copies > 4 x L2, max over ranks) of
+      gemv   the rank's shard product alone;
+      nccl   the product through odi_cuda_matmul_sharded: shard product,
+             in-place ncclAllGather of the slices, layout of [M, N] (C ABI);
+      fused  (M = 1) the shard product storing its slice into every rank's
+             output over NVLink, then the bounded wait for all ranks.
+    GB/s counts the whole weight (all shards) + x + y per product; frac is
+    against world x the measured HBM copy bandwidth."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    import odiengine_b200 as ob
+    from odiengine_b200.sharded import SymmetricBuffer
+
+    L = ob.lib()
+    dev = torch.device("cuda", local_rank)
+    peak, _ = measured_peak()
+    dt = ob.ODI_DTYPE_Q4_K
+    uid = ctypes.create_string_buffer(ob.NCCL_ID_BYTES)
+    if rank == 0:
+        ob.check(L.odi_cuda_nccl_unique_id(uid))
+    box = [uid.raw if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    uid = ctypes.create_string_buffer(box[0], ob.NCCL_ID_BYTES)
+    comm = ctypes.c_void_p()
+    ob.check(L.odi_cuda_nccl_init(uid, world, rank, ctypes.byref(comm)))
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+    rows = []
+
+    def timed(body):
+        with torch.cuda.stream(stream):
+            body()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            body()
+        with torch.cuda.stream(stream):
+            g.replay()
+        stream.synchronize()
+        dist.barrier(device_ids=[local_rank])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        stream.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del g
+        return float(t.item())
+
+    try:
+        for N, K in SHARD_SHAPES:
+            S = N // world
+            R = max(2, -(-4 * L2_BYTES // ob.tiled_bytes(dt, S, K)))
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(100 + rank)
+            wf = torch.empty((S, K), dtype=torch.float32, device=dev).normal_(0.0, 0.02, generator=gen)
+            base = ob.repack(dt, ob.quantize_weight(dt, wf), S, K)
+            del wf
+            ring = [base] + [base.clone() for _ in range(R - 1)]
+            for M in (1, 32):
+                mode = ob.ACT_AUTO
+                gen.manual_seed(7)
+                xs = [torch.empty((M, K), dtype=torch.float32, device=dev).normal_(0.0, 1.0, generator=gen)
+                      for _ in range(R)]
+                ysh = torch.empty((M, S), dtype=torch.float32, device=dev)
+                yfull = torch.empty((M, N), dtype=torch.float32, device=dev)
+                wsg = ob.new_workspace(ob.workspace_bytes(dt, M, S, K, mode), dev)
+                wss = ob.new_workspace(L.odi_cuda_sharded_workspace_bytes(comm, dt, M, S, K, mode), dev)
+
+                def gemv():
+                    for r in range(R):
+                        ob.check(L.odi_cuda_matmul(dt, ring[r].data_ptr(), xs[r].data_ptr(), ysh.data_ptr(), M, S, K,
+                                                   mode, wsg.data_ptr(), wsg.numel(), ob.FLAG_PDL, sp))
+
+                def nccl():
+                    for r in range(R):
+                        ob.check(L.odi_cuda_matmul_sharded(comm, dt, ring[r].data_ptr(), xs[r].data_ptr(),
+                                                           yfull.data_ptr(), M, N, S, K, mode, wss.data_ptr(),
+                                                           wss.numel(), ob.FLAG_PDL, sp))
+
+                row = {"N": N, "K": K, "M": M, "S": S, "ring": R}
+                algo = ob.gguf_bytes(dt, N, K) + M * K * 4 + M * N * 4
+                for name, body in (("gemv", gemv), ("nccl", nccl)):
+                    us = timed(body) * 1e3 / (reps * R)
+                    row["us_" + name] = round(us, 2)
+                    row["frac_" + name] = round(algo / us / 1e3 / (world * peak), 4)
+                if M == 1:
+                    obytes = M * N * 4
+                    sym = SymmetricBuffer(256 + R * obytes)
+                    own = sym.ptrs[rank]
+                    inc = (ctypes.c_uint64 * world)(*([L.odi_cuda_scatter_signals(dt, M, S, K, ob.ACT_Q8)] * world))
+                    scs = []
+                    for r in range(R):
+                        sc = ob.Scatter()
+                        for p in range(world):
+                            sc.out[p] = sym.ptrs[p] + 256 + r * obytes
+                            sc.counters[p] = sym.ptrs[p]
+                        sc.nranks, sc.rank, sc.row0, sc.ld = world, rank, rank * S, N
+                        scs.append(sc)
+                    wsf = ob.new_workspace(ob.workspace_bytes(dt, M, S, K, ob.ACT_Q8), dev)
+
+                    def fused():
+                        for r in range(R):
+                            ob.check(L.odi_cuda_matmul_scatter(dt, ring[r].data_ptr(), xs[r].data_ptr(), M, S, K,
+                                                               ob.ACT_Q8, wsf.data_ptr(), wsf.numel(), ob.FLAG_PDL,
+                                                               ctypes.byref(scs[r]), sp))
+                            ob.check(L.odi_cuda_wait_peers(own, own + 64, inc, world, wsf.data_ptr(), sp))
+
+                    us = timed(fused) * 1e3 / (reps * R)
+                    row["us_fused"] = round(us, 2)
+                    row["frac_fused"] = round(algo / us / 1e3 / (world * peak), 4)
+                    torch.cuda.synchronize()
+                    st = ob.workspace_status(wsf)
+                    dist.barrier(device_ids=[local_rank])
+                    sym.close()
+                    if st:
+                        raise RuntimeError(f"peer wait gave up (error word {st:#x})")
+                for k in ("gemv", "nccl", "fused"):
+                    if "us_" + k in row:
+                        row["GBs_" + k] = round(algo / row["us_" + k] / 1e3, 1)
+                rows.append(row)
+            del ring, base
+            torch.cuda.empty_cache()
+    finally:
+        torch.cuda.synchronize()
+        ob.check(L.odi_cuda_nccl_free(comm))
+    return {"metric": "Q4_K GEMV HBM GB/s, 70B shapes split by rows over the GPUs (strong scaling)",
+            "n_gpus": world, "rows": rows, "peak_per_gpu": peak,
+            "method": "CUDA events around CUDA-graph replays (PDL) over a ring of shard copies > 4 x L2, max over "
+                      "ranks; gemv = the shard product alone, nccl = odi_cuda_matmul_sharded (product + in-place "
+                      "ncclAllGather + [M, N] layout), fused = the product's epilogue storing to every rank over "
+                      "NVLink + the bounded wait"}
 
 
 def time_products(dt, N, K, M, act_mode, reps=20, seed=0, dev=None):
@@ -639,13 +795,15 @@ def run_decode(args, local_rank):
     """7B-shape decode (Llama-2-7B shape: 32 layers, hidden 4096, 32 heads of
     128, ffn 11008, vocab 32000; Q4_K attention and gate/up, Q6_K down and
     output, seeded N(0, 0.02) weights quantised on the device; fp16 KV
-    cache).  The KV cache is filled from 2048 seeded random prompt tokens,
-    then DEC_GEN greedy steps are timed: each step is one replay of the
-    captured decode graph (embed .. argmax, token and position advanced on
-    the device)."""
+    cache), driven by the library's own decoder (odi_cuda_decoder_*, the
+    C-ABI path a C++ engine calls): the KV cache is filled from 2048 seeded
+    random prompt tokens, then DEC_GEN greedy steps are timed on the device
+    (CUDA events around the graph replays, inside the library).  The Python
+    DecodeModel runs the same steps on the same weights as a cross-check of
+    the tokens."""
     import torch
 
-    from odiengine_b200.decode import DecodeModel, LlamaConfig, seeded_model
+    from odiengine_b200.decode import CDecoder, DecodeModel, LlamaConfig, seeded_model
 
     dev = torch.device("cuda", local_rank)
     P, G = args.decode_prompt, args.decode_gen
@@ -654,46 +812,50 @@ def run_decode(args, local_rank):
     mw = seeded_model(cfg, seed=0, device=dev)
     torch.cuda.synchronize()
     t_build = time.perf_counter() - t0
-    dm = DecodeModel(cfg, mw, device=dev)
-    dm.reset(1, 0)
-    dm.generate(1)  # one eager step (kernel attributes), then the graph
-    dm.clear_cache()
-    dm.reset(1, 0)
-    dm.capture()
+    cd = CDecoder(cfg, mw, max_record=G + 16)
     gen = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (P,), generator=gen).tolist()
-    dm.clear_cache()
     t0 = time.perf_counter()
-    dm.prefill(prompt)
+    cd.reset(prompt[0], 0, clear_cache=True)
+    cd.prefill(prompt[:-1])
     t_prefill = time.perf_counter() - t0
 
     def from_prompt_end():
-        # the last prompt token again at its own position: its argmax is the
-        # first generated token
-        dm.reset(prompt[-1], P - 1)
-        dm.stream.synchronize()
+        # the last prompt token at its own position: its argmax is the first
+        # generated token
+        cd.reset(prompt[-1], P - 1)
 
     from_prompt_end()
-    dm.generate(max(3, args.warmup))
+    cd.generate(max(3, args.warmup))  # warm-up steps
     from_prompt_end()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
         clk.wait_first_sample()
-        e0.record(dm.stream)
-        with torch.cuda.stream(dm.stream):
-            for _ in range(G):
-                dm.graph.replay()
-        e1.record(dm.stream)
-        dm.stream.synchronize()
-    ms_tok = e0.elapsed_time(e1) / G
-    toks = dm.record[:G].cpu().tolist()
-    # end to end: the same G steps through DecodeModel.generate (host call,
-    # graph replays, the G tokens read back to the host), wall clock
+        ms = cd.time(G)
+    ms_tok = ms / G
+    toks = cd.tokens(0, G)
+    # end to end: the same G steps through odi_cuda_decoder_generate (one
+    # host call: the replays, the G tokens read back, the error words
+    # checked), wall clock
     from_prompt_end()
     t0 = time.perf_counter()
-    toks2 = dm.generate(G)
+    toks2 = cd.generate(G)
     el = time.perf_counter() - t0
     assert toks2 == toks, "decode is not deterministic"
+    launches = cd.launches_per_step()
+    cd.free()
+    # cross-check: the Python-driven DecodeModel on the same weights
+    dm = DecodeModel(cfg, mw, device=dev)
+    dm.reset(1, 0)
+    dm.generate(1)
+    dm.clear_cache()
+    dm.reset(1, 0)
+    dm.capture()
+    dm.clear_cache()
+    dm.prefill(prompt[:-1])
+    dm.reset(prompt[-1], P - 1)
+    toks_py = dm.generate(G)
+    same = toks_py == toks
+    del dm
     wb = cfg.weight_bytes()
     kvb = cfg.kv_bytes(P + G // 2)  # mean cache length read per step
     bytes_tok = wb + kvb
@@ -702,6 +864,7 @@ def run_decode(args, local_rank):
     res = {
         "metric": "7B-shape Q4_K decode tokens/s (1 sequence, greedy)", "value": round(1e3 / ms_tok, 2),
         "unit": "tokens/s", "ms_per_token": round(ms_tok, 4), "higher_is_better": True,
+        "path": "odi_cuda_decoder (the library's decode step, captured once and replayed per token from C++)",
         "config": {"workload": f"Llama-2-7B-shape decode, {P} prompt tokens in the fp16 KV cache, then {G} greedy "
                                "steps", "layers": cfg.layers, "hidden": cfg.hidden, "heads": cfg.heads,
                    "head_dim": cfg.head_dim, "ffn": cfg.ffn, "vocab": cfg.vocab,
@@ -712,19 +875,20 @@ def run_decode(args, local_rank):
                      "weight_bytes": wb, "kv_bytes_mean": kvb, "peak_kind": peak_kind},
         "e2e": {"value": round(G / el, 2), "unit": "tokens/s", "h2d_bytes_per_step": round(16 / G, 4),
                 "d2h_bytes_per_step": 4,
-                "call": "DecodeModel.generate from the prompt's end (16-byte state written once, graph replays, "
-                        "the tokens read back at the end)"},
-        "gpu_launches_per_token": dm.launches_per_step(),
+                "call": "odi_cuda_decoder_generate from the prompt's end (16-byte state written once, graph replays, "
+                        "the tokens read back and the error words checked at the end)"},
+        "python_path_same_tokens": same,
+        "gpu_launches_per_token": launches,
         "prefill_s": round(t_prefill, 2), "build_s": round(t_build, 2),
         "first_tokens": toks[:8], "clocks": clk.summary(),
         "cpu_baseline": None,
     }
     if not args.no_cpu:
-        nth = os.cpu_count() or 1
+        nth = host_threads()
         t_cpu, sample = cpu_decode_sample(nth)
         res["cpu_baseline"] = {"value": round(1.0 / t_cpu, 4), "unit": "tokens/s", "cores": nth, "kind": "port",
                                "sample": sample}
-    del dm, mw
+    del mw
     torch.cuda.synchronize()
     return res
 

@@ -269,10 +269,9 @@ int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t 
  * (context.cpp:152, 188-190): h_x [M, K] and h_y [M, N] are host memory;
  * the call brings x in, runs the product on the weight's device copy,
  * brings y out and waits.  Uses a library-owned per-device workspace.
- * Page-locked buffers (cudaHostAlloc / cudaHostRegister) are reached from
- * the device directly -- x fetched by a kernel the product overlaps, y
- * stored by the product itself -- which saves the two copies' latency;
- * pageable buffers go through cudaMemcpyAsync.
+ * x goes in with cudaMemcpyAsync; a page-locked h_y (cudaHostAlloc /
+ * cudaHostRegister) is written by the product itself, saving a copy's
+ * latency (the tensor-core path and pageable buffers copy y out).
  * Returns ODI_CUDA_ERR_OPERATION_FAILED (h_y not to be used) when a kernel's
  * bounded wait gave up, as cpu_backend.cpp:177-227 throws on failure. */
 int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
@@ -364,6 +363,70 @@ int odi_cuda_add(float* d_x, const float* d_d, int64_t n, void* stream);
  * step and pos. */
 int odi_cuda_argmax(const float* d_logits, int64_t V, odi_cuda_decode_state* d_state, int32_t* d_record,
                     int record_len, void* stream);
+
+/* --- the decode step as one call per token ----------------------------------
+ * A device-resident decoder of a Llama-shaped model: one token's forward
+ * pass (context.cpp:84-282 for a single token, with cpu_backend.cpp:388-619's
+ * element-wise ops on the device) captured once as a CUDA graph and replayed
+ * per token; the token and position stay on the device and the greedy
+ * argmax advances them.  For a C++ engine that calls it once per token
+ * instead of one Backend call per operation. */
+typedef struct odi_cuda_decoder_config {
+  int layers, hidden, heads, kv_heads, head_dim, ffn, vocab;
+  int ctx;          /* KV cache positions */
+  float eps;        /* RMSNorm epsilon */
+  float theta;      /* RoPE base */
+  int attn_dtype;   /* Q|K|V, O and gate|up weights */
+  int down_dtype;   /* down and output weights */
+} odi_cuda_decoder_config;
+
+/* One layer's device weights, tiled (odi_cuda_weight_data / odi_cuda_repack):
+ * wqkv has (heads + 2 kv_heads) * head_dim rows, Q, K and V stacked; wgu
+ * has 2 * ffn rows, gate and up interleaved 32 rows each per 64-row tile
+ * (row p is gate row 32t + p % 64 when p % 64 < 32, else up row
+ * 32t + p % 64 - 32, t = p / 64).  Norm weights fp32 [hidden]. */
+typedef struct odi_cuda_decoder_layer {
+  const float* attn_norm;
+  const void* wqkv;
+  const void* wo;
+  const float* ffn_norm;
+  const void* wgu;
+  const void* wdown;
+} odi_cuda_decoder_layer;
+
+typedef struct odi_cuda_decoder odi_cuda_decoder;
+
+/* Builds the decoder on the current device: its buffers (fp16 KV cache of
+ * layers * kv_heads * ctx * head_dim per K and V, activations, Q8 records),
+ * one eager step, then the captured step.  The weights stay the caller's
+ * and must outlive the decoder.  token_embd fp32 [vocab][hidden]; output
+ * [vocab rows x hidden]; max_record: tokens the device record holds
+ * between resets.  hidden, ffn and heads * head_dim multiples of 256. */
+int odi_cuda_decoder_create(const odi_cuda_decoder_config* cfg, const float* d_token_embd,
+                            const odi_cuda_decoder_layer* layers, const float* d_out_norm, const void* d_output,
+                            int max_record, odi_cuda_decoder** decoder);
+int odi_cuda_decoder_free(odi_cuda_decoder* decoder);
+/* Next step reads `token` at position `pos`; the record restarts; with
+ * clear_cache the KV cache is zeroed (a new sequence). */
+int odi_cuda_decoder_reset(odi_cuda_decoder* decoder, int token, int pos, int clear_cache);
+/* The prompt into the cache: one step per token at positions pos0.. */
+int odi_cuda_decoder_prefill(odi_cuda_decoder* decoder, const int32_t* tokens, int n, int pos0);
+/* n greedy steps from the current state; out_tokens receives them.  Fails
+ * with ODI_CUDA_ERR_OPERATION_FAILED if a bounded device wait gave up. */
+int odi_cuda_decoder_generate(odi_cuda_decoder* decoder, int n, int32_t* out_tokens);
+/* n greedy steps timed on the device (CUDA events around the replays). */
+int odi_cuda_decoder_time(odi_cuda_decoder* decoder, int n, float* ms);
+/* Tokens [start, start + n) of the device record since the last reset. */
+int odi_cuda_decoder_tokens(odi_cuda_decoder* decoder, int start, int n, int32_t* out_tokens);
+/* The last step's logits, vocab fp32 values. */
+int odi_cuda_decoder_logits(odi_cuda_decoder* decoder, float* out);
+/* Kernel launches in one step. */
+int odi_cuda_decoder_launches_per_step(const odi_cuda_decoder* decoder);
+
+/* A plain device copy of host bytes (norm weights, embedding tables) and its
+ * release. */
+int odi_cuda_buffer_upload(const void* host, size_t bytes, void** d_ptr);
+int odi_cuda_buffer_free(void* d_ptr);
 
 /* --- row-sharded product with the all-gather fused into the GEMV ------------ */
 

@@ -98,6 +98,17 @@ SIGNATURES = {
     "odi_cuda_matmul_scatter": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp, _vp]),
     "odi_cuda_wait_peers": (_int, [_vp, _vp, _vp, _int, _vp, _vp]),
     "odi_cuda_wait_peers_timeout": (_int, [_vp, _vp, _vp, _int, ctypes.c_uint64, _vp, _vp]),
+    "odi_cuda_decoder_create": (_int, [_vp, _vp, _vp, _vp, _vp, _int, ctypes.POINTER(_vp)]),
+    "odi_cuda_decoder_free": (_int, [_vp]),
+    "odi_cuda_decoder_reset": (_int, [_vp, _int, _int, _int]),
+    "odi_cuda_decoder_prefill": (_int, [_vp, _vp, _int, _int]),
+    "odi_cuda_decoder_generate": (_int, [_vp, _int, _vp]),
+    "odi_cuda_decoder_time": (_int, [_vp, _int, ctypes.POINTER(ctypes.c_float)]),
+    "odi_cuda_decoder_tokens": (_int, [_vp, _int, _int, _vp]),
+    "odi_cuda_decoder_logits": (_int, [_vp, _vp]),
+    "odi_cuda_decoder_launches_per_step": (_int, [_vp]),
+    "odi_cuda_buffer_upload": (_int, [_vp, _sz, ctypes.POINTER(_vp)]),
+    "odi_cuda_buffer_free": (_int, [_vp]),
     "odi_cuda_nccl_unique_id": (_int, [_vp]),
     "odi_cuda_nccl_init": (_int, [_vp, _int, _int, ctypes.POINTER(_vp)]),
     "odi_cuda_nccl_free": (_int, [_vp]),
@@ -115,6 +126,7 @@ SIGNATURES = {
 NOALLOC_SCRATCH_BYTES = 8 << 20
 
 MAX_PEERS = 8  # ODI_CUDA_MAX_PEERS
+NCCL_ID_BYTES = 128  # ODI_CUDA_NCCL_ID_BYTES
 IPC_HANDLE_BYTES = 64  # ODI_CUDA_IPC_HANDLE_BYTES
 
 

@@ -238,37 +238,3 @@ cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* til
 
 }  // namespace odi_cuda
 
-namespace odi_cuda {
-
-// Host-buffer fetch: n fp32 values from page-locked host memory (a device
-// address of it, reached over PCIe) into device memory, 16 bytes per thread
-// where both ends allow.  It releases its dependents at once, so a product
-// launched after it with programmatic dependent launch streams its weights
-// while the values cross the bus; that product's griddepcontrol.wait then
-// orders its activation loads after this kernel.
-__global__ void fetch_host_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t n) {
-  pdl_launch_dependents();
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
-  if (vec) {
-    const int64_t n4 = n >> 2;
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    float4* d4 = reinterpret_cast<float4*>(dst);
-    for (int64_t i = t0; i < n4; i += stride) d4[i] = s4[i];
-    for (int64_t i = 4 * n4 + t0; i < n; i += stride) dst[i] = src[i];
-  } else {
-    for (int64_t i = t0; i < n; i += stride) dst[i] = src[i];
-  }
-}
-
-cudaError_t launch_fetch_host(const float* src, float* dst, int64_t n, cudaStream_t s) {
-  if (n <= 0) return cudaSuccess;
-  int64_t blocks = (n / 4 + 255) / 256;
-  if (blocks < 1) blocks = 1;
-  if (blocks > 1184) blocks = 1184;  // eight per SM: the PCIe round trips, not the SMs, set the pace
-  fetch_host_kernel<<<(unsigned)blocks, 256, 0, s>>>(src, dst, n);
-  return cudaGetLastError();
-}
-
-}  // namespace odi_cuda

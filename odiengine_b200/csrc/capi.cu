@@ -29,6 +29,12 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+}  // namespace
+
+int odi_cuda::set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char* what) {
   const int code = (e == cudaErrorMemoryAllocation) ? ODI_CUDA_ERR_GPU_OUT_OF_MEMORY
                                                     : ODI_CUDA_ERR_OPERATION_FAILED;
@@ -724,6 +730,25 @@ int odi_cuda_sym_alloc(size_t bytes, void** d_ptr, void* ipc_handle) {
   return ODI_CUDA_OK;
 }
 
+int odi_cuda_buffer_upload(const void* host, size_t bytes, void** d_ptr) {
+  if (!host || !d_ptr || bytes == 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  *d_ptr = nullptr;
+  void* p = nullptr;
+  CK(dev_malloc(&p, bytes), "cudaMalloc (buffer)");
+  cudaError_t e = cudaMemcpy(p, host, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "buffer upload");
+  }
+  *d_ptr = p;
+  return ODI_CUDA_OK;
+}
+
+int odi_cuda_buffer_free(void* d_ptr) {
+  if (d_ptr) CK(cudaFree(d_ptr), "cudaFree (buffer)");
+  return ODI_CUDA_OK;
+}
+
 int odi_cuda_sym_free(void* d_ptr) {
   if (d_ptr) CK(cudaFree(d_ptr), "cudaFree (symmetric buffer)");
   return ODI_CUDA_OK;
@@ -848,6 +873,8 @@ namespace {
 struct Arena {
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  int* ws_host = nullptr;      // page-locked error-word workspace (WS_HEADER bytes)
+  int* ws_host_dev = nullptr;  // its device address
   float* x = nullptr;
   size_t x_bytes = 0;
   float* y = nullptr;
@@ -906,35 +933,52 @@ extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, 
   if (!w || !h_x || !h_y) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
   if (M < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M");
   if (M == 0) return ODI_CUDA_OK;
+  const int mode = resolve_act_mode(w->dtype, M, act_mode);
+  if (mode < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "unknown act_mode %d", act_mode);
   int dev = 0;
   CK(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev != w->device) return fail(ODI_CUDA_ERR_INVALID_STATE, "weight lives on device %d, current is %d", w->device, dev);
   std::lock_guard<std::mutex> lk(g_arena_mu);
   Arena& A = g_arena[dev & 63];
-  const size_t wsb = odi_cuda_matmul_workspace_bytes(w->dtype, M, w->N, w->K, act_mode);
+  const size_t wsb = odi_cuda_matmul_workspace_bytes(w->dtype, M, w->N, w->K, mode);
   CK(grow(&A.ws, &A.ws_bytes, wsb, true), "workspace alloc");
   CK(grow((void**)&A.x, &A.x_bytes, (size_t)(M * w->K) * sizeof(float), false), "x alloc");
-  CK(grow((void**)&A.y, &A.y_bytes, (size_t)(M * w->N) * sizeof(float), false), "y alloc");
   cudaStream_t s = (cudaStream_t)stream;
-  // Page-locked host buffers are reached from the device directly: x is
-  // fetched by a small kernel that the product follows with programmatic
-  // dependent launch (the product streams its weights meanwhile), and the
-  // product stores y straight into host memory.  Pageable buffers take the
-  // copy engines.
-  const float* dx = device_view(h_x);
-  float* dy = device_view(h_y);
-  const int mode = resolve_act_mode(w->dtype, M, act_mode);
-  if (mode == ODI_CUDA_ACT_F16) dy = nullptr;  // the tensor-core epilogue writes device memory only
-  const bool pdl = dx != nullptr;
-  if (dx)
-    CK(launch_fetch_host(dx, A.x, M * w->K, s), "fetch x");
-  else
-    CK(cudaMemcpyAsync(A.x, h_x, (size_t)(M * w->K) * sizeof(float), cudaMemcpyHostToDevice, s), "H2D x");
-  int rc = odi_cuda_matmul(w->dtype, w->data, A.x, dy ? dy : A.y, M, w->N, w->K, act_mode, A.ws, A.ws_bytes,
-                           pdl ? ODI_CUDA_FLAG_PDL : 0, stream);
+  // A workspace that is only the error word (one-token and fp32 products on
+  // the streaming GEMV) lives in page-locked host memory the device writes
+  // through, so the host reads the word after the sync without a copy.
+  int* werr = nullptr;
+  if (wsb <= WS_HEADER) {
+    if (!A.ws_host) {
+      void* p = nullptr;
+      if (injected() & INJ_ALLOC) return cuda_fail(cudaErrorMemoryAllocation, "cudaHostAlloc (error word)");
+      CK(cudaHostAlloc(&p, WS_HEADER, cudaHostAllocMapped), "cudaHostAlloc (error word)");
+      memset(p, 0, WS_HEADER);
+      A.ws_host = static_cast<int*>(p);
+      CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&A.ws_host_dev), p, 0), "error word device address");
+    }
+    werr = A.ws_host;
+  }
+  // y: a page-locked h_y is written by the product itself (its epilogue
+  // stores reach host memory directly), saving a copy's latency; the
+  // tensor-core path, and pageable buffers, go through the device buffer.
+  float* dy = mode == ODI_CUDA_ACT_F16 ? nullptr : device_view(h_y);
+  if (!dy) CK(grow((void**)&A.y, &A.y_bytes, (size_t)(M * w->N) * sizeof(float), false), "y alloc");
+  CK(cudaMemcpyAsync(A.x, h_x, (size_t)(M * w->K) * sizeof(float), cudaMemcpyHostToDevice, s), "H2D x");
+  int rc = odi_cuda_matmul(w->dtype, w->data, A.x, dy ? dy : A.y, M, w->N, w->K, mode,
+                           werr ? static_cast<void*>(A.ws_host_dev) : A.ws, werr ? (size_t)WS_HEADER : A.ws_bytes, 0,
+                           stream);
   if (rc) return rc;
   if (!dy) CK(cudaMemcpyAsync(h_y, A.y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
-  return finish_host_call(A, s);
+  if (!werr) return finish_host_call(A, s);
+  CK(cudaStreamSynchronize(s), "sync");
+  if (injected() & INJ_WAIT) *werr = ERR_FULL_WAIT;
+  const int err = *reinterpret_cast<volatile int*>(werr);
+  if (err) {
+    *werr = 0;
+    return fail(ODI_CUDA_ERR_OPERATION_FAILED, "a kernel wait gave up (error word 0x%x); the output is invalid", err);
+  }
+  return ODI_CUDA_OK;
 }
 
 extern "C" int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* stream) {

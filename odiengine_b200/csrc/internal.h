@@ -14,9 +14,6 @@ cudaError_t launch_act_records_fused(const float* x, int64_t ldx, int64_t M, int
                                     uint8_t* recs, bool pdl, cudaStream_t stream);
 cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* tiles, bool pdl,
                                 cudaStream_t stream);
-// n fp32 values from page-locked host memory (its device address) to device
-// memory; releases programmatic dependents at once.
-cudaError_t launch_fetch_host(const float* src, float* dst, int64_t n, cudaStream_t s);
 cudaError_t launch_repack(int dt, const void* gguf, void* tiled, int64_t N, int64_t K, cudaStream_t s);
 cudaError_t launch_unpack(int dt, const void* tiled, void* gguf, int64_t N, int64_t K, cudaStream_t s);
 cudaError_t launch_dequant(int dt, const void* tiled, float* out, int64_t N, int64_t K, cudaStream_t s);
@@ -112,6 +109,9 @@ struct PeerWait {
 constexpr unsigned long long PEER_WAIT_DEFAULT_NS = 1000000000ull;  // one second
 cudaError_t launch_wait_peers(const unsigned long long* cnt, unsigned long long* consumed, const PeerWait& w,
                               int* err, cudaStream_t s);
+
+// The C ABI's error record (capi.cu): sets the thread's message, returns code.
+int set_error(int code, const char* msg);
 
 // NCCL, opened at run time (shard.cu).  Each returns 0, or -1 with *why set.
 bool nccl_available();

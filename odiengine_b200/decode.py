@@ -501,3 +501,83 @@ class DecodeModel:
             self._run()
         self._check_status()
         return self.record[start:start + n].cpu().tolist()
+
+
+class DecoderConfig(ctypes.Structure):
+    """odi_cuda_decoder_config (include/odi_cuda.h)."""
+
+    _fields_ = [(n, ctypes.c_int) for n in ("layers", "hidden", "heads", "kv_heads", "head_dim", "ffn", "vocab",
+                                             "ctx")] + [("eps", ctypes.c_float), ("theta", ctypes.c_float),
+                                                        ("attn_dtype", ctypes.c_int), ("down_dtype", ctypes.c_int)]
+
+
+class DecoderLayer(ctypes.Structure):
+    """odi_cuda_decoder_layer (include/odi_cuda.h)."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("attn_norm", "wqkv", "wo", "ffn_norm", "wgu", "wdown")]
+
+
+class CDecoder:
+    """The decode step driven by the library itself (odi_cuda_decoder_*):
+    the same step as DecodeModel's epilogue mode, captured and replayed by
+    the C ABI, the way a C++ engine calls it -- one call per batch of tokens,
+    no Python per step.  The weights stay ``weights``' device tensors (with
+    gate|up interleaved)."""
+
+    def __init__(self, cfg: LlamaConfig, weights: ModelWeights, max_record: int = 4096):
+        if not weights.gu_interleaved:
+            raise ValueError("the library's decoder needs gate|up interleaved (seeded_model / load_llama default)")
+        self.cfg, self.w = cfg, weights
+        c = DecoderConfig(cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab, cfg.ctx,
+                          cfg.eps, cfg.theta, cfg.attn_dtype, cfg.down_dtype)
+        layers = (DecoderLayer * cfg.layers)(*[
+            DecoderLayer(_ptr(lw.attn_norm), lw.wqkv.data_ptr, lw.wo.data_ptr, _ptr(lw.ffn_norm), lw.wgu.data_ptr,
+                         lw.wdown.data_ptr) for lw in weights.layers])
+        h = ctypes.c_void_p()
+        check(lib().odi_cuda_decoder_create(ctypes.byref(c), _ptr(weights.token_embd), layers, _ptr(weights.out_norm),
+                                            weights.output.data_ptr, max_record, ctypes.byref(h)))
+        self.h = h
+
+    def reset(self, token: int, pos: int = 0, clear_cache: bool = False) -> None:
+        check(lib().odi_cuda_decoder_reset(self.h, token, pos, 1 if clear_cache else 0))
+
+    def prefill(self, tokens, pos0: int = 0) -> None:
+        arr = (ctypes.c_int32 * len(tokens))(*tokens)
+        check(lib().odi_cuda_decoder_prefill(self.h, arr, len(tokens), pos0))
+
+    def generate(self, n: int) -> list:
+        out = (ctypes.c_int32 * n)()
+        check(lib().odi_cuda_decoder_generate(self.h, n, out))
+        return list(out)
+
+    def time(self, n: int) -> float:
+        """Milliseconds of n greedy steps on the device (CUDA events)."""
+        ms = ctypes.c_float()
+        check(lib().odi_cuda_decoder_time(self.h, n, ctypes.byref(ms)))
+        return ms.value
+
+    def tokens(self, start: int, n: int) -> list:
+        out = (ctypes.c_int32 * n)()
+        check(lib().odi_cuda_decoder_tokens(self.h, start, n, out))
+        return list(out)
+
+    def logits(self):
+        import numpy as np
+
+        v = np.zeros(self.cfg.vocab, np.float32)
+        check(lib().odi_cuda_decoder_logits(self.h, v.ctypes.data))
+        return v
+
+    def launches_per_step(self) -> int:
+        return int(lib().odi_cuda_decoder_launches_per_step(self.h))
+
+    def free(self) -> None:
+        if getattr(self, "h", None):
+            check(lib().odi_cuda_decoder_free(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

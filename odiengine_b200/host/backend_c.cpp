@@ -7,6 +7,7 @@
 //
 // Every function catches what the backend throws and returns 1 with the
 // message in odi_be_last_error(); 0 on success.
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <exception>
@@ -192,6 +193,78 @@ int odi_be_upload_model(void* be, void* f, int64_t* n_uploaded) {
 int64_t odi_be_cached_weights(void* be) {
   auto* c = dynamic_cast<odi::CUDABackend*>(static_cast<odi::Backend*>(be));
   return c ? (int64_t)c->cached_weights() : -1;
+}
+
+// The decode step of a GGUF Llama model (CUDABackend::create_decoder):
+// NULL on failure (message in odi_be_last_error).
+void* odi_be_decoder_from_gguf(void* be, void* file, int ctx, int max_record) {
+  try {
+    auto* cb = dynamic_cast<odi::CUDABackend*>(static_cast<odi::Backend*>(be));
+    if (!cb) {
+      t_err = "not a CUDA backend";
+      return nullptr;
+    }
+    return cb->create_decoder(*static_cast<odi::GGUFFile*>(file), ctx, max_record).release();
+  } catch (const std::exception& e) {
+    caught(e.what());
+  }
+  return nullptr;
+}
+
+void odi_be_decoder_free(void* dec) { delete static_cast<odi::CudaDecoder*>(dec); }
+
+int odi_be_decoder_reset(void* dec, int token, int pos, int clear_cache) {
+  try {
+    static_cast<odi::CudaDecoder*>(dec)->reset(token, pos, clear_cache != 0);
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_decoder_prefill(void* dec, const int32_t* tokens, int n, int pos0) {
+  try {
+    static_cast<odi::CudaDecoder*>(dec)->prefill(std::vector<int32_t>(tokens, tokens + n), pos0);
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_decoder_generate(void* dec, int n, int32_t* out) {
+  try {
+    const std::vector<int32_t> t = static_cast<odi::CudaDecoder*>(dec)->generate(n);
+    std::copy(t.begin(), t.end(), out);
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_decoder_time(void* dec, int n, float* ms) {
+  try {
+    *ms = static_cast<odi::CudaDecoder*>(dec)->time_steps(n);
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_decoder_logits(void* dec, float* out) {
+  try {
+    const std::vector<float> v = static_cast<odi::CudaDecoder*>(dec)->logits();
+    std::copy(v.begin(), v.end(), out);
+    return 0;
+  } catch (const std::exception& e) {
+    return caught(e.what());
+  }
+}
+
+int odi_be_decoder_config(void* dec, int* fields /* layers hidden heads kv_heads head_dim ffn vocab ctx */) {
+  const odi_cuda_decoder_config& c = static_cast<odi::CudaDecoder*>(dec)->config();
+  const int v[8] = {c.layers, c.hidden, c.heads, c.kv_heads, c.head_dim, c.ffn, c.vocab, c.ctx};
+  std::copy(v, v + 8, fields);
+  return 0;
 }
 
 }  // extern "C"

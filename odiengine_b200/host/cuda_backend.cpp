@@ -151,6 +151,11 @@ size_t CUDABackend::upload_model(const GGUFFile& file) {
   return n;
 }
 
+std::unique_ptr<CudaDecoder> CUDABackend::create_decoder(const GGUFFile& file, int ctx, int max_record) {
+  bind_device();
+  return CudaDecoder::from_gguf(file, ctx, max_record);
+}
+
 void CUDABackend::release_weights() {
   std::lock_guard<std::mutex> lk(mu_);
   int first_rc = ODI_CUDA_OK;

@@ -34,6 +34,7 @@
 #include <tuple>
 
 #include "compute/cpu/cpu_backend.hpp"
+#include "cuda_decoder.hpp"
 #include "odi_cuda.h"
 
 namespace odi {
@@ -85,6 +86,11 @@ class CUDABackend : public CPUBackend {
   // uploaded by this call; throws std::runtime_error if an upload fails.
   // The file must outlive the backend's use of its weights.
   size_t upload_model(const GGUFFile& file);
+
+  // The whole decode step on the device for the Llama model of `file`
+  // (cuda_decoder.hpp): one call per token for a Context::forward that hands
+  // the step to the backend.  ctx: KV-cache positions (0: the file's).
+  std::unique_ptr<CudaDecoder> create_decoder(const GGUFFile& file, int ctx = 0, int max_record = 4096);
 
   // Drops every cached device copy of a weight.  Call it when a model is
   // unloaded: a later tensor at a reused mmap address is recognised by a

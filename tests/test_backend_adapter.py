@@ -45,6 +45,14 @@ FACADE = {
     "odi_be_factory_error": (_int, []),
     "odi_be_factory_message": (ctypes.c_char_p, []),
     "odi_be_cuda_available": (_int, []),
+    "odi_be_decoder_from_gguf": (_vp, [_vp, _vp, _int, _int]),
+    "odi_be_decoder_free": (None, [_vp]),
+    "odi_be_decoder_reset": (_int, [_vp, _int, _int, _int]),
+    "odi_be_decoder_prefill": (_int, [_vp, _vp, _int, _int]),
+    "odi_be_decoder_generate": (_int, [_vp, _int, _vp]),
+    "odi_be_decoder_time": (_int, [_vp, _int, ctypes.POINTER(ctypes.c_float)]),
+    "odi_be_decoder_logits": (_int, [_vp, _vp]),
+    "odi_be_decoder_config": (_int, [_vp, _vp]),
 }
 ODI_ERROR_BACKEND_UNAVAILABLE = 300
 Q8_K = 15  # odi_dtype_t (include/odi/odi_types.h): a block type the CUDA library does not compute

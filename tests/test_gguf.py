@@ -249,3 +249,55 @@ def test_upload_model_hook(cuda_lib, tiny_file):
     finally:
         be.close()
         L.odi_be_gguf_close(f)
+
+
+@pytest.mark.gpu
+def test_cpp_decoder_from_gguf_matches_decode_model(cuda_lib, tiny_file):
+    """CUDABackend::create_decoder on the reference's GGUFFile (Q|K|V stacked
+    and gate|up interleaved on the host, each uploaded once; the decode step
+    driven from C++, one graph replay per token) gives DecodeModel's tokens
+    and logits on the same file bit for bit: same kernels, same order, same
+    weight layout."""
+    from odiengine_b200 import gguf
+    from odiengine_b200.decode import DecodeModel
+
+    need_adapter()
+    cfg, host, path = tiny_file
+    L = Backend.lib()
+    f = L.odi_be_gguf_open(path.encode())
+    assert f, L.odi_be_last_error()
+    be = Backend(BACKEND_CUDA)
+    dec = None
+    try:
+        dec = L.odi_be_decoder_from_gguf(be.h, f, 0, 64)
+        assert dec, L.odi_be_last_error()
+        fields = (ctypes.c_int * 8)()
+        L.odi_be_decoder_config(dec, fields)
+        assert list(fields) == [cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                                cfg.ctx]
+        prompt = [5, 17, 299, 3, 42]
+        n = 6
+        # C++: the prompt into the cache, then n greedy steps from its last token
+        assert L.odi_be_decoder_reset(dec, prompt[0], 0, 1) == 0, L.odi_be_last_error()
+        pa = (ctypes.c_int32 * (len(prompt) - 1))(*prompt[:-1])
+        assert L.odi_be_decoder_prefill(dec, pa, len(prompt) - 1, 0) == 0, L.odi_be_last_error()
+        assert L.odi_be_decoder_reset(dec, prompt[-1], len(prompt) - 1, 0) == 0
+        out = (ctypes.c_int32 * n)()
+        assert L.odi_be_decoder_generate(dec, n, out) == 0, L.odi_be_last_error()
+        logits = np.zeros(cfg.vocab, np.float32)
+        assert L.odi_be_decoder_logits(dec, logits.ctypes.data) == 0
+        # Python: load_llama + DecodeModel, the same sequence
+        cfg2, mw = gguf.load_llama(path)
+        dm = DecodeModel(cfg2, mw)
+        dm.prefill(prompt[:-1])
+        dm.reset(prompt[-1], len(prompt) - 1)
+        want = dm.generate(n)
+        assert list(out) == want
+        assert np.array_equal(logits.view(np.uint32), dm.logits.cpu().numpy().view(np.uint32))
+        ms = ctypes.c_float()
+        assert L.odi_be_decoder_time(dec, 4, ctypes.byref(ms)) == 0 and ms.value > 0
+    finally:
+        if dec:
+            L.odi_be_decoder_free(dec)
+        be.close()
+        L.odi_be_gguf_close(f)

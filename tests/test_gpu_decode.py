@@ -584,3 +584,51 @@ def test_matmul_fused_ssq_slots(cuda_lib, dt):
     torch.cuda.synchronize()
     a, bb = out_a.cpu().numpy(), out_b.cpu().numpy()
     assert np.allclose(a, bb, rtol=1e-4, atol=1e-4 * np.abs(bb).max())
+
+
+
+def test_capi_decoder_matches_decode_model(cuda_lib):
+    """odi_cuda_decoder_* (the decode step driven from the C ABI, for a C++
+    engine) against DecodeModel's epilogue mode on the same device weights:
+    the same tokens, logits bit for bit, and the error words clean."""
+    import ctypes
+
+    import torch
+
+    from odiengine_b200.decode import CDecoder, DecodeModel, LlamaConfig, seeded_model
+
+    ob = cuda_lib
+    L = ob.lib()
+    cfg = LlamaConfig(layers=3, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=700, ctx=96)
+    mw = seeded_model(cfg, seed=4)
+    dm = DecodeModel(cfg, mw)
+    cd = CDecoder(cfg, mw, max_record=256)
+    d = cd.h
+    try:
+        assert L.odi_cuda_decoder_launches_per_step(d) == dm.launches_per_step()
+        prompt = torch.randint(0, cfg.vocab, (20,), generator=torch.Generator().manual_seed(3)).tolist()
+        ob.check(L.odi_cuda_decoder_reset(d, prompt[0], 0, 1))
+        arr = (ctypes.c_int32 * 19)(*prompt[:-1])
+        ob.check(L.odi_cuda_decoder_prefill(d, arr, 19, 0))
+        ob.check(L.odi_cuda_decoder_reset(d, prompt[-1], 19, 0))
+        out = (ctypes.c_int32 * 12)()
+        ob.check(L.odi_cuda_decoder_generate(d, 12, out))
+        logits = np.zeros(cfg.vocab, np.float32)
+        ob.check(L.odi_cuda_decoder_logits(d, logits.ctypes.data))
+        dm.clear_cache()
+        dm.prefill(prompt[:-1])
+        dm.reset(prompt[-1], 19)
+        want = dm.generate(12)
+        assert list(out) == want
+        assert np.array_equal(logits.view(np.uint32), dm.logits.cpu().numpy().view(np.uint32))
+        # the record and the timed replays go on from there
+        ms = ctypes.c_float()
+        ob.check(L.odi_cuda_decoder_time(d, 8, ctypes.byref(ms)))
+        assert ms.value > 0
+        more = (ctypes.c_int32 * 8)()
+        ob.check(L.odi_cuda_decoder_tokens(d, 12, 8, more))
+        assert list(more) == dm.generate(8)
+        with pytest.raises(ob.OdiCudaError, match="out of range"):
+            ob.check(L.odi_cuda_decoder_reset(d, cfg.vocab, 0, 0))
+    finally:
+        cd.free()

@@ -314,11 +314,11 @@ def test_backend_errors(cuda_lib):
 @pytest.mark.parametrize("dt,N,K,M", [(O.Q4_K, 4096, 14336, 1), (O.Q8_0, 300, 1024, 3), (O.Q6_K, 4096, 4096, 9)])
 @pytest.mark.parametrize("offset", [0, 1], ids=["aligned", "offset4"])
 def test_matmul_host_pinned_buffers(cuda_lib, dt, N, K, M, offset):
-    """odi_cuda_matmul_host on page-locked host buffers (x fetched by the
-    device, y stored by the product into host memory) gives the results of
-    the device-buffer product bit for bit; pageable buffers (the copy-engine
-    path) too.  offset4 starts both buffers 4 bytes into a pinned block, so
-    the fetch takes its unaligned path."""
+    """odi_cuda_matmul_host on page-locked host buffers (y stored by the
+    product straight into host memory, the error word read from mapped
+    memory) gives the results of the device-buffer product bit for bit;
+    pageable buffers (the copy-engine path) too.  offset4 starts both buffers
+    4 bytes into a pinned block."""
     import ctypes
 
     import torch
