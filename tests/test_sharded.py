@@ -150,13 +150,18 @@ def test_sharded_two_gpus_match_one():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gpu_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_gpu_worker, args=(r, 2, port, q), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
-    got = q.get(timeout=300)
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    try:
+        got = q.get(timeout=300)
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
     assert all(got[-1]), got[-1]
     got = got[:-1]
     ob.init(0)
@@ -294,13 +299,19 @@ def test_capi_sharded_two_gpus():
     ob.check(ob.lib().odi_cuda_nccl_unique_id(uid))
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_capi_worker, args=(r, 2, uid.raw, q)) for r in range(2)]
+    # daemon children: a rank that never joins cannot keep pytest alive
+    procs = [ctx.Process(target=_capi_worker, args=(r, 2, uid.raw, q), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
-    got = q.get(timeout=300)
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    try:
+        got = q.get(timeout=300)
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
     for (dt, N, K, M, mode), y in zip(CAPI_CASES, got):
         b = O.quantize(dt, O.seeded_weights(N, K, seed=1))
         xs = O.seeded_acts(M, K, seed=2)
