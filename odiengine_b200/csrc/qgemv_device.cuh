@@ -974,16 +974,13 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* local, int rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
   return remote;
 }
-__device__ __forceinline__ void st_dsmem_f32(uint32_t remote, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_dsmem_v4(uint32_t remote, float4 v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "f"(v.x), "f"(v.y), "f"(v.z),
-               "f"(v.w)
+// Asynchronous store into another CTA's shared memory whose completion is
+// counted, in bytes, on that CTA's mbarrier (complete-tx): the receiver
+// waits on the barrier; the sender needs no fence and no arrival.
+__device__ __forceinline__ void st_async_v4(uint32_t remote, float4 v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(remote),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
                : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -1136,10 +1133,12 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 2);  // the two warps of a unit-parity pair
     }
-    // rank 0 receives one arrival per pushing thread of every other rank
-    // (16 float4 per token of the 64-row partial)
-    if (pl.C > 1) mbar_init(redbar, (pl.C - 1) * 16 * a.M);
+    // Rank 0's reduction barrier: its one arrival is rank 0's own expect-tx
+    // of the other ranks' partials (64 rows x M tokens fp32 each), which
+    // their st.async pushes count down as they land.
+    if (pl.C > 1) mbar_init(redbar, 1);
     fence_mbar_init();
+    if (pl.C > 1 && rank == 0) mbar_arrive_expect_tx(redbar, (uint32_t)((pl.C - 1) * UNIT_ROWS * a.M * 4));
   }
   __syncthreads();
   // Cluster barrier, split: arrive now, wait only before the first remote
@@ -1226,8 +1225,8 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
 
   // Tile reduction: unit parities (fixed order) -> CTA partial -> ranks (fixed
   // order).  Ranks other than 0 push their partial into rank 0's shared
-  // memory as float4 stores, each pushing thread then arriving (release) on
-  // rank 0's reduction mbarrier; rank 0 waits, adds, writes y.
+  // memory as asynchronous float4 stores counted on rank 0's reduction
+  // mbarrier; rank 0 waits, adds, writes y.
   if constexpr (TC) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {  // row 32 (warp & 1) + 16 (i >> 2) + 8 ((i >> 1) & 1) + g, token 2t + (i & 1)
@@ -1250,8 +1249,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
       v.y = red[(0 * UNIT_ROWS + r0 + 1) * MT + m] + red[(1 * UNIT_ROWS + r0 + 1) * MT + m];
       v.z = red[(0 * UNIT_ROWS + r0 + 2) * MT + m] + red[(1 * UNIT_ROWS + r0 + 2) * MT + m];
       v.w = red[(0 * UNIT_ROWS + r0 + 3) * MT + m] + red[(1 * UNIT_ROWS + r0 + 3) * MT + m];
-      st_dsmem_v4(dsmem_addr(part + rank * UNIT_ROWS * MT + t0, 0), v);
-      mbar_arrive_remote(dsmem_addr(redbar, 0));  // releases this thread's push
+      st_async_v4(dsmem_addr(part + rank * UNIT_ROWS * MT + t0, 0), v, dsmem_addr(redbar, 0));
     }
   } else {
     for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
