@@ -190,6 +190,16 @@ __device__ __forceinline__ int q8_round(float t) {
   return __float2int_rz(__fadd_rn(t, copysignf(0x1.fffffep-2f, t)));
 }
 
+// Orders this thread's earlier shared-memory accesses (generic proxy) before
+// later async-proxy accesses to shared memory -- a bulk copy that refills a
+// ring slot the thread has read.  Each reading thread fences before the slot
+// is released; the mbarrier ordering alone does not cover the proxy change
+// (reads of a slot still landing after its refill began were observed
+// without it).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Bulk prefetch of global bytes into L2 (no shared-memory destination, no
 // completion to wait on).  src and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {

@@ -327,7 +327,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const float* __restri
         m[g] = mn;
       }
     }
-    __syncthreads();  // every warp is done with stage s
+    fence_proxy_async_smem();  // this thread's reads of stage s before its refill
+    __syncthreads();           // every warp is done with stage s
     if (threadIdx.x == 0 && issued < nmine) issue(issued++);
   }
   if (threadIdx.x == 0) {

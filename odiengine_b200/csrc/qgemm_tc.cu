@@ -481,6 +481,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
       if (!ok) break;
+      fence_async_smem();  // this thread's reads of the raw stage before its refill
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_r[rs]);
     }

@@ -221,6 +221,87 @@ __device__ __forceinline__ void prologue8(const GemvArgs& a, int kb0, int r, int
   }
 }
 
+// Quantise two staged (span, token) records held in registers, one lane =
+// block b = lane / 4, values [32b + 8 part, +8) with part = lane % 4, into
+// Q8 records: codes at rec + 32b + 8part, XRec b at rec + 256 + 16b (the
+// gguf Q8_0 quantiser's arithmetic; see stage_acts).  The second record is
+// written only if `two`.  The caller orders reads of the records' old
+// contents before the call (the codes may land on them).
+__device__ __forceinline__ void q8_quantize2(const float (&vv)[2][8], uint8_t* const (&rec)[2], bool two, int lane) {
+  const int b = lane >> 2, part = lane & 3;
+  float dq[2], dx[2];
+  int sh[2], sf[2], shi[2];
+  uint32_t packed[2][2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    float am = fmaxf(fmaxf(fmaxf(fabsf(vv[i][0]), fabsf(vv[i][1])), fmaxf(fabsf(vv[i][2]), fabsf(vv[i][3]))),
+                     fmaxf(fmaxf(fabsf(vv[i][4]), fabsf(vv[i][5])), fmaxf(fabsf(vv[i][6]), fabsf(vv[i][7]))));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    dq[i] = q8_scale(am);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float id = q8_inv(dq[i]);
+    int qq[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qq[e] = q8_round(__fmul_rn(vv[i][e], id));
+    packed[i][0] = pack4_s8(qq[0], qq[1], qq[2], qq[3]);
+    packed[i][1] = pack4_s8(qq[4], qq[5], qq[6], qq[7]);
+    const int sacc = __dp4a((int)packed[i][1], 0x01010101, __dp4a((int)packed[i][0], 0x01010101, 0));
+    sh[i] = sacc + __shfl_xor_sync(0xffffffffu, sacc, 1);  // 16 codes: parts 0-1 or 2-3
+    sf[i] = sh[i] + __shfl_xor_sync(0xffffffffu, sh[i], 2);
+    shi[i] = __shfl_sync(0xffffffffu, sh[i], (lane & ~3) | 2);
+    dx[i] = __half2float(__float2half_rn(dq[i]));
+  }
+  __syncwarp();  // every lane has read its fp32 values before codes land on them
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    if (i == 1 && !two) break;
+    *reinterpret_cast<uint2*>(rec[i] + 32 * b + 8 * part) = make_uint2(packed[i][0], packed[i][1]);
+    if (part == 0) {
+      XRec rq;
+      rq.dx = dx[i];
+      rq.sdx = __fmul_rn((float)sf[i], dx[i]);
+      rq.sdx_lo = __fmul_rn((float)sh[i], dx[i]);
+      rq.sdx_hi = __fmul_rn((float)shi[i], dx[i]);
+      *reinterpret_cast<XRec*>(rec[i] + 256 + 16 * b) = rq;
+    }
+  }
+}
+
+// ACT_Q8 staging without a prologue, x rows 16-byte aligned (K % 4 == 0):
+// each lane loads the 8 values it quantises straight from global memory
+// (ld.global.cg, 2 x 16 bytes per record, both records' loads in flight
+// together) -- no shared-memory copy of the fp32 values, no barrier between
+// load and quantisation; the records' bytes equal stage_acts'.
+template <int MT>
+__device__ __forceinline__ void stage_q8_direct(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int off = 32 * (lane >> 2) + 8 * (lane & 3);
+  const int nrec = nsp * a.M;
+  for (int r0 = warp; r0 < nrec; r0 += 2 * NCW) {
+    const bool two = r0 + NCW < nrec;
+    uint8_t* rec[2];
+    float vv[2][8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int ri = (i == 1 && two) ? r0 + NCW : r0;
+      const int j = ri / a.M, m = ri - j * a.M;
+      rec[i] = xr + (j * MT + m) * stage_stride(false, MT);
+      const int64_t k = (int64_t)(kb0 + j) * UNIT_COLS + off;
+      const float* p = a.x + (int64_t)m * a.ldx + k;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 v0 = k + 4 <= a.K ? __ldcg(reinterpret_cast<const float4*>(p)) : z;
+      const float4 v1 = k + 8 <= a.K ? __ldcg(reinterpret_cast<const float4*>(p + 4)) : z;
+      vv[i][0] = v0.x; vv[i][1] = v0.y; vv[i][2] = v0.z; vv[i][3] = v0.w;
+      vv[i][4] = v1.x; vv[i][5] = v1.y; vv[i][6] = v1.z; vv[i][7] = v1.w;
+    }
+    q8_quantize2(vv, rec, two, lane);
+  }
+  consumer_sync();
+}
+
 // Staging: x (or the gate half of a SwiGLU input) of every span of the chunk
 // by cp.async in one group, so it costs one memory round trip whatever the
 // chunk length.  The RMSNorm sum of squares is reduced while the copies fly.
@@ -232,6 +313,10 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
   const int tid = threadIdx.x;  // 0..127
   const int warp = tid >> 5, lane = tid & 31;
   const bool vec = (a.K & 3) == 0 && (a.ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+  if (!F32 && vec && !a.fu.swiglu && !a.fu.norm_w) {
+    stage_q8_direct<MT>(a, kb0, nsp, xr);
+    return;
+  }
   // 64 chunks of 4 values per (span, token): threads 0-63 take even tokens, 64-127 odd
   const int q = tid & 63;
   for (int j = 0; j < nsp; ++j) {
@@ -302,45 +387,7 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
       }
       continue;
     }
-    float dq[2], dx[2];
-    int sh[2], sf[2], shi[2];
-    uint32_t packed[2][2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      float am = fmaxf(fmaxf(fmaxf(fabsf(vv[i][0]), fabsf(vv[i][1])), fmaxf(fabsf(vv[i][2]), fabsf(vv[i][3]))),
-                       fmaxf(fmaxf(fabsf(vv[i][4]), fabsf(vv[i][5])), fmaxf(fabsf(vv[i][6]), fabsf(vv[i][7]))));
-      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-      dq[i] = q8_scale(am);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float id = q8_inv(dq[i]);
-      int qq[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) qq[e] = q8_round(__fmul_rn(vv[i][e], id));
-      packed[i][0] = pack4_s8(qq[0], qq[1], qq[2], qq[3]);
-      packed[i][1] = pack4_s8(qq[4], qq[5], qq[6], qq[7]);
-      const int sacc = __dp4a((int)packed[i][1], 0x01010101, __dp4a((int)packed[i][0], 0x01010101, 0));
-      sh[i] = sacc + __shfl_xor_sync(0xffffffffu, sacc, 1);  // 16 codes: parts 0-1 or 2-3
-      sf[i] = sh[i] + __shfl_xor_sync(0xffffffffu, sh[i], 2);
-      shi[i] = __shfl_sync(0xffffffffu, sh[i], (lane & ~3) | 2);
-      dx[i] = __half2float(__float2half_rn(dq[i]));
-    }
-    __syncwarp();  // every lane has read its fp32 values before codes land on them
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      if (i == 1 && !two) break;
-      *reinterpret_cast<uint2*>(rec[i] + 32 * b + 8 * part) = make_uint2(packed[i][0], packed[i][1]);
-      if (part == 0) {
-        XRec rq;
-        rq.dx = dx[i];
-        rq.sdx = __fmul_rn((float)sf[i], dx[i]);
-        rq.sdx_lo = __fmul_rn((float)sh[i], dx[i]);
-        rq.sdx_hi = __fmul_rn((float)shi[i], dx[i]);
-        *reinterpret_cast<XRec*>(rec[i] + 256 + 16 * b) = rq;
-      }
-    }
+    q8_quantize2(vv, rec, two, lane);
     __syncwarp();
   }
   consumer_sync();
@@ -1214,6 +1261,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
       unit_tc<DT, RS>(ring + s * SB, warp & 1, xr + j * MT * RS, acc);
     else
       unit<DT, MT, F32, RS>(ring + s * SB, row, xr + j * MT * RS, a.M, acc);
+    fence_proxy_async_smem();  // this lane's reads of the slot before its refill
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     s += 2;
