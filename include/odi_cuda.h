@@ -269,13 +269,35 @@ int odi_cuda_dequantize(int dtype, const void* d_w_tiled, float* d_out, int64_t 
  * (context.cpp:152, 188-190): h_x [M, K] and h_y [M, N] are host memory;
  * the call brings x in, runs the product on the weight's device copy,
  * brings y out and waits.  Uses a library-owned per-device workspace.
- * x goes in with cudaMemcpyAsync; a page-locked h_y (cudaHostAlloc /
- * cudaHostRegister) is written by the product itself, saving a copy's
+ * A page-locked h_x (cudaHostAlloc / cudaHostRegister) is read by a small
+ * kernel whose loads overlap the start of the product's weight stream
+ * (programmatic dependent launch); pageable x goes in with cudaMemcpyAsync.
+ * A page-locked h_y is written by the product itself, saving a copy's
  * latency (the tensor-core path and pageable buffers copy y out).
  * Returns ODI_CUDA_ERR_OPERATION_FAILED (h_y not to be used) when a kernel's
  * bounded wait gave up, as cpu_backend.cpp:177-227 throws on failure. */
 int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
                          int act_mode, void* stream);
+
+/* odi_cuda_matmul_host without the wait: the product is queued on `stream`
+ * and the call returns.  This is the Backend::matmul / Backend::sync pair
+ * (backend.hpp:38, 130) with sync made meaningful, as a CUDA backend is
+ * allowed to: a caller with several independent products (the seven
+ * per-layer products of a batch of sequences, a prefill split into chunks)
+ * queues them and syncs once, and each product's x arrives while the one
+ * before it runs.  h_x must stay unchanged, and h_y unread, until
+ * odi_cuda_host_sync(stream) returns; products on one stream run in call
+ * order and share the device workspace, so they need not be separated by
+ * syncs.  With page-locked buffers nothing waits; pageable ones make the
+ * copy in or out synchronous. */
+int odi_cuda_matmul_host_async(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
+                               int act_mode, void* stream);
+
+/* Waits for the host-buffer products queued on `stream` (current device)
+ * and reads, then clears, the error word they report into:
+ * ODI_CUDA_ERR_OPERATION_FAILED when a kernel's bounded wait gave up in any
+ * of them (their h_y are then not to be used). */
+int odi_cuda_host_sync(void* stream);
 
 /* Host-buffer form of Backend::dequantize (backend.hpp:111;
  * cpu_backend.cpp:625-648) for an uploaded weight: h_out receives N*K fp32

@@ -77,6 +77,8 @@ SIGNATURES = {
     "odi_cuda_workspace_status": (_int, [_vp, ctypes.POINTER(_int), _vp]),
     "odi_cuda_dequantize": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
     "odi_cuda_matmul_host": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
+    "odi_cuda_matmul_host_async": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
+    "odi_cuda_host_sync": (_int, [_vp]),
     "odi_cuda_matmul_host_noalloc": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
     "odi_cuda_dequantize_host": (_int, [_vp, _vp, _vp]),
     "odi_cuda_tc_supported": (_int, [_int]),

@@ -879,6 +879,7 @@ struct Arena {
   size_t x_bytes = 0;
   float* y = nullptr;
   size_t y_bytes = 0;
+  int pending_err = 0;         // error word of a workspace replaced while products were queued
 };
 std::mutex g_arena_mu;
 Arena g_arena[64];
@@ -926,24 +927,31 @@ int finish_host_call(Arena& A, cudaStream_t s) {
   }
   return ODI_CUDA_OK;
 }
-}  // namespace
 
-extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
-                                    int act_mode, void* stream) {
-  if (!w || !h_x || !h_y) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
-  if (M < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M");
-  if (M == 0) return ODI_CUDA_OK;
-  const int mode = resolve_act_mode(w->dtype, M, act_mode);
-  if (mode < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "unknown act_mode %d", act_mode);
+// Enqueue one host-buffer product on `s`: x into the arena (pulled by a
+// kernel from page-locked memory, or copied from pageable memory), the
+// product, y into h_y (stored by the GEMV epilogue when h_y is page-locked,
+// else copied back).  Takes the arena lock; *werr_out is the page-locked
+// error word the product reports into, or nullptr when the error word is the
+// device workspace's.
+int enqueue_host_product(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M, int mode,
+                         cudaStream_t s, Arena*& arena, int*& werr_out) {
   int dev = 0;
   CK(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev != w->device) return fail(ODI_CUDA_ERR_INVALID_STATE, "weight lives on device %d, current is %d", w->device, dev);
-  std::lock_guard<std::mutex> lk(g_arena_mu);
   Arena& A = g_arena[dev & 63];
+  arena = &A;
   const size_t wsb = odi_cuda_matmul_workspace_bytes(w->dtype, M, w->N, w->K, mode);
+  if (A.ws && wsb > A.ws_bytes) {
+    // queued products may have reported into the workspace about to be
+    // replaced: keep its error word for the next sync
+    int old = 0;
+    CK(cudaMemcpy(&old, A.ws, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+    A.pending_err |= old;
+  }
   CK(grow(&A.ws, &A.ws_bytes, wsb, true), "workspace alloc");
-  CK(grow((void**)&A.x, &A.x_bytes, (size_t)(M * w->K) * sizeof(float), false), "x alloc");
-  cudaStream_t s = (cudaStream_t)stream;
+  const size_t xbytes = (size_t)(M * w->K) * sizeof(float);
+  CK(grow((void**)&A.x, &A.x_bytes, xbytes, false), "x alloc");
   // A workspace that is only the error word (one-token and fp32 products on
   // the streaming GEMV) lives in page-locked host memory the device writes
   // through, so the host reads the word after the sync without a copy.
@@ -959,18 +967,81 @@ extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, 
     }
     werr = A.ws_host;
   }
+  werr_out = werr;
   // y: a page-locked h_y is written by the product itself (its epilogue
   // stores reach host memory directly), saving a copy's latency; the
   // tensor-core path, and pageable buffers, go through the device buffer.
   float* dy = mode == ODI_CUDA_ACT_F16 ? nullptr : device_view(h_y);
   if (!dy) CK(grow((void**)&A.y, &A.y_bytes, (size_t)(M * w->N) * sizeof(float), false), "y alloc");
-  CK(cudaMemcpyAsync(A.x, h_x, (size_t)(M * w->K) * sizeof(float), cudaMemcpyHostToDevice, s), "H2D x");
+  // x: page-locked h_x is pulled by a kernel whose host loads overlap the
+  // previous kernel on the stream; the product then follows it under
+  // programmatic dependent launch, so its weight stream starts while x
+  // arrives.  Pageable x goes through a copy.
+  const float* hxv = device_view(const_cast<float*>(h_x));
+  int flags = 0;
+  if (hxv && (reinterpret_cast<uintptr_t>(hxv) & 3) == 0) {
+    CK(launch_pull_host(hxv, A.x, xbytes, true, s), "x pull launch");
+    flags = ODI_CUDA_FLAG_PDL;
+  } else {
+    CK(cudaMemcpyAsync(A.x, h_x, xbytes, cudaMemcpyHostToDevice, s), "H2D x");
+  }
   int rc = odi_cuda_matmul(w->dtype, w->data, A.x, dy ? dy : A.y, M, w->N, w->K, mode,
-                           werr ? static_cast<void*>(A.ws_host_dev) : A.ws, werr ? (size_t)WS_HEADER : A.ws_bytes, 0,
-                           stream);
+                           werr ? static_cast<void*>(A.ws_host_dev) : A.ws, werr ? (size_t)WS_HEADER : A.ws_bytes,
+                           flags, s);
   if (rc) return rc;
   if (!dy) CK(cudaMemcpyAsync(h_y, A.y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
-  if (!werr) return finish_host_call(A, s);
+  return ODI_CUDA_OK;
+}
+
+// Error words the host-buffer products of a device report into: the
+// page-locked word (read directly) and the device workspace's (copied).
+// Both are read after the stream's work is done, and cleared.
+int finish_host_products(Arena& A, cudaStream_t s) {
+  int err = A.pending_err;
+  A.pending_err = 0;
+  if (A.ws) {
+    if (injected() & INJ_WAIT) CK(cudaMemsetAsync(A.ws, 0x01, 1, s), "injected wait failure");
+    CK(cudaMemcpyAsync(&err, A.ws, sizeof(int), cudaMemcpyDeviceToHost, s), "read error word");
+  }
+  CK(cudaStreamSynchronize(s), "sync");
+  if (A.ws_host) {
+    if (injected() & INJ_WAIT) *A.ws_host = ERR_FULL_WAIT;
+    err |= *reinterpret_cast<volatile int*>(A.ws_host);
+    *A.ws_host = 0;
+  }
+  if (err) {
+    if (A.ws) {
+      CK(cudaMemsetAsync(A.ws, 0, sizeof(int), s), "clear error word");
+      CK(cudaStreamSynchronize(s), "sync");
+    }
+    return fail(ODI_CUDA_ERR_OPERATION_FAILED, "a kernel wait gave up (error word 0x%x); the output is invalid", err);
+  }
+  return ODI_CUDA_OK;
+}
+
+int check_host_product(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M, int act_mode, int* mode) {
+  if (!w || !h_x || !h_y) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null argument");
+  if (M < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M");
+  *mode = 0;
+  if (M == 0) return ODI_CUDA_OK;
+  *mode = resolve_act_mode(w->dtype, M, act_mode);
+  if (*mode < 0) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "unknown act_mode %d", act_mode);
+  return ODI_CUDA_OK;
+}
+}  // namespace
+
+extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
+                                    int act_mode, void* stream) {
+  int mode = 0;
+  int rc = check_host_product(w, h_x, h_y, M, act_mode, &mode);
+  if (rc || M == 0) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  Arena* A = nullptr;
+  int* werr = nullptr;
+  rc = enqueue_host_product(w, h_x, h_y, M, mode, s, A, werr);
+  if (rc) return rc;
+  if (!werr) return finish_host_call(*A, s);
   CK(cudaStreamSynchronize(s), "sync");
   if (injected() & INJ_WAIT) *werr = ERR_FULL_WAIT;
   const int err = *reinterpret_cast<volatile int*>(werr);
@@ -979,6 +1050,24 @@ extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, 
     return fail(ODI_CUDA_ERR_OPERATION_FAILED, "a kernel wait gave up (error word 0x%x); the output is invalid", err);
   }
   return ODI_CUDA_OK;
+}
+
+extern "C" int odi_cuda_matmul_host_async(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
+                                          int act_mode, void* stream) {
+  int mode = 0;
+  int rc = check_host_product(w, h_x, h_y, M, act_mode, &mode);
+  if (rc || M == 0) return rc;
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  Arena* A = nullptr;
+  int* werr = nullptr;
+  return enqueue_host_product(w, h_x, h_y, M, mode, (cudaStream_t)stream, A, werr);
+}
+
+extern "C" int odi_cuda_host_sync(void* stream) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  return finish_host_products(g_arena[dev & 63], (cudaStream_t)stream);
 }
 
 extern "C" int odi_cuda_dequantize_host(const odi_cuda_weight* w, float* h_out, void* stream) {

@@ -17,6 +17,12 @@ cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* til
 cudaError_t launch_repack(int dt, const void* gguf, void* tiled, int64_t N, int64_t K, cudaStream_t s);
 cudaError_t launch_unpack(int dt, const void* tiled, void* gguf, int64_t N, int64_t K, cudaStream_t s);
 cudaError_t launch_dequant(int dt, const void* tiled, float* out, int64_t N, int64_t K, cudaStream_t s);
+// Copy `bytes` (a multiple of 4) from page-locked host memory, given by its
+// device address, into device memory with a small kernel whose host loads
+// start before the programmatic dependency wait (pdl) and whose stores follow
+// it (act.cu).
+cudaError_t launch_pull_host(const void* src_dev_view, void* dst, size_t bytes, bool pdl, cudaStream_t stream);
+
 cudaError_t launch_quant_weights(int dt, const float* w, void* out, int64_t N, int64_t K, cudaStream_t s);
 
 // Work split of the streaming GEMV.  The weight is G row tiles of KB units.

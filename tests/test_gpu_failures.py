@@ -89,6 +89,10 @@ if out["upload"] == 0:
     for fn in ("odi_cuda_matmul_host", "odi_cuda_matmul_host_noalloc"):
         out[fn] = getattr(L, fn)(h, x.ctypes.data_as(ctypes.c_void_p), y.ctypes.data_as(ctypes.c_void_p), 2, 0, None)
         out[fn + "_msg"] = L.odi_cuda_last_error().decode()
+    out["async"] = L.odi_cuda_matmul_host_async(h, x.ctypes.data_as(ctypes.c_void_p),
+                                                y.ctypes.data_as(ctypes.c_void_p), 2, 0, None)
+    out["host_sync"] = L.odi_cuda_host_sync(None)
+    out["host_sync_msg"] = L.odi_cuda_last_error().decode()
     L.odi_cuda_weight_free(h)
 print(repr(out))
 """
@@ -118,6 +122,9 @@ def test_injected_wait_failure_fails_the_host_product(cuda_lib):
     for fn in ("odi_cuda_matmul_host", "odi_cuda_matmul_host_noalloc"):
         assert out[fn] == 6, out  # ODI_CUDA_ERR_OPERATION_FAILED
         assert "wait gave up" in out[fn + "_msg"]
+    # a queued product reports at the sync that closes the queue
+    assert out["async"] == 0, out
+    assert out["host_sync"] == 6 and "wait gave up" in out["host_sync_msg"], out
 
 
 def test_injected_init_failure_is_backend_unavailable(cuda_lib):

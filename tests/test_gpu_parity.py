@@ -345,3 +345,56 @@ def test_matmul_host_pinned_buffers(cuda_lib, dt, N, K, M, offset):
         assert np.array_equal(yp.view(np.uint32), want.view(np.uint32))
     finally:
         L.odi_cuda_weight_free(h)
+
+
+@pytest.mark.parametrize("dt,N,K,M", [(O.Q4_K, 4096, 14336, 1), (O.Q8_0, 300, 1024, 3), (O.Q6_K, 4096, 4096, 9),
+                                      (O.Q4_K, 1024, 4096, 32)])
+def test_matmul_host_async_queue(cuda_lib, dt, N, K, M):
+    """A queue of odi_cuda_matmul_host_async products with distinct inputs,
+    closed by one odi_cuda_host_sync, gives each product of the synchronous
+    odi_cuda_matmul_host bit for bit: page-locked buffers (x pulled by the
+    kernel that runs ahead of each product while the one before it runs, y
+    stored by the product), pageable ones, and a page-locked x 4 bytes into
+    its block (the 4-byte pull).  M = 1 reports into the mapped error word,
+    M = 3 into the device workspace (Q8 records), M = 9 and 32 run on the
+    tensor cores (y copied out)."""
+    import ctypes
+
+    import torch
+
+    ob = cuda_lib
+    L = ob.lib()
+    b, _ = make(dt, N, K, seed=N + M, M=M)
+    h = ctypes.c_void_p()
+    bb = np.ascontiguousarray(b)
+    ob.check(L.odi_cuda_weight_upload(bb.ctypes.data_as(ctypes.c_void_p), dt, N, K, ctypes.byref(h)))
+    try:
+        R = 6
+        xs = [O.seeded_acts(M, K, seed=100 + r) for r in range(R)]
+        want = []
+        for x in xs:
+            y = np.full((M, N), np.nan, np.float32)
+            ob.check(L.odi_cuda_matmul_host(h, x.ctypes.data_as(ctypes.c_void_p), y.ctypes.data_as(ctypes.c_void_p),
+                                            M, ob.ACT_AUTO, None))
+            want.append(y)
+        hx = torch.empty((R, M * K + 4), dtype=torch.float32).pin_memory()
+        hy = torch.full((R, M * N), float("nan"), dtype=torch.float32).pin_memory()
+        pageable = [np.full((M, N), np.nan, np.float32) for _ in range(R)]
+        xo = [1 if r == 4 else 0 for r in range(R)]
+        for r in range(R):
+            hx[r, xo[r]:xo[r] + M * K] = torch.from_numpy(xs[r].reshape(-1))
+        for r in range(R):
+            if r % 3 == 2:  # pageable x and y
+                rc = L.odi_cuda_matmul_host_async(h, xs[r].ctypes.data_as(ctypes.c_void_p),
+                                                  pageable[r].ctypes.data_as(ctypes.c_void_p), M, ob.ACT_AUTO, None)
+            else:
+                rc = L.odi_cuda_matmul_host_async(h, hx[r].data_ptr() + 4 * xo[r], hy[r].data_ptr(), M,
+                                                  ob.ACT_AUTO, None)
+            ob.check(rc)
+        ob.check(L.odi_cuda_host_sync(None))
+        for r in range(R):
+            got = pageable[r] if r % 3 == 2 else hy[r].numpy().reshape(M, N)
+            assert np.array_equal(got.view(np.uint32), want[r].view(np.uint32)), r
+        assert not np.array_equal(want[0], want[1])
+    finally:
+        L.odi_cuda_weight_free(h)
