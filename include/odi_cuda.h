@@ -289,7 +289,10 @@ int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, float* h_y,
  * odi_cuda_host_sync(stream) returns; products on one stream run in call
  * order and share the device workspace, so they need not be separated by
  * syncs.  With page-locked buffers nothing waits; pageable ones make the
- * copy in or out synchronous. */
+ * copy in or out synchronous.  A page-locked h_y is filled by the library
+ * in batches (its output parked on the device, then copied out by one
+ * launch per batch of up to 200 products and at the sync), so the products
+ * themselves touch no host memory. */
 int odi_cuda_matmul_host_async(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M,
                                int act_mode, void* stream);
 

@@ -227,51 +227,6 @@ cudaError_t launch_act_records_fused(const float* x, int64_t ldx, int64_t M, int
   return cudaLaunchKernelEx(&cfg, act_records_fused_kernel, x, ldx, M, K, KB, fu, recs);
 }
 
-// Host activations into a device buffer, read by the SMs from page-locked
-// host memory through its device address.  Each thread issues its first
-// PULL_AHEAD loads before the programmatic dependency wait -- host memory is
-// not written by any kernel, so those PCIe round trips overlap the previous
-// kernel on the stream -- and stores only after it, since that kernel (or
-// an earlier one) may still read the buffer.  The wait also orders every
-// earlier kernel before the stores: each product kernel on this path waits
-// for its own predecessor, so completion is transitive down the stream.
-constexpr int PULL_AHEAD = 2;
-constexpr int PULL_BLOCK = 128;
-
-template <typename T>
-__global__ void __launch_bounds__(PULL_BLOCK) pull_host_kernel(const T* __restrict__ src, T* __restrict__ dst,
-                                                               int64_t n) {
-  pdl_launch_dependents();
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  T v[PULL_AHEAD];
-#pragma unroll
-  for (int u = 0; u < PULL_AHEAD; ++u)
-    if (i0 + u * stride < n) v[u] = src[i0 + u * stride];
-  pdl_wait();
-#pragma unroll
-  for (int u = 0; u < PULL_AHEAD; ++u)
-    if (i0 + u * stride < n) dst[i0 + u * stride] = v[u];
-  for (int64_t i = i0 + PULL_AHEAD * stride; i < n; i += stride) dst[i] = src[i];
-}
-
-cudaError_t launch_pull_host(const void* src_dev_view, void* dst, size_t bytes, bool pdl, cudaStream_t stream) {
-  if (bytes == 0) return cudaSuccess;
-  if (bytes & 3) return cudaErrorInvalidValue;
-  const bool v16 = ((reinterpret_cast<uintptr_t>(src_dev_view) | reinterpret_cast<uintptr_t>(dst) | bytes) & 15) == 0;
-  const int64_t n = (int64_t)(bytes / (v16 ? 16 : 4));
-  int64_t g = (n + (int64_t)PULL_BLOCK * PULL_AHEAD - 1) / ((int64_t)PULL_BLOCK * PULL_AHEAD);
-  if (g > 148 * 4) g = 148 * 4;
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = small_cfg((int)g, pdl, stream, attr);
-  cfg.blockDim = dim3(PULL_BLOCK);
-  if (v16)
-    return cudaLaunchKernelEx(&cfg, pull_host_kernel<uint4>, static_cast<const uint4*>(src_dev_view),
-                              static_cast<uint4*>(dst), n);
-  return cudaLaunchKernelEx(&cfg, pull_host_kernel<uint32_t>, static_cast<const uint32_t*>(src_dev_view),
-                            static_cast<uint32_t*>(dst), n);
-}
-
 cudaError_t launch_act_pack_f32(const float* x, int64_t M, int64_t K, float* tiles, bool pdl,
                                 cudaStream_t stream) {
   const int64_t Kp = (K + 255) / 256 * 256;

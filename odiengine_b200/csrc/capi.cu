@@ -880,7 +880,18 @@ struct Arena {
   float* y = nullptr;
   size_t y_bytes = 0;
   int pending_err = 0;         // error word of a workspace replaced while products were queued
+  // Queued products' outputs (odi_cuda_matmul_host_async with page-locked
+  // h_y): parked in yring by the products, copied out by one gather launch
+  // per batch on the stream they were queued on.
+  float* yring = nullptr;
+  size_t ring_used = 0;
+  GatherTable gt{};
+  // The stream of the queued products not yet closed by a sync: the arena's
+  // buffers are shared, so work on another stream waits for them first.
+  cudaStream_t queue_stream = nullptr;
+  bool queued = false;
 };
+constexpr size_t YRING_BYTES = 64u << 20;
 std::mutex g_arena_mu;
 Arena g_arena[64];
 
@@ -928,6 +939,16 @@ int finish_host_call(Arena& A, cudaStream_t s) {
   return ODI_CUDA_OK;
 }
 
+// Launch the gather of the parked outputs (on their stream, after the
+// products that wrote them) and start a new batch.
+int flush_parked(Arena& A) {
+  if (A.gt.n == 0) return ODI_CUDA_OK;
+  CK(launch_gather_to_host(A.yring, A.gt, true, A.queue_stream), "y gather launch");
+  A.gt.n = 0;
+  A.ring_used = 0;
+  return ODI_CUDA_OK;
+}
+
 // Enqueue one host-buffer product on `s`: x into the arena (pulled by a
 // kernel from page-locked memory, or copied from pageable memory), the
 // product, y into h_y (stored by the GEMV epilogue when h_y is page-locked,
@@ -935,12 +956,18 @@ int finish_host_call(Arena& A, cudaStream_t s) {
 // error word the product reports into, or nullptr when the error word is the
 // device workspace's.
 int enqueue_host_product(const odi_cuda_weight* w, const float* h_x, float* h_y, int64_t M, int mode,
-                         cudaStream_t s, Arena*& arena, int*& werr_out) {
+                         cudaStream_t s, bool queued, Arena*& arena, int*& werr_out) {
   int dev = 0;
   CK(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev != w->device) return fail(ODI_CUDA_ERR_INVALID_STATE, "weight lives on device %d, current is %d", w->device, dev);
   Arena& A = g_arena[dev & 63];
   arena = &A;
+  if (A.queued && A.queue_stream != s) {
+    int rc = flush_parked(A);
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(A.queue_stream), "sync (products queued on another stream)");
+    A.queued = false;
+  }
   const size_t wsb = odi_cuda_matmul_workspace_bytes(w->dtype, M, w->N, w->K, mode);
   if (A.ws && wsb > A.ws_bytes) {
     // queued products may have reported into the workspace about to be
@@ -973,6 +1000,25 @@ int enqueue_host_product(const odi_cuda_weight* w, const float* h_x, float* h_y,
   // tensor-core path, and pageable buffers, go through the device buffer.
   float* dy = mode == ODI_CUDA_ACT_F16 ? nullptr : device_view(h_y);
   if (!dy) CK(grow((void**)&A.y, &A.y_bytes, (size_t)(M * w->N) * sizeof(float), false), "y alloc");
+  // A queued product with page-locked h_y parks its output in the ring (the
+  // gather stores it into h_y later); outputs too large for the ring are
+  // stored straight into h_y.
+  float* ydst = dy;
+  const size_t ybytes = (size_t)(M * w->N) * sizeof(float);
+  const size_t yslot = (ybytes + 15) / 16 * 16;
+  if (queued && dy && yslot <= YRING_BYTES) {
+    if (!A.yring) CK(dev_malloc(reinterpret_cast<void**>(&A.yring), YRING_BYTES), "y ring alloc");
+    if (A.gt.n == GATHER_MAX || A.ring_used + yslot > YRING_BYTES) {
+      int rc = flush_parked(A);
+      if (rc) return rc;
+    }
+    const int e = A.gt.n++;
+    A.gt.dst[e] = (unsigned long long)reinterpret_cast<uintptr_t>(dy);
+    A.gt.off16[e] = (unsigned)(A.ring_used / 16);
+    A.gt.bytes[e] = (unsigned)ybytes;
+    ydst = A.yring + A.ring_used / sizeof(float);
+    A.ring_used += yslot;
+  }
   // x: page-locked h_x is pulled by a kernel whose host loads overlap the
   // previous kernel on the stream; the product then follows it under
   // programmatic dependent launch, so its weight stream starts while x
@@ -985,11 +1031,15 @@ int enqueue_host_product(const odi_cuda_weight* w, const float* h_x, float* h_y,
   } else {
     CK(cudaMemcpyAsync(A.x, h_x, xbytes, cudaMemcpyHostToDevice, s), "H2D x");
   }
-  int rc = odi_cuda_matmul(w->dtype, w->data, A.x, dy ? dy : A.y, M, w->N, w->K, mode,
+  int rc = odi_cuda_matmul(w->dtype, w->data, A.x, ydst ? ydst : A.y, M, w->N, w->K, mode,
                            werr ? static_cast<void*>(A.ws_host_dev) : A.ws, werr ? (size_t)WS_HEADER : A.ws_bytes,
                            flags, s);
   if (rc) return rc;
   if (!dy) CK(cudaMemcpyAsync(h_y, A.y, (size_t)(M * w->N) * sizeof(float), cudaMemcpyDeviceToHost, s), "D2H y");
+  if (queued) {
+    A.queued = true;
+    A.queue_stream = s;
+  }
   return ODI_CUDA_OK;
 }
 
@@ -997,6 +1047,12 @@ int enqueue_host_product(const odi_cuda_weight* w, const float* h_x, float* h_y,
 // page-locked word (read directly) and the device workspace's (copied).
 // Both are read after the stream's work is done, and cleared.
 int finish_host_products(Arena& A, cudaStream_t s) {
+  cudaStream_t qs = A.queue_stream;
+  const bool other = A.queued && qs != s;
+  int rc = flush_parked(A);
+  if (rc) return rc;
+  if (other) CK(cudaStreamSynchronize(qs), "sync (queue stream)");
+  A.queued = false;
   int err = A.pending_err;
   A.pending_err = 0;
   if (A.ws) {
@@ -1039,7 +1095,7 @@ extern "C" int odi_cuda_matmul_host(const odi_cuda_weight* w, const float* h_x, 
   std::lock_guard<std::mutex> lk(g_arena_mu);
   Arena* A = nullptr;
   int* werr = nullptr;
-  rc = enqueue_host_product(w, h_x, h_y, M, mode, s, A, werr);
+  rc = enqueue_host_product(w, h_x, h_y, M, mode, s, false, A, werr);
   if (rc) return rc;
   if (!werr) return finish_host_call(*A, s);
   CK(cudaStreamSynchronize(s), "sync");
@@ -1060,7 +1116,7 @@ extern "C" int odi_cuda_matmul_host_async(const odi_cuda_weight* w, const float*
   std::lock_guard<std::mutex> lk(g_arena_mu);
   Arena* A = nullptr;
   int* werr = nullptr;
-  return enqueue_host_product(w, h_x, h_y, M, mode, (cudaStream_t)stream, A, werr);
+  return enqueue_host_product(w, h_x, h_y, M, mode, (cudaStream_t)stream, true, A, werr);
 }
 
 extern "C" int odi_cuda_host_sync(void* stream) {

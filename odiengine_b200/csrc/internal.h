@@ -20,8 +20,22 @@ cudaError_t launch_dequant(int dt, const void* tiled, float* out, int64_t N, int
 // Copy `bytes` (a multiple of 4) from page-locked host memory, given by its
 // device address, into device memory with a small kernel whose host loads
 // start before the programmatic dependency wait (pdl) and whose stores follow
-// it (act.cu).
+// it (hostio.cu).
 cudaError_t launch_pull_host(const void* src_dev_view, void* dst, size_t bytes, bool pdl, cudaStream_t stream);
+
+// Outputs parked in a device ring, to be copied to page-locked host buffers
+// by one launch (hostio.cu): entry e is bytes[e] bytes (a multiple of 4) at
+// ring + 16 off16[e], for the host buffer whose device address is dst[e].
+// Passed by value (kernel parameters: under 4 KB).
+constexpr int GATHER_MAX = 200;
+struct GatherTable {
+  unsigned long long dst[GATHER_MAX];
+  unsigned off16[GATHER_MAX];
+  unsigned bytes[GATHER_MAX];
+  int n;
+};
+static_assert(sizeof(GatherTable) <= 4000, "kernel parameter space");
+cudaError_t launch_gather_to_host(const void* ring, const GatherTable& t, bool pdl, cudaStream_t stream);
 
 cudaError_t launch_quant_weights(int dt, const float* w, void* out, int64_t N, int64_t K, cudaStream_t s);
 

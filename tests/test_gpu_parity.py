@@ -398,3 +398,75 @@ def test_matmul_host_async_queue(cuda_lib, dt, N, K, M):
         assert not np.array_equal(want[0], want[1])
     finally:
         L.odi_cuda_weight_free(h)
+
+
+def _host_weight(ob, dt, N, K, seed):
+    import ctypes
+
+    b = np.ascontiguousarray(O.quantize(dt, O.seeded_weights(N, K, seed=seed)))
+    h = ctypes.c_void_p()
+    ob.check(ob.lib().odi_cuda_weight_upload(b.ctypes.data_as(ctypes.c_void_p), dt, N, K, ctypes.byref(h)))
+    return h
+
+
+@pytest.mark.parametrize("dt,N,K,M,n", [(O.Q8_0, 300, 1024, 1, 450), (O.Q6_K, 32000, 4096, 4, 140)])
+def test_matmul_host_async_batches(cuda_lib, dt, N, K, M, n):
+    """More queued products than one batch of parked outputs holds: 450
+    one-token products cross the 200-entry gather table twice; 140 products
+    of 4 x 32000 outputs fill the 64 MiB output ring after 128.  Every h_y
+    equals the synchronous call's bit for bit after the one sync."""
+    import ctypes
+
+    import torch
+
+    ob = cuda_lib
+    L = ob.lib()
+    h = _host_weight(ob, dt, N, K, seed=7)
+    try:
+        R = 5
+        hx = torch.stack([torch.from_numpy(O.seeded_acts(M, K, seed=200 + r)) for r in range(R)]).pin_memory()
+        want = []
+        for r in range(R):
+            y = torch.empty((M, N), dtype=torch.float32).pin_memory()
+            ob.check(L.odi_cuda_matmul_host(h, hx[r].data_ptr(), y.data_ptr(), M, ob.ACT_AUTO, None))
+            want.append(y.numpy().copy())
+        hy = torch.full((n, M, N), float("nan"), dtype=torch.float32).pin_memory()
+        for i in range(n):
+            ob.check(L.odi_cuda_matmul_host_async(h, hx[i % R].data_ptr(), hy[i].data_ptr(), M, ob.ACT_AUTO, None))
+        ob.check(L.odi_cuda_host_sync(None))
+        got = hy.numpy()
+        for i in range(n):
+            assert np.array_equal(got[i].view(np.uint32), want[i % R].view(np.uint32)), i
+    finally:
+        L.odi_cuda_weight_free(h)
+
+
+def test_matmul_host_async_two_streams(cuda_lib):
+    """Products queued on one stream, then on another: the library's shared
+    buffers make the second queue wait for the first (its parked outputs sent
+    out on their own stream); each stream's sync then finds its results."""
+    import torch
+
+    ob = cuda_lib
+    L = ob.lib()
+    dt, N, K, M = O.Q4_K, 512, 2048, 2
+    h = _host_weight(ob, dt, N, K, seed=9)
+    try:
+        s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+        xs = [torch.from_numpy(O.seeded_acts(M, K, seed=300 + r)).pin_memory() for r in range(6)]
+        want = []
+        for x in xs:
+            y = torch.empty((M, N), dtype=torch.float32).pin_memory()
+            ob.check(L.odi_cuda_matmul_host(h, x.data_ptr(), y.data_ptr(), M, ob.ACT_Q8, None))
+            want.append(y.numpy().copy())
+        ys = [torch.full((M, N), float("nan"), dtype=torch.float32).pin_memory() for _ in range(6)]
+        for r in range(6):
+            st = s1 if r < 3 else s2
+            ob.check(L.odi_cuda_matmul_host_async(h, xs[r].data_ptr(), ys[r].data_ptr(), M, ob.ACT_Q8,
+                                                  st.cuda_stream))
+        ob.check(L.odi_cuda_host_sync(s2.cuda_stream))
+        ob.check(L.odi_cuda_host_sync(s1.cuda_stream))
+        for r in range(6):
+            assert np.array_equal(ys[r].numpy().view(np.uint32), want[r].view(np.uint32)), r
+    finally:
+        L.odi_cuda_weight_free(h)
