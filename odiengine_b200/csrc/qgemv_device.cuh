@@ -86,6 +86,14 @@ __device__ __forceinline__ bool gemv_check(bool ok, int* err, int code, long lon
 // issue slots than the two-op magic-number form.
 __device__ __forceinline__ float i2f(int v) { return __int2float_rn(v); }
 
+// Packed fp32 (sm_100 FFMA2 / FMUL2): two independent IEEE operations with
+// round-to-nearest in one instruction, each element the same float as
+// fmaf / __fmul_rn of its pair.  Used where two elements share an
+// operation: two tokens of a pass, two rows of a tile, two scales.
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+
 // Byte B of w as the float 2^23 + byte (exact).
 template <int B>
 __device__ __forceinline__ float byte_magic(uint32_t w) {
@@ -95,6 +103,11 @@ __device__ __forceinline__ float byte_magic(uint32_t w) {
 template <int B>
 __device__ __forceinline__ float scale_byte(float d, float nd23, uint32_t w) {
   return fmaf(d, byte_magic<B>(w), nd23);
+}
+// scale_byte of bytes B and B + 1 of w with the pair's own (d, -2^23 d)
+template <int B>
+__device__ __forceinline__ float2 scale_byte2(float2 d, float2 nd23, uint32_t w) {
+  return fma2(d, f2(byte_magic<B>(w), byte_magic<B + 1>(w)), nd23);
 }
 
 __device__ __forceinline__ void consumer_sync() {
@@ -440,23 +453,17 @@ __device__ __forceinline__ void unit_q8_q4k(const uint8_t* __restrict__ sl, cons
   // Q4_K keeps the high nibbles in place (x16): their scales carry 1/16.
   const float dh = five ? d : 0.0625f * d;
   const float nd = -8388608.0f * d, ndh = -8388608.0f * dh, nm = -8388608.0f * dmin;
-  float A[8], B[8];
-  A[0] = scale_byte<0>(d, nd, scL);
-  A[1] = scale_byte<1>(dh, ndh, scL);
-  A[2] = scale_byte<2>(d, nd, scL);
-  A[3] = scale_byte<3>(dh, ndh, scL);
-  A[4] = scale_byte<0>(d, nd, scH);
-  A[5] = scale_byte<1>(dh, ndh, scH);
-  A[6] = scale_byte<2>(d, nd, scH);
-  A[7] = scale_byte<3>(dh, ndh, scH);
-  B[0] = scale_byte<0>(dmin, nm, mnL);
-  B[1] = scale_byte<1>(dmin, nm, mnL);
-  B[2] = scale_byte<2>(dmin, nm, mnL);
-  B[3] = scale_byte<3>(dmin, nm, mnL);
-  B[4] = scale_byte<0>(dmin, nm, mnH);
-  B[5] = scale_byte<1>(dmin, nm, mnH);
-  B[6] = scale_byte<2>(dmin, nm, mnH);
-  B[7] = scale_byte<3>(dmin, nm, mnH);
+  // A[j], B[j]: sub-block j's scale and min, in pairs (j even: d, odd: dh)
+  const float2 dp = f2(d, dh), ndp = f2(nd, ndh), mp = f2(dmin, dmin), nmp = f2(nm, nm);
+  float2 A[4], B[4];
+  A[0] = scale_byte2<0>(dp, ndp, scL);
+  A[1] = scale_byte2<2>(dp, ndp, scL);
+  A[2] = scale_byte2<0>(dp, ndp, scH);
+  A[3] = scale_byte2<2>(dp, ndp, scH);
+  B[0] = scale_byte2<0>(mp, nmp, mnL);
+  B[1] = scale_byte2<2>(mp, nmp, mnL);
+  B[2] = scale_byte2<0>(mp, nmp, mnH);
+  B[3] = scale_byte2<2>(mp, nmp, mnH);
   uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0;
   if (five) {
     h0 = lds128(sl + 16);
@@ -476,21 +483,46 @@ __device__ __forceinline__ void unit_q8_q4k(const uint8_t* __restrict__ sl, cons
       u0 = and4(q0, 0xF0F0F0F0u);
       u1 = and4(q1, 0xF0F0F0F0u);
     }
+    // one token: its two sub-block dots and records
+    auto dots = [&](int m, int& dl, int& du, float4& ra, float4& rb) {
+      const uint8_t* xr = xs + m * RS;
+      const uint4 x0 = lds128(xr + 64 * p), x1 = lds128(xr + 64 * p + 16);
+      const uint4 x2 = lds128(xr + 64 * p + 32), x3 = lds128(xr + 64 * p + 48);
+      ra = lds128f(xr + 256 + 32 * p);
+      rb = lds128f(xr + 256 + 32 * p + 16);
+      dl = dot16<false>(l1, x1, dot16<false>(l0, x0, 0));
+      du = five ? dot16<false>(u1, x3, dot16<false>(u0, x2, 0)) : dot16<true>(u1, x3, dot16<true>(u0, x2, 0));
+    };
+    const float Al = A[p].x, Au = A[p].y, Bl = B[p].x, Bu = B[p].y;
+    if (MT == 1) {
+      int dl, du;
+      float4 ra, rb;
+      dots(0, dl, du, ra, rb);
+      const float2 ar = mul2(A[p], f2(ra.x, rb.x));  // (Al * ra.x, Au * rb.x)
+      float v = acc[0];
+      v = fmaf(i2f(dl), ar.x, v);
+      v = fmaf(-Bl, ra.y, v);
+      v = fmaf(i2f(du), ar.y, v);
+      v = fmaf(-Bu, rb.y, v);
+      acc[0] = v;
+    } else {
+      // tokens in pairs: the same operations per token, two at a time (a
+      // pass's unused second token reads stale records; its sum is dropped)
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      if (m < M) {
-        const uint8_t* xr = xs + m * RS;
-        const uint4 x0 = lds128(xr + 64 * p), x1 = lds128(xr + 64 * p + 16);
-        const uint4 x2 = lds128(xr + 64 * p + 32), x3 = lds128(xr + 64 * p + 48);
-        const float4 ra = lds128f(xr + 256 + 32 * p), rb = lds128f(xr + 256 + 32 * p + 16);
-        const int dl = dot16<false>(l1, x1, dot16<false>(l0, x0, 0));
-        const int du = five ? dot16<false>(u1, x3, dot16<false>(u0, x2, 0)) : dot16<true>(u1, x3, dot16<true>(u0, x2, 0));
-        float v = acc[m];
-        v = fmaf(i2f(dl), A[2 * p] * ra.x, v);
-        v = fmaf(-B[2 * p], ra.y, v);
-        v = fmaf(i2f(du), A[2 * p + 1] * rb.x, v);
-        v = fmaf(-B[2 * p + 1], rb.y, v);
-        acc[m] = v;
+      for (int m = 0; m < MT; m += 2) {
+        if (m < M) {
+          int dl0, du0, dl1, du1;
+          float4 ra0, rb0, ra1, rb1;
+          dots(m, dl0, du0, ra0, rb0);
+          dots(m + 1, dl1, du1, ra1, rb1);
+          float2 v = f2(acc[m], acc[m + 1]);
+          v = fma2(f2(i2f(dl0), i2f(dl1)), mul2(f2(Al, Al), f2(ra0.x, ra1.x)), v);
+          v = fma2(f2(-Bl, -Bl), f2(ra0.y, ra1.y), v);
+          v = fma2(f2(i2f(du0), i2f(du1)), mul2(f2(Au, Au), f2(rb0.x, rb1.x)), v);
+          v = fma2(f2(-Bu, -Bu), f2(rb0.y, rb1.y), v);
+          acc[m] = v.x;
+          acc[m + 1] = v.y;
+        }
       }
     }
   }
@@ -515,39 +547,72 @@ __device__ __forceinline__ void unit_q8_q6k(const uint8_t* __restrict__ sl, floa
       const int sb = 8 * h + 2 * cl;  // sub-blocks sb, sb+1 (c0, c1) and sb+4, sb+5 (c2, c3)
       // scale d * sc with sc signed: the byte sc ^ 0x80 is sc + 128, so
       // magic - (2^23 + 128) is sc exactly
-      float A[4];
+      // A01 = (A[0], A[1]) of sub-blocks sb, sb + 1, A23 of sb + 4, sb + 5
+      float2 A01, A23;
       {
         const uint32_t w = sw[sb >> 2];
         const uint32_t w4 = sw[(sb + 4) >> 2];
         const int o = sb & 3;  // 0 or 2
-        const float a0 = (o == 0 ? byte_magic<0>(w) : byte_magic<2>(w)) - 8388736.0f;
-        const float a1 = (o == 0 ? byte_magic<1>(w) : byte_magic<3>(w)) - 8388736.0f;
-        const float a2 = (o == 0 ? byte_magic<0>(w4) : byte_magic<2>(w4)) - 8388736.0f;
-        const float a3 = (o == 0 ? byte_magic<1>(w4) : byte_magic<3>(w4)) - 8388736.0f;
-        A[0] = d * a0;
-        A[1] = d * a1;
-        A[2] = d * a2;
-        A[3] = d * a3;
+        const float2 off = f2(-8388736.0f, -8388736.0f), dd = f2(d, d);
+        const float2 a01 = __fadd2_rn(o == 0 ? f2(byte_magic<0>(w), byte_magic<1>(w))
+                                             : f2(byte_magic<2>(w), byte_magic<3>(w)), off);
+        const float2 a23 = __fadd2_rn(o == 0 ? f2(byte_magic<0>(w4), byte_magic<1>(w4))
+                                             : f2(byte_magic<2>(w4), byte_magic<3>(w4)), off);
+        A01 = mul2(dd, a01);
+        A23 = mul2(dd, a23);
       }
+      const float2 m32 = f2(-32.0f, -32.0f);
+      const float2 N01 = mul2(m32, A01), N23 = mul2(m32, A23);  // -32 * A: the offset's factor
+      // one token: its four integer dots and records
+      auto dots = [&](int m, int (&dq)[4], float4& ra, float4& rb) {
+        const uint8_t* xr = xs + m * RS;
+        const int xo = 128 * h + 32 * cl;
+        const uint4 x0 = lds128(xr + xo), x1 = lds128(xr + xo + 16);
+        const uint4 x2 = lds128(xr + xo + 64), x3 = lds128(xr + xo + 80);
+        ra = lds128f(xr + 256 + 16 * (4 * h + cl));
+        rb = lds128f(xr + 256 + 16 * (4 * h + cl + 2));
+        dq[0] = dot16<false>(c0, x0, 0);
+        dq[1] = dot16<false>(c1, x1, 0);
+        dq[2] = dot16<false>(c2, x2, 0);
+        dq[3] = dot16<false>(c3, x3, 0);
+      };
+      if (MT == 1) {
+        int dq[4];
+        float4 ra, rb;
+        dots(0, dq, ra, rb);
+        const float2 Aa = mul2(A01, f2(ra.x, ra.x)), Ab = mul2(A23, f2(rb.x, rb.x));
+        float v = acc[0];
+        // (q - 32) . x: integer dot, then -32 * A * sum(x) in fp32
+        v = fmaf(i2f(dq[0]), Aa.x, v);
+        v = fmaf(N01.x, ra.z, v);
+        v = fmaf(i2f(dq[1]), Aa.y, v);
+        v = fmaf(N01.y, ra.w, v);
+        v = fmaf(i2f(dq[2]), Ab.x, v);
+        v = fmaf(N23.x, rb.z, v);
+        v = fmaf(i2f(dq[3]), Ab.y, v);
+        v = fmaf(N23.y, rb.w, v);
+        acc[0] = v;
+      } else {
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        if (m < M) {
-          const uint8_t* xr = xs + m * RS;
-          const int xo = 128 * h + 32 * cl;
-          const uint4 x0 = lds128(xr + xo), x1 = lds128(xr + xo + 16);
-          const uint4 x2 = lds128(xr + xo + 64), x3 = lds128(xr + xo + 80);
-          const float4 ra = lds128f(xr + 256 + 16 * (4 * h + cl)), rb = lds128f(xr + 256 + 16 * (4 * h + cl + 2));
-          float v = acc[m];
-          // (q - 32) . x: integer dot, then -32 * A * sum(x) in fp32
-          v = fmaf(i2f(dot16<false>(c0, x0, 0)), A[0] * ra.x, v);
-          v = fmaf(-32.0f * A[0], ra.z, v);
-          v = fmaf(i2f(dot16<false>(c1, x1, 0)), A[1] * ra.x, v);
-          v = fmaf(-32.0f * A[1], ra.w, v);
-          v = fmaf(i2f(dot16<false>(c2, x2, 0)), A[2] * rb.x, v);
-          v = fmaf(-32.0f * A[2], rb.z, v);
-          v = fmaf(i2f(dot16<false>(c3, x3, 0)), A[3] * rb.x, v);
-          v = fmaf(-32.0f * A[3], rb.w, v);
-          acc[m] = v;
+        for (int m = 0; m < MT; m += 2) {
+          if (m < M) {  // tokens in pairs (an unused second token's sum is dropped)
+            int q0[4], q1[4];
+            float4 ra0, rb0, ra1, rb1;
+            dots(m, q0, ra0, rb0);
+            dots(m + 1, q1, ra1, rb1);
+            const float2 xa = f2(ra0.x, ra1.x), xb = f2(rb0.x, rb1.x);
+            float2 v = f2(acc[m], acc[m + 1]);
+            v = fma2(f2(i2f(q0[0]), i2f(q1[0])), mul2(f2(A01.x, A01.x), xa), v);
+            v = fma2(f2(N01.x, N01.x), f2(ra0.z, ra1.z), v);
+            v = fma2(f2(i2f(q0[1]), i2f(q1[1])), mul2(f2(A01.y, A01.y), xa), v);
+            v = fma2(f2(N01.y, N01.y), f2(ra0.w, ra1.w), v);
+            v = fma2(f2(i2f(q0[2]), i2f(q1[2])), mul2(f2(A23.x, A23.x), xb), v);
+            v = fma2(f2(N23.x, N23.x), f2(rb0.z, rb1.z), v);
+            v = fma2(f2(i2f(q0[3]), i2f(q1[3])), mul2(f2(A23.y, A23.y), xb), v);
+            v = fma2(f2(N23.y, N23.y), f2(rb0.w, rb1.w), v);
+            acc[m] = v.x;
+            acc[m + 1] = v.y;
+          }
         }
       }
     }
@@ -563,14 +628,30 @@ __device__ __forceinline__ void unit_q8_q8_0(const uint8_t* __restrict__ sl, con
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const uint4 q0 = lds128(sl + 16 + 32 * j), q1 = lds128(sl + 32 + 32 * j);
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      if (m < M) {
-        const uint8_t* xr = xs + m * RS;
+    auto dot = [&](int m, float& dx) {
+      const uint8_t* xr = xs + m * RS;
+      const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
+      dx = *reinterpret_cast<const float*>(xr + 256 + 16 * j);
+      return dot16<false>(q1, x1, dot16<false>(q0, x0, 0));
+    };
+    if (MT == 1) {
+      if (M > 0) {
+        const uint8_t* xr = xs;
         const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
         const float dx = *reinterpret_cast<const float*>(xr + 256 + 16 * j);
         const int dd = dot16<false>(q1, x1, dot16<false>(q0, x0, 0));
-        acc[m] = fmaf(i2f(dd), dw[j] * dx, acc[m]);
+        acc[0] = fmaf(i2f(dd), dw[j] * dx, acc[0]);
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < MT; m += 2) {
+        if (m < M) {  // tokens in pairs (an unused second token's sum is dropped)
+          float dx0, dx1;
+          const int d0 = dot(m, dx0), d1 = dot(m + 1, dx1);
+          const float2 v = fma2(f2(i2f(d0), i2f(d1)), mul2(f2(dw[j], dw[j]), f2(dx0, dx1)), f2(acc[m], acc[m + 1]));
+          acc[m] = v.x;
+          acc[m + 1] = v.y;
+        }
       }
     }
   }
@@ -586,16 +667,34 @@ __device__ __forceinline__ void unit_q8_q4_0(const uint8_t* __restrict__ sl, con
   for (int j = 0; j < 8; ++j) {
     const uint4 q = lds128(sl + 16 + 16 * j);
     const uint4 lo = and4(q, 0x0F0F0F0Fu), hi = and4(q, 0xF0F0F0F0u);  // hi kept x16
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      if (m < M) {
-        const uint8_t* xr = xs + m * RS;
+    // (q - 8) . x = lo . x0 + (hi . x1) / 16 - 8 * sum(x); the division is exact
+    auto dot = [&](int m, float2& r) {
+      const uint8_t* xr = xs + m * RS;
+      const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
+      r = *reinterpret_cast<const float2*>(xr + 256 + 16 * j);  // dx, sdx
+      return dot16<false>(lo, x0, 0) + (dot16<true>(hi, x1, 0) >> 4);
+    };
+    if (MT == 1) {
+      if (M > 0) {
+        const uint8_t* xr = xs;
         const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
         const float2 r = *reinterpret_cast<const float2*>(xr + 256 + 16 * j);  // dx, sdx
-        // (q - 8) . x = lo . x0 + (hi . x1) / 16 - 8 * sum(x); the division is exact
         const int dd = dot16<false>(lo, x0, 0) + (dot16<true>(hi, x1, 0) >> 4);
-        float v = fmaf(i2f(dd), dw[j] * r.x, acc[m]);
-        acc[m] = fmaf(-8.0f * dw[j], r.y, v);
+        float v = fmaf(i2f(dd), dw[j] * r.x, acc[0]);
+        acc[0] = fmaf(-8.0f * dw[j], r.y, v);
+      }
+    } else {
+      const float n8 = -8.0f * dw[j];
+#pragma unroll
+      for (int m = 0; m < MT; m += 2) {
+        if (m < M) {  // tokens in pairs (an unused second token's sum is dropped)
+          float2 r0, r1;
+          const int d0 = dot(m, r0), d1 = dot(m + 1, r1);
+          float2 v = fma2(f2(i2f(d0), i2f(d1)), mul2(f2(dw[j], dw[j]), f2(r0.x, r1.x)), f2(acc[m], acc[m + 1]));
+          v = fma2(f2(n8, n8), f2(r0.y, r1.y), v);
+          acc[m] = v.x;
+          acc[m + 1] = v.y;
+        }
       }
     }
   }
@@ -650,16 +749,34 @@ __device__ __forceinline__ void unit_q8_legacy(const uint8_t* __restrict__ sl, c
       lo = and4(q, 0x0F0F0F0Fu);
       hi = and4(q, 0xF0F0F0F0u);  // kept x16
     }
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      if (m < M) {
-        const uint8_t* xr = xs + m * RS;
+    auto dot = [&](int m, float2& r) {
+      const uint8_t* xr = xs + m * RS;
+      const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
+      r = *reinterpret_cast<const float2*>(xr + 256 + 16 * j);  // dx, sdx
+      return FIVE ? dot16<false>(lo, x0, dot16<false>(hi, x1, 0))
+                  : dot16<false>(lo, x0, 0) + (dot16<true>(hi, x1, 0) >> 4);  // exact division
+    };
+    if (MT == 1) {
+      if (M > 0) {
+        const uint8_t* xr = xs;
         const uint4 x0 = lds128(xr + 32 * j), x1 = lds128(xr + 32 * j + 16);
         const float2 r = *reinterpret_cast<const float2*>(xr + 256 + 16 * j);  // dx, sdx
         const int dd = FIVE ? dot16<false>(lo, x0, dot16<false>(hi, x1, 0))
                             : dot16<false>(lo, x0, 0) + (dot16<true>(hi, x1, 0) >> 4);  // exact division
-        float v = fmaf(i2f(dd), dw[j] * r.x, acc[m]);
-        acc[m] = fmaf(bw[j], r.y, v);
+        float v = fmaf(i2f(dd), dw[j] * r.x, acc[0]);
+        acc[0] = fmaf(bw[j], r.y, v);
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < MT; m += 2) {
+        if (m < M) {  // tokens in pairs (an unused second token's sum is dropped)
+          float2 r0, r1;
+          const int d0 = dot(m, r0), d1 = dot(m + 1, r1);
+          float2 v = fma2(f2(i2f(d0), i2f(d1)), mul2(f2(dw[j], dw[j]), f2(r0.x, r1.x)), f2(acc[m], acc[m + 1]));
+          v = fma2(f2(bw[j], bw[j]), f2(r0.y, r1.y), v);
+          acc[m] = v.x;
+          acc[m + 1] = v.y;
+        }
       }
     }
   }
@@ -800,20 +917,22 @@ __device__ __forceinline__ float scale_byte_rt(float d, float nd23, uint32_t w, 
   return fmaf(d, __int_as_float(__byte_perm(w, 0x4Bu, 0x4550u | b)), nd23);
 }
 // acc += D * (A_row * dx_token) [- C_row * sdx_token], the four elements of a
-// tile, in the dp4a units' order of operations
+// tile, in the dp4a units' order of operations; the two tokens of a row as
+// one packed pair
 template <bool MIN>
 __device__ __forceinline__ void tc_apply(float* acc, const int (&d)[4], float A0, float A1, float C0, float C1,
                                          float dx0, float dx1, float s0, float s1) {
-  acc[0] = fmaf(i2f(d[0]), A0 * dx0, acc[0]);
-  acc[1] = fmaf(i2f(d[1]), A0 * dx1, acc[1]);
-  acc[2] = fmaf(i2f(d[2]), A1 * dx0, acc[2]);
-  acc[3] = fmaf(i2f(d[3]), A1 * dx1, acc[3]);
+  const float2 dx = f2(dx0, dx1), sx = f2(s0, s1);
+  float2 v0 = fma2(f2(i2f(d[0]), i2f(d[1])), mul2(f2(A0, A0), dx), f2(acc[0], acc[1]));
+  float2 v1 = fma2(f2(i2f(d[2]), i2f(d[3])), mul2(f2(A1, A1), dx), f2(acc[2], acc[3]));
   if (MIN) {
-    acc[0] = fmaf(-C0, s0, acc[0]);
-    acc[1] = fmaf(-C0, s1, acc[1]);
-    acc[2] = fmaf(-C1, s0, acc[2]);
-    acc[3] = fmaf(-C1, s1, acc[3]);
+    v0 = fma2(f2(-C0, -C0), sx, v0);
+    v1 = fma2(f2(-C1, -C1), sx, v1);
   }
+  acc[0] = v0.x;
+  acc[1] = v0.y;
+  acc[2] = v1.x;
+  acc[3] = v1.y;
 }
 
 // Q4_K / Q5_K header of one row (the unpacking of unit_q8_q4k): d, dmin and
@@ -887,15 +1006,15 @@ __device__ __forceinline__ void unit_tc(const uint8_t* __restrict__ st, int half
             }
           int d[4];
           mma_k32(d, a[0][0], a[1][0], a[0][1], a[1][1], b0, b1);
-          float A[2], C[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const KHead& k = hd[mt][h];
-            const uint32_t scw = j < 4 ? k.scL : k.scH, mnw = j < 4 ? k.mnL : k.mnH;
-            A[h] = scale_byte_rt(k.d, k.nd, scw, j & 3);
-            C[h] = scale_byte_rt(k.dmin, k.nm, mnw, j & 3);
-          }
-          tc_apply<true>(acc + 4 * mt, d, A[0], A[1], C[0], C[1], r0.x, r1.x, r0.y, r1.y);
+          // the scale and min of block j for rows g and g + 8, as pairs
+          const KHead& k0 = hd[mt][0];
+          const KHead& k1 = hd[mt][1];
+          auto mag = [&](uint32_t w) { return __int_as_float(__byte_perm(w, 0x4Bu, 0x4550u | (j & 3))); };
+          const float2 A = fma2(f2(k0.d, k1.d), f2(mag(j < 4 ? k0.scL : k0.scH), mag(j < 4 ? k1.scL : k1.scH)),
+                                f2(k0.nd, k1.nd));
+          const float2 C = fma2(f2(k0.dmin, k1.dmin), f2(mag(j < 4 ? k0.mnL : k0.mnH), mag(j < 4 ? k1.mnL : k1.mnH)),
+                                f2(k0.nm, k1.nm));
+          tc_apply<true>(acc + 4 * mt, d, A.x, A.y, C.x, C.y, r0.x, r1.x, r0.y, r1.y);
         }
       }
     }
@@ -968,17 +1087,20 @@ __device__ __forceinline__ void unit_tc(const uint8_t* __restrict__ st, int half
           int d0[4], d1[4];
           mma_k16(d0, a[0][0], a[1][0], b0);  // values 0..15 of the block
           mma_k16(d1, a[0][1], a[1][1], b1);  // values 16..31
-          // per element: values 0..15 with their scale and -32 * sum, then 16..31
+          // per element: values 0..15 with their scale and -32 * sum, then
+          // 16..31; row h's two tokens as one packed pair
           float* ac = acc + 4 * mt;
+          const float2 dx = f2(r0.x, r1.x), slo = f2(r0.z, r1.z), shi = f2(r0.w, r1.w);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int h = e >> 1;
-            const float dx = (e & 1) ? r1.x : r0.x;
-            const float slo = (e & 1) ? r1.z : r0.z, shi = (e & 1) ? r1.w : r0.w;
-            float v = fmaf(i2f(d0[e]), A[h][0] * dx, ac[e]);
-            v = fmaf(-32.0f * A[h][0], slo, v);
-            v = fmaf(i2f(d1[e]), A[h][1] * dx, v);
-            ac[e] = fmaf(-32.0f * A[h][1], shi, v);
+          for (int h = 0; h < 2; ++h) {
+            const float n0 = -32.0f * A[h][0], n1 = -32.0f * A[h][1];
+            float2 v = fma2(f2(i2f(d0[2 * h]), i2f(d0[2 * h + 1])), mul2(f2(A[h][0], A[h][0]), dx),
+                            f2(ac[2 * h], ac[2 * h + 1]));
+            v = fma2(f2(n0, n0), slo, v);
+            v = fma2(f2(i2f(d1[2 * h]), i2f(d1[2 * h + 1])), mul2(f2(A[h][1], A[h][1]), dx), v);
+            v = fma2(f2(n1, n1), shi, v);
+            ac[2 * h] = v.x;
+            ac[2 * h + 1] = v.y;
           }
         }
       }
