@@ -40,6 +40,14 @@ constexpr int BAR_BYTES = 1024;           // mbarriers
 constexpr int MAX_STAGES = 16;
 constexpr int MAX_MT = 8;
 constexpr int SMEM_PER_CTA = 54 * 1024;   // four CTAs per SM
+// Weight stages the producer fills before the activations are on their way
+// when the kernel quantises fp32 activations itself: the rest wait until
+// every consumer warp has issued its activation loads, so those loads are not
+// queued in HBM behind a whole ring of weight copies (headline Q4_K
+// 4096x14336: 8.02 -> 7.63 us; one early stage: 8.33).  Pre-quantized records
+// come from L2, written by the kernel before: there all stages go out at once
+// (holding two back cost the decode step 1%).
+constexpr int EARLY_STAGES = 2;
 constexpr int XR_BUDGET = 24 * 1024;      // staged activations per CTA
 // One staged (span, token): 256 fp32 values, then 16 fp32 sums of 16 values.
 // ACT_Q8 rewrites it in place as 256 codes followed by 8 XRec (one per
@@ -291,10 +299,12 @@ __device__ __forceinline__ void q8_quantize2(const float (&vv)[2][8], uint8_t* c
 // together) -- no shared-memory copy of the fp32 values, no barrier between
 // load and quantisation; the records' bytes equal stage_acts'.
 template <int MT>
-__device__ __forceinline__ void stage_q8_direct(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr) {
+__device__ __forceinline__ void stage_q8_direct(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr,
+                                                uint64_t* xbar) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int off = 32 * (lane >> 2) + 8 * (lane & 3);
   const int nrec = nsp * a.M;
+  if (warp >= nrec && lane == 0) mbar_arrive(xbar);  // no records: nothing to issue
   for (int r0 = warp; r0 < nrec; r0 += 2 * NCW) {
     const bool two = r0 + NCW < nrec;
     uint8_t* rec[2];
@@ -312,6 +322,7 @@ __device__ __forceinline__ void stage_q8_direct(const GemvArgs& a, int kb0, int 
       vv[i][0] = v0.x; vv[i][1] = v0.y; vv[i][2] = v0.z; vv[i][3] = v0.w;
       vv[i][4] = v1.x; vv[i][5] = v1.y; vv[i][6] = v1.z; vv[i][7] = v1.w;
     }
+    if (r0 == warp && lane == 0) mbar_arrive(xbar);  // the first loads are in flight
     q8_quantize2(vv, rec, two, lane);
   }
   consumer_sync();
@@ -324,12 +335,12 @@ __device__ __forceinline__ void stage_q8_direct(const GemvArgs& a, int kb0, int 
 // a time -- their second inputs loaded together -- and quantises them.
 template <bool F32, int MT>
 __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr,
-                                           float* __restrict__ fuse_smem) {
+                                           float* __restrict__ fuse_smem, uint64_t* xbar) {
   const int tid = threadIdx.x;  // 0..127
   const int warp = tid >> 5, lane = tid & 31;
   const bool vec = (a.K & 3) == 0 && (a.ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
   if (!F32 && vec && !a.fu.swiglu && !a.fu.norm_w) {
-    stage_q8_direct<MT>(a, kb0, nsp, xr);
+    stage_q8_direct<MT>(a, kb0, nsp, xr, xbar);
     return;
   }
   // 64 chunks of 4 values per (span, token): threads 0-63 take even tokens, 64-127 odd
@@ -342,6 +353,7 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
       copy4(xr + (j * MT + m) * stage_stride(false, MT) + 16 * q, a.x + (int64_t)m * a.ldx + (nvalid ? k : 0), nvalid, vec);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
+  if ((threadIdx.x & 31) == 0) mbar_arrive(xbar);  // this warp's copies are in flight
   if (a.fu.norm_w) row_rms<MT>(a, fuse_smem, fuse_smem + MT);  // overlaps the copies
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   consumer_sync();
@@ -414,7 +426,7 @@ __device__ __forceinline__ void stage_acts(const GemvArgs& a, int kb0, int nsp, 
 // xr + (j * MT + m) * Q8_REC_BYTES.
 template <int MT>
 __device__ __forceinline__ void stage_records(const GemvArgs& a, int kb0, int nsp, uint8_t* __restrict__ xr,
-                                              float* __restrict__ fuse_smem) {
+                                              float* __restrict__ fuse_smem, uint64_t* xbar) {
   constexpr int V = Q8_REC_BYTES / 16;  // 16-byte pieces per record
   const int per_span = a.M * V;
   for (int c = threadIdx.x; c < nsp * per_span; c += NCW * 32) {
@@ -424,6 +436,7 @@ __device__ __forceinline__ void stage_records(const GemvArgs& a, int kb0, int ns
                a.recs + ((int64_t)(kb0 + j) * a.rec_ld + m) * Q8_REC_BYTES + 16 * v, 16);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
+  if ((threadIdx.x & 31) == 0) mbar_arrive(xbar);  // this warp's copies are in flight
   if (a.fu.rec_scale) row_rms<MT>(a, fuse_smem, fuse_smem + MT);  // overlaps the copies
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   consumer_sync();
@@ -1190,6 +1203,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 template <int MT>
 struct SmemMap {
   static constexpr int redbar = 512;
+  static constexpr int xbar = 520;  // the consumers' "activation loads issued" barrier
   static constexpr int fuse = 768;  // GemvFuse scratch: rms[MT], partial sums[4][MT]
   static constexpr int red = BAR_BYTES;
   static constexpr int part = red + 2 * UNIT_ROWS * MT * 4;
@@ -1274,6 +1288,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
   uint64_t* redbar = reinterpret_cast<uint64_t*>(smem + SmemMap<MT>::redbar);
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + SmemMap<MT>::xbar);
   float* red = reinterpret_cast<float*>(smem + SmemMap<MT>::red);
   float* part = reinterpret_cast<float*>(smem + SmemMap<MT>::part);
   uint8_t* xr = smem + SmemMap<MT>::xr(pl.C);
@@ -1308,6 +1323,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     // of the other ranks' partials (64 rows x M tokens fp32 each), which
     // their st.async pushes count down as they land.
     if (pl.C > 1) mbar_init(redbar, 1);
+    mbar_init(xbar, NCW);  // one arrival per consumer warp
     fence_mbar_init();
     if (pl.C > 1 && rank == 0) mbar_arrive_expect_tx(redbar, (uint32_t)((pl.C - 1) * UNIT_ROWS * a.M * 4));
   }
@@ -1328,7 +1344,11 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     if (lane == 0) {
       pdl_launch_dependents();
       const int first = nsp < S ? nsp : S;
+      const int early = (PRE || first < EARLY_STAGES) ? first : EARLY_STAGES;
       for (int i = 0; i < first; ++i) {
+        // stages past the early ones once the activation loads are issued
+        // (a wait that gives up is recorded, and the copies still go out)
+        if (i == early) mbar_wait(xbar, 0, a.err, ERR_EMPTY_WAIT);
         mbar_arrive_expect_tx(&full[i], UB);
         bulk_g2s(ring + i * SB, wsrc + (int64_t)i * UB, UB, &full[i]);
       }
@@ -1358,9 +1378,9 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   // ---------------- consumers
   pdl_wait();  // x is written by earlier kernels on the stream; y may be read by them
   if (PRE)
-    stage_records<MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
+    stage_records<MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse), xbar);
   else
-    stage_acts<F32, MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse));
+    stage_acts<F32, MT>(a, kb0, nsp, xr, reinterpret_cast<float*>(smem + SmemMap<MT>::fuse), xbar);
   // L2 lookahead: the ring holds units 0..S-1; ask L2 for units S..2S-1 now
   // that the activations are staged (asked for earlier, these bytes queue
   // ahead of the activation loads and delay them), so HBM streams them while
