@@ -137,7 +137,9 @@ int run_gemv(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int
   if (pre && !ext_recs)
     CK(launch_act_q8_records(d_x, ldx, M, K, reinterpret_cast<uint8_t*>(err) + WS_HEADER, pdl, s),
        "act_q8_records launch");
-  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current(), pre);
+  // the reduce-scatter serves products whose epilogue only stores y
+  const bool rs_ok = !sc && !(fu && (fu->ssq_out || fu->rec_out));
+  const GemvPlan plan = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current(), pre, rs_ok);
   if (plan.C == 0)
     return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
   for (int64_t m0 = 0; m0 < M; m0 += plan.mt) {

@@ -53,6 +53,7 @@ struct GemvPlan {
   int smem_bytes;    // dynamic shared memory per CTA
   int mt;            // tokens per pass (template instantiation)
   int pre;           // activations arrive as Q8 records (Q8_REC_BYTES), quantized beforehand
+  int rs;            // the cluster reduce-scatters (every rank writes 64/C rows; needs C a power of two)
 };
 
 // Output scatter of a row shard into every rank's gathered buffer (the
@@ -114,7 +115,8 @@ struct GemvArgs {
 // Plan for dtype / tokens / fp32-activation mode on a device with num_sms SMs.
 // pre: the activations are quantized beforehand into Q8 records (ACT_Q8
 // only), so a record takes Q8_REC_BYTES of shared memory, not the fp32 staging.
-GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms, bool pre = false);
+GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms, bool pre = false,
+                        bool rs_ok = false);
 cudaError_t launch_gemv(int dt, bool f32act, const GemvPlan& plan, const GemvArgs& a, bool pdl,
                         cudaStream_t s);
 

@@ -11,7 +11,7 @@ static int tokens_per_pass(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 
 // distributed-shared-memory reduction per tile.  Estimated time in units of
 // one span, per CTA slot: waves * (chunk + 1) (+ half a CTA of tail when the
 // grid needs more than one wave) (+ the reduction and cluster cost).
-GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms, bool pre) {
+GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int num_sms, bool pre, bool rs_ok) {
   GemvPlan p{};
   p.G = (int)((N + UNIT_ROWS - 1) / UNIT_ROWS);
   p.KB = (int)((K + UNIT_COLS - 1) / UNIT_COLS);
@@ -56,12 +56,22 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
     }
     p.mt /= 2;
   }
+  // Multi-token passes whose epilogue only stores y reduce-scatter across
+  // the cluster: each rank receives the partials of 64/C rows only, which
+  // keeps the receive buffer at one tile whatever C is (8-token passes with
+  // C = 8 needed 16 KB there and ran three CTAs per SM; reduce-scattered,
+  // four: Q4_K 4096x11008 M = 8 19.3 -> 14.4 us).  One-token passes keep the
+  // gather to rank 0: there the other ranks exit as soon as they have
+  // pushed, and the next launch's CTAs take their slots (reduce-scattered,
+  // the headline took 7.9 us instead of 7.6).
+  p.rs = (rs_ok && p.mt >= 2 && p.C > 1 && (p.C & (p.C - 1)) == 0) ? 1 : 0;
   p.xq_bytes = (p.chunk * p.mt * stage_stride(p.pre, p.mt) + 127) / 128 * 128;
   p.stage_bytes = (unit_bytes(dt) + 127) / 128 * 128;
-  const int xr_off = p.mt == 1 ? SmemMap<1>::xr(p.C)
-                     : p.mt == 2 ? SmemMap<2>::xr(p.C)
-                     : p.mt == 4 ? SmemMap<4>::xr(p.C)
-                                 : SmemMap<8>::xr(p.C);
+  const bool rs = p.rs != 0;
+  const int xr_off = p.mt == 1 ? SmemMap<1>::xr(p.C, rs)
+                     : p.mt == 2 ? SmemMap<2>::xr(p.C, rs)
+                     : p.mt == 4 ? SmemMap<4>::xr(p.C, rs)
+                                 : SmemMap<8>::xr(p.C, rs);
   const int ring_off = xr_off + p.xq_bytes;
   int st = (SMEM_PER_CTA - ring_off) / p.stage_bytes;
   if (st > MAX_STAGES) st = MAX_STAGES;
@@ -90,6 +100,13 @@ static cudaError_t launch_t(const GemvPlan& pl, const GemvArgs& a, bool pdl, cud
   if (!attr_set[dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
     if (e != cudaSuccess) return e;
+    // multi-token passes: the whole unified L1 / shared array as shared
+    // memory, four CTAs of up to SMEM_MAX_CTA per SM (the kernel reads
+    // nothing through L1)
+    if (MT >= 2) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) return e;
+    }
     attr_set[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};

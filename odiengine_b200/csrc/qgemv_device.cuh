@@ -39,7 +39,8 @@ constexpr int CTAS_PER_SM = 4;
 constexpr int BAR_BYTES = 1024;           // mbarriers
 constexpr int MAX_STAGES = 16;
 constexpr int MAX_MT = 8;
-constexpr int SMEM_PER_CTA = 54 * 1024;   // four CTAs per SM
+constexpr int SMEM_PER_CTA = 54 * 1024;   // the ring is sized to this
+constexpr int SMEM_MAX_CTA = 56 * 1024;   // four CTAs per SM (228 KB less 1 KB reserved per CTA)
 // Weight stages the producer fills before the activations are on their way
 // when the kernel quantises fp32 activations itself: the rest wait until
 // every consumer warp has issued its activation loads, so those loads are not
@@ -1193,21 +1194,31 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 // Shared-memory layout of one CTA (offsets in bytes; the host plan holds
 // xr_off and ring_off):
 //   [0, 512)                mbarriers full[16], empty[16]
-//   [512, 520)              reduction mbarrier (rank 0 of a cluster)
-//   red   [2][64][MT] fp32  the two unit-parity sums of each row
-//   part  [C][MT*64] fp32   tile partials; rank 0 receives those of the other
-//                           ranks here over distributed shared memory
+//   [512, 520)              reduction mbarrier
+//   red   [2][64][MT] fp32  (one-token passes) the two unit-parity sums of
+//                           each row
+//   part  partials received over distributed shared memory:
+//         [C][MT][64] fp32  rank 0 gathers the other ranks' tiles, or
+//         [C][MT][64/C]     with the reduce-scatter (pl.rs), every rank the
+//                           C partials of its own 64/C rows
 //   xr    chunk x MT records of stage_stride(PRE, MT) bytes
 //         bytes: staged activations
 //   ring  stages x stage_bytes weight units
+// Multi-token passes write the two unit-parity sums of each row ([64][MT]
+// fp32 each) into ring slots 0 and 1 instead, after a barrier of all
+// consumers: every unit has been consumed, so nothing lands there or is read
+// there after it (4 KB less shared memory at 8 tokens).
 template <int MT>
 struct SmemMap {
+  static constexpr bool red_in_ring = MT >= 2;
   static constexpr int redbar = 512;
   static constexpr int xbar = 520;  // the consumers' "activation loads issued" barrier
   static constexpr int fuse = 768;  // GemvFuse scratch: rms[MT], partial sums[4][MT]
   static constexpr int red = BAR_BYTES;
-  static constexpr int part = red + 2 * UNIT_ROWS * MT * 4;
-  static constexpr int xr(int C) { return (part + C * UNIT_ROWS * MT * 4 + 127) / 128 * 128; }
+  static constexpr int part = red + (red_in_ring ? 0 : 2 * UNIT_ROWS * MT * 4);
+  static constexpr int xr(int C, bool rs) {
+    return (part + (rs ? 1 : C) * UNIT_ROWS * MT * 4 + 127) / 128 * 128;
+  }
 };
 
 // One output element: to y, or -- for a row shard -- to every rank's gathered
@@ -1289,12 +1300,16 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   uint64_t* empty = full + MAX_STAGES;
   uint64_t* redbar = reinterpret_cast<uint64_t*>(smem + SmemMap<MT>::redbar);
   uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + SmemMap<MT>::xbar);
-  float* red = reinterpret_cast<float*>(smem + SmemMap<MT>::red);
   float* part = reinterpret_cast<float*>(smem + SmemMap<MT>::part);
-  uint8_t* xr = smem + SmemMap<MT>::xr(pl.C);
+  uint8_t* xr = smem + SmemMap<MT>::xr(pl.C, pl.rs);
   uint8_t* ring = xr + pl.xq_bytes;
   constexpr int UB = unit_bytes(DT);
   const int S = pl.stages, SB = pl.stage_bytes;
+  // the unit-parity row sums, [64][MT] each: their own region, or ring slots
+  // 0 and 1 (multi-token passes)
+  float* const red0 = SmemMap<MT>::red_in_ring ? reinterpret_cast<float*>(ring)
+                                                : reinterpret_cast<float*>(smem + SmemMap<MT>::red);
+  float* const red1 = SmemMap<MT>::red_in_ring ? reinterpret_cast<float*>(ring + SB) : red0 + UNIT_ROWS * MT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x / pl.C, rank = blockIdx.x - g * pl.C;
   const int kb0 = rank * pl.chunk;
@@ -1325,7 +1340,10 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
     if (pl.C > 1) mbar_init(redbar, 1);
     mbar_init(xbar, NCW);  // one arrival per consumer warp
     fence_mbar_init();
-    if (pl.C > 1 && rank == 0) mbar_arrive_expect_tx(redbar, (uint32_t)((pl.C - 1) * UNIT_ROWS * a.M * 4));
+    if (MT >= 2 && pl.rs)  // every rank receives the other ranks' partials of its 64/C rows
+      mbar_arrive_expect_tx(redbar, (uint32_t)((pl.C - 1) * (UNIT_ROWS / pl.C) * a.M * 4));
+    else if (pl.C > 1 && rank == 0)
+      mbar_arrive_expect_tx(redbar, (uint32_t)((pl.C - 1) * UNIT_ROWS * a.M * 4));
   }
   __syncthreads();
   // Cluster barrier, split: arrive now, wait only before the first remote
@@ -1416,42 +1434,77 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   }
 
   // Tile reduction: unit parities (fixed order) -> CTA partial -> ranks (fixed
-  // order).  Ranks other than 0 push their partial into rank 0's shared
-  // memory as asynchronous float4 stores counted on rank 0's reduction
-  // mbarrier; rank 0 waits, adds, writes y.
+  // order).  Partials travel as asynchronous float4 stores into the
+  // receiver's shared memory, counted on its reduction mbarrier.  Plain
+  // multi-token passes (pl.rs) reduce-scatter: rank j receives the C partials
+  // of rows [j 64/C, (j+1) 64/C), adds them in rank order and writes those
+  // rows.  Otherwise ranks other than 0 push their whole partial to rank 0,
+  // which adds in rank order and writes y -- the same sums either way.
+  // Ring slots 0 and 1 are free once every consumer is past its last unit
+  // (the two warps of a pair share their slots: the barrier keeps one warp's
+  // sums off rows its partner may still be reading).
+  if (SmemMap<MT>::red_in_ring) consumer_sync();
+  float* const redu = up ? red1 : red0;
   if constexpr (TC) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {  // row 32 (warp & 1) + 16 (i >> 2) + 8 ((i >> 1) & 1) + g, token 2t + (i & 1)
       const int r = 32 * (warp & 1) + 16 * (i >> 2) + 8 * ((i >> 1) & 1) + (lane >> 2), m = 2 * (lane & 3) + (i & 1);
-      if (m < a.M) red[(up * UNIT_ROWS + r) * MT + m] = acc[i];
+      if (m < a.M) redu[r * MT + m] = acc[i];
     }
   } else {
 #pragma unroll
     for (int m = 0; m < MT; ++m)
-      if (m < a.M) red[(up * UNIT_ROWS + row) * MT + m] = acc[m];
+      if (m < a.M) redu[row * MT + m] = acc[m];
   }
   consumer_sync();
   const int tid = threadIdx.x;
   if (pl.C > 1) cluster_wait();
+  if (MT >= 2 && pl.rs) {  // (one-token passes never reduce-scatter: compiled out)
+    const int RB = UNIT_ROWS / pl.C, R4 = RB / 4;  // rows per rank; float4s per (rank, token)
+    for (int u = tid; u < pl.C * a.M * R4; u += NCW * 32) {
+      const int q = u / (a.M * R4), rem = u - q * a.M * R4, m = rem / R4, rq = 4 * (rem - m * R4);
+      const int r0 = q * RB + rq;
+      float4 v;
+      v.x = red0[r0 * MT + m] + red1[r0 * MT + m];
+      v.y = red0[(r0 + 1) * MT + m] + red1[(r0 + 1) * MT + m];
+      v.z = red0[(r0 + 2) * MT + m] + red1[(r0 + 2) * MT + m];
+      v.w = red0[(r0 + 3) * MT + m] + red1[(r0 + 3) * MT + m];
+      float* dst = part + (rank * MT + m) * RB + rq;  // slot `rank` of rank q's part
+      if (q == rank)
+        *reinterpret_cast<float4*>(dst) = v;
+      else
+        st_async_v4(dsmem_addr(dst, q), v, dsmem_addr(redbar, q));
+    }
+    mbar_wait_cluster(redbar, 0, a.err, ERR_REDUCE_WAIT);
+    consumer_sync();  // this rank's own slot, written by other threads
+    for (int t = tid; t < a.M * RB; t += NCW * 32) {
+      const int m = t / RB, r = t - m * RB;
+      float v = part[m * RB + r];
+      for (int q = 1; q < pl.C; ++q) v += part[(q * MT + m) * RB + r];
+      const int64_t n = (int64_t)g * UNIT_ROWS + rank * RB + r;
+      if (n < a.N) store_out(a, m, n, v);
+    }
+    return;
+  }
   if (pl.C > 1 && rank != 0) {
     for (int u = tid; u < 16 * a.M; u += NCW * 32) {
       const int t0 = 4 * u, m = t0 >> 6, r0 = t0 & 63;
       float4 v;
-      v.x = red[(0 * UNIT_ROWS + r0) * MT + m] + red[(1 * UNIT_ROWS + r0) * MT + m];
-      v.y = red[(0 * UNIT_ROWS + r0 + 1) * MT + m] + red[(1 * UNIT_ROWS + r0 + 1) * MT + m];
-      v.z = red[(0 * UNIT_ROWS + r0 + 2) * MT + m] + red[(1 * UNIT_ROWS + r0 + 2) * MT + m];
-      v.w = red[(0 * UNIT_ROWS + r0 + 3) * MT + m] + red[(1 * UNIT_ROWS + r0 + 3) * MT + m];
+      v.x = red0[r0 * MT + m] + red1[r0 * MT + m];
+      v.y = red0[(r0 + 1) * MT + m] + red1[(r0 + 1) * MT + m];
+      v.z = red0[(r0 + 2) * MT + m] + red1[(r0 + 2) * MT + m];
+      v.w = red0[(r0 + 3) * MT + m] + red1[(r0 + 3) * MT + m];
       st_async_v4(dsmem_addr(part + rank * UNIT_ROWS * MT + t0, 0), v, dsmem_addr(redbar, 0));
     }
   } else {
     for (int t = tid; t < UNIT_ROWS * a.M; t += NCW * 32) {
       const int m = t >> 6, r = t & 63;
-      const float v = red[(0 * UNIT_ROWS + r) * MT + m] + red[(1 * UNIT_ROWS + r) * MT + m];
+      const float v = red0[r * MT + m] + red1[r * MT + m];
       if (pl.C == 1) {
         const int64_t n = (int64_t)g * UNIT_ROWS + r;
         const float nv = n < a.N ? store_out(a, m, n, v) : 0.f;
-        if (a.fu.ssq_out) red[(0 * UNIT_ROWS + r) * MT + m] = nv * nv;  // the slots this thread just read
-        if (a.fu.rec_out) red[(1 * UNIT_ROWS + r) * MT + m] = nv;
+        if (a.fu.ssq_out) red0[r * MT + m] = nv * nv;  // the slots this thread just read
+        if (a.fu.rec_out) red1[r * MT + m] = nv;
       } else {
         part[t] = v;
       }
@@ -1459,11 +1512,11 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
   }
   if (pl.C == 1 && a.fu.ssq_out) {
     consumer_sync();
-    write_ssq(a, red, MT, 1, g, pl.G);
+    write_ssq(a, red0, MT, 1, g, pl.G);
   }
   if (pl.C == 1 && a.fu.rec_out) {
     consumer_sync();
-    write_records(a, red + UNIT_ROWS * MT, MT, g);
+    write_records(a, red1, MT, g);
   }
   if (pl.C > 1) {
     if (rank == 0) {
@@ -1476,7 +1529,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
         const int64_t n = (int64_t)g * UNIT_ROWS + r;
         const float nv = n < a.N ? store_out(a, m, n, v) : 0.f;
         if (a.fu.ssq_out) part[t] = nv * nv;  // the slot this thread just read
-        if (a.fu.rec_out) red[(UNIT_ROWS + r) * MT + m] = nv;  // red is free by now
+        if (a.fu.rec_out) red1[r * MT + m] = nv;  // red1 is free by now
       }
       if (a.fu.ssq_out) {
         consumer_sync();
@@ -1484,7 +1537,7 @@ __global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM) qgemv_kernel(const Gemv
       }
       if (a.fu.rec_out) {
         consumer_sync();
-        write_records(a, red + UNIT_ROWS * MT, MT, g);
+        write_records(a, red1, MT, g);
       }
       if (a.sc.n) {
         consumer_sync();
