@@ -165,6 +165,25 @@ int odi_cuda_quantize_q8_0(const float* d_x, void* d_blocks, int64_t M, int64_t 
  * (1024 + ceil(M/256)*256 * ceil(K/256)*256 * 2 bytes). */
 size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t K, int act_mode);
 
+/* How the streaming GEMV splits one product of M tokens (ODI_CUDA_ACT_Q8 /
+ * ODI_CUDA_ACT_F32, or ACT_AUTO below ODI_CUDA_TC_MIN_TOKENS), for sizing and
+ * diagnosis: the same plan odi_cuda_matmul launches for a product whose
+ * epilogue only stores y.  Host arithmetic only (no device is touched; without
+ * one the SM count is taken as 148).  A diagnostic of this backend, with no
+ * counterpart in the reference. */
+typedef struct odi_cuda_gemv_plan {
+  int tokens_per_pass;  /* tokens per launch: 1, 2, 4 or 8 */
+  int passes;           /* launches for the M tokens */
+  int cluster;          /* CTAs per 64-row tile (thread-block cluster size) */
+  int spans_per_cta;    /* 256-column spans each CTA streams */
+  int stages;           /* weight ring depth (units in flight per CTA) */
+  int reduce_scatter;   /* 1: the cluster reduce-scatters its partials */
+  int ctas_per_sm;      /* CTAs of this shared-memory size resident per SM (4 is the design point) */
+  int64_t ctas;         /* CTAs per launch */
+  size_t shared_bytes;  /* dynamic shared memory per CTA */
+} odi_cuda_gemv_plan;
+int odi_cuda_gemv_plan_info(int dtype, int64_t M, int64_t N, int64_t K, int act_mode, odi_cuda_gemv_plan* out);
+
 /* 1 if `dtype` has the tensor-core (ODI_CUDA_ACT_F16) path, else 0. */
 int odi_cuda_tc_supported(int dtype);
 

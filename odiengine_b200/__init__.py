@@ -72,6 +72,7 @@ SIGNATURES = {
     "odi_cuda_quantize_weight": (_int, [_int, _vp, _vp, _i64, _i64, _vp]),
     "odi_cuda_quantize_q8_0": (_int, [_vp, _vp, _i64, _i64, _vp]),
     "odi_cuda_matmul_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _int]),
+    "odi_cuda_gemv_plan_info": (_int, [_int, _i64, _i64, _i64, _int, _vp]),
     "odi_cuda_matmul": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp]),
     "odi_cuda_matmul_fused": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _int, _vp, _vp]),
     "odi_cuda_workspace_status": (_int, [_vp, ctypes.POINTER(_int), _vp]),
@@ -146,6 +147,21 @@ class Q8RecOpts(ctypes.Structure):
     _fields_ = [("accumulate", ctypes.c_int), ("out_ssq", ctypes.c_void_p), ("norm_ssq", ctypes.c_void_p),
                 ("norm_ssq_count", ctypes.c_int), ("norm_eps", ctypes.c_float), ("out_records", ctypes.c_void_p),
                 ("out_norm_weight", ctypes.c_void_p), ("out_swiglu", ctypes.c_int)]
+
+
+class GemvPlan(ctypes.Structure):
+    """odi_cuda_gemv_plan (include/odi_cuda.h)."""
+
+    _fields_ = [("tokens_per_pass", ctypes.c_int), ("passes", ctypes.c_int), ("cluster", ctypes.c_int),
+                ("spans_per_cta", ctypes.c_int), ("stages", ctypes.c_int), ("reduce_scatter", ctypes.c_int),
+                ("ctas_per_sm", ctypes.c_int), ("ctas", ctypes.c_int64), ("shared_bytes", ctypes.c_size_t)]
+
+
+def gemv_plan(dtype: int, M: int, N: int, K: int, act_mode: int = 0) -> "GemvPlan":
+    """The streaming GEMV's work split for one product (host arithmetic)."""
+    p = GemvPlan()
+    check(lib().odi_cuda_gemv_plan_info(dtype, M, N, K, act_mode, ctypes.byref(p)))
+    return p
 
 
 class Scatter(ctypes.Structure):

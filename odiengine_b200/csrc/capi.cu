@@ -342,6 +342,32 @@ size_t odi_cuda_matmul_workspace_bytes(int dtype, int64_t M, int64_t N, int64_t 
   return WS_HEADER;  // the device error word; one token's activations are staged on chip
 }
 
+int odi_cuda_gemv_plan_info(int dtype, int64_t M, int64_t N, int64_t K, int act_mode, odi_cuda_gemv_plan* out) {
+  int rc = check_shape(dtype, N, K);
+  if (rc) return rc;
+  if (!out) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "null output");
+  if (M < 1 || M > (1 << 20)) return fail(ODI_CUDA_ERR_INVALID_ARGUMENT, "invalid M=%lld", (long long)M);
+  const int mode = resolve_act_mode(dtype, M, act_mode);
+  if (mode != ODI_CUDA_ACT_Q8 && mode != ODI_CUDA_ACT_F32)
+    return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "act_mode %d does not run on the streaming GEMV", act_mode);
+  const bool f32 = mode == ODI_CUDA_ACT_F32;
+  // as run_gemv with the workspace odi_cuda_matmul_workspace_bytes asks for
+  const GemvPlan p = make_gemv_plan(dtype, N, K, (int)(M < 8 ? M : 8), f32, num_sms_current(),
+                                    wants_records(f32, M, nullptr), true);
+  if (p.C == 0)
+    return fail(ODI_CUDA_ERR_NOT_IMPLEMENTED, "K=%lld too large for the on-chip activation stage", (long long)K);
+  out->tokens_per_pass = p.mt;
+  out->passes = (int)((M + p.mt - 1) / p.mt);
+  out->cluster = p.C;
+  out->spans_per_cta = p.chunk;
+  out->stages = p.stages;
+  out->reduce_scatter = p.rs;
+  out->ctas_per_sm = p.ctas_per_sm;
+  out->ctas = (int64_t)p.G * p.C;
+  out->shared_bytes = (size_t)p.smem_bytes;
+  return ODI_CUDA_OK;
+}
+
 int odi_cuda_matmul(int dtype, const void* d_w_tiled, const float* d_x, float* d_y, int64_t M, int64_t N,
                     int64_t K, int act_mode, void* d_workspace, size_t workspace_bytes, int flags,
                     void* stream) {

@@ -54,6 +54,7 @@ struct GemvPlan {
   int mt;            // tokens per pass (template instantiation)
   int pre;           // activations arrive as Q8 records (Q8_REC_BYTES), quantized beforehand
   int rs;            // the cluster reduce-scatters (every rank writes 64/C rows; needs C a power of two)
+  int ctas_per_sm;   // CTAs of smem_bytes that fit one SM (up to the launch bound)
 };
 
 // Output scatter of a row shard into every rank's gathered buffer (the

@@ -85,6 +85,9 @@ GemvPlan make_gemv_plan(int dt, int64_t N, int64_t K, int M, bool f32act, int nu
   if (st < 2) st = 2;
   p.stages = st;
   p.smem_bytes = ring_off + p.stages * p.stage_bytes;
+  // 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
+  const int fit = (CTAS_PER_SM * (SMEM_MAX_CTA + 1024)) / (p.smem_bytes + 1024);
+  p.ctas_per_sm = fit < CTAS_PER_SM ? fit : CTAS_PER_SM;
   return p;
 }
 
